@@ -1,0 +1,634 @@
+"""Benchmark of the HeadStartLSTM hot path on B200 (one JSON line on rank 0).
+
+Default workload (``--config cfg4``): configs[4] of the benchmark, the
+long-sequence parallel (Heinsen-scan) training step, T=16384, B=256 (global),
+D=512, H=1024, a=0, fp32, fwd + backward of sum(out*G).  The batch is split
+across ranks (strong scaling: the global batch is fixed) and each rank runs
+its share as micro-batches of 32 sequences with gradients accumulated, then
+one NCCL all-reduce SUM of the weight gradients.  Inputs are seeded
+synthetic data with the config's distributions (no dataset exists).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfgX]
+    python bench.py --impl reference ...   # CPU reference arm (the oracle port)
+
+``value``: tokens/s (T*B per step, whole job) with inputs resident in HBM,
+timed with CUDA events on the launching stream, max over ranks.
+``e2e``: the same step through the public module API with the step's inputs
+copied from pinned host memory and the loss read back, inside the timed
+region.  ``roofline``: the dominant kernel of the step, from CUDA events
+around each library call inside the timed region.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+CONFIGS = {
+    "cfg0": dict(T=32, B=16, D=64, H=128, mode="recurrent", a=1e-4),
+    "cfg1": dict(T=128, B=32, D=256, H=256, mode="parallel", a=0.0),
+    "cfg2": dict(T=256, B=32, D=256, H=512, mode="recurrent", a=1e-4),
+    "cfg3": dict(T=64, B=32, D=1024, H=2048, mode="recurrent", a_uniform=(0.0, 0.5)),
+    "cfg4": dict(T=16384, B=256, D=512, H=1024, mode="parallel", a=0.0, bias_spread=8.0),
+}
+MICRO_BATCH = 32
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def _traffic(kernel: str, units: float):
+    """DRAM bytes per launch of `kernel`, scaled from the committed ncu summary
+    (profiles/traffic.json: bytes per element at a captured size)."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(p):
+        return None
+    d = json.load(open(p))
+    e = d.get(kernel)
+    if not e:
+        return None
+    return e["bytes_per_unit"] * units
+
+
+# ------------------------------------------------------------------ inputs
+def make_params(cfg, dtype=torch.float32):
+    from oracle.hs_oracle import init_params  # parameter draw only (as reset_parameters)
+
+    gen = torch.Generator().manual_seed(0)
+    D, H = cfg["D"], cfg["H"]
+    W_ih, W_hh, b_ih, b_hh, a = init_params(D, H, a_init=cfg.get("a", 1e-4), generator=gen,
+                                            dtype=dtype)
+    if "a_uniform" in cfg:
+        a.uniform_(*cfg["a_uniform"], generator=gen)
+    if "bias_spread" in cfg:
+        s = cfg["bias_spread"]
+        b_ih[0:2 * H].uniform_(-s, s, generator=gen)
+    return W_ih, W_hh, b_ih, b_hh, a
+
+
+def make_data(cfg, B_local, rank, dev, mb=None):
+    """x ~ N(0,1) [T,B,D] and G ~ N(0,1) [T,B,H] for this rank.  With `mb`,
+    returned as lists of contiguous micro-batches of mb sequences each."""
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    if mb is None:
+        x = torch.randn(cfg["T"], B_local, cfg["D"], device=dev, generator=g)
+        G = torch.randn(cfg["T"], B_local, cfg["H"], device=dev, generator=g)
+        return x, G
+    n = B_local // mb
+    xs = [torch.randn(cfg["T"], mb, cfg["D"], device=dev, generator=g) for _ in range(n)]
+    Gs = [torch.randn(cfg["T"], mb, cfg["H"], device=dev, generator=g) for _ in range(n)]
+    return xs, Gs
+
+
+# ------------------------------------------------------------------ clocks
+def _gpu_id(dev):
+    """nvidia-smi selector of this device (its UUID), robust to CUDA_VISIBLE_DEVICES."""
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return str(dev.index or 0)
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.strip().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        load = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ our arm
+class ParallelStep:
+    """One parallel-mode training step on this rank through the C ABI, with
+    CUDA events around every library call (the kernel breakdown)."""
+
+    def __init__(self, cfg, params, B_local, dev):
+        from prlstm_b200 import _lib
+
+        self.L = _lib
+        self.cfg = cfg
+        self.dev = dev
+        T, D, H = cfg["T"], cfg["D"], cfg["H"]
+        self.mb = min(MICRO_BATCH, B_local)
+        assert B_local % self.mb == 0
+        self.nmb = B_local // self.mb
+        self.W_ih = params[0].to(dev).contiguous()
+        self.b_ih = params[2].to(dev).contiguous()
+        mb = self.mb
+        self.z = torch.empty(T, mb, 4 * H, device=dev)
+        self.out = torch.empty(T, mb, H, device=dev)
+        self.c = torch.empty(T, mb, H, device=dev)
+        self.c0 = torch.zeros(mb, H, device=dev)
+        self.h_n = torch.empty(mb, H, device=dev)
+        self.c_n = torch.empty(mb, H, device=dev)
+        self.dx = torch.empty(T, mb, D, device=dev)
+        self.dW = torch.zeros(4 * H, D, device=dev)
+        self.db = torch.zeros(4 * H, device=dev)
+        self.dW_mb = torch.empty(4 * H, D, device=dev)
+        self.db_mb = torch.empty(4 * H, device=dev)
+        lib = _lib.load()
+        self.ws = _lib.workspace(lib.hs_scan_workspace_bytes(T, mb, H), dev)
+        self.status = _lib.status_word(dev)
+        self.names = ("proj_gemm", "scan_fwd", "scan_bwd", "dgrad_gemm", "wgrad_gemm")
+        self.ms = {n: 0.0 for n in self.names}
+        self.launches = 0
+
+    def run(self, x, G, record=False):
+        L, P = self.L, self.L.ptr
+        T, D, H = self.cfg["T"], self.cfg["D"], self.cfg["H"]
+        mb = self.mb
+        st = L.stream_ptr(self.dev)
+        M = T * mb
+        evs = []
+        for i in range(self.nmb):
+            xs, Gs = x[i], G[i]
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(6)] if record else None
+            if record:
+                e[0].record()
+            L.call("hs_linear_forward", P(xs), P(self.W_ih), P(self.b_ih), P(self.z), M, 4 * H, D, st)
+            if record:
+                e[1].record()
+            L.call("hs_scan_forward", P(self.z), P(self.c0), P(self.out), P(self.c), P(self.h_n),
+                   P(self.c_n), T, mb, H, 1e-6, P(self.ws), self.ws.numel(), P(self.status), st)
+            if record:
+                e[2].record()
+            L.call("hs_scan_backward", P(self.z), P(self.c), P(self.c0), P(Gs), None, None,
+                   P(self.z), None, P(self.db_mb), T, mb, H, 1e-6, P(self.ws), self.ws.numel(),
+                   P(self.status), st)
+            if record:
+                e[3].record()
+            L.call("hs_linear_dgrad", P(self.z), P(self.W_ih), P(self.dx), M, 4 * H, D, st)
+            if record:
+                e[4].record()
+            L.call("hs_linear_wgrad", P(self.z), P(xs), P(self.dW), M, 4 * H, D, 1 if i else 0, st)
+            if record:
+                e[5].record()
+            self.db.add_(self.db_mb) if i else self.db.copy_(self.db_mb)
+            self.launches += 6  # proj, scan_fwd, scan_bwd, rowsum, dgrad, wgrad
+            if record:
+                evs.append(e)
+        return evs
+
+    def collect(self, evs):
+        for e in evs:
+            for k, n in enumerate(self.names):
+                self.ms[n] += e[k].elapsed_time(e[k + 1])
+
+    def units(self, kernel):
+        T, D, H, mb = self.cfg["T"], self.cfg["D"], self.cfg["H"], self.mb
+        if kernel in ("scan_fwd", "scan_bwd"):
+            return T * mb * H
+        return 2.0 * T * mb * 4 * H * D  # flops of one GEMM launch
+
+
+def run_ours(args, cfg, rank, world, dev):
+    import torch.distributed as dist
+
+    import prlstm_b200
+    from prlstm_b200 import _lib
+
+    T, D, H = cfg["T"], cfg["D"], cfg["H"]
+    B_global = cfg["B"]
+    if cfg["mode"] == "parallel":
+        assert B_global % world == 0
+        B_local = B_global // world
+    else:
+        B_local = B_global  # recurrent configs: every rank runs the full config (replicas)
+    params = make_params(cfg)
+    if cfg["mode"] == "parallel":
+        x, G = make_data(cfg, B_local, rank, dev, mb=min(MICRO_BATCH, B_local))
+    else:
+        x, G = make_data(cfg, B_local, rank, dev)
+    peak_hbm, peak_tf, peak_kind = _peaks()
+
+    def allreduce(tensors):
+        if world > 1:
+            for t in tensors:
+                dist.all_reduce(t, op=dist.ReduceOp.SUM)
+
+    def sync():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    result = {}
+    if cfg["mode"] == "parallel":
+        step = ParallelStep(cfg, params, B_local, dev)
+        for _ in range(args.warmup):
+            step.run(x, G)
+            allreduce([step.dW, step.db])
+        sync()
+        _lib.check_device_status(dev)
+        step.ms = {n: 0.0 for n in step.names}
+        step.launches = 0
+        clocks = ClockSampler(_gpu_id(dev))
+        clocks.start()
+        sync()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        allev = []
+        for _ in range(args.steps):
+            allev.extend(step.run(x, G, record=True))
+            allreduce([step.dW, step.db])
+        t1.record()
+        sync()
+        ck = clocks.stop()
+        ms = t0.elapsed_time(t1)
+        step.collect(allev)
+        _lib.check_device_status(dev)
+        ms = max_over_ranks(ms)
+        tokens = T * B_global * args.steps
+        result["value"] = tokens / (ms / 1e3)
+        result["ms_per_step"] = ms / args.steps
+        result["gpu_launches"] = step.launches
+        result["clocks"] = ck
+        nl = args.steps * step.nmb
+        kern = {}
+        for n in step.names:
+            avg_ms = step.ms[n] / nl
+            if n.startswith("scan"):
+                per_unit = 24.0 if n == "scan_fwd" else 40.0
+                ach = per_unit * step.units(n) / (avg_ms / 1e3) / 1e9
+                kern[n] = {"bound": "hbm", "avg_ms": avg_ms, "achieved": ach, "unit": "GB/s",
+                           "frac": ach / peak_hbm, "share": step.ms[n] / max(1e-9, sum(step.ms.values()))}
+            else:
+                ach = step.units(n) / (avg_ms / 1e3) / 1e12
+                kern[n] = {"bound": "tensor", "avg_ms": avg_ms, "achieved": ach, "unit": "TFLOP/s",
+                           "frac": ach / peak_tf, "share": step.ms[n] / max(1e-9, sum(step.ms.values()))}
+        dom = max(kern, key=lambda n: kern[n]["share"])
+        d = kern[dom]
+        units = step.units(dom)
+        per = {"scan_fwd": 24.0, "scan_bwd": 40.0}.get(dom)
+        result["roofline"] = {
+            "kernel": dom, "bound": d["bound"], "achieved": round(d["achieved"], 2),
+            "peak": peak_hbm if d["bound"] == "hbm" else peak_tf, "unit": d["unit"],
+            "frac": round(d["frac"], 4), "peak_kind": peak_kind,
+            "traffic": _traffic(dom, units),
+            "algorithmic_per_launch": (per * units) if per else units,
+        }
+        result["kernels"] = {n: {k: (round(v, 4) if isinstance(v, float) else v) for k, v in kern[n].items()}
+                             for n in kern}
+        scan = {n: kern[n] for n in ("scan_fwd", "scan_bwd")}
+        tot_ms = scan["scan_fwd"]["avg_ms"] + scan["scan_bwd"]["avg_ms"]
+        ach = 64.0 * step.units("scan_fwd") / (tot_ms / 1e3) / 1e9
+        result["scan_roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak_hbm,
+                                   "unit": "GB/s", "frac": round(ach / peak_hbm, 4),
+                                   "peak_kind": peak_kind}
+        del step
+        torch.cuda.empty_cache()
+        # ---------------- e2e through the public module API, host buffers
+        result["e2e"] = e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync,
+                                     max_over_ranks, allreduce)
+    else:
+        result.update(run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync,
+                                    max_over_ranks, allreduce, peak_tf, peak_kind))
+    return result
+
+
+def e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync, max_over_ranks, allreduce):
+    import prlstm_b200
+
+    T, D, H = cfg["T"], cfg["D"], cfg["H"]
+    mb = min(MICRO_BATCH, B_local)
+    nmb = B_local // mb
+    m = prlstm_b200.HeadStartLSTM(D, H, parallel=True).to(dev)
+    with torch.no_grad():
+        for p, v in zip(m.parameters(), params):
+            p.copy_(v)
+    # the step's inputs, in pinned host memory, one buffer per micro-batch
+    hx = [t.cpu().pin_memory() for t in x]
+    hG = [t.cpu().pin_memory() for t in G]
+    x.clear()
+    G.clear()
+    torch.cuda.empty_cache()
+    loss_host = torch.empty(1, pin_memory=True)
+    copy_stream = torch.cuda.Stream(dev)
+
+    def one_step():
+        m.zero_grad(set_to_none=True)
+        loss = torch.zeros((), device=dev)
+        # double-buffered host->device copies on a side stream
+        nxt = None
+        with torch.cuda.stream(copy_stream):
+            nxt = (hx[0].to(dev, non_blocking=True), hG[0].to(dev, non_blocking=True))
+            ev = torch.cuda.Event()
+            ev.record()
+        for i in range(nmb):
+            torch.cuda.current_stream(dev).wait_event(ev)
+            xd, Gd = nxt
+            xd.requires_grad_(True)
+            xd.record_stream(torch.cuda.current_stream(dev))
+            Gd.record_stream(torch.cuda.current_stream(dev))
+            if i + 1 < nmb:
+                with torch.cuda.stream(copy_stream):
+                    nxt = (hx[i + 1].to(dev, non_blocking=True), hG[i + 1].to(dev, non_blocking=True))
+                    ev = torch.cuda.Event()
+                    ev.record()
+            out, _ = m(xd)
+            lo = (out * Gd).sum()
+            lo.backward()
+            loss += lo.detach()
+        grads = [p.grad for p in m.parameters() if p.grad is not None]
+        allreduce(grads)
+        loss_host.copy_(loss.reshape(1), non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        return float(loss_host.item())
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        one_step()
+    sync()
+    steps = max(1, min(args.steps, 5))
+    t0 = time.perf_counter()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        one_step()
+    e1.record()
+    sync()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    h2d = sum(t.numel() * 4 for t in hx) + sum(t.numel() * 4 for t in hG)
+    return {"value": T * cfg["B"] * steps / (ms / 1e3), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "steps": steps}
+
+
+def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_ranks, allreduce,
+                  peak_tf, peak_kind):
+    import prlstm_b200
+    from prlstm_b200 import _lib
+
+    T, D, H = cfg["T"], cfg["D"], cfg["H"]
+    P = _lib.ptr
+    lib = _lib.load()
+    W_ih, W_hh, b_ih, b_hh, a = (t.to(dev).contiguous() for t in params)
+    h_save = torch.empty(T + 1, B_local, H, device=dev)
+    c_save = torch.empty(T + 1, B_local, H, device=dev)
+    acts = torch.empty(T, B_local, 4 * H, device=dev)
+    dx = torch.empty(T, B_local, D, device=dev)
+    dW_ih, dW_hh = torch.empty_like(W_ih), torch.empty_like(W_hh)
+    db_ih, db_hh, da = torch.empty(4 * H, device=dev), torch.empty(4 * H, device=dev), torch.empty(4, device=dev)
+    ws = _lib.workspace(lib.hs_recurrent_workspace_bytes(T, B_local, D, H), dev)
+    status = _lib.status_word(dev)
+    st = _lib.stream_ptr(dev)
+
+    def step(record=False):
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if record else None
+        if record:
+            e[0].record()
+        _lib.call("hs_recurrent_forward", P(x), None, None, P(W_ih), P(W_hh), P(b_ih), P(b_hh),
+                  P(a), P(h_save), P(c_save), P(acts), T, B_local, D, H, P(ws), ws.numel(),
+                  P(status), st)
+        if record:
+            e[1].record()
+        _lib.call("hs_recurrent_backward", P(x), P(W_ih), P(W_hh), P(b_hh), P(a), P(h_save),
+                  P(c_save), P(acts), P(G), None, None, P(dx), P(dW_ih), P(dW_hh), P(db_ih),
+                  P(db_hh), P(da), T, B_local, D, H, P(ws), ws.numel(), P(status), st)
+        if record:
+            e[2].record()
+        allreduce([dW_ih, dW_hh, db_ih, db_hh, da])
+        return e
+
+    for _ in range(args.warmup):
+        step()
+    sync()
+    _lib.check_device_status(dev)
+    clocks = ClockSampler(_gpu_id(dev))
+    clocks.start()
+    sync()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    evs = [step(record=True) for _ in range(args.steps)]
+    t1.record()
+    sync()
+    ck = clocks.stop()
+    _lib.check_device_status(dev)
+    ms = max_over_ranks(t0.elapsed_time(t1))
+    fwd = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
+    bwd = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
+    flops = 24.0 * T * B_local * H * (D + H)
+    tokens = T * B_local * world * args.steps
+    ach = flops / ((fwd + bwd) / 1e3) / 1e12
+    res = {"value": tokens / (ms / 1e3), "ms_per_step": ms / args.steps, "clocks": ck,
+           "gpu_launches": None,
+           "recurrent": {"fwd_ms": fwd, "bwd_ms": bwd, "us_per_step_fwd": fwd * 1e3 / T,
+                         "us_per_step_bwd": bwd * 1e3 / T},
+           "roofline": {"kernel": "recurrent fwd+bwd", "bound": "tensor", "achieved": round(ach, 3),
+                        "peak": peak_tf, "unit": "TFLOP/s", "frac": round(ach / peak_tf, 5),
+                        "peak_kind": peak_kind, "traffic": None}}
+    # e2e through the module API with host buffers
+    m = prlstm_b200.HeadStartLSTM(D, H).to(dev)
+    with torch.no_grad():
+        for p, v in zip(m.parameters(), params):
+            p.copy_(v)
+    hx_ = x.cpu().pin_memory()
+    hG_ = G.cpu().pin_memory()
+    loss_host = torch.empty(1, pin_memory=True)
+
+    def e2e_step():
+        m.zero_grad(set_to_none=True)
+        xd = hx_.to(dev, non_blocking=True).requires_grad_(True)
+        Gd = hG_.to(dev, non_blocking=True)
+        out, _ = m(xd)
+        lo = (out * Gd).sum()
+        lo.backward()
+        allreduce([p.grad for p in m.parameters()])
+        loss_host.copy_(lo.detach().reshape(1), non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+
+    for _ in range(args.warmup):
+        e2e_step()
+    sync()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    sync()
+    ms_e = max_over_ranks(e0.elapsed_time(e1))
+    res["e2e"] = {"value": tokens / (ms_e / 1e3), "unit": "tokens/s",
+                  "h2d_bytes_per_step": (x.numel() + G.numel()) * 4, "d2h_bytes_per_step": 4}
+    # launches per step: proj GEMM, prep, fwd kernel x ceil(B/32), prep, bwd kernel x ceil(B/32),
+    # 2 wgrad, colsum, dgrad, unscale
+    nb = (B_local + 31) // 32
+    res["gpu_launches"] = args.steps * (2 + nb + 1 + nb + 5)
+    return res
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args, cfg):
+    """The reference's CPU algorithm (oracle/hs_oracle.py, a restatement of
+    the reference torch backend / parallel path) on all host cores, on a
+    bounded sample of the workload per step."""
+    from oracle import hs_oracle as O
+
+    ncores = os.cpu_count() or 1
+    torch.set_num_threads(ncores)
+    T, D, H = cfg["T"], cfg["D"], cfg["H"]
+    params = make_params(cfg)
+    if cfg["mode"] == "parallel":
+        Bs = 1 if T >= 4096 else cfg["B"]
+        sample = f"T={T}, B={Bs} of {cfg['B']} sequences per step (tokens/s scales with B)"
+    else:
+        Bs = cfg["B"]
+        sample = f"full config (T={T}, B={Bs})"
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn(T, Bs, D, generator=gen)
+    G = torch.randn(T, Bs, H, generator=gen)
+
+    def step():
+        O.module_forward_backward(params, x, G, parallel=cfg["mode"] == "parallel")
+
+    for _ in range(args.warmup):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = T * Bs * len(times) / total
+    return value, ncores, sample, total / len(times)
+
+
+# ------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="cfg4", choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    metric = "train-step tokens/s (T*B fwd+bwd)"
+    base = {"metric": metric, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "dtype": "f32",
+            "data": "synthetic (seeded, config distributions)", "vs_baseline": None}
+    workload = (f"{args.config}: {cfg['mode']} mode fwd+bwd of sum(out*G), T={cfg['T']}, "
+                f"B={cfg['B']}, D={cfg['D']}, H={cfg['H']}")
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        value, cores, sample, sec = run_reference(args, cfg)
+        line = dict(base, impl="reference", value=value, ms_per_step=sec * 1e3,
+                    scaling="strong" if cfg["mode"] == "parallel" else "weak",
+                    config={"workload": workload, "T": cfg["T"], "B": cfg["B"], "D": cfg["D"],
+                            "H": cfg["H"], "mode": cfg["mode"], "parallelism": "cpu"},
+                    cpu_baseline={"value": value, "unit": "tokens/s", "cores": cores,
+                                  "kind": "port", "sample": sample},
+                    e2e={"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                         "d2h_bytes_per_step": 0},
+                    gpu_launches=0)
+        print(json.dumps(line), flush=True)
+        return
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    res = run_ours(args, cfg, rank, world, dev)
+    line = dict(base)
+    line.update(value=res["value"], ms_per_step=res["ms_per_step"],
+                scaling="strong" if cfg["mode"] == "parallel" else "weak",
+                config={"workload": workload, "T": cfg["T"], "B": cfg["B"], "D": cfg["D"],
+                        "H": cfg["H"], "mode": cfg["mode"],
+                        "micro_batch": MICRO_BATCH if cfg["mode"] == "parallel" else None,
+                        "parallelism": f"dp{world}",
+                        "l2": "inputs larger than L2 (z of one micro-batch is 8.6 GB)"
+                        if args.config == "cfg4" else "no flush; per-step working set noted"},
+                roofline=res.get("roofline"), e2e=res.get("e2e"), clocks=res.get("clocks"),
+                gpu_launches=res.get("gpu_launches"))
+    for k in ("kernels", "scan_roofline", "recurrent"):
+        if k in res:
+            line[k] = res[k]
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ref_args = argparse.Namespace(warmup=1, steps=2)
+        value, cores, sample, _ = run_reference(ref_args, cfg)
+        line["cpu_baseline"] = {"value": value, "unit": "tokens/s", "cores": cores,
+                                "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,177 @@
+/*
+ * headstartlstm_b200.h -- C ABI of the B200 (sm_100a) HeadStartLSTM library.
+ *
+ * The library implements the two hot paths of HeadStartLSTM
+ * (m-j-tilley/prLSTM, package `headstartlstm`):
+ *   - the recurrent cell: input projection, per-step a-scaled W_hh.h
+ *     recurrence with the sigmoid-g cell, and its BPTT backward;
+ *   - the parallel=True Heinsen scan over time, forward and backward.
+ *
+ * Conventions
+ *   - Every pointer is a DEVICE pointer to contiguous row-major fp32 data
+ *     unless stated otherwise.  Shapes use T (time), B (batch), D (input
+ *     features), H (hidden units); the gate axis has 4H entries in the order
+ *     [i, f, g, o] (nn.LSTM order).
+ *   - Ownership: the caller allocates every tensor and every workspace.  The
+ *     library never allocates or frees device memory.
+ *   - Streams: every call is asynchronous and stream-ordered on `stream`
+ *     (a cudaStream_t; NULL means the legacy default stream).
+ *   - Status: 0 (HS_OK) on success, else an HS_ERR_* code.  Argument checks
+ *     run on the host before any launch; a call that fails them launches
+ *     nothing.  Device-side failures (a bounded wait that gave up) are
+ *     recorded in the caller's `dev_status` word (a device int, sticky: the
+ *     first nonzero code stays until the caller clears it) and can be read
+ *     with hs_read_status().
+ *   - Workspace: calls that need scratch take (`workspace`, `workspace_bytes`);
+ *     the matching *_workspace_bytes() query returns the size to allocate.
+ *     Calls that overlap on the GPU must not share a workspace.
+ */
+#ifndef HEADSTARTLSTM_B200_H
+#define HEADSTARTLSTM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *hs_stream_t; /* == cudaStream_t */
+
+#if defined(__GNUC__)
+#define HS_API __attribute__((visibility("default")))
+#else
+#define HS_API
+#endif
+
+enum {
+  HS_OK = 0,
+  HS_ERR_INVALID_ARG = 1,   /* bad shape, null pointer or misaligned buffer   */
+  HS_ERR_WORKSPACE = 2,     /* workspace missing or smaller than required     */
+  HS_ERR_UNSUPPORTED = 3,   /* shape outside what the kernels implement       */
+  HS_ERR_CUDA = 4,          /* a CUDA runtime call or launch failed           */
+  HS_ERR_DEVICE_TIMEOUT = 5 /* a device-side bounded wait gave up             */
+};
+
+/* Library identity and diagnostics. */
+HS_API int hs_abi_version(void);
+HS_API const char *hs_status_string(int status);
+/* Text of the last host-side error on the calling thread (never NULL). */
+HS_API const char *hs_last_error_message(void);
+/* Copy the device status word to *host_status (synchronises `stream`). */
+HS_API int hs_read_status(const int *dev_status, int *host_status, hs_stream_t stream);
+/* Reset the device status word to HS_OK (stream-ordered). */
+HS_API int hs_clear_status(int *dev_status, hs_stream_t stream);
+/* Failure-detection self test: launches one CTA that waits on *flag (a
+ * device word nothing sets) with the library's bounded wait, shortened to
+ * limit_ns.  The wait gives up, records HS_ERR_DEVICE_TIMEOUT in *dev_status
+ * and the kernel returns; the context stays usable.  No reference counterpart
+ * (the reference has no device-side waits). */
+HS_API int hs_selftest_bounded_wait(const unsigned *flag, int *dev_status, uint64_t limit_ns,
+                                    hs_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Linear-layer GEMMs (fp32 in, fp32 out, fp32-accurate).
+ * Replace the cuBLAS/ATen calls of the reference:
+ *   forward projection  F.linear(x, W_ih, b_ih)   _torch.py:96, _parallel.py:56,
+ *                                                  _triton.py:345
+ *   input gradient      dgates_flat @ W_ih         _torch.py:162, _triton.py:456
+ *   weight gradients    dgates_flat.t() @ h / x    _torch.py:157-158, _triton.py:451-452
+ *   bias gradient       dgates_flat.sum(dim=0)     _torch.py:159, _triton.py:453
+ * ---------------------------------------------------------------------- */
+/* y[M,N] = x[M,K] . w[N,K]^T (+ bias[N] if bias != NULL) */
+HS_API int hs_linear_forward(const float *x, const float *w, const float *bias, float *y,
+                      int64_t M, int64_t N, int64_t K, hs_stream_t stream);
+/* dx[M,K] = dy[M,N] . w[N,K] */
+HS_API int hs_linear_dgrad(const float *dy, const float *w, float *dx,
+                    int64_t M, int64_t N, int64_t K, hs_stream_t stream);
+/* dw[N,K] = beta * dw + dy[M,N]^T . x[M,K]   (beta is 0 or 1) */
+HS_API int hs_linear_wgrad(const float *dy, const float *x, float *dw,
+                    int64_t M, int64_t N, int64_t K, int beta, hs_stream_t stream);
+/* db[N] = beta * db + sum_m dy[m, N]   (beta is 0 or 1) */
+HS_API int hs_colsum(const float *dy, float *db, int64_t M, int64_t N, int beta,
+              hs_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Parallel (Heinsen) path.  Replaces headstartlstm_parallel and
+ * _log_parallel_scan (_parallel.py:21-74) and the autograd backward the
+ * reference traces through them.  c_t = max(f_t,eps) c_{t-1} + max(i_t g_t,eps)
+ * with c_{-1} = max(c0, eps), out_t = o_t tanh(c_t).
+ * ---------------------------------------------------------------------- */
+HS_API size_t hs_scan_workspace_bytes(int64_t T, int64_t B, int64_t H);
+
+/* Fused gate activations + chunked scan over T (single pass, decoupled
+ * look-back).  z [T,B,4H] gate pre-activations (x W_ih^T + b_ih);
+ * c0 [B,H] (NULL = zeros).  Writes out [T,B,H], c [T,B,H] (kept for the
+ * backward), h_n [B,H], c_n [B,H] (either may be NULL). */
+HS_API int hs_scan_forward(const float *z, const float *c0, float *out, float *c, float *h_n,
+                    float *c_n, int64_t T, int64_t B, int64_t H, float eps,
+                    void *workspace, size_t workspace_bytes, int *dev_status,
+                    hs_stream_t stream);
+
+/* Reverse-time scan of the gradient.  dout [T,B,H] = dL/dout; dh_n, dc_n
+ * [B,H] (NULL = zeros) are the gradients of h_n and c_n.  Writes dz [T,B,4H]
+ * (may alias z: each element is read before it is overwritten by the same
+ * thread), dc0 [B,H] (NULL = not wanted) and db [4H] = sum over (t,b) of dz
+ * (NULL = not wanted; reduced deterministically from per-chunk sums). */
+HS_API int hs_scan_backward(const float *z, const float *c, const float *c0, const float *dout,
+                     const float *dh_n, const float *dc_n, float *dz, float *dc0,
+                     float *db, int64_t T, int64_t B, int64_t H, float eps,
+                     void *workspace, size_t workspace_bytes, int *dev_status,
+                     hs_stream_t stream);
+
+/* Whole parallel-mode forward: z = x W_ih^T + b_ih (z is caller-owned
+ * [T,B,4H] scratch kept for the backward), then hs_scan_forward. */
+HS_API int hs_parallel_forward(const float *x, const float *c0, const float *w_ih,
+                        const float *b_ih, float *z, float *out, float *c, float *h_n,
+                        float *c_n, int64_t T, int64_t B, int64_t D, int64_t H, float eps,
+                        void *workspace, size_t workspace_bytes, int *dev_status,
+                        hs_stream_t stream);
+
+/* Whole parallel-mode backward.  z is overwritten with dz.  Outputs:
+ * dx [T,B,D] (NULL = not wanted), dw_ih [4H,D], db_ih [4H], dc0 [B,H] (NULL =
+ * not wanted).  The reference returns no gradient for W_hh, b_hh, a and h0
+ * in this mode (_parallel.py:41-43); neither does this call. */
+HS_API int hs_parallel_backward(const float *x, const float *w_ih, float *z, const float *c,
+                         const float *c0, const float *dout, const float *dh_n,
+                         const float *dc_n, float *dx, float *dw_ih, float *db_ih,
+                         float *dc0, int64_t T, int64_t B, int64_t D, int64_t H, float eps,
+                         void *workspace, size_t workspace_bytes, int *dev_status,
+                         hs_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Recurrent path.  Replaces HeadStartLSTMTorchFn / HeadStartLSTMTritonFn
+ * (_torch.py:78-176, _triton.py:327-470) and the C++ headstartlstm_forward
+ * (_csrc/lstm_cell.cpp:28-78).
+ * ---------------------------------------------------------------------- */
+HS_API size_t hs_recurrent_workspace_bytes(int64_t T, int64_t B, int64_t D, int64_t H);
+
+/* Whole recurrent forward.  Inputs x [T,B,D], h0/c0 [B,H] (NULL = zeros),
+ * w_ih [4H,D], w_hh [4H,H], b_ih/b_hh [4H], a [4].  Outputs:
+ *   h_save [T+1,B,H]  (h_save[0]=h0; out = h_save[1:], h_n = h_save[T])
+ *   c_save [T+1,B,H]  (c_n = c_save[T])
+ *   acts   [T,B,4H]   gate activations i,f,g,o kept for the backward. */
+HS_API int hs_recurrent_forward(const float *x, const float *h0, const float *c0,
+                         const float *w_ih, const float *w_hh, const float *b_ih,
+                         const float *b_hh, const float *a, float *h_save, float *c_save,
+                         float *acts, int64_t T, int64_t B, int64_t D, int64_t H,
+                         void *workspace, size_t workspace_bytes, int *dev_status,
+                         hs_stream_t stream);
+
+/* Whole recurrent backward (hand-written BPTT, _torch.py:133-170).
+ * acts is overwritten with dgates.  dout [T,B,H]; dh_n, dc_n [B,H] (NULL =
+ * zeros).  Outputs dx [T,B,D] (NULL = not wanted), dw_ih [4H,D], dw_hh [4H,H],
+ * db_ih [4H], db_hh [4H], da [4].  Like the reference, no gradient for h0/c0. */
+HS_API int hs_recurrent_backward(const float *x, const float *w_ih, const float *w_hh,
+                          const float *b_hh, const float *a, const float *h_save,
+                          const float *c_save, float *acts, const float *dout,
+                          const float *dh_n, const float *dc_n, float *dx, float *dw_ih,
+                          float *dw_hh, float *db_ih, float *db_hh, float *da,
+                          int64_t T, int64_t B, int64_t D, int64_t H,
+                          void *workspace, size_t workspace_bytes, int *dev_status,
+                          hs_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HEADSTARTLSTM_B200_H */

@@ -1,0 +1,186 @@
+// C ABI of the library: argument checks, status handling, the linear-layer
+// GEMM entry points and the whole-path parallel-mode calls.
+// (Declarations and reference citations: include/headstartlstm_b200.h.)
+#include <stdarg.h>
+#include <string.h>
+
+#include "hs_common.cuh"
+
+namespace hs {
+
+namespace {
+thread_local char g_msg[512] = "";
+}
+
+int fail(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char *what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return HS_OK;
+  return fail(HS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int gemm_simt(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
+              int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kcontig, bool b_kcontig,
+              int beta, cudaStream_t st);
+int gemm_tc_try(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
+                int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kcontig, bool b_kcontig,
+                int beta, cudaStream_t st, bool *done);
+int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st);
+int scan_forward(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
+                 int64_t T, int64_t B, int64_t H, float eps, void *ws, size_t ws_bytes,
+                 int *status, cudaStream_t st);
+int scan_backward(const float *z, const float *c, const float *c0, const float *dout,
+                  const float *dh_n, const float *dc_n, float *dz, float *dc0, float *db,
+                  int64_t T, int64_t B, int64_t H, float eps, void *ws, size_t ws_bytes,
+                  int *status, cudaStream_t st);
+
+// One GEMM: tensor-core path when it takes the shape, FFMA path otherwise.
+static int gemm(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
+                int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kc, bool b_kc, int beta,
+                cudaStream_t st) {
+  bool done = false;
+  if (int e = gemm_tc_try(A, B, C, bias, M, N, K, lda, ldb, ldc, a_kc, b_kc, beta, st, &done)) return e;
+  if (done) return HS_OK;
+  return gemm_simt(A, B, C, bias, M, N, K, lda, ldb, ldc, a_kc, b_kc, beta, st);
+}
+
+static int check_gemm(const void *a, const void *b, const void *c, int64_t M, int64_t N, int64_t K) {
+  if (M < 0 || N < 0 || K < 0) return fail(HS_ERR_INVALID_ARG, "negative GEMM extent");
+  if ((M && N && K) && (!a || !b)) return fail(HS_ERR_INVALID_ARG, "null GEMM operand");
+  if (M && N && !c) return fail(HS_ERR_INVALID_ARG, "null GEMM output");
+  return HS_OK;
+}
+
+int linear_forward(const float *x, const float *w, const float *bias, float *y, int64_t M,
+                   int64_t N, int64_t K, cudaStream_t st) {
+  if (int e = check_gemm(x, w, y, M, N, K)) return e;
+  return gemm(x, w, y, bias, M, N, K, K, K, N, true, true, 0, st);
+}
+int linear_dgrad(const float *dy, const float *w, float *dx, int64_t M, int64_t N, int64_t K,
+                 cudaStream_t st) {
+  if (int e = check_gemm(dy, w, dx, M, N, K)) return e;
+  // dx[M,K] = dy[M,N] . w[N,K]: reduction over N; w is K-contiguous = output-contiguous
+  return gemm(dy, w, dx, nullptr, M, K, N, N, K, K, true, false, 0, st);
+}
+int linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t N, int64_t K,
+                 int beta, cudaStream_t st) {
+  if (int e = check_gemm(dy, x, dw, M, N, K)) return e;
+  // dw[N,K] = dy[M,N]^T . x[M,K]: reduction over M; both operands output-contiguous
+  return gemm(dy, x, dw, nullptr, N, K, M, N, K, K, false, false, beta, st);
+}
+
+int parallel_forward(const float *x, const float *c0, const float *w_ih, const float *b_ih,
+                     float *z, float *out, float *c, float *h_n, float *c_n, int64_t T, int64_t B,
+                     int64_t D, int64_t H, float eps, void *ws, size_t ws_bytes, int *status,
+                     cudaStream_t st) {
+  if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return fail(HS_ERR_INVALID_ARG, "T, B, D, H must be positive");
+  if (!x || !w_ih || !z) return fail(HS_ERR_INVALID_ARG, "parallel_forward: null x/w_ih/z");
+  if (int e = linear_forward(x, w_ih, b_ih, z, T * B, 4 * H, D, st)) return e;
+  return scan_forward(z, c0, out, c, h_n, c_n, T, B, H, eps, ws, ws_bytes, status, st);
+}
+
+int parallel_backward(const float *x, const float *w_ih, float *z, const float *c,
+                      const float *c0, const float *dout, const float *dh_n, const float *dc_n,
+                      float *dx, float *dw_ih, float *db_ih, float *dc0, int64_t T, int64_t B,
+                      int64_t D, int64_t H, float eps, void *ws, size_t ws_bytes, int *status,
+                      cudaStream_t st) {
+  if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return fail(HS_ERR_INVALID_ARG, "T, B, D, H must be positive");
+  if (!x || !w_ih || !z || !dw_ih || !db_ih) return fail(HS_ERR_INVALID_ARG, "parallel_backward: null x/w_ih/z/dw_ih/db_ih");
+  if (int e = scan_backward(z, c, c0, dout, dh_n, dc_n, z, dc0, db_ih, T, B, H, eps, ws, ws_bytes, status, st)) return e;
+  if (dx)
+    if (int e = linear_dgrad(z, w_ih, dx, T * B, 4 * H, D, st)) return e;
+  return linear_wgrad(z, x, dw_ih, T * B, 4 * H, D, 0, st);
+}
+
+namespace {
+__global__ void selftest_wait_kernel(const unsigned *flag, int *status, uint64_t limit_ns) {
+  if (threadIdx.x == 0) (void)wait_flag(flag, status, limit_ns);
+}
+}  // namespace
+
+}  // namespace hs
+
+extern "C" {
+
+int hs_abi_version(void) { return 1; }
+
+const char *hs_status_string(int status) {
+  switch (status) {
+    case HS_OK: return "ok";
+    case HS_ERR_INVALID_ARG: return "invalid argument";
+    case HS_ERR_WORKSPACE: return "workspace missing or too small";
+    case HS_ERR_UNSUPPORTED: return "unsupported shape";
+    case HS_ERR_CUDA: return "CUDA error";
+    case HS_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char *hs_last_error_message(void) { return hs::g_msg; }
+
+int hs_read_status(const int *dev_status, int *host_status, hs_stream_t stream) {
+  if (!dev_status || !host_status) return hs::fail(HS_ERR_INVALID_ARG, "null status pointer");
+  if (cudaMemcpyAsync(host_status, dev_status, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream) != cudaSuccess)
+    return hs::check_launch("hs_read_status");
+  if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return hs::check_launch("hs_read_status sync");
+  return HS_OK;
+}
+
+int hs_clear_status(int *dev_status, hs_stream_t stream) {
+  if (!dev_status) return hs::fail(HS_ERR_INVALID_ARG, "null status pointer");
+  if (cudaMemsetAsync(dev_status, 0, sizeof(int), (cudaStream_t)stream) != cudaSuccess)
+    return hs::check_launch("hs_clear_status");
+  return HS_OK;
+}
+
+int hs_selftest_bounded_wait(const unsigned *flag, int *dev_status, uint64_t limit_ns,
+                             hs_stream_t stream) {
+  if (!flag || !dev_status) return hs::fail(HS_ERR_INVALID_ARG, "null flag/status");
+  if (limit_ns > hs::kWaitLimitNs) return hs::fail(HS_ERR_INVALID_ARG, "limit above the library's wait bound");
+  hs::selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flag, dev_status, limit_ns);
+  return hs::check_launch("selftest_wait_kernel");
+}
+
+int hs_linear_forward(const float *x, const float *w, const float *bias, float *y, int64_t M,
+                      int64_t N, int64_t K, hs_stream_t stream) {
+  return hs::linear_forward(x, w, bias, y, M, N, K, (cudaStream_t)stream);
+}
+int hs_linear_dgrad(const float *dy, const float *w, float *dx, int64_t M, int64_t N, int64_t K,
+                    hs_stream_t stream) {
+  return hs::linear_dgrad(dy, w, dx, M, N, K, (cudaStream_t)stream);
+}
+int hs_linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t N, int64_t K,
+                    int beta, hs_stream_t stream) {
+  return hs::linear_wgrad(dy, x, dw, M, N, K, beta, (cudaStream_t)stream);
+}
+int hs_colsum(const float *dy, float *db, int64_t M, int64_t N, int beta, hs_stream_t stream) {
+  if (M < 0 || N < 0 || (N && !db) || (M && N && !dy)) return hs::fail(HS_ERR_INVALID_ARG, "hs_colsum: bad arguments");
+  return hs::colsum(dy, db, M, N, beta, (cudaStream_t)stream);
+}
+
+int hs_parallel_forward(const float *x, const float *c0, const float *w_ih, const float *b_ih,
+                        float *z, float *out, float *c, float *h_n, float *c_n, int64_t T,
+                        int64_t B, int64_t D, int64_t H, float eps, void *workspace,
+                        size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
+  return hs::parallel_forward(x, c0, w_ih, b_ih, z, out, c, h_n, c_n, T, B, D, H, eps, workspace,
+                              workspace_bytes, dev_status, (cudaStream_t)stream);
+}
+
+int hs_parallel_backward(const float *x, const float *w_ih, float *z, const float *c,
+                         const float *c0, const float *dout, const float *dh_n,
+                         const float *dc_n, float *dx, float *dw_ih, float *db_ih, float *dc0,
+                         int64_t T, int64_t B, int64_t D, int64_t H, float eps, void *workspace,
+                         size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
+  return hs::parallel_backward(x, w_ih, z, c, c0, dout, dh_n, dc_n, dx, dw_ih, db_ih, dc0, T, B,
+                               D, H, eps, workspace, workspace_bytes, dev_status,
+                               (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,171 @@
+// fp32 FFMA GEMM for the linear-layer products of HeadStartLSTM.
+//
+// Used for every shape the tensor-core path (gemm_tc.cu) does not take:
+// small or ragged M/N/K (the reference's own test shapes have D=8, H=12),
+// and as the exact-fp32 cross-check of that path.
+//
+// C[M,N] = sum_k A(m,k) B(k,n), with each operand either K-contiguous or
+// M/N-contiguous, covering the three products of a linear layer:
+//   forward  y  = x  w^T    A = x  [M,K] K-contig, B = w [N,K] K-contig
+//   dgrad    dx = dy w      A = dy [M,N] K-contig, B = w [N,K] N-contig
+//   wgrad    dw = dy^T x    A = dy [M,N] M-contig, B = x [M,K] N-contig
+// 128x128 output tile per 256-thread CTA, 8x8 outputs per thread, k-step 8,
+// register-prefetched double buffering of the shared-memory tiles.
+#include "hs_common.cuh"
+
+namespace hs {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 8, NT = 256;
+
+struct GemmArgs {
+  const float *A, *B;
+  float *C;
+  const float *bias;   // [N] or null
+  int64_t M, N, K;
+  int64_t lda, ldb, ldc;
+  int a_kcontig, b_kcontig;
+  int beta;            // 0 or 1: C = beta*C + A.B (+bias)
+};
+
+__device__ __forceinline__ float ldA(const GemmArgs &g, int64_t m, int64_t k) {
+  if (m >= g.M || k >= g.K) return 0.f;
+  return g.a_kcontig ? g.A[m * g.lda + k] : g.A[k * g.lda + m];
+}
+__device__ __forceinline__ float ldB(const GemmArgs &g, int64_t k, int64_t n) {
+  if (n >= g.N || k >= g.K) return 0.f;
+  return g.b_kcontig ? g.B[n * g.ldb + k] : g.B[k * g.ldb + n];
+}
+
+__global__ void __launch_bounds__(NT) gemm_simt_kernel(GemmArgs g) {
+  __shared__ __align__(16) float As[2][BK][BM];
+  __shared__ __align__(16) float Bs[2][BK][BN];
+  const int tid = threadIdx.x;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  const int tx = tid % 16, ty = tid / 16;
+
+  // Load mapping: 1024 elements per operand tile, 4 per thread.  For a
+  // K-contiguous operand consecutive threads walk k first; otherwise m/n.
+  float ra[4], rb[4];
+  auto gload = [&](int64_t k0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = tid + i * NT;
+      int mm, kk;
+      if (g.a_kcontig) { mm = e / BK; kk = e % BK; } else { mm = e % BM; kk = e / BM; }
+      ra[i] = ldA(g, m0 + mm, k0 + kk);
+      int nn, kb;
+      if (g.b_kcontig) { nn = e / BK; kb = e % BK; } else { nn = e % BN; kb = e / BN; }
+      rb[i] = ldB(g, k0 + kb, n0 + nn);
+    }
+  };
+  auto sstore = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = tid + i * NT;
+      int mm, kk;
+      if (g.a_kcontig) { mm = e / BK; kk = e % BK; } else { mm = e % BM; kk = e / BM; }
+      As[buf][kk][mm] = ra[i];
+      int nn, kb;
+      if (g.b_kcontig) { nn = e / BK; kb = e % BK; } else { nn = e % BN; kb = e / BN; }
+      Bs[buf][kb][nn] = rb[i];
+    }
+  };
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+  const int64_t nk = (g.K + BK - 1) / BK;
+  gload(0);
+  sstore(0);
+  __syncthreads();
+  for (int64_t kt = 0; kt < nk; ++kt) {
+    const int buf = kt & 1;
+    if (kt + 1 < nk) gload((kt + 1) * BK);
+#pragma unroll
+    for (int k = 0; k < BK; ++k) {
+      float a[8], b[8];
+      const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][k][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][k][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[buf][k][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[buf][k][64 + tx * 4]);
+      a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
+      a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
+      b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
+      b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    if (kt + 1 < nk) sstore(buf ^ 1);
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    if (m >= g.M) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+      if (n >= g.N) continue;
+      float v = acc[i][j];
+      if (g.bias) v += g.bias[n];
+      float *cp = g.C + m * g.ldc + n;
+      if (g.beta) v += *cp;
+      *cp = v;
+    }
+  }
+}
+
+// Column sums in one pass with a fixed summation order: a CTA owns 32
+// columns, warp w sums rows w, w+8, ... (coalesced 128-byte rows), and the 8
+// warp partials are added in order.
+__global__ void __launch_bounds__(256) colsum_kernel(const float *__restrict__ x, float *__restrict__ out,
+                                                     int64_t M, int64_t N, int beta) {
+  __shared__ float part[8][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t n = (int64_t)blockIdx.x * 32 + lane;
+  float s0 = 0.f, s1 = 0.f;
+  if (n < N) {
+    int64_t r = w;
+    for (; r + 8 < M; r += 16) {
+      s0 += x[r * N + n];
+      s1 += x[(r + 8) * N + n];
+    }
+    for (; r < M; r += 8) s0 += x[r * N + n];
+  }
+  part[w][lane] = s0 + s1;
+  __syncthreads();
+  if (w == 0 && n < N) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += part[i][lane];
+    out[n] = beta ? out[n] + s : s;
+  }
+}
+
+}  // namespace
+
+int gemm_simt(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
+              int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kcontig, bool b_kcontig,
+              int beta, cudaStream_t st) {
+  if (M == 0 || N == 0) return HS_OK;
+  GemmArgs g{A, B, C, bias, M, N, K, lda, ldb, ldc, a_kcontig ? 1 : 0, b_kcontig ? 1 : 0, beta};
+  const int64_t gy = (M + BM - 1) / BM, gx = (N + BN - 1) / BN;
+  if (gy > 65535) return fail(HS_ERR_UNSUPPORTED, "gemm: M=%lld too large for the FFMA path", (long long)M);
+  gemm_simt_kernel<<<dim3((unsigned)gx, (unsigned)gy), NT, 0, st>>>(g);
+  return check_launch("gemm_simt_kernel");
+}
+
+int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st) {
+  if (N == 0) return HS_OK;
+  colsum_kernel<<<(unsigned)((N + 31) / 32), 256, 0, st>>>(x, out, M, N, beta);
+  return check_launch("colsum_kernel");
+}
+
+}  // namespace hs

@@ -1,0 +1,82 @@
+"""The C ABI: the library loads, exports exactly what include/*.h declares,
+and its host-side argument checks reject bad calls before any launch.  No
+kernel runs here (CPU only)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "headstartlstm_b200.h")
+
+
+def _declared():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"HS_API\s+[\w\s\*]+?\b(hs_\w+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from prlstm_b200 import _lib
+
+    if not os.path.exists(_lib.LIB_PATH):
+        from prlstm_b200 import build
+
+        build.build()
+    return _lib.load()
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    for n in ("hs_parallel_forward", "hs_parallel_backward", "hs_recurrent_forward",
+              "hs_recurrent_backward", "hs_scan_forward", "hs_scan_backward",
+              "hs_linear_forward", "hs_linear_dgrad", "hs_linear_wgrad"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for n in _declared():
+        assert hasattr(lib, n), f"{n} declared in the header but not exported"
+
+
+def test_binding_covers_header():
+    from prlstm_b200 import _lib
+
+    assert sorted(_lib.SIGNATURES) == _declared()
+
+
+def test_status_strings(lib):
+    assert lib.hs_abi_version() == 1
+    assert lib.hs_status_string(0) == b"ok"
+    assert b"timed out" in lib.hs_status_string(5)
+    assert lib.hs_status_string(99) == b"unknown status"
+
+
+def test_workspace_queries(lib):
+    assert lib.hs_scan_workspace_bytes(0, 1, 1) == 0
+    n1 = lib.hs_scan_workspace_bytes(128, 32, 256)
+    n2 = lib.hs_scan_workspace_bytes(16384, 32, 1024)
+    assert 0 < n1 < n2
+    assert lib.hs_recurrent_workspace_bytes(256, 32, 256, 512) > 4 * 2048 * 512
+    assert lib.hs_recurrent_workspace_bytes(0, 32, 256, 512) == 0
+
+
+@pytest.mark.parametrize("T,B,H", [(0, 2, 8), (4, 0, 8), (4, 2, -1)])
+def test_scan_rejects_bad_shapes_before_launch(lib, T, B, H):
+    P = ctypes.c_void_p
+    rc = lib.hs_scan_forward(P(16), P(16), P(16), P(16), None, None, T, B, H, 1e-6, P(256), 1 << 20,
+                             P(16), None)
+    assert rc == 1
+    assert b"positive" in lib.hs_last_error_message()
+
+
+def test_recurrent_rejects_null_pointers(lib):
+    rc = lib.hs_recurrent_forward(*([None] * 11), 4, 2, 3, 8, None, 0, None, None)
+    assert rc == 1
+
+
+def test_gemm_rejects_negative_extent(lib):
+    P = ctypes.c_void_p
+    assert lib.hs_linear_forward(P(16), P(16), None, P(16), -1, 4, 4, None) == 1
