@@ -270,8 +270,8 @@ def test_loss_through_final_state(parallel):
 def test_batch_first_and_hx_golden():
     g = load_golden("rec_hx_bf_t6_b5_d10_h20_f32")
     params, x, G, hx = case_tensors(g)
-    ours = run_ours(params, x.transpose(0, 1).contiguous(), G.transpose(0, 1).contiguous(),
-                    parallel=False, hx=hx, batch_first=True)
+    # case_tensors gives [T,B,*]; run_ours feeds the module [B,T,*] when batch_first
+    ours = run_ours(params, x, G, parallel=False, hx=hx, batch_first=True)
     exp = golden_expect(g)
     assert_close(ours, exp, REC_TOL, "batch_first+hx")
 
