@@ -120,6 +120,23 @@ HS_API int hs_scan_backward(const float *z, const float *c, const float *c0, con
                      void *workspace, size_t workspace_bytes, int *dev_status,
                      hs_stream_t stream);
 
+/* hs_scan_forward without a workspace argument, for callers that cannot
+ * allocate device memory (for example a host framework that passes the
+ * library only its input and output buffers, or a latency-critical path that
+ * must not pay cudaMalloc's implicit synchronisation).  No counterpart in the
+ * reference, which allocates through PyTorch.  The look-back scratch is a
+ * fixed 8 MiB device array inside the library (held by every GPU that loads
+ * it, until exit); shapes whose scratch exceeds it are rejected with
+ * HS_ERR_UNSUPPORTED before any launch (roughly T*B*H <= 22M elements).
+ * The first call on each device looks up the array's device address, so
+ * make that first call before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU (other streams, other threads) race
+ * and must be serialised by the caller.  dev_status may be NULL (a status
+ * word inside the library is used).  Allocates nothing. */
+HS_API int hs_scan_forward_noalloc(const float *z, const float *c0, float *out, float *c,
+                                   float *h_n, float *c_n, int64_t T, int64_t B, int64_t H,
+                                   float eps, int *dev_status, hs_stream_t stream);
+
 /* Whole parallel-mode forward: z = x W_ih^T + b_ih (z is caller-owned
  * [T,B,4H] scratch kept for the backward), then hs_scan_forward. */
 HS_API int hs_parallel_forward(const float *x, const float *c0, const float *w_ih,

@@ -41,6 +41,7 @@ SIGNATURES = {
     "hs_colsum": (_i32, [_c_p, _c_p, _i64, _i64, _i32, _c_p]),
     "hs_scan_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "hs_scan_forward": (_i32, [_c_p] * 6 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),
+    "hs_scan_forward_noalloc": (_i32, [_c_p] * 6 + [_i64] * 3 + [_f32, _c_p, _c_p]),
     "hs_scan_backward": (_i32, [_c_p] * 9 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_parallel_forward": (_i32, [_c_p] * 9 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_parallel_backward": (_i32, [_c_p] * 12 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p]),

@@ -23,6 +23,8 @@
 // (L = NW*S steps) x (one sequence b) x (32*VEC units).  Tiles are handed out
 // in time-major order by an atomic ticket, so a tile's predecessor has always
 // started before it (the look-back can never wait on an unscheduled CTA).
+#include <mutex>
+
 #include "hs_common.cuh"
 
 namespace hs {
@@ -590,6 +592,72 @@ int scan_backward(const float *z, const float *c, const float *c0, const float *
   return HS_OK;
 }
 
+// ------------------------------------------------------------------ no-allocation variant
+// Some callers cannot allocate device memory at all: a host framework that
+// hands this library only its input and output buffers (no device allocator
+// of its own), or a latency-critical path where cudaMalloc's implicit device
+// synchronisation is not acceptable.  hs_scan_forward_noalloc serves them:
+// its look-back scratch lives in this fixed, file-scope device array instead
+// of a caller workspace.  Every GPU that loads the library holds the array
+// until the process exits.
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ int g_noalloc_status;
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kMaxDevices];
+int *g_noalloc_status_ptr[kMaxDevices];
+
+// Device address of the scratch array on the current device.  In host code
+// the array's name is only a host-side stand-in, so the address comes from
+// cudaGetSymbolAddress, once per device with that device current.
+int noalloc_scratch(void **scratch, int **status) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(HS_ERR_CUDA, "hs_scan_forward_noalloc: no current CUDA device");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    int *q = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return fail(HS_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    e = cudaGetSymbolAddress((void **)&q, g_noalloc_status);
+    if (e != cudaSuccess)
+      return fail(HS_ERR_CUDA, "cudaGetSymbolAddress(status): %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+    g_noalloc_status_ptr[dev] = q;
+  }
+  *scratch = g_noalloc_ptr[dev];
+  *status = g_noalloc_status_ptr[dev];
+  return HS_OK;
+}
+}  // namespace
+
+int scan_forward_noalloc(const float *z, const float *c0, float *out, float *c, float *h_n,
+                         float *c_n, int64_t T, int64_t B, int64_t H, float eps,
+                         int *dev_status, cudaStream_t st) {
+  if (int e = check_scan_args(T, B, H)) return e;
+  if (!z || !out || !c) return fail(HS_ERR_INVALID_ARG, "scan_forward_noalloc: null z/out/c");
+  const int VEC = pick_vec(H, {z, c0, out, c, h_n, c_n});
+  const int HW = 32 * VEC;
+  const size_t need = ws_layout(make_shape(T, B, H, kFwdS * kFwdNW, HW), HW, false, nullptr, nullptr);
+  if (need > kNoAllocScratchBytes)
+    return fail(HS_ERR_UNSUPPORTED,
+                "hs_scan_forward_noalloc: T=%lld B=%lld H=%lld needs %zu bytes of scratch, above "
+                "the fixed %zu-byte array; use hs_scan_forward with a caller workspace",
+                (long long)T, (long long)B, (long long)H, need, kNoAllocScratchBytes);
+  void *scratch = nullptr;
+  int *own_status = nullptr;
+  if (int e = noalloc_scratch(&scratch, &own_status)) return e;
+  // scan_forward clears the ticket and flags (all that must start at zero)
+  // with a stream-ordered memset before its launch.
+  return scan_forward(z, c0, out, c, h_n, c_n, T, B, H, eps, scratch, kNoAllocScratchBytes,
+                      dev_status ? dev_status : own_status, st);
+}
+
 }  // namespace hs
 
 extern "C" {
@@ -613,6 +681,13 @@ int hs_scan_backward(const float *z, const float *c, const float *c0, const floa
                      size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
   return hs::scan_backward(z, c, c0, dout, dh_n, dc_n, dz, dc0, db, T, B, H, eps, workspace,
                            workspace_bytes, dev_status, (cudaStream_t)stream);
+}
+
+int hs_scan_forward_noalloc(const float *z, const float *c0, float *out, float *c, float *h_n,
+                            float *c_n, int64_t T, int64_t B, int64_t H, float eps,
+                            int *dev_status, hs_stream_t stream) {
+  return hs::scan_forward_noalloc(z, c0, out, c, h_n, c_n, T, B, H, eps, dev_status,
+                                  (cudaStream_t)stream);
 }
 
 }  // extern "C"
