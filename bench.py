@@ -183,7 +183,7 @@ class ParallelStep:
         self.dW_mb = torch.empty(4 * H, D, device=dev)
         self.db_mb = torch.empty(4 * H, device=dev)
         lib = _lib.load()
-        self.ws = _lib.workspace(lib.hs_scan_workspace_bytes(T, mb, H), dev)
+        self.ws = _lib.workspace(lib.hs_parallel_workspace_bytes(T, mb, D, H), dev)
         self.status = _lib.status_word(dev)
         self.names = ("proj_gemm", "scan_fwd", "scan_bwd", "dgrad_gemm", "wgrad_gemm")
         self.ms = {n: 0.0 for n in self.names}
@@ -201,7 +201,8 @@ class ParallelStep:
             e = [torch.cuda.Event(enable_timing=True) for _ in range(6)] if record else None
             if record:
                 e[0].record()
-            L.call("hs_linear_forward", P(xs), P(self.W_ih), P(self.b_ih), P(self.z), M, 4 * H, D, st)
+            L.call("hs_linear_forward", P(xs), P(self.W_ih), P(self.b_ih), P(self.z), M, 4 * H, D,
+                   P(self.ws), self.ws.numel(), P(self.status), st)
             if record:
                 e[1].record()
             L.call("hs_scan_forward", P(self.z), P(self.c0), P(self.out), P(self.c), P(self.h_n),
@@ -213,10 +214,12 @@ class ParallelStep:
                    P(self.status), st)
             if record:
                 e[3].record()
-            L.call("hs_linear_dgrad", P(self.z), P(self.W_ih), P(self.dx), M, 4 * H, D, st)
+            L.call("hs_linear_dgrad", P(self.z), P(self.W_ih), P(self.dx), M, 4 * H, D,
+                   P(self.ws), self.ws.numel(), P(self.status), st)
             if record:
                 e[4].record()
-            L.call("hs_linear_wgrad", P(self.z), P(xs), P(self.dW), M, 4 * H, D, 1 if i else 0, st)
+            L.call("hs_linear_wgrad", P(self.z), P(xs), P(self.dW), M, 4 * H, D, 1 if i else 0,
+                   P(self.ws), self.ws.numel(), P(self.status), st)
             if record:
                 e[5].record()
             self.db.add_(self.db_mb) if i else self.db.copy_(self.db_mb)

@@ -79,15 +79,22 @@ HS_API int hs_selftest_bounded_wait(const unsigned *flag, int *dev_status, uint6
  *   weight gradients    dgates_flat.t() @ h / x    _torch.py:157-158, _triton.py:451-452
  *   bias gradient       dgates_flat.sum(dim=0)     _torch.py:159, _triton.py:453
  * ---------------------------------------------------------------------- */
+/* Scratch (bytes) any of the three products below may use for a split-K
+ * reduction on these extents; pass at least this much, or NULL/0 (then the
+ * product runs unsplit, slower on small outputs, same result). */
+HS_API size_t hs_linear_workspace_bytes(int64_t M, int64_t N, int64_t K);
 /* y[M,N] = x[M,K] . w[N,K]^T (+ bias[N] if bias != NULL) */
 HS_API int hs_linear_forward(const float *x, const float *w, const float *bias, float *y,
-                      int64_t M, int64_t N, int64_t K, hs_stream_t stream);
+                             int64_t M, int64_t N, int64_t K, void *workspace,
+                             size_t workspace_bytes, int *dev_status, hs_stream_t stream);
 /* dx[M,K] = dy[M,N] . w[N,K] */
-HS_API int hs_linear_dgrad(const float *dy, const float *w, float *dx,
-                    int64_t M, int64_t N, int64_t K, hs_stream_t stream);
+HS_API int hs_linear_dgrad(const float *dy, const float *w, float *dx, int64_t M, int64_t N,
+                           int64_t K, void *workspace, size_t workspace_bytes, int *dev_status,
+                           hs_stream_t stream);
 /* dw[N,K] = beta * dw + dy[M,N]^T . x[M,K]   (beta is 0 or 1) */
-HS_API int hs_linear_wgrad(const float *dy, const float *x, float *dw,
-                    int64_t M, int64_t N, int64_t K, int beta, hs_stream_t stream);
+HS_API int hs_linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t N,
+                           int64_t K, int beta, void *workspace, size_t workspace_bytes,
+                           int *dev_status, hs_stream_t stream);
 /* db[N] = beta * db + sum_m dy[m, N]   (beta is 0 or 1) */
 HS_API int hs_colsum(const float *dy, float *db, int64_t M, int64_t N, int beta,
               hs_stream_t stream);
@@ -99,6 +106,8 @@ HS_API int hs_colsum(const float *dy, float *db, int64_t M, int64_t N, int beta,
  * with c_{-1} = max(c0, eps), out_t = o_t tanh(c_t).
  * ---------------------------------------------------------------------- */
 HS_API size_t hs_scan_workspace_bytes(int64_t T, int64_t B, int64_t H);
+/* Workspace of hs_parallel_forward / hs_parallel_backward (scan + GEMMs). */
+HS_API size_t hs_parallel_workspace_bytes(int64_t T, int64_t B, int64_t D, int64_t H);
 
 /* Fused gate activations + chunked scan over T (single pass, decoupled
  * look-back).  z [T,B,4H] gate pre-activations (x W_ih^T + b_ih);

@@ -35,11 +35,13 @@ SIGNATURES = {
     "hs_read_status": (_i32, [_c_p, _c_p, _c_p]),
     "hs_clear_status": (_i32, [_c_p, _c_p]),
     "hs_selftest_bounded_wait": (_i32, [_c_p, _c_p, ctypes.c_uint64, _c_p]),
-    "hs_linear_forward": (_i32, [_c_p, _c_p, _c_p, _c_p, _i64, _i64, _i64, _c_p]),
-    "hs_linear_dgrad": (_i32, [_c_p, _c_p, _c_p, _i64, _i64, _i64, _c_p]),
-    "hs_linear_wgrad": (_i32, [_c_p, _c_p, _c_p, _i64, _i64, _i64, _i32, _c_p]),
+    "hs_linear_workspace_bytes": (_sz, [_i64] * 3),
+    "hs_linear_forward": (_i32, [_c_p] * 4 + [_i64] * 3 + [_c_p, _sz, _c_p, _c_p]),
+    "hs_linear_dgrad": (_i32, [_c_p] * 3 + [_i64] * 3 + [_c_p, _sz, _c_p, _c_p]),
+    "hs_linear_wgrad": (_i32, [_c_p] * 3 + [_i64] * 3 + [_i32, _c_p, _sz, _c_p, _c_p]),
     "hs_colsum": (_i32, [_c_p, _c_p, _i64, _i64, _i32, _c_p]),
     "hs_scan_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "hs_parallel_workspace_bytes": (_sz, [_i64] * 4),
     "hs_scan_forward": (_i32, [_c_p] * 6 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_scan_forward_noalloc": (_i32, [_c_p] * 6 + [_i64] * 3 + [_f32, _c_p, _c_p]),
     "hs_scan_backward": (_i32, [_c_p] * 9 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),

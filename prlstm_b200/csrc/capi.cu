@@ -4,6 +4,8 @@
 #include <stdarg.h>
 #include <string.h>
 
+#include <algorithm>
+
 #include "hs_common.cuh"
 
 namespace hs {
@@ -30,8 +32,10 @@ int gemm_simt(const float *A, const float *B, float *C, const float *bias, int64
               int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kcontig, bool b_kcontig,
               int beta, cudaStream_t st);
 int gemm_tc_try(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
-                int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kcontig, bool b_kcontig,
-                int beta, cudaStream_t st, bool *done);
+                int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kc, bool b_kc, int beta,
+                void *ws, size_t ws_bytes, int *status, cudaStream_t st, bool *done);
+size_t gemm_tc_workspace_bound(int64_t M, int64_t N, int64_t K);
+size_t scan_workspace(int64_t T, int64_t B, int64_t H);
 int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st);
 int scan_forward(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
                  int64_t T, int64_t B, int64_t H, float eps, void *ws, size_t ws_bytes,
@@ -44,11 +48,19 @@ int scan_backward(const float *z, const float *c, const float *c0, const float *
 // One GEMM: tensor-core path when it takes the shape, FFMA path otherwise.
 static int gemm(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
                 int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kc, bool b_kc, int beta,
-                cudaStream_t st) {
+                void *ws, size_t ws_bytes, int *status, cudaStream_t st) {
   bool done = false;
-  if (int e = gemm_tc_try(A, B, C, bias, M, N, K, lda, ldb, ldc, a_kc, b_kc, beta, st, &done)) return e;
+  if (int e = gemm_tc_try(A, B, C, bias, M, N, K, lda, ldb, ldc, a_kc, b_kc, beta, ws, ws_bytes, status,
+                          st, &done))
+    return e;
   if (done) return HS_OK;
   return gemm_simt(A, B, C, bias, M, N, K, lda, ldb, ldc, a_kc, b_kc, beta, st);
+}
+
+// Scratch any of the three linear-layer products of these extents may use.
+size_t linear_ws_bytes(int64_t M, int64_t N, int64_t K) {
+  return std::max({gemm_tc_workspace_bound(M, N, K), gemm_tc_workspace_bound(M, K, N),
+                   gemm_tc_workspace_bound(N, K, M)});
 }
 
 static int check_gemm(const void *a, const void *b, const void *c, int64_t M, int64_t N, int64_t K) {
@@ -59,21 +71,25 @@ static int check_gemm(const void *a, const void *b, const void *c, int64_t M, in
 }
 
 int linear_forward(const float *x, const float *w, const float *bias, float *y, int64_t M,
-                   int64_t N, int64_t K, cudaStream_t st) {
+                   int64_t N, int64_t K, void *ws, size_t ws_bytes, int *status, cudaStream_t st) {
   if (int e = check_gemm(x, w, y, M, N, K)) return e;
-  return gemm(x, w, y, bias, M, N, K, K, K, N, true, true, 0, st);
+  return gemm(x, w, y, bias, M, N, K, K, K, N, true, true, 0, ws, ws_bytes, status, st);
 }
 int linear_dgrad(const float *dy, const float *w, float *dx, int64_t M, int64_t N, int64_t K,
-                 cudaStream_t st) {
+                 void *ws, size_t ws_bytes, int *status, cudaStream_t st) {
   if (int e = check_gemm(dy, w, dx, M, N, K)) return e;
   // dx[M,K] = dy[M,N] . w[N,K]: reduction over N; w is K-contiguous = output-contiguous
-  return gemm(dy, w, dx, nullptr, M, K, N, N, K, K, true, false, 0, st);
+  return gemm(dy, w, dx, nullptr, M, K, N, N, K, K, true, false, 0, ws, ws_bytes, status, st);
 }
 int linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t N, int64_t K,
-                 int beta, cudaStream_t st) {
+                 int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st) {
   if (int e = check_gemm(dy, x, dw, M, N, K)) return e;
   // dw[N,K] = dy[M,N]^T . x[M,K]: reduction over M; both operands output-contiguous
-  return gemm(dy, x, dw, nullptr, N, K, M, N, K, K, false, false, beta, st);
+  return gemm(dy, x, dw, nullptr, N, K, M, N, K, K, false, false, beta, ws, ws_bytes, status, st);
+}
+
+size_t parallel_ws_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
+  return std::max(scan_workspace(T, B, H), linear_ws_bytes(T * B, 4 * H, D));
 }
 
 int parallel_forward(const float *x, const float *c0, const float *w_ih, const float *b_ih,
@@ -82,7 +98,7 @@ int parallel_forward(const float *x, const float *c0, const float *w_ih, const f
                      cudaStream_t st) {
   if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return fail(HS_ERR_INVALID_ARG, "T, B, D, H must be positive");
   if (!x || !w_ih || !z) return fail(HS_ERR_INVALID_ARG, "parallel_forward: null x/w_ih/z");
-  if (int e = linear_forward(x, w_ih, b_ih, z, T * B, 4 * H, D, st)) return e;
+  if (int e = linear_forward(x, w_ih, b_ih, z, T * B, 4 * H, D, ws, ws_bytes, status, st)) return e;
   return scan_forward(z, c0, out, c, h_n, c_n, T, B, H, eps, ws, ws_bytes, status, st);
 }
 
@@ -95,8 +111,8 @@ int parallel_backward(const float *x, const float *w_ih, float *z, const float *
   if (!x || !w_ih || !z || !dw_ih || !db_ih) return fail(HS_ERR_INVALID_ARG, "parallel_backward: null x/w_ih/z/dw_ih/db_ih");
   if (int e = scan_backward(z, c, c0, dout, dh_n, dc_n, z, dc0, db_ih, T, B, H, eps, ws, ws_bytes, status, st)) return e;
   if (dx)
-    if (int e = linear_dgrad(z, w_ih, dx, T * B, 4 * H, D, st)) return e;
-  return linear_wgrad(z, x, dw_ih, T * B, 4 * H, D, 0, st);
+    if (int e = linear_dgrad(z, w_ih, dx, T * B, 4 * H, D, ws, ws_bytes, status, st)) return e;
+  return linear_wgrad(z, x, dw_ih, T * B, 4 * H, D, 0, ws, ws_bytes, status, st);
 }
 
 namespace {
@@ -148,17 +164,29 @@ int hs_selftest_bounded_wait(const unsigned *flag, int *dev_status, uint64_t lim
   return hs::check_launch("selftest_wait_kernel");
 }
 
+size_t hs_linear_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  return hs::linear_ws_bytes(M, N, K);
+}
+size_t hs_parallel_workspace_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
+  if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return 0;
+  return hs::parallel_ws_bytes(T, B, D, H);
+}
 int hs_linear_forward(const float *x, const float *w, const float *bias, float *y, int64_t M,
-                      int64_t N, int64_t K, hs_stream_t stream) {
-  return hs::linear_forward(x, w, bias, y, M, N, K, (cudaStream_t)stream);
+                      int64_t N, int64_t K, void *workspace, size_t workspace_bytes, int *dev_status,
+                      hs_stream_t stream) {
+  return hs::linear_forward(x, w, bias, y, M, N, K, workspace, workspace_bytes, dev_status,
+                            (cudaStream_t)stream);
 }
 int hs_linear_dgrad(const float *dy, const float *w, float *dx, int64_t M, int64_t N, int64_t K,
-                    hs_stream_t stream) {
-  return hs::linear_dgrad(dy, w, dx, M, N, K, (cudaStream_t)stream);
+                    void *workspace, size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
+  return hs::linear_dgrad(dy, w, dx, M, N, K, workspace, workspace_bytes, dev_status,
+                          (cudaStream_t)stream);
 }
 int hs_linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t N, int64_t K,
-                    int beta, hs_stream_t stream) {
-  return hs::linear_wgrad(dy, x, dw, M, N, K, beta, (cudaStream_t)stream);
+                    int beta, void *workspace, size_t workspace_bytes, int *dev_status,
+                    hs_stream_t stream) {
+  return hs::linear_wgrad(dy, x, dw, M, N, K, beta, workspace, workspace_bytes, dev_status,
+                          (cudaStream_t)stream);
 }
 int hs_colsum(const float *dy, float *db, int64_t M, int64_t N, int beta, hs_stream_t stream) {
   if (M < 0 || N < 0 || (N && !db) || (M && N && !dy)) return hs::fail(HS_ERR_INVALID_ARG, "hs_colsum: bad arguments");

@@ -1,12 +1,574 @@
-// Tensor-core (tcgen05) GEMM path.  Takes no shape yet: every product runs on
-// the FFMA kernel in gemm_simt.cu.
+// tcgen05 / TMEM / TMA GEMM with float32 accuracy (3xTF32) for the
+// linear-layer products of HeadStartLSTM (input projection x.W_ih^T + b_ih,
+// input gradient dZ.W_ih, weight gradients dZ^T.x and dG^T.h).
+//
+// fp32 parity on tensor cores.  kind::tf32 reads fp32 words from shared
+// memory and uses their top 19 bits (the low 13 mantissa bits are dropped).
+// Each operand x is split as x = hi + lo with hi = x itself (the tensor core
+// drops the low bits) and lo = x - trunc19(x) (exact in fp32), and
+//     A.B ~= A.B_hi-part + A.B_lo + A_lo.B      (three MMAs per k-step)
+// which leaves only the lo*lo product and the tf32 rounding of lo (~2^-21
+// of |a||b| per term; measured ~7e-7 normwise, the level of an FFMA GEMM).
+//
+// Accumulation.  The tensor core adds each MMA's products into the fp32 TMEM
+// accumulator with truncation (measured here: a bias toward zero of ~1e-6
+// per 32-deep k-block, growing linearly with K).  Two measures keep the
+// result at fp32 accuracy for any K:
+//   * the big A.B product goes to its own accumulator (1 MMA per k-step);
+//     the two small correction products (2^-11 of it) go to a second one;
+//   * every PROMOTE k-blocks both accumulators are folded into fp32 register
+//     totals (round-to-nearest adds) by the epilogue warps and restarted.
+//     The accumulator pairs are double-buffered (4 x 128 of the 512 TMEM
+//     columns) so the MMAs of the next group run while one is folded.
+//
+// Kernel structure (one 128 x 128 output tile per CTA, 1 CTA per SM):
+//   warp 0      TMA producer: raw A/B k-blocks (32 fp32 = one 128-byte
+//               swizzle row) into a 3-stage ring;
+//   warp 1      allocates 512 TMEM columns; one lane issues tcgen05.mma and
+//               commits stages back to the producer and finished groups to
+//               the epilogue warps;
+//   warps 2..5  compute lo for every stage in shared memory (elementwise, so
+//               the swizzled layout is kept), fold finished groups into their
+//               row's register totals, and finally store the tile (bias,
+//               beta) or a split-K partial.
+// No cluster multicast anywhere.  Every mbarrier wait is bounded.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "hs_common.cuh"
 
 namespace hs {
 
-int gemm_tc_try(const float *, const float *, float *, const float *, int64_t, int64_t, int64_t,
-                int64_t, int64_t, int64_t, bool, bool, int, cudaStream_t, bool *done) {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3, PROMOTE = 4;
+constexpr int NTHREADS = 192;
+constexpr int A_BYTES = BM * BK * 4;                 // 16 KB
+constexpr int B_BYTES = BN * BK * 4;                 // 16 KB
+constexpr int RAW_BYTES = A_BYTES + B_BYTES;         // 32 KB
+constexpr int STAGE_BYTES = 2 * RAW_BYTES;           // raw + lo
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t TMEM_COLS = 512;                  // 2 buffers x (main, correction) x 128
+
+HS_DEV uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// lo = x - (x with its low 13 mantissa bits cleared), exact in fp32, then
+// rounded to the nearest tf32 value so the tensor core's own truncation of
+// it is exact (no bias toward zero).
+HS_DEV float lo_part(float x) {
+  const float r = x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  return __uint_as_float((__float_as_uint(r) + 0x1000u) & 0xFFFFE000u);
+}
+
+HS_DEV void mbar_init(uint64_t *b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
+}
+HS_DEV void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+HS_DEV void mbar_arrive(uint64_t *b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+HS_DEV bool mbar_try(uint64_t *b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on a phase; gives up (status set) after kWaitLimitNs or as
+// soon as another CTA has recorded a failure.
+HS_DEV bool mbar_wait(uint64_t *b, uint32_t parity, int *status) {
+  if (mbar_try(b, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  unsigned n = 0;
+  while (!mbar_try(b, parity)) {
+    if ((++n & 63u) == 0) {
+      if (ld_status(status) != 0) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        set_status(status, HS_ERR_DEVICE_TIMEOUT);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+HS_DEV void tma_2d(void *dst, const CUtensorMap *tm, uint64_t *bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(su32(dst)),
+      "l"(tm), "r"(c0), "r"(c1), "r"(su32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor (sm100 version bits).  Layout type 2 is
+// the 128-byte swizzle of K-major tiles (16-byte chunks XOR row%8); layout
+// type 1 is the 128-byte swizzle with 32-byte atoms (32-byte chunks XOR
+// row%4), the only layout tf32 accepts for M/N-major operands.
+HS_DEV uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)layout << 61;
+  return d;
+}
+
+// Instruction descriptor: D f32, A/B tf32, majors, N>>3, M>>4.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+HS_DEV void mma_tf32(uint32_t dt, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(dt),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+HS_DEV void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+               : "memory");
+}
+
+HS_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+struct TcArgs {
+  float *C;
+  const float *bias;
+  float *partial;  // split-K partials [splits][M][N] or null
+  int64_t M, N, K;
+  int64_t ldc;
+  int beta;
+  int kb_per_split;
+  int nkb;
+  int *status;
+};
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(NTHREADS, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcArgs p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  uint64_t *xformed = full + STAGES;
+  uint64_t *empty = xformed + STAGES;
+  uint64_t *pfull = empty + STAGES;   // [2] group finished in accumulator pair b
+  uint64_t *pempty = pfull + 2;       // [2] accumulator pair b folded, reusable
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(pempty + 2);
+  int *abort_flag = reinterpret_cast<int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  const int kb0 = blockIdx.z * p.kb_per_split;
+  const int kb1 = min(p.nkb, kb0 + p.kb_per_split);
+  const int nk = kb1 - kb0;
+  const int ngroups = (nk + PROMOTE - 1) / PROMOTE;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&xformed[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pfull[b], 1);
+      mbar_init(&pempty[b], 4);
+    }
+    *abort_flag = ld_status(p.status) != 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_holder)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_holder;
+  const bool skip = *abort_flag != 0 || nk <= 0;
+
+  if (!skip && warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, p.status)) break;
+        ++issued;
+        unsigned char *st = smem + s * STAGE_BYTES;
+        mbar_expect_tx(&full[s], RAW_BYTES);
+        const int k0 = (kb0 + i) * BK;
+        // M/N-major operands arrive as 32 x 32 boxes (128-byte rows of 32
+        // M/N elements, 32 k rows), one 4 KB block per 32 rows of M/N.
+        if (A_MN) {
+#pragma unroll
+          for (int j = 0; j < BM / 32; ++j) tma_2d(st + j * 4096, &tmA, &full[s], (int)m0 + 32 * j, k0);
+        } else {
+          tma_2d(st, &tmA, &full[s], k0, (int)m0);
+        }
+        if (B_MN) {
+#pragma unroll
+          for (int j = 0; j < BN / 32; ++j) tma_2d(st + A_BYTES + j * 4096, &tmB, &full[s], (int)n0 + 32 * j, k0);
+        } else {
+          tma_2d(st + A_BYTES, &tmB, &full[s], k0, (int)n0);
+        }
+      }
+      // Never leave while a copy into this CTA's shared memory is in flight:
+      // wait (bounded) for the last load issued into each stage.
+      for (int i = std::max(0, issued - STAGES); i < issued; ++i) {
+        int dummy = 0;
+        (void)mbar_wait(&full[i % STAGES], (i / STAGES) & 1, ld_status(p.status) ? &dummy : p.status);
+      }
+    }
+  } else if (!skip && warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
+      bool ok = true;
+      for (int i = 0; i < nk && ok; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        const int g = i / PROMOTE, b = g & 1;
+        const bool gstart = (i % PROMOTE) == 0;
+        if (gstart && !mbar_wait(&pempty[b], ((g >> 1) & 1) ^ 1, p.status)) break;
+        if (!mbar_wait(&xformed[s], ph, p.status)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_raw = su32(smem + s * STAGE_BYTES);
+        const uint32_t b_raw = a_raw + A_BYTES;
+        const uint32_t a_lo = a_raw + RAW_BYTES;
+        const uint32_t b_lo = b_raw + RAW_BYTES;
+        const uint32_t t_main = tmem + (uint32_t)(b * 2 * BN);
+        const uint32_t t_corr = t_main + BN;
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          // K-major (layout 2): the 8 k of this step are 32 bytes into each
+          // 128-byte row; 8-row groups are 1 KB apart (SBO).
+          // M/N-major (layout 1): the 8 k are the next 8 rows of 128 bytes
+          // (two 512-byte atoms of 4 rows, SBO = 512); the 32-wide M/N blocks
+          // are 4 KB apart (LBO).
+          const uint32_t ao = A_MN ? kk * 1024 : kk * 32;
+          const uint32_t bo = B_MN ? kk * 1024 : kk * 32;
+          const uint32_t la = A_MN ? 1u : 2u, lb = B_MN ? 1u : 2u;
+          const uint32_t albo = A_MN ? 4096 : 16, asbo = A_MN ? 512 : 1024;
+          const uint32_t blbo = B_MN ? 4096 : 16, bsbo = B_MN ? 512 : 1024;
+          const uint64_t dA = sdesc(a_raw + ao, albo, asbo, la), dAl = sdesc(a_lo + ao, albo, asbo, la);
+          const uint64_t dB = sdesc(b_raw + bo, blbo, bsbo, lb), dBl = sdesc(b_lo + bo, blbo, bsbo, lb);
+          const uint32_t acc = (gstart && kk == 0) ? 0u : 1u;
+          mma_tf32(t_main, dA, dB, idesc, acc);
+          mma_tf32(t_corr, dA, dBl, idesc, acc);
+          mma_tf32(t_corr, dAl, dB, idesc, 1u);
+        }
+        mma_commit(&empty[s]);
+        if ((i % PROMOTE) == PROMOTE - 1 || i == nk - 1) mma_commit(&pfull[b]);
+      }
+    }
+  } else if (!skip) {
+    // ---------------- transform (lo parts), folding, epilogue
+    const int t = threadIdx.x - 64;  // 0..127
+    const int q = warp & 3;          // TMEM lane quadrant of this warp
+    float tot[BN];
+#pragma unroll
+    for (int j = 0; j < BN; ++j) tot[j] = 0.f;
+    bool ok = true;
+    int drained = 0;
+    auto fold = [&](int g) -> bool {
+      const int b = g & 1;
+      if (!mbar_wait(&pfull[b], (g >> 1) & 1, p.status)) return false;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 2 * BN);
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(base + BN + c, v);  // correction first: tot += (corr + main)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tot[c + j] += v[j];
+        tmem_ld32(base + c, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tot[c + j] += v[j];
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pempty[b]);
+      return true;
+    };
+    for (int i = 0; i < nk && ok; ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = (i / STAGES) & 1;
+      if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
+      const float4 *raw = reinterpret_cast<const float4 *>(smem + s * STAGE_BYTES);
+      float4 *lo = reinterpret_cast<float4 *>(smem + s * STAGE_BYTES + RAW_BYTES);
+#pragma unroll 4
+      for (int j = t; j < RAW_BYTES / 16; j += 128) {
+        const float4 v = raw[j];
+        lo[j] = make_float4(lo_part(v.x), lo_part(v.y), lo_part(v.z), lo_part(v.w));
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xformed[s]);
+      // fold group g once the transform is 3 k-blocks into group g+1
+      if (drained < ngroups && i >= PROMOTE * (drained + 1) + 2) {
+        if (!fold(drained)) { ok = false; break; }
+        ++drained;
+      }
+    }
+    while (ok && drained < ngroups) {
+      if (!fold(drained)) { ok = false; break; }
+      ++drained;
+    }
+    if (ok) {
+      const int64_t m = m0 + q * 32 + lane;
+      if (m < p.M) {
+        float *dst = p.partial ? p.partial + (int64_t)blockIdx.z * p.M * p.N : p.C;
+        const int64_t ld = p.partial ? p.N : p.ldc;
+        const bool direct = p.partial == nullptr;
+        float *row = dst + m * ld + n0;
+        if (n0 + BN <= p.N && (ld % 4) == 0) {
+#pragma unroll
+          for (int j = 0; j < BN; j += 4) {
+            float4 o = make_float4(tot[j], tot[j + 1], tot[j + 2], tot[j + 3]);
+            if (direct && p.bias) {
+              o.x += p.bias[n0 + j]; o.y += p.bias[n0 + j + 1];
+              o.z += p.bias[n0 + j + 2]; o.w += p.bias[n0 + j + 3];
+            }
+            if (direct && p.beta) {
+              const float4 old = *reinterpret_cast<const float4 *>(row + j);
+              o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+            }
+            *reinterpret_cast<float4 *>(row + j) = o;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN; ++j) {
+            if (n0 + j < p.N) {
+              float o = tot[j];
+              if (direct && p.bias) o += p.bias[n0 + j];
+              if (direct && p.beta) o += row[j];
+              row[j] = o;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// C[m,n] = beta*C + sum_z partial[z][m][n] (+ bias[n]); fixed order over z.
+__global__ void splitk_reduce_kernel(const float *__restrict__ part, float *__restrict__ C,
+                                     const float *__restrict__ bias, int64_t M, int64_t N,
+                                     int64_t ldc, int splits, int beta) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= M * N) return;
+  const int64_t m = idx / N, n = idx % N;
+  float s = 0.f;
+  for (int z = 0; z < splits; ++z) s += part[(int64_t)z * M * N + idx];
+  if (bias) s += bias[n];
+  float *c = C + m * ldc + n;
+  *c = beta ? *c + s : s;
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Operand view: element (r, k) of an R x K operand (R = M for A, N for B).
+//   K-major:  ptr[r*ld + k]   -> 2D map {K, R}, box {32, rows}
+//   MN-major: ptr[k*ld + r]   -> 2D map {R, K}, box {32, 32}
+bool make_map(CUtensorMap *tm, const float *ptr, int64_t R, int64_t K, int64_t ld, bool mn, int rows) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  CUresult r;
+  if (!mn) {
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)R};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+    cuuint32_t box[2] = {32, (cuuint32_t)rows};
+    cuuint32_t es[2] = {1, 1};
+    r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)ptr, dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    (void)rows;
+    cuuint64_t dims[2] = {(cuuint64_t)R, (cuuint64_t)K};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t es[2] = {1, 1};
+    r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)ptr, dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  return r == CUDA_SUCCESS;
+}
+
+int g_disable = -1;  // HS_DISABLE_TC=1 forces the FFMA path (cross-checks)
+
+bool tc_enabled() {
+  if (g_disable < 0) {
+    const char *e = getenv("HS_DISABLE_TC");
+    g_disable = (e && e[0] == '1') ? 1 : 0;
+  }
+  return g_disable == 0;
+}
+
+// Smallest M*N*K the tensor-core path takes (HS_TC_MIN_MNK overrides, for
+// exercising the tensor-core path on small shapes in tests).
+double tc_min_mnk() {
+  static double v = -1;
+  if (v < 0) {
+    const char *e = getenv("HS_TC_MIN_MNK");
+    v = e ? atof(e) : 3.3e7;
+  }
+  return v;
+}
+
+int device_sms() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+struct TcPlan {
+  bool ok = false;
+  int splits = 1;
+  int nkb = 0;
+  int kbps = 0;
+  size_t ws = 0;
+};
+
+int split_count(int64_t M, int64_t N, int nkb, int nsm) {
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  int splits = 1;
+  if (tiles < nsm / 2 && nkb >= 16) splits = (int)std::max<int64_t>(1, std::min<int64_t>(nsm / tiles, nkb / 8));
+  const int kbps = (nkb + splits - 1) / splits;
+  return (nkb + kbps - 1) / kbps;
+}
+
+TcPlan plan_tc(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K, int64_t lda,
+               int64_t ldb, int64_t ldc, bool a_kc, bool b_kc) {
+  TcPlan pl;
+  if (!tc_enabled()) return pl;
+  if ((double)M * N * K < tc_min_mnk()) return pl;  // small products: FFMA path
+  auto al = [](const void *p) { return aligned(p, 16); };
+  if (!al(A) || !al(B) || !al(C) || lda % 4 || ldb % 4) return pl;
+  if (a_kc ? (K % 4) : (M % 4)) return pl;
+  if (b_kc ? (K % 4) : (N % 4)) return pl;
+  if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) return pl;
+  pl.nkb = (int)((K + BK - 1) / BK);
+  pl.splits = split_count(M, N, pl.nkb, device_sms());
+  pl.kbps = (pl.nkb + pl.splits - 1) / pl.splits;  // every split gets >= 1 k-block
+  pl.ws = pl.splits > 1 ? (size_t)pl.splits * M * N * 4 : 0;
+  pl.ok = true;
+  return pl;
+}
+
+}  // namespace
+
+size_t gemm_tc_workspace(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K,
+                         int64_t lda, int64_t ldb, int64_t ldc, bool a_kc, bool b_kc) {
+  TcPlan pl = plan_tc(A, B, C, M, N, K, lda, ldb, ldc, a_kc, b_kc);
+  return pl.ok ? pl.ws : 0;
+}
+
+// Upper bound of the split-K scratch of one M x N x K product on any device
+// with up to 256 SMs (the split count only grows with the SM count).
+size_t gemm_tc_workspace_bound(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const int splits = split_count(M, N, (int)((K + BK - 1) / BK), 256);
+  return splits > 1 ? (size_t)splits * M * N * 4 : 0;
+}
+
+int gemm_tc_try(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
+                int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kc, bool b_kc, int beta,
+                void *ws, size_t ws_bytes, int *status, cudaStream_t st, bool *done) {
+  if (!status) return HS_OK;  // the tensor-core path needs a status word for its bounded waits
   *done = false;
+  TcPlan pl = plan_tc(A, B, C, M, N, K, lda, ldb, ldc, a_kc, b_kc);
+  if (!pl.ok) return HS_OK;
+  if (pl.splits > 1 && (!ws || ws_bytes < pl.ws || !aligned(ws, 16))) {
+    // not enough scratch for split-K: run unsplit (fewer CTAs, still exact)
+    pl.splits = 1;
+    pl.kbps = pl.nkb;
+    pl.ws = 0;
+  }
+  CUtensorMap ta, tb;
+  if (!make_map(&ta, A, M, K, lda, !a_kc, BM)) return HS_OK;
+  if (!make_map(&tb, B, N, K, ldb, !b_kc, BN)) return HS_OK;
+  TcArgs args;
+  args.C = C;
+  args.bias = bias;
+  args.partial = pl.splits > 1 ? static_cast<float *>(ws) : nullptr;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.ldc = ldc;
+  args.beta = beta;
+  args.kb_per_split = pl.kbps;
+  args.nkb = pl.nkb;
+  args.status = status;
+  const dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), (unsigned)pl.splits);
+  void (*fn)(const CUtensorMap, const CUtensorMap, TcArgs);
+  if (!a_kc && !b_kc) fn = gemm_tc_kernel<true, true>;
+  else if (!a_kc) fn = gemm_tc_kernel<true, false>;
+  else if (!b_kc) fn = gemm_tc_kernel<false, true>;
+  else fn = gemm_tc_kernel<false, false>;
+  static std::once_flag attr_once[4];
+  const int which = (a_kc ? 0 : 2) + (b_kc ? 0 : 1);
+  std::call_once(attr_once[which], [&] {
+    cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  });
+  if (grid.y > 65535) return HS_OK;
+  fn<<<grid, NTHREADS, SMEM_BYTES, st>>>(ta, tb, args);
+  if (int e = check_launch("gemm_tc_kernel")) return e;
+  if (pl.splits > 1) {
+    const int64_t n = M * N;
+    splitk_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(static_cast<float *>(ws), C, bias, M, N,
+                                                                      ldc, pl.splits, beta);
+    if (int e = check_launch("splitk_reduce_kernel")) return e;
+  }
+  *done = true;
   return HS_OK;
 }
 

@@ -33,11 +33,12 @@ int gemm_simt(const float *A, const float *B, float *C, const float *bias, int64
               int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kcontig, bool b_kcontig,
               int beta, cudaStream_t st);
 int linear_forward(const float *x, const float *w, const float *bias, float *y, int64_t M,
-                   int64_t N, int64_t K, cudaStream_t st);
+                   int64_t N, int64_t K, void *ws, size_t ws_bytes, int *status, cudaStream_t st);
 int linear_dgrad(const float *dy, const float *w, float *dx, int64_t M, int64_t N, int64_t K,
-                 cudaStream_t st);
+                 void *ws, size_t ws_bytes, int *status, cudaStream_t st);
 int linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t N, int64_t K,
-                 int beta, cudaStream_t st);
+                 int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st);
+size_t linear_ws_bytes(int64_t M, int64_t N, int64_t K);
 int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st);
 
 namespace {
@@ -571,9 +572,9 @@ size_t rec_ws_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
   Plan p;
   const int nsm = num_sms();
   if (!make_plan(p, B, H, nsm > 0 ? nsm : 148)) return 0;
-  (void)T;
-  (void)D;
-  return p.total;
+  // the GEMMs run before the persistent kernels (forward) or after them
+  // (backward), so they reuse the same scratch
+  return std::max(p.total, std::max(linear_ws_bytes(T * B, 4 * H, D), linear_ws_bytes(T * B, 4 * H, H)));
 }
 
 int rec_forward(const float *x, const float *h0, const float *c0, const float *w_ih,
@@ -591,7 +592,7 @@ int rec_forward(const float *x, const float *h0, const float *c0, const float *w
   if (!aligned(ws, 256)) return fail(HS_ERR_INVALID_ARG, "workspace must be 256-byte aligned");
   char *w = static_cast<char *>(ws);
   // Z = x W_ih^T + b_ih, written into acts (_torch.py:96)
-  if (int e = linear_forward(x, w_ih, b_ih, acts, T * B, 4 * H, D, st)) return e;
+  if (int e = linear_forward(x, w_ih, b_ih, acts, T * B, 4 * H, D, ws, ws_bytes, status, st)) return e;
   rec_prep_kernel<<<4 * nsm, 256, 0, st>>>(w_hh, b_hh, a, (float *)(w + pl.o_wf), (float *)(w + pl.o_bf),
                                            (float *)(w + pl.o_wb), H, pl.U, pl.ncta, pl.fwd.rows_pad,
                                            pl.fwd.K_pad, pl.bwd.rows_pad, pl.bwd.K_pad);
@@ -676,11 +677,11 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
   }
   // Batched parameter gradients (_torch.py:153-162); acts now holds dgates.
   const int64_t M = T * B, N = 4 * H;
-  if (int e = linear_wgrad(acts, h_save, dw_hh, M, N, H, 0, st)) return e;   // dW_hh_s
-  if (int e = linear_wgrad(acts, x, dw_ih, M, N, D, 0, st)) return e;
+  if (int e = linear_wgrad(acts, h_save, dw_hh, M, N, H, 0, ws, ws_bytes, status, st)) return e;  // dW_hh_s
+  if (int e = linear_wgrad(acts, x, dw_ih, M, N, D, 0, ws, ws_bytes, status, st)) return e;
   if (int e = colsum(acts, db_ih, M, N, 0, st)) return e;
   if (dx)
-    if (int e = linear_dgrad(acts, w_ih, dx, M, N, D, st)) return e;
+    if (int e = linear_dgrad(acts, w_ih, dx, M, N, D, ws, ws_bytes, status, st)) return e;
   rec_unscale_kernel<<<4, 256, 0, st>>>(w_hh, b_hh, a, dw_hh, db_ih, db_hh, da, H);
   return check_launch("rec_unscale_kernel");
 }

@@ -542,6 +542,8 @@ int check_scan_args(int64_t T, int64_t B, int64_t H) {
 
 }  // namespace
 
+size_t scan_workspace(int64_t T, int64_t B, int64_t H) { return scan_ws_bytes(T, B, H); }
+
 // ------------------------------------------------------------------ host API
 int scan_forward(const float *z, const float *c0, float *out, float *c, float *h_n,
                  float *c_n, int64_t T, int64_t B, int64_t H, float eps, void *ws_base,

@@ -55,6 +55,9 @@ def test_status_strings(lib):
 
 
 def test_workspace_queries(lib):
+    assert lib.hs_linear_workspace_bytes(8192, 2048, 512) > 0      # small output: split-K scratch
+    assert lib.hs_linear_workspace_bytes(0, 2048, 512) == 0
+    assert lib.hs_parallel_workspace_bytes(128, 32, 256, 256) >= lib.hs_scan_workspace_bytes(128, 32, 256)
     assert lib.hs_scan_workspace_bytes(0, 1, 1) == 0
     n1 = lib.hs_scan_workspace_bytes(128, 32, 256)
     n2 = lib.hs_scan_workspace_bytes(16384, 32, 1024)
@@ -79,4 +82,4 @@ def test_recurrent_rejects_null_pointers(lib):
 
 def test_gemm_rejects_negative_extent(lib):
     P = ctypes.c_void_p
-    assert lib.hs_linear_forward(P(16), P(16), None, P(16), -1, 4, 4, None) == 1
+    assert lib.hs_linear_forward(P(16), P(16), None, P(16), -1, 4, 4, None, 0, None, None) == 1

@@ -1,0 +1,103 @@
+"""The three linear-layer GEMMs through the C ABI against a float64 product.
+
+Shapes are chosen so the tcgen05 (3xTF32) path takes them: aligned and
+ragged extents, bias, beta (accumulate), split-K with and without scratch.
+Bound: normwise 2e-6 (3xTF32 with promoted accumulation measures ~1e-6; plain TF32 would be ~7e-4, so
+the bound also proves the lo-part MMAs run)."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-6
+
+
+def _rel(a, b):
+    a = a.double().cpu()
+    b = b.double().cpu()
+    e = ((a - b).abs().max() / b.abs().max()).item()
+    print(f"GEMMERR {e:.3e}")
+    return e
+
+
+def _lib():
+    from prlstm_b200 import _lib as L
+
+    return L
+
+
+def _ws(L, M, N, K, dev, use=True):
+    if not use:
+        return None, 0
+    n = L.load().hs_linear_workspace_bytes(M, N, K)
+    t = L.workspace(n, dev)
+    return t, t.numel()
+
+
+@pytest.mark.parametrize("M,N,K,bias", [(4096, 1024, 256, True), (1000, 520, 132, True),
+                                        (8192, 2048, 100, False), (2048, 8192, 1024, True)])
+def test_linear_forward(M, N, K, bias):
+    L = _lib()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(M + N + K)
+    x = torch.randn(M, K, device=dev, generator=g)
+    w = torch.randn(N, K, device=dev, generator=g) / K ** 0.5
+    b = torch.randn(N, device=dev, generator=g) if bias else None
+    y = torch.empty(M, N, device=dev)
+    ws, n = _ws(L, M, N, K, dev)
+    P = L.ptr
+    L.call("hs_linear_forward", P(x), P(w), P(b), P(y), M, N, K, P(ws), n, P(L.status_word(dev)),
+           L.stream_ptr(dev))
+    ref = x.double().cpu() @ w.double().cpu().t()
+    if bias:
+        ref += b.double().cpu()
+    assert _rel(y, ref) < TOL
+    L.check_device_status(dev)
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 1024, 256), (8192, 2048, 512), (999, 96, 40)])
+def test_linear_dgrad(M, N, K):
+    L = _lib()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(7 + M)
+    dy = torch.randn(M, N, device=dev, generator=g)
+    w = torch.randn(N, K, device=dev, generator=g) / N ** 0.5
+    dx = torch.empty(M, K, device=dev)
+    ws, n = _ws(L, M, N, K, dev)
+    P = L.ptr
+    L.call("hs_linear_dgrad", P(dy), P(w), P(dx), M, N, K, P(ws), n, P(L.status_word(dev)),
+           L.stream_ptr(dev))
+    assert _rel(dx, dy.double().cpu() @ w.double().cpu()) < TOL
+    L.check_device_status(dev)
+
+
+@pytest.mark.parametrize("M,N,K,beta,use_ws", [(8192, 2048, 512, 0, True), (8192, 2048, 512, 1, True),
+                                               (8192, 2048, 512, 1, False), (65536, 4096, 512, 0, True),
+                                               (2000, 1024, 256, 0, True)])
+def test_linear_wgrad(M, N, K, beta, use_ws):
+    L = _lib()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(11 + M + beta)
+    dy = torch.randn(M, N, device=dev, generator=g) * 0.1
+    x = torch.randn(M, K, device=dev, generator=g)
+    dw = torch.randn(N, K, device=dev, generator=g) if beta else torch.empty(N, K, device=dev)
+    ref = dy.double().cpu().t() @ x.double().cpu()
+    if beta:
+        ref += dw.double().cpu()
+    ws, n = _ws(L, M, N, K, dev, use_ws)
+    P = L.ptr
+    L.call("hs_linear_wgrad", P(dy), P(x), P(dw), M, N, K, beta, P(ws), n, P(L.status_word(dev)),
+           L.stream_ptr(dev))
+    assert _rel(dw, ref) < TOL
+    L.check_device_status(dev)
+
+
+def test_colsum_matches():
+    L = _lib()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(3)
+    dy = torch.randn(5000, 1000, device=dev, generator=g)
+    db = torch.empty(1000, device=dev)
+    P = L.ptr
+    L.call("hs_colsum", P(dy), P(db), 5000, 1000, 0, L.stream_ptr(dev))
+    assert _rel(db, dy.double().cpu().sum(0)) < 1e-6
