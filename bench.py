@@ -344,8 +344,9 @@ def run_ours(args, cfg, rank, world, dev):
         del step
         torch.cuda.empty_cache()
         # ---------------- e2e through the public module API, host buffers
-        result["e2e"] = e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync,
-                                     max_over_ranks, allreduce)
+        if not args.no_e2e:
+            result["e2e"] = e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync,
+                                         max_over_ranks, allreduce)
     else:
         result.update(run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync,
                                     max_over_ranks, allreduce, peak_tf, peak_kind))
@@ -483,6 +484,8 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
            "roofline": {"kernel": "recurrent fwd+bwd", "bound": "tensor", "achieved": round(ach, 3),
                         "peak": peak_tf, "unit": "TFLOP/s", "frac": round(ach / peak_tf, 5),
                         "peak_kind": peak_kind, "traffic": None}}
+    if args.no_e2e:
+        return res
     # e2e through the module API with host buffers
     m = prlstm_b200.HeadStartLSTM(D, H).to(dev)
     with torch.no_grad():
@@ -568,8 +571,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="cfg4", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the global batch (small cases for profiling)")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.batch:
+        cfg["B"] = args.batch
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

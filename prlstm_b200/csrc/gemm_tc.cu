@@ -108,6 +108,20 @@ HS_DEV void tma_2d(void *dst, const CUtensorMap *tm, uint64_t *bar, int c0, int 
       : "memory");
 }
 
+// Output maps are 3D {N, M, splits}: a split-K partial is clipped to its own
+// M rows, and the unsplit output is the splits = 1 case.
+HS_DEV void tma_store_3d(const CUtensorMap *tm, const void *src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(tm),
+               "r"(c0), "r"(c1), "r"(c2), "r"(su32(src))
+               : "memory");
+}
+HS_DEV void tma_reduce_add_3d(const CUtensorMap *tm, const void *src, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(tm),
+      "r"(c0), "r"(c1), "r"(c2), "r"(su32(src))
+      : "memory");
+}
+
 // Shared-memory matrix descriptor (sm100 version bits).  Layout type 2 is
 // the 128-byte swizzle of K-major tiles (16-byte chunks XOR row%8); layout
 // type 1 is the 128-byte swizzle with 32-byte atoms (32-byte chunks XOR
@@ -171,7 +185,8 @@ struct TcArgs {
 
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(NTHREADS, 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcArgs p) {
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmC, TcArgs p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
@@ -344,38 +359,47 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       ++drained;
     }
     if (ok) {
-      const int64_t m = m0 + q * 32 + lane;
-      if (m < p.M) {
-        float *dst = p.partial ? p.partial + (int64_t)blockIdx.z * p.M * p.N : p.C;
-        const int64_t ld = p.partial ? p.N : p.ldc;
-        const bool direct = p.partial == nullptr;
-        float *row = dst + m * ld + n0;
-        if (n0 + BN <= p.N && (ld % 4) == 0) {
+      // Stage the tile in shared memory (stage 0 is free: every MMA has
+      // completed) as four 128-row x 32-column boxes with the 128-byte
+      // swizzle (conflict-free row-per-thread writes), then write it with
+      // TMA bulk stores (reduce-add when beta = 1).
+      const int r = q * 32 + lane;
+      const bool direct = p.partial == nullptr;
+      float *box0 = reinterpret_cast<float *>(smem);
 #pragma unroll
-          for (int j = 0; j < BN; j += 4) {
-            float4 o = make_float4(tot[j], tot[j + 1], tot[j + 2], tot[j + 3]);
-            if (direct && p.bias) {
-              o.x += p.bias[n0 + j]; o.y += p.bias[n0 + j + 1];
-              o.z += p.bias[n0 + j + 2]; o.w += p.bias[n0 + j + 3];
-            }
-            if (direct && p.beta) {
-              const float4 old = *reinterpret_cast<const float4 *>(row + j);
-              o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
-            }
-            *reinterpret_cast<float4 *>(row + j) = o;
-          }
-        } else {
+      for (int c = 0; c < BN / 32; ++c) {
+        float *boxc = box0 + c * (BM * 32);
 #pragma unroll
-          for (int j = 0; j < BN; ++j) {
-            if (n0 + j < p.N) {
-              float o = tot[j];
-              if (direct && p.bias) o += p.bias[n0 + j];
-              if (direct && p.beta) o += row[j];
-              row[j] = o;
+        for (int j = 0; j < 8; ++j) {
+          float4 o = make_float4(tot[c * 32 + 4 * j], tot[c * 32 + 4 * j + 1], tot[c * 32 + 4 * j + 2],
+                                 tot[c * 32 + 4 * j + 3]);
+          if (direct && p.bias) {
+            const int64_t n = n0 + c * 32 + 4 * j;
+            if (n + 3 < p.N) {
+              const float4 bb = *reinterpret_cast<const float4 *>(p.bias + n);
+              o.x += bb.x; o.y += bb.y; o.z += bb.z; o.w += bb.w;
+            } else {
+              if (n < p.N) o.x += p.bias[n];
+              if (n + 1 < p.N) o.y += p.bias[n + 1];
+              if (n + 2 < p.N) o.z += p.bias[n + 2];
             }
           }
+          *reinterpret_cast<float4 *>(boxc + r * 32 + ((j ^ (r & 7)) * 4)) = o;
         }
       }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (t == 0) {
+        const int zc = p.partial ? (int)blockIdx.z : 0;
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          if (direct && p.beta) tma_reduce_add_3d(&tmC, box0 + c * (BM * 32), (int)n0 + 32 * c, (int)m0, zc);
+          else tma_store_3d(&tmC, box0 + c * (BM * 32), (int)n0 + 32 * c, (int)m0, zc);
+        }
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
     }
   }
 
@@ -412,6 +436,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   });
   return fn;
+}
+
+// Output map: C [splits][M][N] fp32 with row stride ld; 32-column x 128-row
+// boxes, 128-byte swizzle (matches the epilogue's shared-memory staging).
+bool make_out_map(CUtensorMap *tm, float *ptr, int64_t splits, int64_t M, int64_t N, int64_t ld) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)splits};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)(ld * M * 4)};
+  cuuint32_t box[3] = {32, (cuuint32_t)BM, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)ptr, dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Operand view: element (r, k) of an R x K operand (R = M for A, N for B).
@@ -492,7 +530,7 @@ TcPlan plan_tc(const float *A, const float *B, float *C, int64_t M, int64_t N, i
   if (!tc_enabled()) return pl;
   if ((double)M * N * K < tc_min_mnk()) return pl;  // small products: FFMA path
   auto al = [](const void *p) { return aligned(p, 16); };
-  if (!al(A) || !al(B) || !al(C) || lda % 4 || ldb % 4) return pl;
+  if (!al(A) || !al(B) || !al(C) || lda % 4 || ldb % 4 || ldc % 4 || N % 4) return pl;
   if (a_kc ? (K % 4) : (M % 4)) return pl;
   if (b_kc ? (K % 4) : (N % 4)) return pl;
   if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) return pl;
@@ -533,9 +571,11 @@ int gemm_tc_try(const float *A, const float *B, float *C, const float *bias, int
     pl.kbps = pl.nkb;
     pl.ws = 0;
   }
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tc;
   if (!make_map(&ta, A, M, K, lda, !a_kc, BM)) return HS_OK;
   if (!make_map(&tb, B, N, K, ldb, !b_kc, BN)) return HS_OK;
+  float *cdst = pl.splits > 1 ? static_cast<float *>(ws) : C;
+  if (!make_out_map(&tc, cdst, pl.splits, M, N, pl.splits > 1 ? N : ldc)) return HS_OK;
   TcArgs args;
   args.C = C;
   args.bias = bias;
@@ -549,7 +589,7 @@ int gemm_tc_try(const float *A, const float *B, float *C, const float *bias, int
   args.nkb = pl.nkb;
   args.status = status;
   const dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), (unsigned)pl.splits);
-  void (*fn)(const CUtensorMap, const CUtensorMap, TcArgs);
+  void (*fn)(const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs);
   if (!a_kc && !b_kc) fn = gemm_tc_kernel<true, true>;
   else if (!a_kc) fn = gemm_tc_kernel<true, false>;
   else if (!b_kc) fn = gemm_tc_kernel<false, true>;
@@ -560,7 +600,7 @@ int gemm_tc_try(const float *A, const float *B, float *C, const float *bias, int
     cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   });
   if (grid.y > 65535) return HS_OK;
-  fn<<<grid, NTHREADS, SMEM_BYTES, st>>>(ta, tb, args);
+  fn<<<grid, NTHREADS, SMEM_BYTES, st>>>(ta, tb, tc, args);
   if (int e = check_launch("gemm_tc_kernel")) return e;
   if (pl.splits > 1) {
     const int64_t n = M * N;

@@ -73,7 +73,7 @@ def test_linear_dgrad(M, N, K):
 
 @pytest.mark.parametrize("M,N,K,beta,use_ws", [(8192, 2048, 512, 0, True), (8192, 2048, 512, 1, True),
                                                (8192, 2048, 512, 1, False), (65536, 4096, 512, 0, True),
-                                               (2000, 1024, 256, 0, True)])
+                                               (2000, 1024, 256, 0, True), (2000, 1000, 260, 1, True)])
 def test_linear_wgrad(M, N, K, beta, use_ws):
     L = _lib()
     dev = torch.device("cuda", 0)
