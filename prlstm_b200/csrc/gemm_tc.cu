@@ -99,6 +99,13 @@ HS_DEV bool mbar_wait(uint64_t *b, uint32_t parity, int *status) {
   }
   return true;
 }
+// Bounded wait that records nothing (used when draining on an abort path).
+HS_DEV void mbar_drain(uint64_t *b, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try(b, parity)) {
+    if (globaltimer() - t0 > kWaitLimitNs) return;
+  }
+}
 
 HS_DEV void tma_2d(void *dst, const CUtensorMap *tm, uint64_t *bar, int c0, int c1) {
   asm volatile(
@@ -259,8 +266,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       // Never leave while a copy into this CTA's shared memory is in flight:
       // wait (bounded) for the last load issued into each stage.
       for (int i = std::max(0, issued - STAGES); i < issued; ++i) {
-        int dummy = 0;
-        (void)mbar_wait(&full[i % STAGES], (i / STAGES) & 1, ld_status(p.status) ? &dummy : p.status);
+        if (ld_status(p.status)) mbar_drain(&full[i % STAGES], (i / STAGES) & 1);
+        else (void)mbar_wait(&full[i % STAGES], (i / STAGES) & 1, p.status);
       }
     }
   } else if (!skip && warp == 1) {

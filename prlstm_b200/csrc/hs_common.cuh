@@ -96,6 +96,14 @@ template <> struct Vec<4> {
   HS_DEV void store_cs(float *p) const { __stcs(reinterpret_cast<float4 *>(p), make_float4(v[0], v[1], v[2], v[3])); }
 };
 
+// Look-back state shared by the scan kernels (scan.cu, scan_tma.cu).
+struct ScanTmaWs {
+  unsigned *ticket;
+  unsigned *flags;  // per tile slot: 0 empty, 1 aggregate ready, 2 inclusive ready
+  float *agg_a, *agg_c, *incl;
+  float *db_part;   // bias-gradient partial rows (backward)
+};
+
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 

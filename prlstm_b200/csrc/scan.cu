@@ -28,6 +28,18 @@
 #include "hs_common.cuh"
 
 namespace hs {
+
+int scan_tma_fwd_chunk();
+int scan_tma_bwd_chunk();
+int scan_tma_grid(unsigned ntiles);
+int scan_fwd_tma_launch(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
+                        int64_t T, int64_t B, int64_t H, float eps, const ScanTmaWs &ws, int nchunk, int nhb,
+                        int *status, cudaStream_t st, bool *done);
+int scan_bwd_tma_launch(const float *z, const float *c, const float *c0, const float *dout,
+                        const float *dh_n, const float *dc_n, float *dz, float *dc0, int64_t T, int64_t B,
+                        int64_t H, float eps, const ScanTmaWs &ws, int nchunk, int nhb, int *status,
+                        cudaStream_t st, bool *done);
+
 namespace {
 
 struct ScanWs {
@@ -44,8 +56,25 @@ struct ScanShape {
   int nchunk, nhb;
 };
 
-constexpr int kFwdS = 4, kFwdNW = 8;
-constexpr int kBwdS = 4, kBwdNW = 8;
+// Tile geometry of the per-tile kernels (compile-time; the defaults are the
+// measured best on B200 for the benchmark shapes).
+#ifndef HS_SCAN_FWD_S
+#define HS_SCAN_FWD_S 4
+#endif
+#ifndef HS_SCAN_FWD_NW
+#define HS_SCAN_FWD_NW 8
+#endif
+#ifndef HS_SCAN_BWD_S
+#define HS_SCAN_BWD_S 4
+#endif
+#ifndef HS_SCAN_BWD_NW
+#define HS_SCAN_BWD_NW 8
+#endif
+#ifndef HS_SCAN_USE_TMA
+#define HS_SCAN_USE_TMA 1
+#endif
+constexpr int kFwdS = HS_SCAN_FWD_S, kFwdNW = HS_SCAN_FWD_NW;
+constexpr int kBwdS = HS_SCAN_BWD_S, kBwdNW = HS_SCAN_BWD_NW;
 
 template <int VEC> __host__ __device__ constexpr int hw() { return 32 * VEC; }
 
@@ -62,7 +91,10 @@ size_t ws_layout(const ScanShape &s, int HW, bool with_db, ScanWs *out, void *ba
   size_t o_a = take(sizeof(float) * nslot * HW);
   size_t o_c = take(sizeof(float) * nslot * HW);
   size_t o_i = take(sizeof(float) * nslot * HW);
-  size_t o_db = with_db ? take(sizeof(float) * (size_t)s.nchunk * s.B * 4 * s.H) : off;
+  // bias partial rows: one per (chunk, sequence) for the per-tile kernel, one
+  // per CTA (<= 256) for the persistent kernel
+  const size_t db_rows = std::max<int64_t>((int64_t)s.nchunk * s.B, 256);
+  size_t o_db = with_db ? take(sizeof(float) * db_rows * 4 * s.H) : off;
   if (out) {
     char *b = static_cast<char *>(base);
     out->ticket = reinterpret_cast<unsigned *>(b + o_ticket);
@@ -81,6 +113,14 @@ size_t ws_zero_bytes(const ScanShape &s) {
   const int64_t nslot = (int64_t)s.nchunk * s.B * s.nhb;
   return round_up(sizeof(unsigned), 256) + sizeof(unsigned) * nslot;
 }
+
+#ifndef HS_SCAN_FAST_SIG
+#define HS_SCAN_FAST_SIG 0
+#endif
+#if HS_SCAN_FAST_SIG
+// hardware exp2 with a correctly rounded reciprocal (see scan_tma.cu)
+#define sigm(x) __frcp_rn(1.0f + __expf(-(x)))
+#endif
 
 // ============================================================== forward
 template <int VEC, int S, int NW>
@@ -525,10 +565,11 @@ ScanShape make_shape(int64_t T, int64_t B, int64_t H, int L, int HW) {
 size_t scan_ws_bytes(int64_t T, int64_t B, int64_t H) {
   size_t m = 0;
   for (int HW : {32, 128}) {
-    ScanShape f = make_shape(T, B, H, kFwdS * kFwdNW, HW);
-    ScanShape b = make_shape(T, B, H, kBwdS * kBwdNW, HW);
-    m = std::max(m, ws_layout(f, HW, false, nullptr, nullptr));
-    m = std::max(m, ws_layout(b, HW, true, nullptr, nullptr));
+    for (int L : {kFwdS * kFwdNW, kBwdS * kBwdNW, scan_tma_fwd_chunk(), scan_tma_bwd_chunk()}) {
+      ScanShape f = make_shape(T, B, H, L, HW);
+      m = std::max(m, ws_layout(f, HW, false, nullptr, nullptr));
+      m = std::max(m, ws_layout(f, HW, true, nullptr, nullptr));
+    }
   }
   return m;
 }
@@ -552,11 +593,22 @@ int scan_forward(const float *z, const float *c0, float *out, float *c, float *h
   if (!z || !out || !c || !status) return fail(HS_ERR_INVALID_ARG, "scan_forward: null z/out/c/status");
   const int VEC = pick_vec(H, {z, c0, out, c, h_n, c_n});
   const int HW = 32 * VEC;
+  if (!ws_base || !aligned(ws_base, 256)) return fail(HS_ERR_INVALID_ARG, "workspace must be non-null and 256-byte aligned");
+  if (VEC == 4 && HS_SCAN_USE_TMA) {  // persistent TMA kernel
+    ScanShape sh = make_shape(T, B, H, scan_tma_fwd_chunk(), HW);
+    ScanWs w;
+    const size_t need = ws_layout(sh, HW, false, &w, ws_base);
+    if (ws_bytes < need) return fail(HS_ERR_WORKSPACE, "scan_forward: workspace %zu < %zu bytes", ws_bytes, need);
+    if (cudaMemsetAsync(ws_base, 0, ws_zero_bytes(sh), st) != cudaSuccess) return check_launch("scan_forward memset");
+    ScanTmaWs tw{w.ticket, w.flags, w.agg_a, w.agg_c, w.incl, nullptr};
+    bool done = false;
+    if (int e = scan_fwd_tma_launch(z, c0, out, c, h_n, c_n, T, B, H, eps, tw, sh.nchunk, sh.nhb, status, st, &done)) return e;
+    if (done) return HS_OK;
+  }
   ScanShape sh = make_shape(T, B, H, kFwdS * kFwdNW, HW);
   ScanWs ws;
   const size_t need = ws_layout(sh, HW, false, &ws, ws_base);
-  if (!ws_base || ws_bytes < need) return fail(HS_ERR_WORKSPACE, "scan_forward: workspace %zu < %zu bytes", ws_bytes, need);
-  if (!aligned(ws_base, 256)) return fail(HS_ERR_INVALID_ARG, "workspace must be 256-byte aligned");
+  if (ws_bytes < need) return fail(HS_ERR_WORKSPACE, "scan_forward: workspace %zu < %zu bytes", ws_bytes, need);
   if (cudaMemsetAsync(ws_base, 0, ws_zero_bytes(sh), st) != cudaSuccess) return check_launch("scan_forward memset");
   const unsigned ntile = (unsigned)((int64_t)sh.nchunk * B * sh.nhb);
   if (VEC == 4)
@@ -574,11 +626,32 @@ int scan_backward(const float *z, const float *c, const float *c0, const float *
   if (!z || !c || !dout || !dz || !status) return fail(HS_ERR_INVALID_ARG, "scan_backward: null z/c/dout/dz/status");
   const int VEC = pick_vec(H, {z, c, c0, dout, dh_n, dc_n, dz, dc0});
   const int HW = 32 * VEC;
+  if (!ws_base || !aligned(ws_base, 256)) return fail(HS_ERR_INVALID_ARG, "workspace must be non-null and 256-byte aligned");
+  if (VEC == 4 && HS_SCAN_USE_TMA) {  // persistent TMA kernel
+    ScanShape sh = make_shape(T, B, H, scan_tma_bwd_chunk(), HW);
+    ScanWs w;
+    const size_t need = ws_layout(sh, HW, db != nullptr, &w, ws_base);
+    if (ws_bytes < need) return fail(HS_ERR_WORKSPACE, "scan_backward: workspace %zu < %zu bytes", ws_bytes, need);
+    if (cudaMemsetAsync(ws_base, 0, ws_zero_bytes(sh), st) != cudaSuccess) return check_launch("scan_backward memset");
+    ScanTmaWs tw{w.ticket, w.flags, w.agg_a, w.agg_c, w.incl, w.db_part};
+    bool done = false;
+    if (int e = scan_bwd_tma_launch(z, c, c0, dout, dh_n, dc_n, dz, dc0, T, B, H, eps, tw, sh.nchunk, sh.nhb, status,
+                                    st, &done))
+      return e;
+    if (done) {
+      if (db) {
+        const int64_t N = 4 * H;
+        const int64_t R = scan_tma_grid((unsigned)((int64_t)sh.nchunk * B * sh.nhb));
+        rowsum_kernel<<<(unsigned)((N + 255) / 256), 256, 0, st>>>(w.db_part, db, R, N, 0);
+        return check_launch("rowsum_kernel");
+      }
+      return HS_OK;
+    }
+  }
   ScanShape sh = make_shape(T, B, H, kBwdS * kBwdNW, HW);
   ScanWs ws;
   const size_t need = ws_layout(sh, HW, db != nullptr, &ws, ws_base);
-  if (!ws_base || ws_bytes < need) return fail(HS_ERR_WORKSPACE, "scan_backward: workspace %zu < %zu bytes", ws_bytes, need);
-  if (!aligned(ws_base, 256)) return fail(HS_ERR_INVALID_ARG, "workspace must be 256-byte aligned");
+  if (ws_bytes < need) return fail(HS_ERR_WORKSPACE, "scan_backward: workspace %zu < %zu bytes", ws_bytes, need);
   if (cudaMemsetAsync(ws_base, 0, ws_zero_bytes(sh), st) != cudaSuccess) return check_launch("scan_backward memset");
   const unsigned ntile = (unsigned)((int64_t)sh.nchunk * B * sh.nhb);
   if (VEC == 4)
