@@ -245,6 +245,7 @@ def run_ours(args, cfg, rank, world, dev):
 
     import prlstm_b200
     from prlstm_b200 import _lib
+    from prlstm_b200.data_parallel import GradAllReducer
 
     T, D, H = cfg["T"], cfg["D"], cfg["H"]
     B_global = cfg["B"]
@@ -260,10 +261,13 @@ def run_ours(args, cfg, rank, world, dev):
         x, G = make_data(cfg, B_local, rank, dev)
     peak_hbm, peak_tf, peak_kind = _peaks()
 
+    # one SUM all-reduce of the packed gradients per step (batch sharding:
+    # summed shard gradients equal the full-batch gradients)
+    reducer = GradAllReducer()
+
     def allreduce(tensors):
         if world > 1:
-            for t in tensors:
-                dist.all_reduce(t, op=dist.ReduceOp.SUM)
+            reducer(tensors)
 
     def sync():
         torch.cuda.synchronize(dev)

@@ -69,6 +69,13 @@ HS_API int hs_clear_status(int *dev_status, hs_stream_t stream);
  * (the reference has no device-side waits). */
 HS_API int hs_selftest_bounded_wait(const unsigned *flag, int *dev_status, uint64_t limit_ns,
                                     hs_stream_t stream);
+/* Accuracy self test of the scan kernels' activation functions: evaluates
+ * the logistic sigmoid on n points of [-lim, lim] and tanh on n points of
+ * (0, lim] (half of them in (0, 0.25)) and writes the largest relative errors
+ * against double precision to max_rel_err[0] (sigmoid) and [1] (tanh), a
+ * device array of two floats.  No reference counterpart (the reference calls
+ * ATen's sigmoid and tanh). */
+HS_API int hs_selftest_activations(float *max_rel_err, int n, float lim, hs_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Linear-layer GEMMs (fp32 in, fp32 out, fp32-accurate).
@@ -136,7 +143,8 @@ HS_API int hs_scan_backward(const float *z, const float *c, const float *c0, con
  * reference, which allocates through PyTorch.  The look-back scratch is a
  * fixed 8 MiB device array inside the library (held by every GPU that loads
  * it, until exit); shapes whose scratch exceeds it are rejected with
- * HS_ERR_UNSUPPORTED before any launch (roughly T*B*H <= 22M elements).
+ * HS_ERR_UNSUPPORTED before any launch: the scratch is ceil(T/8) * B *
+ * ceil(H/32) * 256 bytes, so roughly T*B*H <= 8M elements.
  * The first call on each device looks up the array's device address, so
  * make that first call before any stream capture.  All calls share the
  * array: calls that overlap on the GPU (other streams, other threads) race

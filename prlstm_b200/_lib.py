@@ -35,6 +35,7 @@ SIGNATURES = {
     "hs_read_status": (_i32, [_c_p, _c_p, _c_p]),
     "hs_clear_status": (_i32, [_c_p, _c_p]),
     "hs_selftest_bounded_wait": (_i32, [_c_p, _c_p, ctypes.c_uint64, _c_p]),
+    "hs_selftest_activations": (_i32, [_c_p, _i32, _f32, _c_p]),
     "hs_linear_workspace_bytes": (_sz, [_i64] * 3),
     "hs_linear_forward": (_i32, [_c_p] * 4 + [_i64] * 3 + [_c_p, _sz, _c_p, _c_p]),
     "hs_linear_dgrad": (_i32, [_c_p] * 3 + [_i64] * 3 + [_c_p, _sz, _c_p, _c_p]),

@@ -119,6 +119,27 @@ namespace {
 __global__ void selftest_wait_kernel(const unsigned *flag, int *status, uint64_t limit_ns) {
   if (threadIdx.x == 0) (void)wait_flag(flag, status, limit_ns);
 }
+
+// Relative errors of the scan's activations against double precision:
+// sigf over x in [-lim, lim] and tanh_pos over c in (0, lim], n points each
+// (uniform in x, plus the small-argument range of tanh_pos densely), folded
+// into out[0] (sigmoid) and out[1] (tanh) as max |rel err| by atomicMax on
+// the float bits (valid for non-negative floats).
+__global__ void selftest_activation_kernel(float *out, int n, float lim) {
+  float es = 0.f, et = 0.f;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float u = (i + 0.5f) / n;
+    const float x = -lim + 2.f * lim * u;
+    const double sd = 1.0 / (1.0 + exp(-(double)x));
+    const float sg = sigf(x);
+    if (sd > 1e-30) es = fmaxf(es, (float)(fabs((double)sg - sd) / sd));
+    const float c = i & 1 ? lim * u : 0.25f * u;  // odd points: (0, lim]; even: (0, 0.25)
+    const double td = tanh((double)c);
+    et = fmaxf(et, (float)(fabs((double)tanh_pos(c) - td) / td));
+  }
+  atomicMax(reinterpret_cast<unsigned *>(out), __float_as_uint(es));
+  atomicMax(reinterpret_cast<unsigned *>(out + 1), __float_as_uint(et));
+}
 }  // namespace
 
 }  // namespace hs
@@ -162,6 +183,14 @@ int hs_selftest_bounded_wait(const unsigned *flag, int *dev_status, uint64_t lim
   if (limit_ns > hs::kWaitLimitNs) return hs::fail(HS_ERR_INVALID_ARG, "limit above the library's wait bound");
   hs::selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flag, dev_status, limit_ns);
   return hs::check_launch("selftest_wait_kernel");
+}
+
+int hs_selftest_activations(float *max_rel_err, int n, float lim, hs_stream_t stream) {
+  if (!max_rel_err || n <= 0 || !(lim > 0.f)) return hs::fail(HS_ERR_INVALID_ARG, "selftest_activations: bad args");
+  if (cudaMemsetAsync(max_rel_err, 0, 2 * sizeof(float), (cudaStream_t)stream) != cudaSuccess)
+    return hs::check_launch("selftest_activations memset");
+  hs::selftest_activation_kernel<<<148, 256, 0, (cudaStream_t)stream>>>(max_rel_err, n, lim);
+  return hs::check_launch("selftest_activation_kernel");
 }
 
 size_t hs_linear_workspace_bytes(int64_t M, int64_t N, int64_t K) {

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <atomic>
 #include <stdint.h>
 #include <stdio.h>
 
@@ -23,6 +24,55 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 // ---------------------------------------------------------------- math
 // Logistic sigmoid from expf; 1/(1+inf) = 0 keeps the large-negative tail exact.
 HS_DEV float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
+#ifndef HS_SIGF_NR
+#define HS_SIGF_NR 1
+#endif
+#ifndef HS_TANH_POLY
+#define HS_TANH_POLY 1
+#endif
+// Reciprocal of d >= 1: the hardware approximation refined by one
+// Newton-Raphson step, r' = r + r (1 - d r) (the classical iteration for 1/d,
+// which squares the relative error of the seed).  One step brings the ~1 ulp
+// seed to within rounding of the correctly rounded result, for three
+// instructions instead of the IEEE-rounded reciprocal's longer sequence.
+// d = +inf gives 0 (the step itself would form inf*0); a NaN stays NaN.
+HS_DEV float rcp_nr(float d) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  const float n = fmaf(r, fmaf(-d, r, 1.0f), r);
+  return d == __int_as_float(0x7f800000) ? 0.0f : n;
+}
+// Scan-path sigmoid: hardware exp and a reciprocal rounded to (nearly) the
+// correctly rounded value.  The rounding of the reciprocal matters: an
+// approximate divide biases every forget gate by about an ulp, which the
+// product of thousands of gates turns into a 1e-5 error of c at T = 2048.
+HS_DEV float sigf(float x) {
+#if HS_SIGF_NR
+  return rcp_nr(1.0f + __expf(-x));
+#else
+  return __frcp_rn(1.0f + __expf(-x));
+#endif
+}
+// tanh for c >= 0 (the scan's cell state is positive): (1 - e^-2c)/(1 + e^-2c)
+// from the hardware exp.  Below 0.25 that form loses relative accuracy to
+// cancellation, so small arguments use the odd Taylor series of tanh,
+//   c - c^3/3 + 2c^5/15 - 17c^7/315 + 62c^9/2835,
+// whose first omitted term (1382/155925 c^11) is below 1e-8 relative there.
+HS_DEV float tanh_pos(float c) {
+#if HS_TANH_POLY
+  if (c < 0.25f) {
+    const float u = c * c;
+    float p = fmaf(u, 62.0f / 2835.0f, -17.0f / 315.0f);
+    p = fmaf(p, u, 2.0f / 15.0f);
+    p = fmaf(p, u, -1.0f / 3.0f);
+    return fmaf(p * u, c, c);
+  }
+#else
+  if (c < 0.25f) return tanhf(c);
+#endif
+  const float e = __expf(-2.0f * c);
+  return __fdividef(1.0f - e, 1.0f + e);
+}
 
 // ---------------------------------------------------------------- memory model
 HS_DEV uint64_t globaltimer() {
@@ -96,13 +146,19 @@ template <> struct Vec<4> {
   HS_DEV void store_cs(float *p) const { __stcs(reinterpret_cast<float4 *>(p), make_float4(v[0], v[1], v[2], v[3])); }
 };
 
-// Look-back state shared by the scan kernels (scan.cu, scan_tma.cu).
-struct ScanTmaWs {
-  unsigned *ticket;
-  unsigned *flags;  // per tile slot: 0 empty, 1 aggregate ready, 2 inclusive ready
-  float *agg_a, *agg_c, *incl;
-  float *db_part;   // bias-gradient partial rows (backward)
-};
+// Raises a kernel's dynamic shared-memory limit to `bytes`, once per device
+// (the attribute belongs to the device's context); `done` is the kernel's
+// bit mask of devices already set.
+inline int allow_dynamic_smem(const void *fn, size_t bytes, std::atomic<unsigned long long> *done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("cudaGetDevice");
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done->load(std::memory_order_relaxed) & bit) return HS_OK;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
+    return check_launch("cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+  done->fetch_or(bit);
+  return HS_OK;
+}
 
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }

@@ -17,651 +17,531 @@
 // e_t = f'_t (dcd_t + e_{t+1}), the gradient reaching c_{t-1}; the autograd
 // backward of _parallel.py:21-74 computes the same quantities through ATen.
 //
-// Layout: z [T,B,4H] (gate order i,f,g,o), c/out/dout [T,B,H].  A warp owns
-// 32*VEC consecutive hidden units (float4 when H%4==0), a thread owns S
-// consecutive time steps, a CTA stacks NW warps along time: a tile is
-// (L = NW*S steps) x (one sequence b) x (32*VEC units).  Tiles are handed out
-// in time-major order by an atomic ticket, so a tile's predecessor has always
-// started before it (the look-back can never wait on an unscheduled CTA).
+// Layout: z [T,B,4H] (gate order i,f,g,o), c/out/dout [T,B,H].
+//
+// Work split: a warp tile is L consecutive time steps x 32 consecutive hidden
+// units of one sequence; lane l owns unit h0+l and walks the L steps itself.
+// The warp stages its tile into shared memory with cp.async (16-byte copies
+// when H%4 == 0, so in-flight data holds no registers and many tiles per SM
+// are in flight), computes its summary, runs its own look-back (one 64-bit
+// word per lane, no block barrier), and writes its outputs.  A CTA stacks WPC
+// warps on WPC consecutive chunks of the same 32-unit column; the backward
+// adds the CTA's bias-gradient sums in a fixed order into one partial row.
+//
+// Ordering: blockIdx.x runs over tiles in scan order (chunk-group major), so
+// every predecessor of a tile sits in a lower-indexed block, or in a lower
+// warp of the same block, and is dispatched no later than the tile itself;
+// every wait is also bounded in time and reports HS_ERR_DEVICE_TIMEOUT
+// instead of hanging.
+//
+// When the columns (sequence x 32 units) alone fill the GPU, the one-CTA-per-
+// column kernels of scan_chain.cu run instead (see scan_chain_wanted): they
+// pass the carry between the warps of a CTA through shared memory and need
+// no look-back scratch.
 #include <mutex>
 
 #include "hs_common.cuh"
 
 namespace hs {
 
-int scan_tma_fwd_chunk();
-int scan_tma_bwd_chunk();
-int scan_tma_grid(unsigned ntiles);
-int scan_fwd_tma_launch(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
-                        int64_t T, int64_t B, int64_t H, float eps, const ScanTmaWs &ws, int nchunk, int nhb,
-                        int *status, cudaStream_t st, bool *done);
-int scan_bwd_tma_launch(const float *z, const float *c, const float *c0, const float *dout,
-                        const float *dh_n, const float *dc_n, float *dz, float *dc0, int64_t T, int64_t B,
-                        int64_t H, float eps, const ScanTmaWs &ws, int nchunk, int nhb, int *status,
-                        cudaStream_t st, bool *done);
+bool scan_chain_wanted(int64_t T, int64_t B, int64_t H);
+int scan_fwd_chain_launch(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
+                          int64_t T, int64_t B, int64_t H, float eps, int *status, cudaStream_t st);
+int scan_bwd_chain_launch(const float *z, const float *c, const float *c0, const float *dout,
+                          const float *dh_n, const float *dc_n, float *dz, float *dc0, float *db_part,
+                          int64_t T, int64_t B, int64_t H, float eps, int *status, cudaStream_t st);
 
 namespace {
 
+// Look-back state.  One 64-bit word per (tile, hidden unit), stored
+// complemented so that the all-zero word means "not published yet" and the
+// workspace is cleared with a plain zero memset:
+//   hi == kInclusive : lo holds the tile's inclusive value (the carry out)
+//   otherwise        : the tile's aggregate, hi = bits of A, lo = bits of C.
+// A = prod f' lies in [0, 1] (never a NaN pattern) and hi == kInclusive is a
+// NaN pattern, so the three states cannot be confused.  Flag and payload
+// travel in one single-copy-atomic store: a reader that sees the word sees
+// its value, with no fence between them.
 struct ScanWs {
-  unsigned *ticket;
-  unsigned *flags;   // [nslot]: 0 empty, 1 aggregate ready, 2 inclusive ready
-  float *agg_a;      // [nslot][HW]
-  float *agg_c;      // [nslot][HW]
-  float *incl;       // [nslot][HW]
-  float *db_part;    // [nchunk*B][4H] (backward only)
+  unsigned long long *words;  // [nchunk][B*ncol][32]
+  float *db_part;             // [ngroup*B][4H] (backward only)
 };
 
 struct ScanShape {
   int64_t T, B, H;
-  int nchunk, nhb;
+  int nchunk;  // ceil(T / L)
+  int ncol;    // ceil(H / 32)
+  int ngroup;  // ceil(nchunk / WPC): CTAs along time per column
 };
 
-// Tile geometry of the per-tile kernels (compile-time; the defaults are the
-// measured best on B200 for the benchmark shapes).
-#ifndef HS_SCAN_FWD_S
-#define HS_SCAN_FWD_S 4
+// Tile geometry (compile-time; the defaults are the measured best on B200
+// for the benchmark shapes).  L = steps per warp tile, WPC = warps per CTA.
+#ifndef HS_SCAN_FWD_L
+#define HS_SCAN_FWD_L 8
 #endif
-#ifndef HS_SCAN_FWD_NW
-#define HS_SCAN_FWD_NW 8
+#ifndef HS_SCAN_FWD_WPC
+#define HS_SCAN_FWD_WPC 4
 #endif
-#ifndef HS_SCAN_BWD_S
-#define HS_SCAN_BWD_S 4
+#ifndef HS_SCAN_BWD_L
+#define HS_SCAN_BWD_L 8
 #endif
-#ifndef HS_SCAN_BWD_NW
-#define HS_SCAN_BWD_NW 8
+#ifndef HS_SCAN_BWD_WPC
+#define HS_SCAN_BWD_WPC 8
 #endif
-#ifndef HS_SCAN_USE_TMA
-#define HS_SCAN_USE_TMA 1
-#endif
-constexpr int kFwdS = HS_SCAN_FWD_S, kFwdNW = HS_SCAN_FWD_NW;
-constexpr int kBwdS = HS_SCAN_BWD_S, kBwdNW = HS_SCAN_BWD_NW;
+constexpr int kFwdL = HS_SCAN_FWD_L, kFwdWPC = HS_SCAN_FWD_WPC;
+constexpr int kBwdL = HS_SCAN_BWD_L, kBwdWPC = HS_SCAN_BWD_WPC;
+constexpr unsigned kInclusive = 0xFFFFFFFEu;
+constexpr int kFwdRow = 4 * 32;  // staged floats per forward step: z_i, z_f, z_g, z_o
+constexpr int kBwdRow = 6 * 32;  // backward: z_i, z_f, z_g, z_o, c, dout
+constexpr size_t kFwdSmem = sizeof(float) * kFwdWPC * kFwdL * kFwdRow;
+constexpr size_t kBwdSmem = sizeof(float) * kBwdWPC * (kBwdL * kBwdRow + 32);
 
-template <int VEC> __host__ __device__ constexpr int hw() { return 32 * VEC; }
-
-size_t ws_layout(const ScanShape &s, int HW, bool with_db, ScanWs *out, void *base) {
-  const int64_t nslot = (int64_t)s.nchunk * s.B * s.nhb;
-  size_t off = 0;
-  auto take = [&](size_t bytes) {
-    size_t o = off;
-    off = round_up(off + bytes, 256);
-    return o;
-  };
-  size_t o_ticket = take(sizeof(unsigned));
-  size_t o_flags = take(sizeof(unsigned) * nslot);
-  size_t o_a = take(sizeof(float) * nslot * HW);
-  size_t o_c = take(sizeof(float) * nslot * HW);
-  size_t o_i = take(sizeof(float) * nslot * HW);
-  // bias partial rows: one per (chunk, sequence) for the per-tile kernel, one
-  // per CTA (<= 256) for the persistent kernel
-  const size_t db_rows = std::max<int64_t>((int64_t)s.nchunk * s.B, 256);
-  size_t o_db = with_db ? take(sizeof(float) * db_rows * 4 * s.H) : off;
-  if (out) {
-    char *b = static_cast<char *>(base);
-    out->ticket = reinterpret_cast<unsigned *>(b + o_ticket);
-    out->flags = reinterpret_cast<unsigned *>(b + o_flags);
-    out->agg_a = reinterpret_cast<float *>(b + o_a);
-    out->agg_c = reinterpret_cast<float *>(b + o_c);
-    out->incl = reinterpret_cast<float *>(b + o_i);
-    out->db_part = with_db ? reinterpret_cast<float *>(b + o_db) : nullptr;
-  }
-  (void)o_db;
-  return off;
-}
-
-// Bytes of the part of the workspace that must be zero at launch (ticket+flags).
-size_t ws_zero_bytes(const ScanShape &s) {
-  const int64_t nslot = (int64_t)s.nchunk * s.B * s.nhb;
-  return round_up(sizeof(unsigned), 256) + sizeof(unsigned) * nslot;
-}
-
-#ifndef HS_SCAN_FAST_SIG
-#define HS_SCAN_FAST_SIG 0
-#endif
-#if HS_SCAN_FAST_SIG
-// hardware exp2 with a correctly rounded reciprocal (see scan_tma.cu)
-#define sigm(x) __frcp_rn(1.0f + __expf(-(x)))
-#endif
-
-// ============================================================== forward
-template <int VEC, int S, int NW>
-__global__ void __launch_bounds__(NW * 32)
-scan_fwd_kernel(const float *__restrict__ z, const float *__restrict__ c0,
-                float *__restrict__ out, float *__restrict__ cbuf,
-                float *__restrict__ h_n, float *__restrict__ c_n,
-                ScanShape sh, float eps, ScanWs ws, int *status) {
-  constexpr int HW = hw<VEC>();
-  constexpr int L = S * NW;
-  __shared__ float sA[NW][HW];
-  __shared__ float sC[NW][HW];
-  __shared__ float s_carry[HW];
-  __shared__ unsigned s_tile;
-  __shared__ int s_abort;
-
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (threadIdx.x == 0) {
-    s_tile = atomicAdd(ws.ticket, 1u);
-    s_abort = ld_status(status) != 0;
-  }
-  __syncthreads();
-  if (s_abort) return;
-  const unsigned tile = s_tile;
-  const int64_t T = sh.T, B = sh.B, H = sh.H;
-  const unsigned per_chunk = (unsigned)(B * sh.nhb);
-  const int j = tile / per_chunk;
-  const unsigned r = tile - j * per_chunk;
-  const int64_t b = r / sh.nhb;
-  const int hb = r - b * sh.nhb;
-  const int64_t h = (int64_t)hb * HW + lane * VEC;
-  const bool hv = h < H;
-  const int64_t t0 = (int64_t)j * L + warp * S;
-
-  // Pass 1: activations and this thread's summary over its S steps.
-  float fp[S][VEC], bp[S][VEC], og[S][VEC];
-#pragma unroll
-  for (int s = 0; s < S; ++s) {
-    const int64_t t = t0 + s;
-    if (hv && t < T) {
-      const float *zr = z + (t * B + b) * 4 * H + h;
-      Vec<VEC> zi, zf, zg, zo;
-      zi.load_cs(zr);
-      zf.load_cs(zr + H);
-      zg.load_cs(zr + 2 * H);
-      zo.load_cs(zr + 3 * H);
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        const float ig = sigm(zi.v[v]) * sigm(zg.v[v]);
-        fp[s][v] = fmaxf(sigm(zf.v[v]), eps);
-        bp[s][v] = fmaxf(ig, eps);
-        og[s][v] = sigm(zo.v[v]);
-      }
-    } else {
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) { fp[s][v] = 1.f; bp[s][v] = 0.f; og[s][v] = 0.f; }
-    }
-  }
-  float A[VEC], C[VEC];
-#pragma unroll
-  for (int v = 0; v < VEC; ++v) { A[v] = 1.f; C[v] = 0.f; }
-#pragma unroll
-  for (int s = 0; s < S; ++s)
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) { C[v] = fmaf(fp[s][v], C[v], bp[s][v]); A[v] *= fp[s][v]; }
-#pragma unroll
-  for (int v = 0; v < VEC; ++v) { sA[warp][lane * VEC + v] = A[v]; sC[warp][lane * VEC + v] = C[v]; }
-  __syncthreads();
-
-  // Tile summary, publication and look-back (warp 0; each lane is an
-  // independent chain for its VEC hidden units).
-  if (warp == 0) {
-    float TA[VEC], TC[VEC], cin[VEC];
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) { TA[v] = 1.f; TC[v] = 0.f; }
-#pragma unroll
-    for (int w = 0; w < NW; ++w)
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        const float a = sA[w][lane * VEC + v];
-        TC[v] = fmaf(a, TC[v], sC[w][lane * VEC + v]);
-        TA[v] *= a;
-      }
-    const int64_t slot = ((int64_t)j * B + b) * sh.nhb + hb;
-    float *my_incl = ws.incl + slot * HW + lane * VEC;
-    bool ok = true;
-    if (j == 0) {
-#pragma unroll
-      for (int v = 0; v < VEC; ++v)
-        cin[v] = fmaxf((c0 && hv) ? c0[b * H + h + v] : 0.f, eps);
-    } else {
-      Vec<VEC> va, vc;
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) { va.v[v] = TA[v]; vc.v[v] = TC[v]; }
-      va.store_cg(ws.agg_a + slot * HW + lane * VEC);
-      vc.store_cg(ws.agg_c + slot * HW + lane * VEC);
-      __threadfence();
-      __syncwarp();
-      if (lane == 0) st_release(ws.flags + slot, 1u);
-      float ra[VEC], rc[VEC];
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) { ra[v] = 1.f; rc[v] = 0.f; }
-      for (int k = j - 1; k >= 0; --k) {
-        const int64_t ks = ((int64_t)k * B + b) * sh.nhb + hb;
-        const unsigned f = wait_flag(ws.flags + ks, status);
-        if (f == 0) { ok = false; break; }
-        if (f == 2u) {
-          Vec<VEC> p;
-          p.load_cg(ws.incl + ks * HW + lane * VEC);
-#pragma unroll
-          for (int v = 0; v < VEC; ++v) cin[v] = fmaf(ra[v], p.v[v], rc[v]);
-          break;
-        }
-        Vec<VEC> ka, kc;
-        ka.load_cg(ws.agg_a + ks * HW + lane * VEC);
-        kc.load_cg(ws.agg_c + ks * HW + lane * VEC);
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) { rc[v] = fmaf(ra[v], kc.v[v], rc[v]); ra[v] *= ka.v[v]; }
-      }
-    }
-    if (ok) {
-      Vec<VEC> p;
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) p.v[v] = fmaf(TA[v], cin[v], TC[v]);
-      p.store_cg(my_incl);
-      __threadfence();
-    }
-    __syncwarp();
-    const bool all_ok = __all_sync(0xffffffffu, ok);
-    if (all_ok && lane == 0) st_release(ws.flags + slot, 2u);
-    if (lane == 0) s_abort = !all_ok;
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) s_carry[lane * VEC + v] = cin[v];
-  }
-  __syncthreads();
-  if (s_abort) return;
-
-  // Pass 2: carry into this warp's steps, then the exact recurrence.
-  float c[VEC];
-#pragma unroll
-  for (int v = 0; v < VEC; ++v) c[v] = s_carry[lane * VEC + v];
-  for (int w = 0; w < warp; ++w)
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) c[v] = fmaf(sA[w][lane * VEC + v], c[v], sC[w][lane * VEC + v]);
-  if (!hv) return;
-#pragma unroll
-  for (int s = 0; s < S; ++s) {
-    const int64_t t = t0 + s;
-    if (t >= T) break;
-    Vec<VEC> vc, vo;
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) {
-      c[v] = fmaf(fp[s][v], c[v], bp[s][v]);
-      vc.v[v] = c[v];
-      vo.v[v] = og[s][v] * tanhf(c[v]);
-    }
-    const int64_t o = (t * B + b) * H + h;
-    vc.store(cbuf + o);
-    vo.store(out + o);
-    if (t == T - 1) {
-      if (c_n) vc.store(c_n + b * H + h);
-      if (h_n) vo.store(h_n + b * H + h);
-    }
-  }
-}
-
-// ============================================================== backward
-template <int VEC, int S, int NW>
-__global__ void __launch_bounds__(NW * 32)
-scan_bwd_kernel(const float *z, const float *__restrict__ cbuf,
-                const float *__restrict__ c0, const float *__restrict__ dout,
-                const float *__restrict__ dh_n, const float *__restrict__ dc_n,
-                float *dz, float *__restrict__ dc0, ScanShape sh, float eps,
-                ScanWs ws, int *status) {
-  constexpr int HW = hw<VEC>();
-  constexpr int L = S * NW;
-  __shared__ float sA[NW][HW];
-  __shared__ float sC[NW][HW];
-  __shared__ float s_carry[HW];
-  __shared__ unsigned s_tile;
-  __shared__ int s_abort;
-
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (threadIdx.x == 0) {
-    s_tile = atomicAdd(ws.ticket, 1u);
-    s_abort = ld_status(status) != 0;
-  }
-  __syncthreads();
-  if (s_abort) return;
-  const unsigned tile = s_tile;
-  const int64_t T = sh.T, B = sh.B, H = sh.H;
-  const unsigned per_chunk = (unsigned)(B * sh.nhb);
-  const int q = tile / per_chunk;           // 0 = last chunk in time
-  const int j = sh.nchunk - 1 - q;
-  const unsigned r = tile - q * per_chunk;
-  const int64_t b = r / sh.nhb;
-  const int hb = r - b * sh.nhb;
-  const int64_t h = (int64_t)hb * HW + lane * VEC;
-  const bool hv = h < H;
-  const int64_t t0 = (int64_t)j * L + warp * S;
-
-  // Pass 1 (reverse time): per-step coefficients, the o-gate gradient (final
-  // already), and this thread's summary of e over its steps.
-  float FP[S][VEC], DCD[S][VEC], KI[S][VEC], KF[S][VEC], KG[S][VEC];
-  float acc[4][VEC];
-#pragma unroll
-  for (int g = 0; g < 4; ++g)
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) acc[g][v] = 0.f;
-  float cprev[VEC];
-  if (hv && t0 < T) {
-    if (t0 == 0) {
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) cprev[v] = fmaxf(c0 ? c0[b * H + h + v] : 0.f, eps);
-    } else {
-      Vec<VEC> t;
-      t.load(cbuf + ((t0 - 1) * B + b) * H + h);
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) cprev[v] = t.v[v];
-    }
-  }
-#pragma unroll
-  for (int s = 0; s < S; ++s) {
-    const int64_t t = t0 + s;
-    if (hv && t < T) {
-      const int64_t zo = (t * B + b) * 4 * H + h;
-      const int64_t so = (t * B + b) * H + h;
-      Vec<VEC> zi, zf, zg, zz, vc, vd;
-      zi.load_cs(z + zo);
-      zf.load_cs(z + zo + H);
-      zg.load_cs(z + zo + 2 * H);
-      zz.load_cs(z + zo + 3 * H);
-      vc.load(cbuf + so);
-      vd.load_cs(dout + so);
-      if (t == T - 1 && dh_n) {
-        Vec<VEC> e;
-        e.load(dh_n + b * H + h);
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) vd.v[v] += e.v[v];
-      }
-      Vec<VEC> dzo;
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        const float i = sigm(zi.v[v]), f = sigm(zf.v[v]), g = sigm(zg.v[v]), o = sigm(zz.v[v]);
-        const float th = tanhf(vc.v[v]);
-        const float mb = (i * g >= eps) ? 1.f : 0.f;
-        const float mf = (f >= eps) ? 1.f : 0.f;
-        FP[s][v] = fmaxf(f, eps);
-        DCD[s][v] = vd.v[v] * o * (1.f - th * th);
-        KI[s][v] = g * i * (1.f - i) * mb;
-        KF[s][v] = cprev[v] * f * (1.f - f) * mf;
-        KG[s][v] = i * g * (1.f - g) * mb;
-        dzo.v[v] = vd.v[v] * th * o * (1.f - o);
-        acc[3][v] += dzo.v[v];
-        cprev[v] = vc.v[v];
-      }
-      if (t == T - 1 && dc_n) {
-        Vec<VEC> e;
-        e.load(dc_n + b * H + h);
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) DCD[s][v] += e.v[v];
-      }
-      dzo.store_cs(dz + zo + 3 * H);
-    } else {
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) { FP[s][v] = 1.f; DCD[s][v] = 0.f; KI[s][v] = KF[s][v] = KG[s][v] = 0.f; }
-    }
-  }
-  float A[VEC], C[VEC];
-#pragma unroll
-  for (int v = 0; v < VEC; ++v) { A[v] = 1.f; C[v] = 0.f; }
-#pragma unroll
-  for (int s = S - 1; s >= 0; --s)
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) {
-      C[v] = FP[s][v] * (C[v] + DCD[s][v]);
-      A[v] *= FP[s][v];
-    }
-#pragma unroll
-  for (int v = 0; v < VEC; ++v) { sA[warp][lane * VEC + v] = A[v]; sC[warp][lane * VEC + v] = C[v]; }
-  __syncthreads();
-
-  if (warp == 0) {
-    float TA[VEC], TC[VEC], cin[VEC];
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) { TA[v] = 1.f; TC[v] = 0.f; cin[v] = 0.f; }
-#pragma unroll
-    for (int w = NW - 1; w >= 0; --w)
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        const float a = sA[w][lane * VEC + v];
-        TC[v] = fmaf(a, TC[v], sC[w][lane * VEC + v]);
-        TA[v] *= a;
-      }
-    const int64_t slot = ((int64_t)q * B + b) * sh.nhb + hb;
-    bool ok = true;
-    if (q > 0) {
-      Vec<VEC> va, vc;
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) { va.v[v] = TA[v]; vc.v[v] = TC[v]; }
-      va.store_cg(ws.agg_a + slot * HW + lane * VEC);
-      vc.store_cg(ws.agg_c + slot * HW + lane * VEC);
-      __threadfence();
-      __syncwarp();
-      if (lane == 0) st_release(ws.flags + slot, 1u);
-      float ra[VEC], rc[VEC];
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) { ra[v] = 1.f; rc[v] = 0.f; }
-      for (int k = q - 1; k >= 0; --k) {
-        const int64_t ks = ((int64_t)k * B + b) * sh.nhb + hb;
-        const unsigned f = wait_flag(ws.flags + ks, status);
-        if (f == 0) { ok = false; break; }
-        if (f == 2u) {
-          Vec<VEC> p;
-          p.load_cg(ws.incl + ks * HW + lane * VEC);
-#pragma unroll
-          for (int v = 0; v < VEC; ++v) cin[v] = fmaf(ra[v], p.v[v], rc[v]);
-          break;
-        }
-        Vec<VEC> ka, kc;
-        ka.load_cg(ws.agg_a + ks * HW + lane * VEC);
-        kc.load_cg(ws.agg_c + ks * HW + lane * VEC);
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) { rc[v] = fmaf(ra[v], kc.v[v], rc[v]); ra[v] *= ka.v[v]; }
-      }
-    }
-    if (ok) {
-      Vec<VEC> p;
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) p.v[v] = fmaf(TA[v], cin[v], TC[v]);
-      p.store_cg(ws.incl + slot * HW + lane * VEC);
-      __threadfence();
-    }
-    __syncwarp();
-    const bool all_ok = __all_sync(0xffffffffu, ok);
-    if (all_ok && lane == 0) st_release(ws.flags + slot, 2u);
-    if (lane == 0) s_abort = !all_ok;
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) s_carry[lane * VEC + v] = cin[v];
-  }
-  __syncthreads();
-  if (s_abort) return;
-
-  // Pass 2: e entering this warp's last step, then the exact reverse recurrence.
-  float e[VEC];
-#pragma unroll
-  for (int v = 0; v < VEC; ++v) e[v] = s_carry[lane * VEC + v];
-  for (int w = NW - 1; w > warp; --w)
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) e[v] = fmaf(sA[w][lane * VEC + v], e[v], sC[w][lane * VEC + v]);
-  if (hv) {
-#pragma unroll
-    for (int s = S - 1; s >= 0; --s) {
-      const int64_t t = t0 + s;
-      if (t >= T) continue;
-      Vec<VEC> di, df, dg;
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        const float dc = DCD[s][v] + e[v];
-        e[v] = FP[s][v] * dc;
-        di.v[v] = dc * KI[s][v];
-        df.v[v] = dc * KF[s][v];
-        dg.v[v] = dc * KG[s][v];
-        acc[0][v] += di.v[v];
-        acc[1][v] += df.v[v];
-        acc[2][v] += dg.v[v];
-      }
-      const int64_t zo = (t * B + b) * 4 * H + h;
-      di.store_cs(dz + zo);
-      df.store_cs(dz + zo + H);
-      dg.store_cs(dz + zo + 2 * H);
-      if (t == 0 && dc0) {
-        Vec<VEC> d;
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) d.v[v] = (c0 && c0[b * H + h + v] >= eps) ? e[v] : 0.f;
-        d.store(dc0 + b * H + h);
-      }
-    }
-  }
-
-  // Per-chunk column sums of dz for the bias gradient (deterministic order).
-  if (ws.db_part) {
-    __syncthreads();
-    float *red = &sA[0][0];  // reuse: NW x HW floats per gate
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) red[warp * HW + lane * VEC + v] = acc[g][v];
-      __syncthreads();
-      if (warp == 0 && hv) {
-        Vec<VEC> sum;
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) {
-          float a = 0.f;
-          for (int w = 0; w < NW; ++w) a += red[w * HW + lane * VEC + v];
-          sum.v[v] = a;
-        }
-        sum.store(ws.db_part + ((int64_t)j * B + b) * 4 * H + g * H + h);
-      }
-      __syncthreads();
-    }
-  }
-}
-
-// db[n] = beta*db[n] + sum_r part[r][n], fixed summation order.
-__global__ void rowsum_kernel(const float *__restrict__ part, float *__restrict__ db,
-                              int64_t R, int64_t N, int beta) {
-  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= N) return;
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-  int64_t r = 0;
-  for (; r + 4 <= R; r += 4) {
-    s0 += part[(r + 0) * N + n];
-    s1 += part[(r + 1) * N + n];
-    s2 += part[(r + 2) * N + n];
-    s3 += part[(r + 3) * N + n];
-  }
-  for (; r < R; ++r) s0 += part[r * N + n];
-  const float s = (s0 + s1) + (s2 + s3);
-  db[n] = beta ? db[n] + s : s;
-}
-
-int pick_vec(int64_t H, std::initializer_list<const void *> ptrs) {
-  if (H % 4 == 0) {
-    bool ok = true;
-    for (const void *p : ptrs) ok = ok && (p == nullptr || aligned(p, 16));
-    if (ok) return 4;
-  }
-  return 1;
-}
-
-ScanShape make_shape(int64_t T, int64_t B, int64_t H, int L, int HW) {
+ScanShape make_shape(int64_t T, int64_t B, int64_t H, int L, int WPC) {
   ScanShape s;
   s.T = T;
   s.B = B;
   s.H = H;
   s.nchunk = (int)((T + L - 1) / L);
-  s.nhb = (int)((H + HW - 1) / HW);
+  s.ncol = (int)((H + 31) / 32);
+  s.ngroup = (s.nchunk + WPC - 1) / WPC;
   return s;
 }
 
-size_t scan_ws_bytes(int64_t T, int64_t B, int64_t H) {
-  size_t m = 0;
-  for (int HW : {32, 128}) {
-    for (int L : {kFwdS * kFwdNW, kBwdS * kBwdNW, scan_tma_fwd_chunk(), scan_tma_bwd_chunk()}) {
-      ScanShape f = make_shape(T, B, H, L, HW);
-      m = std::max(m, ws_layout(f, HW, false, nullptr, nullptr));
-      m = std::max(m, ws_layout(f, HW, true, nullptr, nullptr));
+size_t ws_words_bytes(const ScanShape &s) {
+  return round_up(sizeof(unsigned long long) * (size_t)s.nchunk * s.B * s.ncol * 32, 256);
+}
+
+size_t ws_layout(const ScanShape &s, bool with_db, ScanWs *out, void *base) {
+  size_t off = ws_words_bytes(s);
+  const size_t o_db = off;
+  if (with_db) off += round_up(sizeof(float) * (size_t)s.ngroup * s.B * 4 * s.H, 256);
+  if (out) {
+    char *b = static_cast<char *>(base);
+    out->words = reinterpret_cast<unsigned long long *>(b);
+    out->db_part = with_db ? reinterpret_cast<float *>(b + o_db) : nullptr;
+  }
+  return off;
+}
+
+// ------------------------------------------------------------------ device helpers
+HS_DEV void cp_async16(float *dst, const float *src) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+HS_DEV void cp_async4(float *dst, const float *src) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+}
+HS_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+HS_DEV unsigned long long pack(unsigned hi, float lo) {
+  return ~(((unsigned long long)hi << 32) | __float_as_uint(lo));
+}
+HS_DEV void st_word(unsigned long long *p, unsigned long long w) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+HS_DEV unsigned long long ld_word(const unsigned long long *p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+
+// Decoupled look-back of one lane's unit.  (TA, TC) is the tile's own map
+// c_out = TA c_in + TC; k is the tile's position in scan order along its
+// chain, and the predecessors' words sit at my - m*stride.  On entry cin
+// holds the chain's initial carry (used when k == 0); on return it holds the
+// carry into this tile, and this tile's inclusive value is published.
+//
+// The aggregate is published first, so that successors can pass over this
+// tile while it looks back; then the predecessors are composed nearest first
+// (an aggregate extends the map, an inclusive value ends the look-back).
+// Reading several predecessors per round trip measured slower on B200 than
+// this one-at-a-time walk: the predecessors are mostly published already and
+// the extra polling loads cost more than the round trips they save.  Every
+// wait is bounded by kWaitLimitNs and by the sticky status word (a waiter
+// that already gave up makes every other waiter leave).
+HS_DEV bool look_back(unsigned long long *my, int64_t stride, int k, float TA, float TC, float &cin,
+                      int *status) {
+  if (k > 0) {
+    st_word(my, pack(__float_as_uint(TA), TC));
+    float ra = 1.f, rc = 0.f;
+    const unsigned long long *p = my - stride;
+    uint64_t t0 = 0;
+    for (unsigned n = 0;; ++n) {
+      const unsigned long long v = ld_word(p);
+      if (v != 0ull) {
+        const unsigned long long x = ~v;
+        const unsigned hi = (unsigned)(x >> 32);
+        const float lo = __uint_as_float((unsigned)x);
+        if (hi == kInclusive) {
+          cin = fmaf(ra, lo, rc);
+          break;
+        }
+        rc = fmaf(ra, lo, rc);
+        ra *= __uint_as_float(hi);
+        p -= stride;  // tile 0 publishes only an inclusive value: p stays in range
+        continue;
+      }
+      if (n >= 2) {  // the nearest unread predecessor is not published yet
+        __nanosleep(64);
+        if ((n & 15) == 0) {
+          if (t0 == 0) t0 = globaltimer();
+          if (ld_status(status) != 0) return false;
+          if (globaltimer() - t0 > kWaitLimitNs) {
+            set_status(status, HS_ERR_DEVICE_TIMEOUT);
+            return false;
+          }
+        }
+      }
     }
   }
-  return m;
+  st_word(my, pack(kInclusive, fmaf(TA, cin, TC)));
+  return true;
+}
+
+// ============================================================== forward
+template <bool V16>
+__global__ void __launch_bounds__(kFwdWPC * 32)
+scan_fwd_kernel(const float *__restrict__ z, const float *__restrict__ c0, float *__restrict__ out,
+                float *__restrict__ cbuf, float *__restrict__ h_n, float *__restrict__ c_n, ScanShape sh,
+                float eps, ScanWs ws, int *status) {
+  constexpr int L = kFwdL;
+  extern __shared__ float4 smem_f4[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float *zs = reinterpret_cast<float *>(smem_f4) + warp * (L * kFwdRow);
+  const int64_t T = sh.T, B = sh.B, H = sh.H;
+  const int64_t per_chunk = B * sh.ncol;
+  const int64_t grp = blockIdx.x / per_chunk;
+  const int64_t col = blockIdx.x - grp * per_chunk;
+  const int j = (int)(grp * kFwdWPC + warp);
+  if (j >= sh.nchunk) return;  // no block barrier in this kernel
+  if (ld_status(status) != 0) return;
+  const int64_t b = col / sh.ncol;
+  const int64_t h0 = (col - b * sh.ncol) * 32;
+  const int64_t h = h0 + lane;
+  const bool hv = h < H;
+  const int64_t t0 = (int64_t)j * L;
+  const int nst = (int)min((int64_t)L, T - t0);
+  const int64_t zstep = B * 4 * H;
+
+  // Stage z[t0 .. t0+nst) for units h0 .. h0+31 (4 gate rows per step).
+  if (V16) {
+    const int g = lane >> 3, k = (lane & 7) * 4;
+    if (h0 + k < H) {
+      const float *src = z + (t0 * B + b) * 4 * H + g * H + h0 + k;
+      float *dst = zs + g * 32 + k;
+#pragma unroll 4
+      for (int s = 0; s < nst; ++s) cp_async16(dst + s * kFwdRow, src + s * zstep);
+    }
+  } else if (hv) {
+    const float *src = z + (t0 * B + b) * 4 * H + h;
+    for (int s = 0; s < nst; ++s)
+#pragma unroll
+      for (int g = 0; g < 4; ++g) cp_async4(zs + s * kFwdRow + g * 32 + lane, src + s * zstep + g * H);
+  }
+  cp_async_wait_all();
+  __syncwarp();
+
+  // Pass 1: activations (kept in place: slot i <- b', f <- f', o <- sigma(z_o))
+  // and the tile's map.
+  float A = 1.f, C = 0.f;
+  if (hv) {
+#pragma unroll
+    for (int s = 0; s < L; ++s) {
+      if (s < nst) {
+        float *r = zs + s * kFwdRow + lane;
+        const float fp = fmaxf(sigf(r[32]), eps);
+        const float bp = fmaxf(sigf(r[0]) * sigf(r[64]), eps);
+        r[0] = bp;
+        r[32] = fp;
+        r[96] = sigf(r[96]);
+        C = fmaf(fp, C, bp);
+        A *= fp;
+      }
+    }
+  }
+  float cin = fmaxf((j == 0 && c0 && hv) ? c0[b * H + h] : 0.f, eps);
+  if (!look_back(ws.words + ((int64_t)j * per_chunk + col) * 32 + lane, per_chunk * 32, j, A, C, cin, status))
+    return;
+  if (!hv) return;
+
+  // Pass 2: the exact recurrence from the carry.
+  float c = cin;
+  const int64_t os = B * H;
+  float *ob = out + (t0 * B + b) * H + h;
+  float *cb = cbuf + (t0 * B + b) * H + h;
+#pragma unroll
+  for (int s = 0; s < L; ++s) {
+    if (s < nst) {
+      const float *r = zs + s * kFwdRow + lane;
+      c = fmaf(r[32], c, r[0]);
+      const float o = r[96] * tanh_pos(c);
+      __stcs(cb + s * os, c);
+      __stcs(ob + s * os, o);
+      if (t0 + s == T - 1) {
+        if (c_n) c_n[b * H + h] = c;
+        if (h_n) h_n[b * H + h] = o;
+      }
+    }
+  }
+}
+
+// ============================================================== backward
+template <bool V16>
+__global__ void __launch_bounds__(kBwdWPC * 32)
+scan_bwd_kernel(const float *z, const float *__restrict__ cbuf, const float *__restrict__ c0,
+                const float *__restrict__ dout, const float *__restrict__ dh_n, const float *__restrict__ dc_n,
+                float *dz, float *__restrict__ dc0, ScanShape sh, float eps, ScanWs ws, int *status) {
+  constexpr int L = kBwdL;
+  extern __shared__ float4 smem_f4[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float *bs = reinterpret_cast<float *>(smem_f4) + warp * (L * kBwdRow + 32);
+  float *cprev_row = bs + L * kBwdRow;
+  const int64_t T = sh.T, B = sh.B, H = sh.H;
+  const int64_t per_chunk = B * sh.ncol;
+  const int64_t grp = blockIdx.x / per_chunk;
+  const int64_t col = blockIdx.x - grp * per_chunk;
+  const int q = (int)(grp * kBwdWPC + warp);  // scan order: 0 = last chunk in time
+  bool active = q < sh.nchunk && ld_status(status) == 0;
+  const int j = sh.nchunk - 1 - q;
+  const int64_t b = col / sh.ncol;
+  const int64_t h0 = (col - b * sh.ncol) * 32;
+  const int64_t h = h0 + lane;
+  const bool hv = h < H;
+  const int64_t t0 = (int64_t)j * L;
+  const int nst = active ? (int)min((int64_t)L, T - t0) : 0;
+  const int64_t zstep = B * 4 * H, sstep = B * H;
+  float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+
+  if (active) {
+    // Stage z (4 rows), c and dout of each step, and c_{t0-1}.
+    if (V16) {
+      const int g = lane >> 3, k = (lane & 7) * 4;
+      if (h0 + k < H) {
+        const float *zsrc = z + (t0 * B + b) * 4 * H + g * H + h0 + k;
+        const float *ssrc = (g == 0 ? cbuf : dout) + (t0 * B + b) * H + h0 + k;
+        float *dst = bs + g * 32 + k;
+#pragma unroll 4
+        for (int s = 0; s < nst; ++s) {
+          cp_async16(dst + s * kBwdRow, zsrc + s * zstep);
+          if (g < 2) cp_async16(dst + s * kBwdRow + 128, ssrc + s * sstep);
+        }
+        if (g == 0 && t0 > 0) cp_async16(cprev_row + k, cbuf + ((t0 - 1) * B + b) * H + h0 + k);
+      }
+    } else if (hv) {
+      const float *zsrc = z + (t0 * B + b) * 4 * H + h;
+      const float *csrc = cbuf + (t0 * B + b) * H + h;
+      const float *dsrc = dout + (t0 * B + b) * H + h;
+      for (int s = 0; s < nst; ++s) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) cp_async4(bs + s * kBwdRow + g * 32 + lane, zsrc + s * zstep + g * H);
+        cp_async4(bs + s * kBwdRow + 128 + lane, csrc + s * sstep);
+        cp_async4(bs + s * kBwdRow + 160 + lane, dsrc + s * sstep);
+      }
+      if (t0 > 0) cp_async4(cprev_row + lane, cbuf + ((t0 - 1) * B + b) * H + h);
+    }
+    cp_async_wait_all();
+    __syncwarp();
+
+    // Pass 1 (reverse time): per-step coefficients kept in place
+    // (slot i <- KI, f <- KF, g <- KG, o <- f', dout <- dcd; the c slot stays,
+    // it is the next step's c_{t-1}), the o-gate gradient (already final),
+    // and the tile's map of e.
+    float A = 1.f, C = 0.f;
+    if (hv) {
+      const float c_init = (t0 > 0) ? cprev_row[lane] : fmaxf(c0 ? c0[b * H + h] : 0.f, eps);
+#pragma unroll
+      for (int s = L - 1; s >= 0; --s) {
+        if (s < nst) {
+          float *r = bs + s * kBwdRow + lane;
+          const int64_t t = t0 + s;
+          float d = r[160];
+          if (t == T - 1 && dh_n) d += dh_n[b * H + h];
+          const float cp = s > 0 ? r[128 - kBwdRow] : c_init;
+          const float i = sigf(r[0]), f = sigf(r[32]), g = sigf(r[64]), o = sigf(r[96]);
+          const float th = tanh_pos(r[128]);
+          const float mb = (i * g >= eps) ? 1.f : 0.f;
+          const float mf = (f >= eps) ? 1.f : 0.f;
+          const float fp = fmaxf(f, eps);
+          float dcd = d * o * (1.f - th * th);
+          if (t == T - 1 && dc_n) dcd += dc_n[b * H + h];
+          const float dzo = d * th * o * (1.f - o);
+          __stcs(dz + (t * B + b) * 4 * H + 3 * H + h, dzo);
+          acc3 += dzo;
+          r[0] = g * i * (1.f - i) * mb;
+          r[32] = cp * f * (1.f - f) * mf;
+          r[64] = i * g * (1.f - g) * mb;
+          r[96] = fp;
+          r[160] = dcd;
+          C = fp * (C + dcd);
+          A *= fp;
+        }
+      }
+    }
+    float e = 0.f;
+    active = look_back(ws.words + ((int64_t)q * per_chunk + col) * 32 + lane, per_chunk * 32, q, A, C, e, status);
+
+    // Pass 2: e entering this tile's last step, then the exact reverse recurrence.
+    if (active && hv) {
+#pragma unroll
+      for (int s = L - 1; s >= 0; --s) {
+        if (s < nst) {
+          const float *r = bs + s * kBwdRow + lane;
+          const int64_t t = t0 + s;
+          const float dc = r[160] + e;
+          e = r[96] * dc;
+          const float di = dc * r[0], df = dc * r[32], dg = dc * r[64];
+          float *dzr = dz + (t * B + b) * 4 * H + h;
+          __stcs(dzr, di);
+          __stcs(dzr + H, df);
+          __stcs(dzr + 2 * H, dg);
+          acc0 += di;
+          acc1 += df;
+          acc2 += dg;
+        }
+      }
+      if (t0 == 0 && dc0) dc0[b * H + h] = (c0 && c0[b * H + h] >= eps) ? e : 0.f;
+    }
+  }
+
+  // Bias-gradient sums of this CTA's WPC tiles, added in a fixed order.
+  if (ws.db_part) {
+    __syncthreads();  // every warp is done with its staging area
+    float *red = reinterpret_cast<float *>(smem_f4);  // [WPC][4][32]
+    red[(warp * 4 + 0) * 32 + lane] = acc0;
+    red[(warp * 4 + 1) * 32 + lane] = acc1;
+    red[(warp * 4 + 2) * 32 + lane] = acc2;
+    red[(warp * 4 + 3) * 32 + lane] = acc3;
+    __syncthreads();
+    if (hv) {
+      for (int g = warp; g < 4; g += kBwdWPC) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < kBwdWPC; ++w) s += red[(w * 4 + g) * 32 + lane];
+        ws.db_part[(grp * B + b) * 4 * H + g * H + h] = s;
+      }
+    }
+  }
+}
+
+// db[n] = beta*db[n] + sum_r part[r][n]: 32 columns per CTA, 8 warps over
+// rows, partials added in a fixed order.
+__global__ void __launch_bounds__(256) rowsum_kernel(const float *__restrict__ part, float *__restrict__ db,
+                                                     int64_t R, int64_t N, int beta) {
+  __shared__ float red[8][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t n = (int64_t)blockIdx.x * 32 + lane;
+  float s0 = 0.f, s1 = 0.f;
+  if (n < N) {
+    int64_t r = w;
+    for (; r + 8 < R; r += 16) {
+      s0 += part[r * N + n];
+      s1 += part[(r + 8) * N + n];
+    }
+    for (; r < R; r += 8) s0 += part[r * N + n];
+  }
+  red[w][lane] = s0 + s1;
+  __syncthreads();
+  if (w == 0 && n < N) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += red[i][lane];
+    db[n] = beta ? db[n] + s : s;
+  }
+}
+
+bool all_aligned16(std::initializer_list<const void *> ptrs) {
+  for (const void *p : ptrs)
+    if (p && !aligned(p, 16)) return false;
+  return true;
+}
+
+size_t scan_ws_bytes(int64_t T, int64_t B, int64_t H) {
+  const size_t f = ws_layout(make_shape(T, B, H, kFwdL, kFwdWPC), false, nullptr, nullptr);
+  const size_t g = ws_layout(make_shape(T, B, H, kBwdL, kBwdWPC), true, nullptr, nullptr);
+  return std::max(f, g);
 }
 
 int check_scan_args(int64_t T, int64_t B, int64_t H) {
-  if (T <= 0 || B <= 0 || H <= 0) return fail(HS_ERR_INVALID_ARG, "T, B, H must be positive (got %lld, %lld, %lld)", (long long)T, (long long)B, (long long)H);
-  if ((T + 31) / 32 * B * ((H + 31) / 32) >= (1ll << 31)) return fail(HS_ERR_UNSUPPORTED, "scan grid too large");
-  if (B * 4 * H >= (1ll << 40)) return fail(HS_ERR_UNSUPPORTED, "B*4H too large");
+  if (T <= 0 || B <= 0 || H <= 0)
+    return fail(HS_ERR_INVALID_ARG, "T, B, H must be positive (got %lld, %lld, %lld)", (long long)T, (long long)B,
+                (long long)H);
+  const int Lmin = std::min(kFwdL, kBwdL);
+  const int Wmin = std::min(kFwdWPC, kBwdWPC);
+  if ((T + (int64_t)Lmin * Wmin - 1) / ((int64_t)Lmin * Wmin) * B * ((H + 31) / 32) >= (1ll << 31))
+    return fail(HS_ERR_UNSUPPORTED, "scan grid too large");
+  if ((T + Lmin - 1) / Lmin >= (1ll << 30)) return fail(HS_ERR_UNSUPPORTED, "T too large");
   return HS_OK;
 }
+
+std::atomic<unsigned long long> g_fwd_smem_set[2], g_bwd_smem_set[2];
 
 }  // namespace
 
 size_t scan_workspace(int64_t T, int64_t B, int64_t H) { return scan_ws_bytes(T, B, H); }
 
 // ------------------------------------------------------------------ host API
-int scan_forward(const float *z, const float *c0, float *out, float *c, float *h_n,
-                 float *c_n, int64_t T, int64_t B, int64_t H, float eps, void *ws_base,
-                 size_t ws_bytes, int *status, cudaStream_t st) {
+int scan_forward(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n, int64_t T,
+                 int64_t B, int64_t H, float eps, void *ws_base, size_t ws_bytes, int *status, cudaStream_t st) {
   if (int e = check_scan_args(T, B, H)) return e;
   if (!z || !out || !c || !status) return fail(HS_ERR_INVALID_ARG, "scan_forward: null z/out/c/status");
-  const int VEC = pick_vec(H, {z, c0, out, c, h_n, c_n});
-  const int HW = 32 * VEC;
-  if (!ws_base || !aligned(ws_base, 256)) return fail(HS_ERR_INVALID_ARG, "workspace must be non-null and 256-byte aligned");
-  if (VEC == 4 && HS_SCAN_USE_TMA) {  // persistent TMA kernel
-    ScanShape sh = make_shape(T, B, H, scan_tma_fwd_chunk(), HW);
-    ScanWs w;
-    const size_t need = ws_layout(sh, HW, false, &w, ws_base);
-    if (ws_bytes < need) return fail(HS_ERR_WORKSPACE, "scan_forward: workspace %zu < %zu bytes", ws_bytes, need);
-    if (cudaMemsetAsync(ws_base, 0, ws_zero_bytes(sh), st) != cudaSuccess) return check_launch("scan_forward memset");
-    ScanTmaWs tw{w.ticket, w.flags, w.agg_a, w.agg_c, w.incl, nullptr};
-    bool done = false;
-    if (int e = scan_fwd_tma_launch(z, c0, out, c, h_n, c_n, T, B, H, eps, tw, sh.nchunk, sh.nhb, status, st, &done)) return e;
-    if (done) return HS_OK;
-  }
-  ScanShape sh = make_shape(T, B, H, kFwdS * kFwdNW, HW);
+  if (scan_chain_wanted(T, B, H))  // one CTA per column, no scratch
+    return scan_fwd_chain_launch(z, c0, out, c, h_n, c_n, T, B, H, eps, status, st);
+  if (!ws_base || !aligned(ws_base, 256))
+    return fail(HS_ERR_INVALID_ARG, "workspace must be non-null and 256-byte aligned");
+  const ScanShape sh = make_shape(T, B, H, kFwdL, kFwdWPC);
   ScanWs ws;
-  const size_t need = ws_layout(sh, HW, false, &ws, ws_base);
+  const size_t need = ws_layout(sh, false, &ws, ws_base);
   if (ws_bytes < need) return fail(HS_ERR_WORKSPACE, "scan_forward: workspace %zu < %zu bytes", ws_bytes, need);
-  if (cudaMemsetAsync(ws_base, 0, ws_zero_bytes(sh), st) != cudaSuccess) return check_launch("scan_forward memset");
-  const unsigned ntile = (unsigned)((int64_t)sh.nchunk * B * sh.nhb);
-  if (VEC == 4)
-    scan_fwd_kernel<4, kFwdS, kFwdNW><<<ntile, kFwdNW * 32, 0, st>>>(z, c0, out, c, h_n, c_n, sh, eps, ws, status);
+  if (cudaMemsetAsync(ws.words, 0, ws_words_bytes(sh), st) != cudaSuccess) return check_launch("scan memset");
+  const bool v16 = H % 4 == 0 && aligned(z, 16);
+  const void *fn = v16 ? (const void *)scan_fwd_kernel<true> : (const void *)scan_fwd_kernel<false>;
+  if (int e = allow_dynamic_smem(fn, kFwdSmem, &g_fwd_smem_set[v16])) return e;
+  const unsigned grid = (unsigned)((int64_t)sh.ngroup * B * sh.ncol);
+  if (v16)
+    scan_fwd_kernel<true><<<grid, kFwdWPC * 32, kFwdSmem, st>>>(z, c0, out, c, h_n, c_n, sh, eps, ws, status);
   else
-    scan_fwd_kernel<1, kFwdS, kFwdNW><<<ntile, kFwdNW * 32, 0, st>>>(z, c0, out, c, h_n, c_n, sh, eps, ws, status);
+    scan_fwd_kernel<false><<<grid, kFwdWPC * 32, kFwdSmem, st>>>(z, c0, out, c, h_n, c_n, sh, eps, ws, status);
   return check_launch("scan_fwd_kernel");
 }
 
-int scan_backward(const float *z, const float *c, const float *c0, const float *dout,
-                  const float *dh_n, const float *dc_n, float *dz, float *dc0, float *db,
-                  int64_t T, int64_t B, int64_t H, float eps, void *ws_base, size_t ws_bytes,
-                  int *status, cudaStream_t st) {
+int scan_backward(const float *z, const float *c, const float *c0, const float *dout, const float *dh_n,
+                  const float *dc_n, float *dz, float *dc0, float *db, int64_t T, int64_t B, int64_t H, float eps,
+                  void *ws_base, size_t ws_bytes, int *status, cudaStream_t st) {
   if (int e = check_scan_args(T, B, H)) return e;
   if (!z || !c || !dout || !dz || !status) return fail(HS_ERR_INVALID_ARG, "scan_backward: null z/c/dout/dz/status");
-  const int VEC = pick_vec(H, {z, c, c0, dout, dh_n, dc_n, dz, dc0});
-  const int HW = 32 * VEC;
-  if (!ws_base || !aligned(ws_base, 256)) return fail(HS_ERR_INVALID_ARG, "workspace must be non-null and 256-byte aligned");
-  if (VEC == 4 && HS_SCAN_USE_TMA) {  // persistent TMA kernel
-    ScanShape sh = make_shape(T, B, H, scan_tma_bwd_chunk(), HW);
-    ScanWs w;
-    const size_t need = ws_layout(sh, HW, db != nullptr, &w, ws_base);
-    if (ws_bytes < need) return fail(HS_ERR_WORKSPACE, "scan_backward: workspace %zu < %zu bytes", ws_bytes, need);
-    if (cudaMemsetAsync(ws_base, 0, ws_zero_bytes(sh), st) != cudaSuccess) return check_launch("scan_backward memset");
-    ScanTmaWs tw{w.ticket, w.flags, w.agg_a, w.agg_c, w.incl, w.db_part};
-    bool done = false;
-    if (int e = scan_bwd_tma_launch(z, c, c0, dout, dh_n, dc_n, dz, dc0, T, B, H, eps, tw, sh.nchunk, sh.nhb, status,
-                                    st, &done))
-      return e;
-    if (done) {
-      if (db) {
-        const int64_t N = 4 * H;
-        const int64_t R = scan_tma_grid((unsigned)((int64_t)sh.nchunk * B * sh.nhb));
-        rowsum_kernel<<<(unsigned)((N + 255) / 256), 256, 0, st>>>(w.db_part, db, R, N, 0);
-        return check_launch("rowsum_kernel");
-      }
-      return HS_OK;
-    }
-  }
-  ScanShape sh = make_shape(T, B, H, kBwdS * kBwdNW, HW);
+  if (!ws_base || !aligned(ws_base, 256))
+    return fail(HS_ERR_INVALID_ARG, "workspace must be non-null and 256-byte aligned");
+  const ScanShape sh = make_shape(T, B, H, kBwdL, kBwdWPC);
   ScanWs ws;
-  const size_t need = ws_layout(sh, HW, db != nullptr, &ws, ws_base);
+  const size_t need = ws_layout(sh, db != nullptr, &ws, ws_base);
   if (ws_bytes < need) return fail(HS_ERR_WORKSPACE, "scan_backward: workspace %zu < %zu bytes", ws_bytes, need);
-  if (cudaMemsetAsync(ws_base, 0, ws_zero_bytes(sh), st) != cudaSuccess) return check_launch("scan_backward memset");
-  const unsigned ntile = (unsigned)((int64_t)sh.nchunk * B * sh.nhb);
-  if (VEC == 4)
-    scan_bwd_kernel<4, kBwdS, kBwdNW><<<ntile, kBwdNW * 32, 0, st>>>(z, c, c0, dout, dh_n, dc_n, dz, dc0, sh, eps, ws, status);
+  const int64_t N = 4 * H;
+  const bool v16 = H % 4 == 0 && all_aligned16({z, c, dout});
+  if (scan_chain_wanted(T, B, H)) {
+    // one CTA per column; bias sums per sequence
+    if (int e = scan_bwd_chain_launch(z, c, c0, dout, dh_n, dc_n, dz, dc0, db ? ws.db_part : nullptr, T, B, H, eps,
+                                      status, st))
+      return e;
+    if (db) {
+      rowsum_kernel<<<(unsigned)((N + 31) / 32), 256, 0, st>>>(ws.db_part, db, B, N, 0);
+      return check_launch("rowsum_kernel");
+    }
+    return HS_OK;
+  }
+  if (cudaMemsetAsync(ws.words, 0, ws_words_bytes(sh), st) != cudaSuccess) return check_launch("scan memset");
+  const void *fn = v16 ? (const void *)scan_bwd_kernel<true> : (const void *)scan_bwd_kernel<false>;
+  if (int e = allow_dynamic_smem(fn, kBwdSmem, &g_bwd_smem_set[v16])) return e;
+  const unsigned grid = (unsigned)((int64_t)sh.ngroup * B * sh.ncol);
+  if (v16)
+    scan_bwd_kernel<true><<<grid, kBwdWPC * 32, kBwdSmem, st>>>(z, c, c0, dout, dh_n, dc_n, dz, dc0, sh, eps, ws,
+                                                                status);
   else
-    scan_bwd_kernel<1, kBwdS, kBwdNW><<<ntile, kBwdNW * 32, 0, st>>>(z, c, c0, dout, dh_n, dc_n, dz, dc0, sh, eps, ws, status);
+    scan_bwd_kernel<false><<<grid, kBwdWPC * 32, kBwdSmem, st>>>(z, c, c0, dout, dh_n, dc_n, dz, dc0, sh, eps, ws,
+                                                                 status);
   if (int e = check_launch("scan_bwd_kernel")) return e;
   if (db) {
-    const int64_t N = 4 * H, R = (int64_t)sh.nchunk * B;
-    rowsum_kernel<<<(unsigned)((N + 255) / 256), 256, 0, st>>>(ws.db_part, db, R, N, 0);
+    rowsum_kernel<<<(unsigned)((N + 31) / 32), 256, 0, st>>>(ws.db_part, db, (int64_t)sh.ngroup * B, N, 0);
     return check_launch("rowsum_kernel");
   }
   return HS_OK;
@@ -716,9 +596,7 @@ int scan_forward_noalloc(const float *z, const float *c0, float *out, float *c, 
                          int *dev_status, cudaStream_t st) {
   if (int e = check_scan_args(T, B, H)) return e;
   if (!z || !out || !c) return fail(HS_ERR_INVALID_ARG, "scan_forward_noalloc: null z/out/c");
-  const int VEC = pick_vec(H, {z, c0, out, c, h_n, c_n});
-  const int HW = 32 * VEC;
-  const size_t need = ws_layout(make_shape(T, B, H, kFwdS * kFwdNW, HW), HW, false, nullptr, nullptr);
+  const size_t need = ws_layout(make_shape(T, B, H, kFwdL, kFwdWPC), false, nullptr, nullptr);
   if (need > kNoAllocScratchBytes)
     return fail(HS_ERR_UNSUPPORTED,
                 "hs_scan_forward_noalloc: T=%lld B=%lld H=%lld needs %zu bytes of scratch, above "
@@ -727,8 +605,9 @@ int scan_forward_noalloc(const float *z, const float *c0, float *out, float *c, 
   void *scratch = nullptr;
   int *own_status = nullptr;
   if (int e = noalloc_scratch(&scratch, &own_status)) return e;
-  // scan_forward clears the ticket and flags (all that must start at zero)
-  // with a stream-ordered memset before its launch.
+  // scan_forward zeroes the look-back words (all that must start at zero)
+  // with a stream-ordered memset before its launch; the chain kernels it may
+  // pick instead use no scratch.
   return scan_forward(z, c0, out, c, h_n, c_n, T, B, H, eps, scratch, kNoAllocScratchBytes,
                       dev_status ? dev_status : own_status, st);
 }

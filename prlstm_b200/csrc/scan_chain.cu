@@ -1,0 +1,435 @@
+// Parallel-mode scan, one CTA per column: the path for shapes with many
+// independent columns (a column = one sequence x 32 consecutive hidden units)
+// and long T, such as the configs[4] training step (B x H/32 = 1024 columns of
+// 16384 steps per 32-sequence micro-batch).
+//
+// The recurrence is the one of scan.cu (c_t = max(f,eps) c_{t-1} +
+// max(i g,eps); reference src/headstartlstm/_parallel.py:21-74), split over
+// time inside the CTA instead of across CTAs: time is cut into chunks of L
+// steps and warp w takes chunks w, w+NW, w+2NW, ... of the CTA's column, lane
+// l owning hidden unit h0+l.  For each chunk the warp computes the gate
+// activations and the chunk's affine map (A, C) while it waits for nothing,
+// then takes the carry into the chunk from a shared-memory slot written by the
+// warp of the previous chunk, hands A*carry + C on to the next warp at once,
+// and only then writes the chunk's outputs.  The carry therefore moves
+// through the CTA at shared-memory latency (one slot write per chunk) while
+// every warp's loads, math and stores overlap; no other CTA and no global
+// scratch is involved, so nothing has to be cleared between calls.
+//
+// Inputs stream into a per-warp double buffer with 16-byte cp.async copies
+// (L2 -> shared, no L1 allocation) issued two chunks ahead.  Rows of 32
+// floats are 128-byte aligned segments: every warp access is one full line.
+// Per (t,b,h) element the forward moves its 24 algorithmic bytes and the
+// backward its 40, plus one c row per backward chunk (c_{t0-1}).
+#include "hs_common.cuh"
+
+namespace hs {
+namespace {
+
+// Chunk length L and warps per CTA NW (compile-time; the defaults are the
+// measured best on B200 for the benchmark shapes).  The shared memory per
+// CTA is sized so that seven CTAs fit on an SM: 1036 resident CTAs on 148
+// SMs hold all 1024 columns of a 32-sequence, H=1024 micro-batch at once.
+#ifndef HS_CHAIN_FWD_L
+#define HS_CHAIN_FWD_L 6
+#endif
+#ifndef HS_CHAIN_FWD_NW
+#define HS_CHAIN_FWD_NW 4
+#endif
+#ifndef HS_CHAIN_BWD_L
+#define HS_CHAIN_BWD_L 4
+#endif
+#ifndef HS_CHAIN_BWD_NW
+#define HS_CHAIN_BWD_NW 4
+#endif
+#ifndef HS_CHAIN_MIN_CTAS
+#define HS_CHAIN_MIN_CTAS 7
+#endif
+// Resident CTAs per SM the register budget allows on the 16-byte path; the
+// 4-byte path (H % 4 != 0 or unaligned inputs) needs more registers and
+// takes two fewer.
+constexpr int kMinCtas = HS_CHAIN_MIN_CTAS;
+constexpr int kFL = HS_CHAIN_FWD_L, kFNW = HS_CHAIN_FWD_NW;
+constexpr int kBL = HS_CHAIN_BWD_L, kBNW = HS_CHAIN_BWD_NW;
+constexpr int kFRow = 4 * 32;              // staged floats per forward step: z_i, z_f, z_g, z_o
+constexpr int kBRow = 6 * 32;              // backward: z_i, z_f, z_g, z_o, c, dout
+constexpr int kFBuf = kFL * kFRow;         // floats per forward chunk buffer
+constexpr int kBBuf = kBL * kBRow + 32;    // backward, + the c_{t0-1} row
+constexpr size_t kFSmem = sizeof(float) * kFNW * 2 * kFBuf + sizeof(unsigned long long) * kFNW * 32;
+constexpr size_t kBSmem = sizeof(float) * kBNW * 2 * kBBuf + sizeof(unsigned long long) * kBNW * 32;
+static_assert(kBNW * 2 * kBBuf >= kBNW * 4 * 32, "db reduction area");
+
+// 16- and 4-byte copies global -> shared; .cg bypasses L1, so in-flight lines
+// do not compete with the shared-memory carve-out.
+// Destinations are shared-window addresses (see sa()).
+HS_DEV void cp16(unsigned dst, const float *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+HS_DEV void cp4(unsigned dst, const float *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+HS_DEV unsigned sa(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
+HS_DEV void commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> HS_DEV void wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Carry slots: one 64-bit shared word per (consumer warp, lane), holding
+// (chunk index << 32) | float bits.  The consumer of chunk c (c >= 1) waits for
+// tag c, so the initial zero is never mistaken for a carry.  A slot is written
+// again (tag c+NW) only after its consumer has read tag c: the producer's next
+// carry depends, around the ring of warps, on the consumer's own next carry.
+HS_DEV void slot_put(unsigned long long *s, unsigned tag, float v) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+  asm volatile("st.volatile.shared.u64 [%0], %1;" ::"r"((unsigned)__cvta_generic_to_shared(s)), "l"(w) : "memory");
+}
+HS_DEV unsigned long long slot_get(const unsigned long long *s) {
+  unsigned long long w;
+  asm volatile("ld.volatile.shared.u64 %0, [%1];" : "=l"(w) : "r"((unsigned)__cvta_generic_to_shared(s)) : "memory");
+  return w;
+}
+// Waits for tag in *s; bounded by kWaitLimitNs and by the sticky status word.
+HS_DEV bool slot_wait(const unsigned long long *s, unsigned tag, float *v, int *status) {
+  uint64_t t0 = 0;
+  for (unsigned n = 0;; ++n) {
+    const unsigned long long w = slot_get(s);
+    if ((unsigned)(w >> 32) == tag) {
+      *v = __uint_as_float((unsigned)w);
+      return true;
+    }
+    if (n >= 32) {
+      __nanosleep(32);
+      if ((n & 63) == 0) {
+        if (t0 == 0) t0 = globaltimer();
+        if (ld_status(status) != 0) return false;
+        if (globaltimer() - t0 > kWaitLimitNs) {
+          set_status(status, HS_ERR_DEVICE_TIMEOUT);
+          return false;
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ forward
+template <bool V16>
+__global__ void __launch_bounds__(kFNW * 32, V16 ? kMinCtas : kMinCtas - 2)
+scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, float *__restrict__ out,
+                    float *__restrict__ cbuf, float *__restrict__ h_n, float *__restrict__ c_n, int64_t T,
+                    int64_t B, int64_t H, float eps, int *status) {
+  extern __shared__ float4 smem_f4[];
+  float *sm = reinterpret_cast<float *>(smem_f4);
+  unsigned long long *slots = reinterpret_cast<unsigned long long *>(sm + kFNW * 2 * kFBuf);  // [NW][32]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t ncol = (H + 31) / 32;
+  const int64_t b = blockIdx.x / ncol;
+  const int64_t h0 = (blockIdx.x - b * ncol) * 32;
+  const int64_t h = h0 + lane;
+  const bool hv = h < H;
+  const int64_t nchunk = (T + kFL - 1) / kFL;
+  const int64_t zstep = B * 4 * H, ostep = B * H;
+  const float *zb = z + b * 4 * H;
+  float *buf0 = sm + warp * 2 * kFBuf;
+  slots[warp * 32 + lane] = 0ull;
+  __syncthreads();
+
+  // Copies of one chunk into a buffer: pointers advance by one step per copy
+  // (no per-step index products).
+  auto stage = [&](int64_t c, float *dst) {
+    const int64_t t0 = c * kFL;
+    const int n = (int)min((int64_t)kFL, T - t0);
+    if (V16) {
+      const int g = lane >> 3, k = (lane & 7) * 4;
+      if (h0 + k < H) {
+        const float *src = zb + t0 * zstep + g * H + h0 + k;
+        unsigned d = sa(dst + g * 32 + k);
+        for (int s = 0; s < n; ++s, src += zstep, d += kFRow * 4) cp16(d, src);
+      }
+    } else if (hv) {
+      const float *src = zb + t0 * zstep + h;
+      unsigned d = sa(dst + lane);
+#pragma unroll 1
+      for (int s = 0; s < n; ++s, src += zstep, d += kFRow * 4)
+#pragma unroll
+        for (int g = 0; g < 4; ++g) cp4(d + g * 128, src + g * H);
+    }
+  };
+
+  int64_t c = warp;
+  if (c < nchunk) stage(c, buf0);
+  commit();
+  if (c + kFNW < nchunk) stage(c + kFNW, buf0 + kFBuf);
+  commit();
+  for (int i = 0; c < nchunk; c += kFNW, ++i) {
+    float *buf = buf0 + (i & 1) * kFBuf;
+    wait_group<1>();  // this chunk's copies are done (the next chunk's may still fly)
+    __syncwarp();
+    const int64_t t0 = c * kFL;
+    const int n = (int)min((int64_t)kFL, T - t0);
+    float fp[kFL], bp[kFL], og[kFL];
+    float A = 1.f, C = 0.f;
+#pragma unroll
+    for (int s = 0; s < kFL; ++s) {
+      fp[s] = 1.f;
+      bp[s] = 0.f;
+      og[s] = 0.f;
+      if (s < n && hv) {
+        const float *r = buf + s * kFRow + lane;
+        fp[s] = fmaxf(sigf(r[32]), eps);
+        bp[s] = fmaxf(sigf(r[0]) * sigf(r[64]), eps);
+        og[s] = sigf(r[96]);
+        C = fmaf(fp[s], C, bp[s]);
+        A *= fp[s];
+      }
+    }
+    __syncwarp();  // every lane has read the buffer before it is refilled
+    if (c + 2 * kFNW < nchunk) stage(c + 2 * kFNW, buf);
+    commit();
+    float cin = fmaxf((c == 0 && c0 && hv) ? c0[b * H + h] : 0.f, eps);
+    const bool ok = c == 0 || slot_wait(&slots[warp * 32 + lane], (unsigned)c, &cin, status);
+    if (!__all_sync(0xffffffffu, ok)) break;
+    if (c + 1 < nchunk) slot_put(&slots[((warp + 1) % kFNW) * 32 + lane], (unsigned)(c + 1), fmaf(A, cin, C));
+    if (hv) {
+      float cc = cin, o = 0.f;
+      float *ob = out + (t0 * B + b) * H + h;
+      float *cb = cbuf + (t0 * B + b) * H + h;
+#pragma unroll
+      for (int s = 0; s < kFL; ++s) {
+        if (s < n) {
+          cc = fmaf(fp[s], cc, bp[s]);
+          o = og[s] * tanh_pos(cc);
+          __stcs(cb, cc);
+          __stcs(ob, o);
+          cb += ostep;
+          ob += ostep;
+        }
+      }
+      if (t0 + n == T) {  // the chunk that ends the sequence
+        if (c_n) c_n[b * H + h] = cc;
+        if (h_n) h_n[b * H + h] = o;
+      }
+    }
+  }
+  wait_group<0>();  // no copy is left in flight at exit
+}
+
+// ------------------------------------------------------------------ backward
+// Scan order q = 0, 1, ... runs over chunks from the last in time (j =
+// nchunk-1-q); the carry is e, the gradient reaching c_{t0-1} of the chunk
+// after in time.  Bias sums are kept per lane over all of a warp's chunks and
+// added over the CTA's warps in a fixed order at the end: one partial row per
+// sequence.
+template <bool V16>
+__global__ void __launch_bounds__(kBNW * 32, V16 ? kMinCtas : kMinCtas - 2)
+scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float *__restrict__ c0,
+                    const float *__restrict__ dout, const float *__restrict__ dh_n, const float *__restrict__ dc_n,
+                    float *dz, float *__restrict__ dc0, float *__restrict__ db_part, int64_t T, int64_t B,
+                    int64_t H, float eps, int *status) {
+  extern __shared__ float4 smem_f4[];
+  float *sm = reinterpret_cast<float *>(smem_f4);
+  unsigned long long *slots = reinterpret_cast<unsigned long long *>(sm + kBNW * 2 * kBBuf);  // [NW][32]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t ncol = (H + 31) / 32;
+  const int64_t b = blockIdx.x / ncol;
+  const int64_t h0 = (blockIdx.x - b * ncol) * 32;
+  const int64_t h = h0 + lane;
+  const bool hv = h < H;
+  const int64_t nchunk = (T + kBL - 1) / kBL;
+  const int64_t zstep = B * 4 * H, sstep = B * H;
+  float *buf0 = sm + warp * 2 * kBBuf;
+  slots[warp * 32 + lane] = 0ull;
+  __syncthreads();
+  const float c0p = fmaxf((c0 && hv) ? c0[b * H + h] : 0.f, eps);
+
+  auto stage = [&](int64_t q, float *dst) {
+    const int64_t t0 = (nchunk - 1 - q) * kBL;
+    const int n = (int)min((int64_t)kBL, T - t0);
+    if (V16) {
+      const int g = lane >> 3, k = (lane & 7) * 4;
+      if (h0 + k < H) {
+        const float *zsrc = z + (t0 * B + b) * 4 * H + g * H + h0 + k;
+        const float *ssrc = (g == 0 ? cbuf : dout) + (t0 * B + b) * H + h0 + k;
+        unsigned d = sa(dst + g * 32 + k);
+        for (int s = 0; s < n; ++s, zsrc += zstep, ssrc += sstep, d += kBRow * 4) {
+          cp16(d, zsrc);
+          if (g < 2) cp16(d + 512, ssrc);
+        }
+        if (g == 0 && t0 > 0) cp16(sa(dst + kBL * kBRow + k), cbuf + ((t0 - 1) * B + b) * H + h0 + k);
+      }
+    } else if (hv) {
+      const float *zsrc = z + (t0 * B + b) * 4 * H + h;
+      const float *csrc = cbuf + (t0 * B + b) * H + h;
+      const float *dsrc = dout + (t0 * B + b) * H + h;
+      unsigned d = sa(dst + lane);
+#pragma unroll 1
+      for (int s = 0; s < n; ++s, zsrc += zstep, csrc += sstep, dsrc += sstep, d += kBRow * 4) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) cp4(d + g * 128, zsrc + g * H);
+        cp4(d + 512, csrc);
+        cp4(d + 640, dsrc);
+      }
+      if (t0 > 0) cp4(sa(dst + kBL * kBRow + lane), cbuf + ((t0 - 1) * B + b) * H + h);
+    }
+  };
+
+  float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+  int64_t q = warp;
+  if (q < nchunk) stage(q, buf0);
+  commit();
+  if (q + kBNW < nchunk) stage(q + kBNW, buf0 + kBBuf);
+  commit();
+  for (int i = 0; q < nchunk; q += kBNW, ++i) {
+    float *buf = buf0 + (i & 1) * kBBuf;
+    wait_group<1>();
+    __syncwarp();
+    const int64_t t0 = (nchunk - 1 - q) * kBL;
+    const int n = (int)min((int64_t)kBL, T - t0);
+    // dh_n joins dout of the last step (in the staged copy); dc_n is the
+    // initial carry of the reverse scan (below).
+    if (q == 0 && dh_n && hv) buf[(n - 1) * kBRow + 160 + lane] += dh_n[b * H + h];
+    // Pass 1 (reverse time): per-step coefficients, the o-gate gradient
+    // (final already) and the chunk's map of e.
+    float FP[kBL], DCD[kBL], KI[kBL], KF[kBL], KG[kBL];
+    float A = 1.f, C = 0.f;
+    float *dzs = dz + (t0 * B + b) * 4 * H + h;  // dz row of step t0, unit h
+#pragma unroll
+    for (int s = kBL - 1; s >= 0; --s) {
+      FP[s] = 1.f;
+      DCD[s] = KI[s] = KF[s] = KG[s] = 0.f;
+      if (s < n && hv) {
+        const float *r = buf + s * kBRow + lane;
+        const float d = r[160];
+        const float cp = s > 0 ? r[128 - kBRow] : (t0 > 0 ? buf[kBL * kBRow + lane] : c0p);
+        const float ig = sigf(r[0]), f = sigf(r[32]), g = sigf(r[64]), o = sigf(r[96]);
+        const float th = tanh_pos(r[128]);
+        const float mb = (ig * g >= eps) ? 1.f : 0.f;
+        const float mf = (f >= eps) ? 1.f : 0.f;
+        const float dcd = d * o * (1.f - th * th);
+        const float dzo = d * th * o * (1.f - o);
+        __stcs(dzs + s * zstep + 3 * H, dzo);
+        acc3 += dzo;
+        FP[s] = fmaxf(f, eps);
+        DCD[s] = dcd;
+        KI[s] = g * ig * (1.f - ig) * mb;
+        KF[s] = cp * f * (1.f - f) * mf;
+        KG[s] = ig * g * (1.f - g) * mb;
+        C = FP[s] * (C + dcd);
+        A *= FP[s];
+      }
+    }
+    __syncwarp();
+    if (q + 2 * kBNW < nchunk) stage(q + 2 * kBNW, buf);
+    commit();
+    float e = (q == 0 && dc_n && hv) ? dc_n[b * H + h] : 0.f;
+    const bool ok = q == 0 || slot_wait(&slots[warp * 32 + lane], (unsigned)q, &e, status);
+    if (!__all_sync(0xffffffffu, ok)) break;
+    if (q + 1 < nchunk) slot_put(&slots[((warp + 1) % kBNW) * 32 + lane], (unsigned)(q + 1), fmaf(A, e, C));
+    if (hv) {
+#pragma unroll
+      for (int s = kBL - 1; s >= 0; --s) {
+        if (s < n) {
+          const float dc = DCD[s] + e;
+          e = FP[s] * dc;
+          const float di = dc * KI[s], df = dc * KF[s], dg = dc * KG[s];
+          float *dzr = dzs + s * zstep;
+          __stcs(dzr, di);
+          __stcs(dzr + H, df);
+          __stcs(dzr + 2 * H, dg);
+          acc0 += di;
+          acc1 += df;
+          acc2 += dg;
+        }
+      }
+      if (t0 == 0 && dc0) dc0[b * H + h] = (c0 && c0[b * H + h] >= eps) ? e : 0.f;
+    }
+  }
+  wait_group<0>();
+  if (db_part) {
+    __syncthreads();  // every warp is done with its buffers
+    float *red = sm;  // [NW][4][32]
+    red[(warp * 4 + 0) * 32 + lane] = acc0;
+    red[(warp * 4 + 1) * 32 + lane] = acc1;
+    red[(warp * 4 + 2) * 32 + lane] = acc2;
+    red[(warp * 4 + 3) * 32 + lane] = acc3;
+    __syncthreads();
+    if (hv) {
+      for (int g = warp; g < 4; g += kBNW) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < kBNW; ++w) s += red[(w * 4 + g) * 32 + lane];
+        db_part[b * 4 * H + g * H + h] = s;
+      }
+    }
+  }
+}
+
+// Path choice: HS_SCAN_PATH=chain|lookback forces one (tests); otherwise the
+// per-column kernels whenever the columns alone fill the GPU.
+int path_override() {
+  const char *e = getenv("HS_SCAN_PATH");
+  if (!e) return 0;
+  if (e[0] == 'c') return 1;
+  if (e[0] == 'l') return 2;
+  return 0;
+}
+
+int sm_count() {
+  static std::atomic<int> cached[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  cached[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+std::atomic<unsigned long long> g_fwd_attr[2], g_bwd_attr[2];
+
+}  // namespace
+
+#ifndef HS_CHAIN_MIN_COLS_PER_SM
+#define HS_CHAIN_MIN_COLS_PER_SM 4
+#endif
+
+bool scan_chain_wanted(int64_t T, int64_t B, int64_t H) {
+  const int o = path_override();
+  if (o) return o == 1;
+  const int64_t ncol = B * ((H + 31) / 32);
+  return T >= 64 && ncol >= (int64_t)HS_CHAIN_MIN_COLS_PER_SM * sm_count();
+}
+
+int scan_fwd_chain_launch(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
+                          int64_t T, int64_t B, int64_t H, float eps, int *status, cudaStream_t st) {
+  const int64_t grid = B * ((H + 31) / 32);
+  if (grid >= (1ll << 31)) return fail(HS_ERR_UNSUPPORTED, "scan: too many columns");
+  if ((T + kFL - 1) / kFL >= (1ll << 32)) return fail(HS_ERR_UNSUPPORTED, "scan: T too large");
+  const bool v16 = H % 4 == 0 && aligned(z, 16);
+  const void *fn = v16 ? (const void *)scan_fwd_col_kernel<true> : (const void *)scan_fwd_col_kernel<false>;
+  if (int e = allow_dynamic_smem(fn, kFSmem, &g_fwd_attr[v16])) return e;
+  if (v16)
+    scan_fwd_col_kernel<true><<<(unsigned)grid, kFNW * 32, kFSmem, st>>>(z, c0, out, c, h_n, c_n, T, B, H, eps,
+                                                                       status);
+  else
+    scan_fwd_col_kernel<false><<<(unsigned)grid, kFNW * 32, kFSmem, st>>>(z, c0, out, c, h_n, c_n, T, B, H, eps,
+                                                                        status);
+  return check_launch("scan_fwd_col_kernel");
+}
+
+int scan_bwd_chain_launch(const float *z, const float *c, const float *c0, const float *dout, const float *dh_n,
+                          const float *dc_n, float *dz, float *dc0, float *db_part, int64_t T, int64_t B, int64_t H,
+                          float eps, int *status, cudaStream_t st) {
+  const int64_t grid = B * ((H + 31) / 32);
+  if (grid >= (1ll << 31)) return fail(HS_ERR_UNSUPPORTED, "scan: too many columns");
+  if ((T + kBL - 1) / kBL >= (1ll << 32)) return fail(HS_ERR_UNSUPPORTED, "scan: T too large");
+  const bool v16 = H % 4 == 0 && aligned(z, 16) && aligned(c, 16) && aligned(dout, 16);
+  const void *fn = v16 ? (const void *)scan_bwd_col_kernel<true> : (const void *)scan_bwd_col_kernel<false>;
+  if (int e = allow_dynamic_smem(fn, kBSmem, &g_bwd_attr[v16])) return e;
+  if (v16)
+    scan_bwd_col_kernel<true><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(z, c, c0, dout, dh_n, dc_n, dz, dc0,
+                                                                       db_part, T, B, H, eps, status);
+  else
+    scan_bwd_col_kernel<false><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(z, c, c0, dout, dh_n, dc_n, dz, dc0,
+                                                                        db_part, T, B, H, eps, status);
+  return check_launch("scan_bwd_col_kernel");
+}
+
+}  // namespace hs

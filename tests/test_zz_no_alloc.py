@@ -69,7 +69,7 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
 
     lib = L.load()
     P = ctypes.c_void_p
-    # 16384 x 32 x 1024 needs ~190 MiB of look-back scratch: rejected on the host
+    # 16384 x 32 x 1024 needs 512 MiB of look-back scratch: rejected on the host
     rc = lib.hs_scan_forward_noalloc(P(256), None, P(256), P(256), None, None, 16384, 32, 1024,
                                      1e-6, None, None)
     assert rc == 3
