@@ -53,6 +53,11 @@ def _peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def _peaks_raw():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    return json.load(open(p)) if os.path.exists(p) else {}
+
+
 def _traffic(kernel: str, units: float):
     """DRAM bytes per launch of `kernel`, scaled from the committed ncu summary
     (profiles/traffic.json: bytes per element at a captured size)."""
@@ -481,13 +486,31 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
     flops = 24.0 * T * B_local * H * (D + H)
     tokens = T * B_local * world * args.steps
     ach = flops / ((fwd + bwd) / 1e3) / 1e12
+    # Per-step latency bound of the recurrence: the larger of the step's
+    # FLOPs at the tensor peak and the step's W_hh bytes at the aggregate
+    # shared-memory bandwidth (128 B/clk/SM at the measured under-load clock).
+    # The forward step is one [B,H]x[H,4H] product, the backward step two.
+    pk = _peaks_raw()
+    mhz = (pk.get("clocks_under_load") or {}).get("sm_mhz_median") or pk.get("sm_max_mhz") or 1965.0
+    nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+    smem_bw = 128.0 * nsm * mhz * 1e6  # bytes/s
+    whh_bytes = 4.0 * H * H * 4
+    step_flop = 8.0 * B_local * H * H
+    bound_f = max(step_flop / (peak_tf * 1e12), whh_bytes / smem_bw) * 1e6
+    bound_b = max(2 * step_flop / (peak_tf * 1e12), whh_bytes / smem_bw) * 1e6
+    us_f, us_b = fwd * 1e3 / T, bwd * 1e3 / T
     res = {"value": tokens / (ms / 1e3), "ms_per_step": ms / args.steps, "clocks": ck,
            "gpu_launches": None,
-           "recurrent": {"fwd_ms": fwd, "bwd_ms": bwd, "us_per_step_fwd": fwd * 1e3 / T,
-                         "us_per_step_bwd": bwd * 1e3 / T},
+           "recurrent": {"fwd_ms": fwd, "bwd_ms": bwd, "us_per_step_fwd": us_f,
+                         "us_per_step_bwd": us_b,
+                         "step_bound_us": {"fwd": round(bound_f, 3), "bwd": round(bound_b, 3),
+                                           "smem_gbs": round(smem_bw / 1e9, 1), "sm_mhz": mhz},
+                         "frac_of_step_bound": {"fwd": round(bound_f / us_f, 4),
+                                                "bwd": round(bound_b / us_b, 4)}},
            "roofline": {"kernel": "recurrent fwd+bwd", "bound": "tensor", "achieved": round(ach, 3),
                         "peak": peak_tf, "unit": "TFLOP/s", "frac": round(ach / peak_tf, 5),
-                        "peak_kind": peak_kind, "traffic": None}}
+                        "peak_kind": peak_kind, "traffic": None,
+                        "note": "latency-bound recurrence: see recurrent.frac_of_step_bound"}}
     if args.no_e2e:
         return res
     # e2e through the module API with host buffers
@@ -578,10 +601,14 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the global batch (small cases for profiling)")
+    ap.add_argument("--seq-len", type=int, default=None,
+                    help="override T (small cases for profiling)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.batch:
         cfg["B"] = args.batch
+    if args.seq_len:
+        cfg["T"] = args.seq_len
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

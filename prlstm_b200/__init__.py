@@ -29,6 +29,8 @@ from ._lib import check_device_status, clear_device_status
 
 __version__ = "0.1.0"
 
+_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
+
 
 class HeadStartLSTM(nn.Module):
     """LSTM with a sigmoid g-gate and a learnable per-gate recurrent scale
@@ -74,8 +76,23 @@ class HeadStartLSTM(nn.Module):
             self.a.fill_(self.a_init)
 
     def forward(self, x: torch.Tensor, hx=None):
+        """``x`` [T, B, D] (or [B, T, D] with batch_first) -> ``(out, (h_n, c_n))``.
+
+        float32 is the native precision.  bfloat16 and float16 modules and
+        inputs are the reduced-precision variant: the kernels read the
+        bf16-valued inputs and weights exactly (widened to float32), keep
+        float32 accumulation and state, and the outputs come back in the
+        input's dtype, as the reference returns them (its parameters, data and
+        results share one dtype); parameter gradients arrive in the
+        parameters' dtype.  float64 is refused: every kernel computes in
+        float32, and silently returning float32-accurate results under a
+        float64 dtype would misstate their precision."""
         if x.dim() != 3:
             raise RuntimeError("input must be [T, B, input_size]")
+        if x.dtype not in _DTYPES:
+            raise TypeError(f"prlstm_b200 computes in float32; got input dtype {x.dtype} "
+                            "(use float32, bfloat16 or float16)")
+        out_dtype = x.dtype
         if self.batch_first:
             x = x.transpose(0, 1).contiguous()
         T, B, D = x.shape
@@ -100,6 +117,8 @@ class HeadStartLSTM(nn.Module):
             output, h_n, c_n = headstartlstm_recurrent(
                 x, h0, c0, self.weight_ih_l0, self.weight_hh_l0,
                 self.bias_ih_l0, self.bias_hh_l0, self.a)
+        if out_dtype != torch.float32:
+            output, h_n, c_n = output.to(out_dtype), h_n.to(out_dtype), c_n.to(out_dtype)
         if self.batch_first:
             output = output.transpose(0, 1).contiguous()
         return output, (h_n.unsqueeze(0), c_n.unsqueeze(0))

@@ -1,0 +1,67 @@
+"""Reduced-precision variant: a bfloat16 module fed bfloat16 inputs.
+
+The reference runs the same module in bfloat16 end to end and checks its
+backends against each other at 1e-2 absolute (tests/test_parallel.py:24,
+tests/test_triton.py:22).  Here the variant is checked against the float64
+oracle fed the same bf16-rounded inputs and weights, with the stated
+tolerance of 2e-2 normwise (outputs and gradients are returned in bfloat16,
+whose rounding alone is 2^-9 relative).  Output and gradient dtypes must be
+the module's."""
+
+import pytest
+import torch
+
+from oracle import hs_oracle as O
+from _cases import make_inputs, rel_err
+
+pytestmark = pytest.mark.gpu
+TOL_BF16 = 2e-2
+
+
+@pytest.mark.parametrize("parallel,T,B,D,H,a", [
+    (False, 64, 8, 64, 128, 1e-4),
+    (False, 32, 4, 96, 256, 0.3),
+    (True, 256, 8, 64, 128, 0.0),
+])
+def test_bf16_module_against_float64_oracle(parallel, T, B, D, H, a):
+    import prlstm_b200
+
+    dev = torch.device("cuda", 0)
+    params, x, G = make_inputs(T, B, D, H, a=a, seed=T + H)
+    params = tuple(p.to(torch.bfloat16) for p in params)
+    x = x.to(torch.bfloat16)
+    G = G.to(torch.bfloat16)
+    m = prlstm_b200.HeadStartLSTM(D, H, parallel=parallel).to(dev, torch.bfloat16)
+    with torch.no_grad():
+        for p, v in zip(m.parameters(), params):
+            p.copy_(v)
+    xd = x.to(dev).requires_grad_(True)
+    out, (h_n, c_n) = m(xd)
+    assert out.dtype == h_n.dtype == c_n.dtype == torch.bfloat16
+    (out.float() * G.to(dev).float()).sum().backward()
+    torch.cuda.synchronize()
+    prlstm_b200.check_device_status()
+    truth = O.module_forward_backward(tuple(p.double() for p in params), x.double(), G.double(),
+                                      parallel=parallel, linear_truth=True)
+    got = dict(out=out, h_n=h_n[0], c_n=c_n[0], dx=xd.grad)
+    for name, key in zip(("weight_ih_l0", "weight_hh_l0", "bias_ih_l0", "bias_hh_l0", "a"),
+                         ("dW_ih", "dW_hh", "db_ih", "db_hh", "da")):
+        g = dict(m.named_parameters())[name].grad
+        if truth[key] is None:
+            assert g is None, name
+            continue
+        assert g.dtype == torch.bfloat16, name
+        got[key] = g
+    assert xd.grad.dtype == torch.bfloat16
+    for k, v in got.items():
+        e = rel_err(v.float().cpu(), truth[k])
+        print(f"BF16ERR parallel={parallel} {k} {e:.3e}")
+        assert e < TOL_BF16, f"{k}: {e:.3e}"
+
+
+def test_float64_is_refused():
+    import prlstm_b200
+
+    m = prlstm_b200.HeadStartLSTM(8, 16).cuda().double()
+    with pytest.raises(TypeError):
+        m(torch.zeros(4, 2, 8, dtype=torch.float64, device="cuda"))
