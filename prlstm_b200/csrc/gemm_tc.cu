@@ -23,14 +23,17 @@
 //
 // Kernel structure (one 128 x 128 output tile per CTA, 1 CTA per SM):
 //   warp 0      TMA producer: raw A/B k-blocks (32 fp32 = one 128-byte
-//               swizzle row) into a 3-stage ring;
+//               swizzle row) into a ring of HS_TC_RAW_STAGES stages;
 //   warp 1      allocates 512 TMEM columns; one lane issues tcgen05.mma and
-//               commits stages back to the producer and finished groups to
-//               the epilogue warps;
-//   warps 2..5  compute lo for every stage in shared memory (elementwise, so
-//               the swizzled layout is kept), fold finished groups into their
-//               row's register totals, and finally store the tile (bias,
-//               beta) or a split-K partial.
+//               commits raw stages back to the producer, lo slots back to
+//               the transform and finished groups to the epilogue warps;
+//   warps 2..5  compute lo for every k-block into a ring of HS_TC_LO_SLOTS
+//               slots in shared memory (elementwise, so the swizzled layout
+//               is kept);
+//   warps 6..9  fold finished groups into their row's register totals (one
+//               TMEM lane quadrant each) and finally store the tile (bias,
+//               beta) or a split-K partial.  Folding in separate warps keeps
+//               the transform running ahead of the tensor core.
 // No cluster multicast anywhere.  Every mbarrier wait is bounded.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -43,13 +46,26 @@ namespace hs {
 
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3, PROMOTE = 4;
-constexpr int NTHREADS = 192;
+// Raw operand stages (TMA targets) and lo slots (transform outputs) are
+// separate rings: a raw stage is busy from its TMA issue until its MMAs
+// complete, a lo slot only from the transform until the same MMAs, so a deep
+// raw ring (load latency) and a short lo ring fit in shared memory together.
+#ifndef HS_TC_RAW_STAGES
+#define HS_TC_RAW_STAGES 3
+#endif
+#ifndef HS_TC_LO_SLOTS
+#define HS_TC_LO_SLOTS 3
+#endif
+constexpr int BM = 128, BN = 128, BK = 32, PROMOTE = 4;
+constexpr int STAGES = HS_TC_RAW_STAGES, LOS = HS_TC_LO_SLOTS;
+constexpr int NTHREADS = 320;  // producer, MMA, 4 transform, 4 fold/epilogue warps
 constexpr int A_BYTES = BM * BK * 4;                 // 16 KB
 constexpr int B_BYTES = BN * BK * 4;                 // 16 KB
 constexpr int RAW_BYTES = A_BYTES + B_BYTES;         // 32 KB
-constexpr int STAGE_BYTES = 2 * RAW_BYTES;           // raw + lo
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int LO_OFF = STAGES * RAW_BYTES;           // lo slots follow the raw stages
+constexpr int SMEM_BYTES = (STAGES + LOS) * RAW_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+static_assert(SMEM_BYTES <= 232448, "shared memory per block");
+static_assert((STAGES + LOS) * RAW_BYTES >= BM * BN * 4, "epilogue staging area");
 constexpr uint32_t TMEM_COLS = 512;                  // 2 buffers x (main, correction) x 128
 
 HS_DEV uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -190,16 +206,64 @@ struct TcArgs {
   int *status;
 };
 
+// Epilogue of the fold warps (128 threads, thread = tile row q*32+lane):
+// stage the tile in shared memory (free: every MMA and load has completed) as
+// four 128-row x 32-column boxes with the 128-byte swizzle (conflict-free
+// row-per-thread writes), then write it with TMA bulk stores (reduce-add
+// when beta = 1), or store a split-K partial.
+HS_DEV void store_tile(const float (&tot)[BN], unsigned char *smem, const CUtensorMap *tmC_, const TcArgs &p,
+                       int q, int lane, int t, int64_t m0, int64_t n0) {
+  const CUtensorMap &tmC = *tmC_;
+  const int r = q * 32 + lane;
+  const bool direct = p.partial == nullptr;
+  float *box0 = reinterpret_cast<float *>(smem);
+#pragma unroll
+  for (int c = 0; c < BN / 32; ++c) {
+    float *boxc = box0 + c * (BM * 32);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 o = make_float4(tot[c * 32 + 4 * j], tot[c * 32 + 4 * j + 1], tot[c * 32 + 4 * j + 2],
+                             tot[c * 32 + 4 * j + 3]);
+      if (direct && p.bias) {
+        const int64_t n = n0 + c * 32 + 4 * j;
+        if (n + 3 < p.N) {
+          const float4 bb = *reinterpret_cast<const float4 *>(p.bias + n);
+          o.x += bb.x; o.y += bb.y; o.z += bb.z; o.w += bb.w;
+        } else {
+          if (n < p.N) o.x += p.bias[n];
+          if (n + 1 < p.N) o.y += p.bias[n + 1];
+          if (n + 2 < p.N) o.z += p.bias[n + 2];
+        }
+      }
+      *reinterpret_cast<float4 *>(boxc + r * 32 + ((j ^ (r & 7)) * 4)) = o;
+    }
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  if (t == 0) {
+    const int zc = p.partial ? (int)blockIdx.z : 0;
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c) {
+      if (direct && p.beta) tma_reduce_add_3d(&tmC, box0 + c * (BM * 32), (int)n0 + 32 * c, (int)m0, zc);
+      else tma_store_3d(&tmC, box0 + c * (BM * 32), (int)n0 + 32 * c, (int)m0, zc);
+    }
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(NTHREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, TcArgs p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
-  uint64_t *xformed = full + STAGES;
-  uint64_t *empty = xformed + STAGES;
-  uint64_t *pfull = empty + STAGES;   // [2] group finished in accumulator pair b
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + (STAGES + LOS) * RAW_BYTES);
+  uint64_t *empty = full + STAGES;
+  uint64_t *xformed = empty + STAGES;  // [LOS] lo slot written
+  uint64_t *lofree = xformed + LOS;    // [LOS] lo slot consumed by its MMAs
+  uint64_t *pfull = lofree + LOS;     // [2] group finished in accumulator pair b
   uint64_t *pempty = pfull + 2;       // [2] accumulator pair b folded, reusable
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(pempty + 2);
   int *abort_flag = reinterpret_cast<int *>(tmem_holder + 1);
@@ -214,8 +278,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&xformed[s], 4);
       mbar_init(&empty[s], 1);
+    }
+    for (int l = 0; l < LOS; ++l) {
+      mbar_init(&xformed[l], 4);
+      mbar_init(&lofree[l], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&pfull[b], 1);
@@ -245,7 +312,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const uint32_t ph = (i / STAGES) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, p.status)) break;
         ++issued;
-        unsigned char *st = smem + s * STAGE_BYTES;
+        unsigned char *st = smem + s * RAW_BYTES;
         mbar_expect_tx(&full[s], RAW_BYTES);
         const int k0 = (kb0 + i) * BK;
         // M/N-major operands arrive as 32 x 32 boxes (128-byte rows of 32
@@ -278,15 +345,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       for (int i = 0; i < nk && ok; ++i) {
         const int s = i % STAGES;
         const uint32_t ph = (i / STAGES) & 1;
+        const int l = i % LOS;
+        const uint32_t lph = (i / LOS) & 1;
         const int g = i / PROMOTE, b = g & 1;
         const bool gstart = (i % PROMOTE) == 0;
         if (gstart && !mbar_wait(&pempty[b], ((g >> 1) & 1) ^ 1, p.status)) break;
-        if (!mbar_wait(&xformed[s], ph, p.status)) break;
+        if (!mbar_wait(&xformed[l], lph, p.status)) break;  // implies full[s] of this k-block
+        (void)ph;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a_raw = su32(smem + s * STAGE_BYTES);
+        const uint32_t a_raw = su32(smem + s * RAW_BYTES);
         const uint32_t b_raw = a_raw + A_BYTES;
-        const uint32_t a_lo = a_raw + RAW_BYTES;
-        const uint32_t b_lo = b_raw + RAW_BYTES;
+        const uint32_t a_lo = su32(smem + LO_OFF + l * RAW_BYTES);
+        const uint32_t b_lo = a_lo + A_BYTES;
         const uint32_t t_main = tmem + (uint32_t)(b * 2 * BN);
         const uint32_t t_corr = t_main + BN;
 #pragma unroll
@@ -309,21 +379,42 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           mma_tf32(t_corr, dAl, dB, idesc, 1u);
         }
         mma_commit(&empty[s]);
+        mma_commit(&lofree[l]);
         if ((i % PROMOTE) == PROMOTE - 1 || i == nk - 1) mma_commit(&pfull[b]);
       }
     }
-  } else if (!skip) {
-    // ---------------- transform (lo parts), folding, epilogue
+  } else if (!skip && warp < 6) {
+    // ---------------- transform: lo parts of every k-block
     const int t = threadIdx.x - 64;  // 0..127
-    const int q = warp & 3;          // TMEM lane quadrant of this warp
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = (i / STAGES) & 1;
+      const int l = i % LOS;
+      const uint32_t lph = (i / LOS) & 1;
+      if (!mbar_wait(&lofree[l], lph ^ 1, p.status)) break;
+      if (!mbar_wait(&full[s], ph, p.status)) break;
+      const float4 *raw = reinterpret_cast<const float4 *>(smem + s * RAW_BYTES);
+      float4 *lo = reinterpret_cast<float4 *>(smem + LO_OFF + l * RAW_BYTES);
+#pragma unroll 4
+      for (int j = t; j < RAW_BYTES / 16; j += 128) {
+        const float4 v = raw[j];
+        lo[j] = make_float4(lo_part(v.x), lo_part(v.y), lo_part(v.z), lo_part(v.w));
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xformed[l]);
+    }
+  } else if (!skip) {
+    // ---------------- fold finished groups into register totals, epilogue
+    const int t = threadIdx.x - 192;  // 0..127
+    const int q = warp & 3;           // TMEM lane quadrant of this warp
     float tot[BN];
 #pragma unroll
     for (int j = 0; j < BN; ++j) tot[j] = 0.f;
     bool ok = true;
-    int drained = 0;
-    auto fold = [&](int g) -> bool {
+    for (int g = 0; g < ngroups; ++g) {
       const int b = g & 1;
-      if (!mbar_wait(&pfull[b], (g >> 1) & 1, p.status)) return false;
+      if (!mbar_wait(&pfull[b], (g >> 1) & 1, p.status)) { ok = false; break; }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 2 * BN);
 #pragma unroll
@@ -339,75 +430,256 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&pempty[b]);
-      return true;
-    };
-    for (int i = 0; i < nk && ok; ++i) {
-      const int s = i % STAGES;
-      const uint32_t ph = (i / STAGES) & 1;
-      if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
-      const float4 *raw = reinterpret_cast<const float4 *>(smem + s * STAGE_BYTES);
-      float4 *lo = reinterpret_cast<float4 *>(smem + s * STAGE_BYTES + RAW_BYTES);
-#pragma unroll 4
-      for (int j = t; j < RAW_BYTES / 16; j += 128) {
-        const float4 v = raw[j];
-        lo[j] = make_float4(lo_part(v.x), lo_part(v.y), lo_part(v.z), lo_part(v.w));
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&xformed[s]);
-      // fold group g once the transform is 3 k-blocks into group g+1
-      if (drained < ngroups && i >= PROMOTE * (drained + 1) + 2) {
-        if (!fold(drained)) { ok = false; break; }
-        ++drained;
-      }
-    }
-    while (ok && drained < ngroups) {
-      if (!fold(drained)) { ok = false; break; }
-      ++drained;
     }
     if (ok) {
       // Stage the tile in shared memory (stage 0 is free: every MMA has
       // completed) as four 128-row x 32-column boxes with the 128-byte
       // swizzle (conflict-free row-per-thread writes), then write it with
       // TMA bulk stores (reduce-add when beta = 1).
-      const int r = q * 32 + lane;
-      const bool direct = p.partial == nullptr;
-      float *box0 = reinterpret_cast<float *>(smem);
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        float *boxc = box0 + c * (BM * 32);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float4 o = make_float4(tot[c * 32 + 4 * j], tot[c * 32 + 4 * j + 1], tot[c * 32 + 4 * j + 2],
-                                 tot[c * 32 + 4 * j + 3]);
-          if (direct && p.bias) {
-            const int64_t n = n0 + c * 32 + 4 * j;
-            if (n + 3 < p.N) {
-              const float4 bb = *reinterpret_cast<const float4 *>(p.bias + n);
-              o.x += bb.x; o.y += bb.y; o.z += bb.z; o.w += bb.w;
-            } else {
-              if (n < p.N) o.x += p.bias[n];
-              if (n + 1 < p.N) o.y += p.bias[n + 1];
-              if (n + 2 < p.N) o.z += p.bias[n + 2];
-            }
-          }
-          *reinterpret_cast<float4 *>(boxc + r * 32 + ((j ^ (r & 7)) * 4)) = o;
-        }
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (t == 0) {
-        const int zc = p.partial ? (int)blockIdx.z : 0;
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          if (direct && p.beta) tma_reduce_add_3d(&tmC, box0 + c * (BM * 32), (int)n0 + 32 * c, (int)m0, zc);
-          else tma_store_3d(&tmC, box0 + c * (BM * 32), (int)n0 + 32 * c, (int)m0, zc);
-        }
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      store_tile(tot, smem, &tmC, p, q, lane, t, m0, n0);
     }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+
+// ---------------------------------------------------------------- operand A in TMEM
+// Variant for K-major A (the projection x.W_ih^T and the input gradient
+// dZ.W_ih).  Shared memory is the bound of the kernel above: per 32-deep
+// k-block the three MMAs read 96 KB of operands, the TMA writes 32 KB and the
+// lo transform reads 32 KB and writes 32 KB, against 128 B/clk per SM.  Here
+// the transform warps copy each k-block's A rows into tensor memory, both the
+// raw words and their lo parts (tcgen05.st, one row per thread), and the MMAs
+// take A from TMEM ("TS" form): per k-block shared memory then carries the
+// TMA's 32 KB, the transform's 32 KB of reads and 16 KB of B_lo writes, and
+// the MMAs' 48 KB of B reads.
+//
+// TMEM columns: [0,128) and [128,256) are two accumulators (one per group,
+// double-buffered as above, but each holds the main product and both
+// corrections); [256 + 64 l, +32) and [+32, +64) hold A raw / A lo of lo-slot
+// l.  With every product in one accumulator each MMA adds into a value of the
+// group's magnitude, so groups are kept short (TA_PROMOTE k-blocks) and
+// folded into float32 register totals by the fold warps.
+#ifndef HS_TA_STAGES
+#define HS_TA_STAGES 4
+#endif
+#ifndef HS_TA_LOS
+#define HS_TA_LOS 3
+#endif
+#ifndef HS_TA_PROMOTE
+#define HS_TA_PROMOTE 2
+#endif
+constexpr int TA_STAGES = HS_TA_STAGES, TA_LOS = HS_TA_LOS, TA_PROMOTE = HS_TA_PROMOTE;
+constexpr int TA_BLO_OFF = TA_STAGES * RAW_BYTES;                 // B_lo slots after the raw stages
+constexpr int TA_SMEM_BYTES = TA_STAGES * RAW_BYTES + TA_LOS * B_BYTES + 1024 + 256;
+constexpr uint32_t TA_ACOL = 2 * BN;                              // first A-slot column
+static_assert(TA_ACOL + TA_LOS * 64 <= TMEM_COLS, "TMEM columns");
+static_assert(TA_SMEM_BYTES <= 232448, "shared memory per block");
+static_assert(TA_STAGES * RAW_BYTES + TA_LOS * B_BYTES >= BM * BN * 4, "epilogue staging area");
+
+HS_DEV void mma_tf32_ts(uint32_t dt, uint32_t at, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(dt),
+      "r"(at), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+HS_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+template <bool B_MN>
+__global__ void __launch_bounds__(NTHREADS, 1)
+gemm_ta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmC, TcArgs p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + TA_STAGES * RAW_BYTES + TA_LOS * B_BYTES);
+  uint64_t *empty = full + TA_STAGES;
+  uint64_t *xformed = empty + TA_STAGES;  // [TA_LOS] A slot + B_lo slot written
+  uint64_t *lofree = xformed + TA_LOS;    // [TA_LOS] consumed by their MMAs
+  uint64_t *pfull = lofree + TA_LOS;      // [2] group finished in accumulator b
+  uint64_t *pempty = pfull + 2;           // [2] accumulator b folded, reusable
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(pempty + 2);
+  int *abort_flag = reinterpret_cast<int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  const int kb0 = blockIdx.z * p.kb_per_split;
+  const int kb1 = min(p.nkb, kb0 + p.kb_per_split);
+  const int nk = kb1 - kb0;
+  const int ngroups = (nk + TA_PROMOTE - 1) / TA_PROMOTE;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TA_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int l = 0; l < TA_LOS; ++l) {
+      mbar_init(&xformed[l], 4);
+      mbar_init(&lofree[l], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pfull[b], 1);
+      mbar_init(&pempty[b], 4);
+    }
+    *abort_flag = ld_status(p.status) != 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_holder)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_holder;
+  const bool skip = *abort_flag != 0 || nk <= 0;
+
+  if (!skip && warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % TA_STAGES;
+        const uint32_t ph = (i / TA_STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, p.status)) break;
+        ++issued;
+        unsigned char *st = smem + s * RAW_BYTES;
+        mbar_expect_tx(&full[s], RAW_BYTES);
+        const int k0 = (kb0 + i) * BK;
+        tma_2d(st, &tmA, &full[s], k0, (int)m0);
+        if (B_MN) {
+#pragma unroll
+          for (int j = 0; j < BN / 32; ++j) tma_2d(st + A_BYTES + j * 4096, &tmB, &full[s], (int)n0 + 32 * j, k0);
+        } else {
+          tma_2d(st + A_BYTES, &tmB, &full[s], k0, (int)n0);
+        }
+      }
+      for (int i = std::max(0, issued - TA_STAGES); i < issued; ++i) {
+        if (ld_status(p.status)) mbar_drain(&full[i % TA_STAGES], (i / TA_STAGES) & 1);
+        else (void)mbar_wait(&full[i % TA_STAGES], (i / TA_STAGES) & 1, p.status);
+      }
+    }
+  } else if (!skip && warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(BM, BN, false, B_MN);
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % TA_STAGES;
+        const int l = i % TA_LOS;
+        const uint32_t lph = (i / TA_LOS) & 1;
+        const int g = i / TA_PROMOTE, b = g & 1;
+        const bool gstart = (i % TA_PROMOTE) == 0;
+        if (gstart && !mbar_wait(&pempty[b], ((g >> 1) & 1) ^ 1, p.status)) break;
+        if (!mbar_wait(&xformed[l], lph, p.status)) break;  // implies full[s] of this k-block
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t b_raw = su32(smem + s * RAW_BYTES) + A_BYTES;
+        const uint32_t b_lo = su32(smem + TA_BLO_OFF + l * B_BYTES);
+        const uint32_t t_acc = tmem + (uint32_t)(b * BN);
+        const uint32_t a_raw = tmem + TA_ACOL + (uint32_t)(l * 64);
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          const uint32_t bo = B_MN ? kk * 1024 : kk * 32;
+          const uint32_t lb = B_MN ? 1u : 2u;
+          const uint32_t blbo = B_MN ? 4096 : 16, bsbo = B_MN ? 512 : 1024;
+          const uint64_t dB = sdesc(b_raw + bo, blbo, bsbo, lb), dBl = sdesc(b_lo + bo, blbo, bsbo, lb);
+          const uint32_t acc = (gstart && kk == 0) ? 0u : 1u;
+          mma_tf32_ts(t_acc, a_raw + kk * 8, dB, idesc, acc);
+          mma_tf32_ts(t_acc, a_raw + kk * 8, dBl, idesc, 1u);
+          mma_tf32_ts(t_acc, a_raw + 32 + kk * 8, dB, idesc, 1u);
+        }
+        mma_commit(&empty[s]);
+        mma_commit(&lofree[l]);
+        if ((i % TA_PROMOTE) == TA_PROMOTE - 1 || i == nk - 1) mma_commit(&pfull[b]);
+      }
+    }
+  } else if (!skip && warp < 6) {
+    // ---------------- transform: A rows -> TMEM (raw, lo), B -> B_lo in smem
+    const int t = threadIdx.x - 64;  // 0..127
+    const int q = warp & 3;          // TMEM lane quadrant this warp may access
+    const int r = q * 32 + lane;     // A row (TMEM lane) of this thread
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % TA_STAGES;
+      const uint32_t ph = (i / TA_STAGES) & 1;
+      const int l = i % TA_LOS;
+      const uint32_t lph = (i / TA_LOS) & 1;
+      if (!mbar_wait(&lofree[l], lph ^ 1, p.status)) break;
+      if (!mbar_wait(&full[s], ph, p.status)) break;
+      // A: row r of the K-major 128-byte-swizzled tile; 16-byte chunk c of
+      // the row (k = 4c..4c+3) sits at chunk position c ^ (r % 8).
+      const unsigned char *arow = smem + s * RAW_BYTES + r * 128;
+      uint32_t hi[32], lo[32];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float4 v = *reinterpret_cast<const float4 *>(arow + ((c ^ (r & 7)) << 4));
+        hi[4 * c + 0] = __float_as_uint(v.x);
+        hi[4 * c + 1] = __float_as_uint(v.y);
+        hi[4 * c + 2] = __float_as_uint(v.z);
+        hi[4 * c + 3] = __float_as_uint(v.w);
+        lo[4 * c + 0] = __float_as_uint(lo_part(v.x));
+        lo[4 * c + 1] = __float_as_uint(lo_part(v.y));
+        lo[4 * c + 2] = __float_as_uint(lo_part(v.z));
+        lo[4 * c + 3] = __float_as_uint(lo_part(v.w));
+      }
+      const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + TA_ACOL + (uint32_t)(l * 64);
+      tmem_st32(ta, hi);
+      tmem_st32(ta + 32, lo);
+      // B: elementwise lo parts (the swizzled layout is kept)
+      const float4 *braw = reinterpret_cast<const float4 *>(smem + s * RAW_BYTES + A_BYTES);
+      float4 *blo = reinterpret_cast<float4 *>(smem + TA_BLO_OFF + l * B_BYTES);
+#pragma unroll 4
+      for (int j = t; j < B_BYTES / 16; j += 128) {
+        const float4 v = braw[j];
+        blo[j] = make_float4(lo_part(v.x), lo_part(v.y), lo_part(v.z), lo_part(v.w));
+      }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xformed[l]);
+    }
+  } else if (!skip) {
+    // ---------------- fold finished groups into register totals, epilogue
+    const int t = threadIdx.x - 192;  // 0..127
+    const int q = warp & 3;
+    float tot[BN];
+#pragma unroll
+    for (int j = 0; j < BN; ++j) tot[j] = 0.f;
+    bool ok = true;
+    for (int g = 0; g < ngroups; ++g) {
+      const int b = g & 1;
+      if (!mbar_wait(&pfull[b], (g >> 1) & 1, p.status)) { ok = false; break; }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN);
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(base + c, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tot[c + j] += v[j];
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pempty[b]);
+    }
+    if (ok) store_tile(tot, smem, &tmC, p, q, lane, t, m0, n0);
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -485,6 +757,17 @@ bool make_map(CUtensorMap *tm, const float *ptr, int64_t R, int64_t K, int64_t l
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   }
   return r == CUDA_SUCCESS;
+}
+
+// HS_TC_TMEM_A=0 runs K-major-A products on the shared-memory-A kernel
+// (cross-checks of the two tensor-core kernels).
+bool tmem_a_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char *e = getenv("HS_TC_TMEM_A");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
 }
 
 int g_disable = -1;  // HS_DISABLE_TC=1 forces the FFMA path (cross-checks)
@@ -597,17 +880,18 @@ int gemm_tc_try(const float *A, const float *B, float *C, const float *bias, int
   args.status = status;
   const dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), (unsigned)pl.splits);
   void (*fn)(const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs);
-  if (!a_kc && !b_kc) fn = gemm_tc_kernel<true, true>;
+  const bool tmem_a = a_kc && tmem_a_enabled();
+  if (tmem_a) fn = b_kc ? gemm_ta_kernel<false> : gemm_ta_kernel<true>;
+  else if (!a_kc && !b_kc) fn = gemm_tc_kernel<true, true>;
   else if (!a_kc) fn = gemm_tc_kernel<true, false>;
   else if (!b_kc) fn = gemm_tc_kernel<false, true>;
   else fn = gemm_tc_kernel<false, false>;
-  static std::once_flag attr_once[4];
-  const int which = (a_kc ? 0 : 2) + (b_kc ? 0 : 1);
-  std::call_once(attr_once[which], [&] {
-    cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  });
+  const int smem_bytes = tmem_a ? TA_SMEM_BYTES : SMEM_BYTES;
+  static std::atomic<unsigned long long> attr_set[6];
+  const int which = tmem_a ? 4 + (b_kc ? 0 : 1) : (a_kc ? 0 : 2) + (b_kc ? 0 : 1);
+  if (int e = allow_dynamic_smem((const void *)fn, smem_bytes, &attr_set[which])) return e;
   if (grid.y > 65535) return HS_OK;
-  fn<<<grid, NTHREADS, SMEM_BYTES, st>>>(ta, tb, tc, args);
+  fn<<<grid, NTHREADS, smem_bytes, st>>>(ta, tb, tc, args);
   if (int e = check_launch("gemm_tc_kernel")) return e;
   if (pl.splits > 1) {
     const int64_t n = M * N;

@@ -101,3 +101,52 @@ def test_colsum_matches():
     P = L.ptr
     L.call("hs_colsum", P(dy), P(db), 5000, 1000, 0, L.stream_ptr(dev))
     assert _rel(db, dy.double().cpu().sum(0)) < 1e-6
+
+
+def test_both_tensor_core_kernels_agree():
+    """K-major-A products run on the TMEM-A kernel by default; HS_TC_TMEM_A=0
+    selects the shared-memory-A kernel.  Run the forward and the input
+    gradient once each way (the switch is read once per process, so the
+    second run is a child process) and compare both with float64."""
+    import os
+    import subprocess
+    import sys
+
+    code = r'''
+import sys, torch
+sys.path.insert(0, ".")
+from prlstm_b200 import _lib as L
+dev = torch.device("cuda", 0)
+g = torch.Generator(device=dev).manual_seed(7)
+M, N, K = 4096, 1024, 512
+x = torch.randn(M, K, device=dev, generator=g)
+w = torch.randn(N, K, device=dev, generator=g) / K ** 0.5
+b = torch.randn(N, device=dev, generator=g)
+dy = torch.randn(M, N, device=dev, generator=g)
+y = torch.empty(M, N, device=dev)
+dx = torch.empty(M, K, device=dev)
+lib = L.load()
+ws = L.workspace(lib.hs_linear_workspace_bytes(M, N, K), dev)
+P = L.ptr
+st = L.stream_ptr(dev)
+L.call("hs_linear_forward", P(x), P(w), P(b), P(y), M, N, K, P(ws), ws.numel(), P(L.status_word(dev)), st)
+L.call("hs_linear_dgrad", P(dy), P(w), P(dx), M, N, K, P(ws), ws.numel(), P(L.status_word(dev)), st)
+torch.cuda.synchronize()
+L.check_device_status(dev)
+ry = x.double().cpu() @ w.double().cpu().t() + b.double().cpu()
+rx = dy.double().cpu() @ w.double().cpu()
+ey = ((y.double().cpu() - ry).abs().max() / ry.abs().max()).item()
+ex = ((dx.double().cpu() - rx).abs().max() / rx.abs().max()).item()
+print(f"{ey:.3e} {ex:.3e}")
+'''
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    errs = {}
+    for v in ("1", "0"):
+        env = dict(os.environ, HS_TC_TMEM_A=v)
+        out = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True,
+                             text=True, timeout=300)
+        assert out.returncode == 0, out.stderr[-2000:]
+        errs[v] = [float(t) for t in out.stdout.split()[-2:]]
+        print(f"GEMMERR HS_TC_TMEM_A={v}: forward {errs[v][0]:.3e} dgrad {errs[v][1]:.3e}")
+    for v, (ey, ex) in errs.items():
+        assert ey < TOL and ex < TOL, (v, ey, ex)
