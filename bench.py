@@ -245,6 +245,40 @@ class ParallelStep:
         return 2.0 * T * mb * 4 * H * D  # flops of one GEMM launch
 
 
+def cublas_refs(cfg, mb, dev):
+    """cuBLAS TF32 and FP32 throughput (TF/s) on one micro-batch's three GEMM
+    shapes: projection [TB,D]x[D,4H], dgrad [TB,4H]x[4H,D], wgrad
+    [4H,TB]x[TB,D]."""
+    T, D, H = cfg["T"], cfg["D"], cfg["H"]
+    M, N, K = T * mb, 4 * H, D
+    shapes = {"proj_gemm": (M, K, N), "dgrad_gemm": (M, N, K), "wgrad_gemm": (N, M, K)}
+    out = {}
+    old = torch.backends.cuda.matmul.allow_tf32
+    try:
+        for name, (m, k, n) in shapes.items():
+            a = torch.randn(m, k, device=dev)
+            b = torch.randn(k, n, device=dev)
+            r = {}
+            for tf32, key in ((True, "cublas_tf32_tflops"), (False, "cublas_fp32_tflops")):
+                torch.backends.cuda.matmul.allow_tf32 = tf32
+                c = a @ b
+                torch.cuda.synchronize(dev)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(3):
+                    c = a @ b
+                e1.record()
+                torch.cuda.synchronize(dev)
+                r[key] = 2.0 * m * n * k * 3 / (e0.elapsed_time(e1) / 1e3) / 1e12
+            out[name] = r
+            del a, b, c
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, cfg, rank, world, dev):
     import torch.distributed as dist
 
@@ -342,6 +376,21 @@ def run_ours(args, cfg, rank, world, dev):
             "traffic": _traffic(dom, units),
             "algorithmic_per_launch": (per * units) if per else units,
         }
+        # Library references for the GEMMs, timed here on the same shapes:
+        # cuBLAS TF32 (one tf32 product, ~1e-3 accurate; three of them bound
+        # an fp32-accurate 3xTF32 GEMM) and cuBLAS FP32 (the same accuracy as
+        # ours).  Measured after the timed region, outside it.
+        if not args.no_cublas_ref:
+            refs = cublas_refs(cfg, step.mb, dev)
+            for n, r in refs.items():
+                kern[n].update(r)
+                kern[n]["tf32x3_ceiling_tflops"] = r["cublas_tf32_tflops"] / 3.0
+                kern[n]["frac_of_tf32x3_ceiling"] = kern[n]["achieved"] / kern[n]["tf32x3_ceiling_tflops"]
+                kern[n]["speedup_vs_cublas_fp32"] = kern[n]["achieved"] / r["cublas_fp32_tflops"]
+            result["roofline"]["tf32x3_ceiling"] = (
+                round(kern[dom]["tf32x3_ceiling_tflops"], 1) if dom in refs else None)
+            result["roofline"]["frac_of_tf32x3_ceiling"] = (
+                round(kern[dom]["frac_of_tf32x3_ceiling"], 4) if dom in refs else None)
         result["kernels"] = {n: {k: (round(v, 4) if isinstance(v, float) else v) for k, v in kern[n].items()}
                              for n in kern}
         scan = {n: kern[n] for n in ("scan_fwd", "scan_bwd")}
@@ -589,18 +638,72 @@ def run_reference(args, cfg):
     return value, ncores, sample, total / len(times)
 
 
+def run_reference_gpu(args, cfg, dev):
+    """The reference's own GPU paths on this GPU, for comparison (not the
+    driver's reference arm): the Triton backend (CUDA graphs over per-step
+    Triton cell kernels and cuBLAS, _triton.py:327-470) for recurrent
+    configs, the parallel=True torch path (_parallel.py:38-74, ATen on CUDA)
+    for parallel configs, each fwd + sum(out*G).backward() with x requiring
+    grad.  Imports the reference package installed under baseline/_ref (an
+    offline pip install of the reference tree; absent -> unavailable).
+    Parallel configs run micro-batches of MICRO_BATCH sequences, as ours do;
+    tokens/s counts the whole batch."""
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "headstartlstm")):
+        return None, "reference package not installed under baseline/_ref"
+    sys.path.insert(0, ref_root)
+    import headstartlstm
+
+    T, D, H = cfg["T"], cfg["D"], cfg["H"]
+    params = make_params(cfg)
+    parallel = cfg["mode"] == "parallel"
+    mb = min(MICRO_BATCH, cfg["B"]) if parallel else cfg["B"]
+    nmb = cfg["B"] // mb
+    m = headstartlstm.HeadStartLSTM(D, H, backend="triton" if not parallel else "torch",
+                                    parallel=parallel).to(dev)
+    with torch.no_grad():
+        for pp, v in zip(m.parameters(), params):
+            pp.copy_(v)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(T, mb, D, device=dev, generator=gen)
+    G = torch.randn(T, mb, H, device=dev, generator=gen)
+
+    def step():
+        for _ in range(nmb):
+            xd = x.detach().requires_grad_(True)
+            out, _ = m(xd)
+            (out * G).sum().backward()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    backend = "parallel torch path (ATen CUDA)" if parallel else "triton backend"
+    return {"value": T * cfg["B"] / (ms / 1e3), "ms_per_step": ms, "backend": backend,
+            "micro_batch": mb if parallel else None}, None
+
+
 # ------------------------------------------------------------------ main
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"])
     ap.add_argument("--config", default="cfg4", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the global batch (small cases for profiling)")
+    ap.add_argument("--no-cublas-ref", action="store_true",
+                    help="skip timing cuBLAS TF32/FP32 on the GEMM shapes (GEMM ceilings)")
     ap.add_argument("--seq-len", type=int, default=None,
                     help="override T (small cases for profiling)")
     args = ap.parse_args()
@@ -637,6 +740,21 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.impl == "reference-gpu":
+        if rank != 0:
+            return
+        res, why = run_reference_gpu(args, cfg, dev)
+        if res is None:
+            print(json.dumps({"impl": "reference-gpu", "unavailable": why}), flush=True)
+            return
+        line = dict(base, impl="reference-gpu", value=res["value"], ms_per_step=res["ms_per_step"],
+                    scaling="strong" if cfg["mode"] == "parallel" else "weak",
+                    config={"workload": workload, "T": cfg["T"], "B": cfg["B"], "D": cfg["D"],
+                            "H": cfg["H"], "mode": cfg["mode"], "micro_batch": res["micro_batch"],
+                            "parallelism": "dp1", "backend": res["backend"]},
+                    gpu_launches=None)
+        print(json.dumps(line), flush=True)
+        return
     if world > 1:
         import datetime
 

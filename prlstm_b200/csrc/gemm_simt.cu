@@ -125,26 +125,31 @@ __global__ void __launch_bounds__(NT) gemm_simt_kernel(GemmArgs g) {
 // Column sums in one pass with a fixed summation order: a CTA owns 32
 // columns, warp w sums rows w, w+8, ... (coalesced 128-byte rows), and the 8
 // warp partials are added in order.
-__global__ void __launch_bounds__(256) colsum_kernel(const float *__restrict__ x, float *__restrict__ out,
-                                                     int64_t M, int64_t N, int beta) {
-  __shared__ float part[8][33];
+// out[n] = beta*out[n] + sum_m x[m][n]: 32 columns per CTA, 32 warps over
+// rows with four independent accumulators each (enough loads in flight to
+// stream from HBM), warp partials added in a fixed order.
+__global__ void __launch_bounds__(1024) colsum_kernel(const float *__restrict__ x, float *__restrict__ out,
+                                                      int64_t M, int64_t N, int beta) {
+  __shared__ float part[32][33];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int64_t n = (int64_t)blockIdx.x * 32 + lane;
-  float s0 = 0.f, s1 = 0.f;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
   if (n < N) {
     int64_t r = w;
-    for (; r + 8 < M; r += 16) {
+    for (; r + 96 < M; r += 128) {
       s0 += x[r * N + n];
-      s1 += x[(r + 8) * N + n];
+      s1 += x[(r + 32) * N + n];
+      s2 += x[(r + 64) * N + n];
+      s3 += x[(r + 96) * N + n];
     }
-    for (; r < M; r += 8) s0 += x[r * N + n];
+    for (; r < M; r += 32) s0 += x[r * N + n];
   }
-  part[w][lane] = s0 + s1;
+  part[w][lane] = (s0 + s1) + (s2 + s3);
   __syncthreads();
   if (w == 0 && n < N) {
     float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) s += part[i][lane];
+    for (int i = 0; i < 32; ++i) s += part[i][lane];
     out[n] = beta ? out[n] + s : s;
   }
 }
@@ -164,7 +169,7 @@ int gemm_simt(const float *A, const float *B, float *C, const float *bias, int64
 
 int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st) {
   if (N == 0) return HS_OK;
-  colsum_kernel<<<(unsigned)((N + 31) / 32), 256, 0, st>>>(x, out, M, N, beta);
+  colsum_kernel<<<(unsigned)((N + 31) / 32), 1024, 0, st>>>(x, out, M, N, beta);
   return check_launch("colsum_kernel");
 }
 

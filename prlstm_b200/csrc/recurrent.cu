@@ -128,15 +128,16 @@ bool make_plan(Plan &p, int64_t B, int64_t H, int nsm) {
 // Wf[c][k][ri] = a[g] W_hh[g*H+u][k], ri = ul*4+g, u = c*U+ul   (forward slice)
 // bf[c][ri]    = a[g] b_hh[g*H+u]
 // Wb[c][r][ul] = a[g(r)] W_hh[r][c*U+ul]                          (backward slice)
+// wf/bf are built when wf != null (forward), wb when wb != null (backward).
 __global__ void rec_prep_kernel(const float *__restrict__ w_hh, const float *__restrict__ b_hh,
                                 const float *__restrict__ a, float *__restrict__ wf,
                                 float *__restrict__ bf, float *__restrict__ wb, int64_t H, int U,
                                 int ncta, int rpf, int64_t kpf, int rpb, int64_t kpb) {
-  const int64_t nf = (int64_t)ncta * kpf * rpf;
-  const int64_t nb = (int64_t)ncta * kpb * rpb;
+  const int64_t nf = wf ? (int64_t)ncta * kpf * rpf : 0;
+  const int64_t nb = wb ? (int64_t)ncta * kpb * rpb : 0;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nf + nb + (int64_t)ncta * rpf;
-       i += stride) {
+  const int64_t nbias = wf ? (int64_t)ncta * rpf : 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nf + nb + nbias; i += stride) {
     if (i < nf) {
       const int ri = (int)(i % rpf);
       const int64_t k = (i / rpf) % kpf;
@@ -486,36 +487,49 @@ __global__ void __launch_bounds__(NT, 1) rec_bwd_kernel(RecArgs p) {
 
 // a-unscaling (_torch.py:165-168): dW_hh = a_exp*dW_hh_s (in place),
 // db_hh = a_exp*db, da[g] = sum_{r in g} (sum_k W_hh*dW_hh_s + b_hh*db).
-// One CTA per gate, fixed reduction order.
+// Pass 1: grid (kUnscaleParts, 4 gates); part j of gate g takes rows
+// [j*H/P, (j+1)*H/P) of that gate, scales them and writes its partial sum.
+// Pass 2: one warp per gate adds the partials in a fixed order.
+constexpr int kUnscaleParts = 128;
+
 __global__ void __launch_bounds__(256) rec_unscale_kernel(const float *__restrict__ w_hh,
                                                           const float *__restrict__ b_hh,
                                                           const float *__restrict__ a,
                                                           float *__restrict__ dw_hh,
                                                           const float *__restrict__ db,
                                                           float *__restrict__ db_hh,
-                                                          float *__restrict__ da, int64_t H) {
-  const int g = blockIdx.x;
+                                                          float *__restrict__ part, int64_t H) {
+  const int g = blockIdx.y, j = blockIdx.x;
   const float ag = a[g];
+  const int64_t r0 = H * j / kUnscaleParts, r1 = H * (j + 1) / kUnscaleParts;
   float s = 0.f;
-  for (int64_t i = threadIdx.x; i < H * H; i += 256) {
-    const int64_t idx = (int64_t)g * H * H + i;
-    const float dws = dw_hh[idx];
-    s = fmaf(w_hh[idx], dws, s);
-    dw_hh[idx] = ag * dws;
+  for (int64_t i = (int64_t)g * H * H + r0 * H + threadIdx.x; i < (int64_t)g * H * H + r1 * H; i += 256) {
+    const float dws = dw_hh[i];
+    s = fmaf(w_hh[i], dws, s);
+    dw_hh[i] = ag * dws;
   }
-  for (int64_t r = threadIdx.x; r < H; r += 256) {
+  for (int64_t r = r0 + threadIdx.x; r < r1; r += 256) {
     const int64_t idx = (int64_t)g * H + r;
     s = fmaf(b_hh[idx], db[idx], s);
     db_hh[idx] = ag * db[idx];
   }
-  __shared__ float part[256];
-  part[threadIdx.x] = s;
+  __shared__ float red[256];
+  red[threadIdx.x] = s;
   __syncthreads();
   for (int w = 128; w > 0; w >>= 1) {
-    if (threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
+    if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
     __syncthreads();
   }
-  if (threadIdx.x == 0) da[g] = part[0];
+  if (threadIdx.x == 0) part[g * kUnscaleParts + j] = red[0];
+}
+
+__global__ void rec_da_kernel(const float *__restrict__ part, float *__restrict__ da) {
+  const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float s = 0.f;
+  for (int j = lane; j < kUnscaleParts; j += 32) s += part[g * kUnscaleParts + j];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) da[g] = s;
 }
 
 using KernelFn = void (*)(RecArgs);
@@ -594,7 +608,7 @@ int rec_forward(const float *x, const float *h0, const float *c0, const float *w
   // Z = x W_ih^T + b_ih, written into acts (_torch.py:96)
   if (int e = linear_forward(x, w_ih, b_ih, acts, T * B, 4 * H, D, ws, ws_bytes, status, st)) return e;
   rec_prep_kernel<<<4 * nsm, 256, 0, st>>>(w_hh, b_hh, a, (float *)(w + pl.o_wf), (float *)(w + pl.o_bf),
-                                           (float *)(w + pl.o_wb), H, pl.U, pl.ncta, pl.fwd.rows_pad,
+                                           nullptr, H, pl.U, pl.ncta, pl.fwd.rows_pad,
                                            pl.fwd.K_pad, pl.bwd.rows_pad, pl.bwd.K_pad);
   if (int e = check_launch("rec_prep_kernel")) return e;
   KernelFn fn = pick_fwd(pl.BG, pl.fwd.RG);
@@ -643,11 +657,11 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
   if (!make_plan(pl, B, H, nsm)) return fail(HS_ERR_UNSUPPORTED, "recurrent: no tiling for B=%lld H=%lld on %d SMs", (long long)B, (long long)H, nsm);
   if (!ws || ws_bytes < pl.total) return fail(HS_ERR_WORKSPACE, "recurrent_backward: workspace %zu < %zu bytes", ws_bytes, pl.total);
   char *w = static_cast<char *>(ws);
-  // The scaled weight slices are rebuilt here so a backward never depends on
-  // workspace contents left by its forward.
-  rec_prep_kernel<<<4 * nsm, 256, 0, st>>>(w_hh, b_hh, a, (float *)(w + pl.o_wf), (float *)(w + pl.o_bf),
-                                           (float *)(w + pl.o_wb), H, pl.U, pl.ncta, pl.fwd.rows_pad,
-                                           pl.fwd.K_pad, pl.bwd.rows_pad, pl.bwd.K_pad);
+  // The scaled backward slices are built here so a backward never depends
+  // on workspace contents left by its forward.
+  rec_prep_kernel<<<4 * nsm, 256, 0, st>>>(w_hh, b_hh, a, nullptr, nullptr, (float *)(w + pl.o_wb), H,
+                                           pl.U, pl.ncta, pl.fwd.rows_pad, pl.fwd.K_pad, pl.bwd.rows_pad,
+                                           pl.bwd.K_pad);
   if (int e = check_launch("rec_prep_kernel")) return e;
   KernelFn fn = pick_bwd(pl.BG, pl.bwd.RG);
   if (!fn) return fail(HS_ERR_UNSUPPORTED, "recurrent_backward: no kernel for BG=%d RG=%d", pl.BG, pl.bwd.RG);
@@ -682,8 +696,12 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
   if (int e = colsum(acts, db_ih, M, N, 0, st)) return e;
   if (dx)
     if (int e = linear_dgrad(acts, w_ih, dx, M, N, D, ws, ws_bytes, status, st)) return e;
-  rec_unscale_kernel<<<4, 256, 0, st>>>(w_hh, b_hh, a, dw_hh, db_ih, db_hh, da, H);
-  return check_launch("rec_unscale_kernel");
+  // partial sums of da in the (now free) workspace
+  float *part = reinterpret_cast<float *>(w);
+  rec_unscale_kernel<<<dim3(kUnscaleParts, 4), 256, 0, st>>>(w_hh, b_hh, a, dw_hh, db_ih, db_hh, part, H);
+  if (int e = check_launch("rec_unscale_kernel")) return e;
+  rec_da_kernel<<<1, 128, 0, st>>>(part, da);
+  return check_launch("rec_da_kernel");
 }
 
 }  // namespace hs
