@@ -16,7 +16,9 @@ import threading
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libhsb200.so")
+# HS_B200_LIB names another build of the library (e.g. one with different
+# compile-time tile knobs); by default the in-tree build is loaded.
+LIB_PATH = os.environ.get("HS_B200_LIB") or os.path.join(HERE, "libhsb200.so")
 
 HS_OK = 0
 HS_ERR_DEVICE_TIMEOUT = 5

@@ -43,6 +43,10 @@ int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStrea
 
 namespace {
 
+#ifndef HS_REC_KUNROLL
+#define HS_REC_KUNROLL 1
+#endif
+constexpr int kKUnroll = HS_REC_KUNROLL;  // k-loop unroll of the step matvec
 constexpr int NW = 8;          // warps per CTA
 constexpr int NT = NW * 32;
 constexpr int kMaxPairs = 4;   // (unit, batch) pairs per thread in the epilogue
@@ -246,6 +250,7 @@ HS_DEV void step_matvec(const float *wres, const float *wsrc, const float *xsrc,
     __syncthreads();
     const float *X = xbuf + cur * xfl;
     const float *W = wres ? wres + (int64_t)c * wfl : wbuf + cur * wfl;
+#pragma unroll kKUnroll
     for (int k = q; k < d.KC; k += QN) {
       const float4 xv = *reinterpret_cast<const float4 *>(X + k * BP + bg * 4);
 #pragma unroll
