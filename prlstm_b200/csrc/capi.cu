@@ -34,7 +34,7 @@ int gemm_simt(const float *A, const float *B, float *C, const float *bias, int64
 int gemm_tc_try(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
                 int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kc, bool b_kc, int beta,
                 void *ws, size_t ws_bytes, int *status, cudaStream_t st, bool *done);
-size_t gemm_tc_workspace_bound(int64_t M, int64_t N, int64_t K);
+size_t gemm_tc_workspace_bound(int64_t M, int64_t N, int64_t K, bool kmajor_both);
 size_t scan_workspace(int64_t T, int64_t B, int64_t H);
 int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st);
 int scan_forward(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
@@ -59,8 +59,8 @@ static int gemm(const float *A, const float *B, float *C, const float *bias, int
 
 // Scratch any of the three linear-layer products of these extents may use.
 size_t linear_ws_bytes(int64_t M, int64_t N, int64_t K) {
-  return std::max({gemm_tc_workspace_bound(M, N, K), gemm_tc_workspace_bound(M, K, N),
-                   gemm_tc_workspace_bound(N, K, M)});
+  return std::max({gemm_tc_workspace_bound(M, N, K, true), gemm_tc_workspace_bound(M, K, N, false),
+                   gemm_tc_workspace_bound(N, K, M, false)});
 }
 
 static int check_gemm(const void *a, const void *b, const void *c, int64_t M, int64_t N, int64_t K) {

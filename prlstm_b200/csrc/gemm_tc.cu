@@ -36,6 +36,7 @@
 //               the transform running ahead of the tensor core.
 // No cluster multicast anywhere.  Every mbarrier wait is bounded.
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -689,6 +690,222 @@ gemm_ta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   }
 }
 
+
+// ---------------------------------------------------------------- 3 x fp16 split
+// K-major products (the projection x.W_ih^T) on the f16 tensor-core kind,
+// which runs at twice the tf32 rate and reads half the operand bytes.  Each
+// operand is scaled by a power of two s (so that max|x s| lies in
+// [2^14, 2^15)) and split into two fp16 words,
+//     hi = fp16(x s),   lo = fp16((x s - hi) * 2^11),
+// which keep 22 significand bits together (as tf32 hi + lo do), and
+//     A.B ~= [Ah.Bh + 2^-11 (Ah.Bl + Al.Bh)] / (s_A s_B)
+// in three MMAs per k-step, with the same two-accumulator promotion scheme
+// as the tf32 kernel.  Elements far below the tensor's maximum lose relative
+// precision in fp16's subnormal range; their absolute error stays below
+// 2^-38 of the largest element, far under the float32 result's own rounding.
+// The split runs as a separate pass over each operand (absmax, then split),
+// into caller workspace.
+HS_DEV float pow2_scale(unsigned absmax_bits) {
+  const float m = __uint_as_float(absmax_bits);
+  if (!(m > 0.f) || !(m < 3.0e38f)) return 1.0f;  // zero, inf or NaN: no scaling
+  int e;
+  (void)frexpf(m, &e);            // m = f 2^e, f in [0.5, 1): floor(log2 m) = e - 1
+  const int k = max(e - 1, -100);
+  return ldexpf(1.0f, 14 - k);
+}
+
+// Rows are taken one warp at a time (warps of the whole grid round-robin),
+// lanes stride over the columns: coalesced, no per-element index division.
+__global__ void absmax_kernel(const float *__restrict__ x, int64_t rows, int64_t cols, int64_t ld,
+                              unsigned *out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarp = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  float m = 0.f;
+  for (int64_t r = warp; r < rows; r += nwarp) {
+    const float *row = x + r * ld;
+    for (int64_t c = lane; c < cols; c += 32) m = fmaxf(m, fabsf(row[c]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) atomicMax(out, __float_as_uint(m));
+}
+
+// hi/lo [rows][ldo] fp16, ldo = cols rounded up to 8 (zero padding).
+__global__ void split_h2_kernel(const float *__restrict__ x, int64_t rows, int64_t cols, int64_t ld,
+                                const unsigned *__restrict__ absmax, __half *__restrict__ hi,
+                                __half *__restrict__ lo, int64_t ldo) {
+  const float s = pow2_scale(*absmax);
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarp = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < rows; r += nwarp) {
+    const float *row = x + r * ld;
+    __half *hr = hi + r * ldo, *lr = lo + r * ldo;
+    for (int64_t c = lane; c < ldo; c += 32) {
+      const float v = c < cols ? row[c] * s : 0.f;
+      const __half h = __float2half_rn(v);
+      hr[c] = h;
+      lr[c] = __float2half_rn((v - __half2float(h)) * 2048.0f);
+    }
+  }
+}
+
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+HS_DEV void mma_f16(uint32_t dt, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dt),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+constexpr int H3_BK = 64;                        // fp16 k per block: one 128-byte row
+constexpr int H3_TILE = 128 * H3_BK * 2;         // 16 KB per operand part
+constexpr int H3_STAGE = 4 * H3_TILE;            // Ah, Al, Bh, Bl
+constexpr int H3_STAGES = 3;
+constexpr int H3_PROMOTE = 4;
+constexpr int H3_THREADS = 192;                  // producer, MMA, 4 fold/epilogue warps
+constexpr int H3_SMEM_BYTES = H3_STAGES * H3_STAGE + 1024 + 256;
+static_assert(H3_SMEM_BYTES <= 232448, "shared memory per block");
+
+__global__ void __launch_bounds__(H3_THREADS, 1)
+gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+               const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
+               const __grid_constant__ CUtensorMap tmC, TcArgs p, const unsigned *absmax) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + H3_STAGES * H3_STAGE);
+  uint64_t *empty = full + H3_STAGES;
+  uint64_t *pfull = empty + H3_STAGES;
+  uint64_t *pempty = pfull + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(pempty + 2);
+  int *abort_flag = reinterpret_cast<int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  const int kb0 = blockIdx.z * p.kb_per_split;
+  const int kb1 = min(p.nkb, kb0 + p.kb_per_split);
+  const int nk = kb1 - kb0;
+  const int ngroups = (nk + H3_PROMOTE - 1) / H3_PROMOTE;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < H3_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pfull[b], 1);
+      mbar_init(&pempty[b], 4);
+    }
+    *abort_flag = ld_status(p.status) != 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_holder)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_holder;
+  const bool skip = *abort_flag != 0 || nk <= 0;
+
+  if (!skip && warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % H3_STAGES;
+        const uint32_t ph = (i / H3_STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, p.status)) break;
+        ++issued;
+        unsigned char *st = smem + s * H3_STAGE;
+        mbar_expect_tx(&full[s], H3_STAGE);
+        const int k0 = (kb0 + i) * H3_BK;
+        tma_2d(st, &tmAh, &full[s], k0, (int)m0);
+        tma_2d(st + H3_TILE, &tmAl, &full[s], k0, (int)m0);
+        tma_2d(st + 2 * H3_TILE, &tmBh, &full[s], k0, (int)n0);
+        tma_2d(st + 3 * H3_TILE, &tmBl, &full[s], k0, (int)n0);
+      }
+      for (int i = std::max(0, issued - H3_STAGES); i < issued; ++i) {
+        if (ld_status(p.status)) mbar_drain(&full[i % H3_STAGES], (i / H3_STAGES) & 1);
+        else (void)mbar_wait(&full[i % H3_STAGES], (i / H3_STAGES) & 1, p.status);
+      }
+    }
+  } else if (!skip && warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(BM, BN);
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % H3_STAGES;
+        const uint32_t ph = (i / H3_STAGES) & 1;
+        const int g = i / H3_PROMOTE, b = g & 1;
+        const bool gstart = (i % H3_PROMOTE) == 0;
+        if (gstart && !mbar_wait(&pempty[b], ((g >> 1) & 1) ^ 1, p.status)) break;
+        if (!mbar_wait(&full[s], ph, p.status)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t ah = su32(smem + s * H3_STAGE);
+        const uint32_t al = ah + H3_TILE, bh = ah + 2 * H3_TILE, bl = ah + 3 * H3_TILE;
+        const uint32_t t_main = tmem + (uint32_t)(b * 2 * BN);
+        const uint32_t t_corr = t_main + BN;
+#pragma unroll
+        for (int kk = 0; kk < H3_BK / 16; ++kk) {
+          // 16 fp16 = 32 bytes of each 128-byte K-major row per k-step
+          const uint32_t o = kk * 32;
+          const uint64_t dAh = sdesc(ah + o, 16, 1024, 2), dAl = sdesc(al + o, 16, 1024, 2);
+          const uint64_t dBh = sdesc(bh + o, 16, 1024, 2), dBl = sdesc(bl + o, 16, 1024, 2);
+          const uint32_t acc = (gstart && kk == 0) ? 0u : 1u;
+          mma_f16(t_main, dAh, dBh, idesc, acc);
+          mma_f16(t_corr, dAh, dBl, idesc, acc);
+          mma_f16(t_corr, dAl, dBh, idesc, 1u);
+        }
+        mma_commit(&empty[s]);
+        if ((i % H3_PROMOTE) == H3_PROMOTE - 1 || i == nk - 1) mma_commit(&pfull[b]);
+      }
+    }
+  } else if (!skip) {
+    const int t = threadIdx.x - 64;  // 0..127
+    const int q = warp & 3;
+    float tot[BN];
+#pragma unroll
+    for (int j = 0; j < BN; ++j) tot[j] = 0.f;
+    bool ok = true;
+    for (int g = 0; g < ngroups; ++g) {
+      const int b = g & 1;
+      if (!mbar_wait(&pfull[b], (g >> 1) & 1, p.status)) { ok = false; break; }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 2 * BN);
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        float v[32], w[32];
+        tmem_ld32(base + BN + c, w);
+        tmem_ld32(base + c, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tot[c + j] += fmaf(w[j], 1.0f / 2048.0f, v[j]);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pempty[b]);
+    }
+    if (ok) {
+      const float inv = 1.0f / (pow2_scale(absmax[0]) * pow2_scale(absmax[1]));  // exact: a power of two
+#pragma unroll
+      for (int j = 0; j < BN; ++j) tot[j] *= inv;
+      store_tile(tot, smem, &tmC, p, q, lane, t, m0, n0);
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
 // C[m,n] = beta*C + sum_z partial[z][m][n] (+ bias[n]); fixed order over z.
 __global__ void splitk_reduce_kernel(const float *__restrict__ part, float *__restrict__ C,
                                      const float *__restrict__ bias, int64_t M, int64_t N,
@@ -832,6 +1049,106 @@ TcPlan plan_tc(const float *A, const float *B, float *C, int64_t M, int64_t N, i
   return pl;
 }
 
+// ---------------------------------------------------------------- 3 x fp16 host side
+bool h3_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char *e = getenv("HS_TC_F16");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+int64_t round8(int64_t x) { return (x + 7) / 8 * 8; }
+// absmax words (256 B), then Ah, Al [M][K8] and Bh, Bl [N][K8] fp16
+size_t h3_scratch(int64_t M, int64_t N, int64_t K) {
+  return 256 + round_up((size_t)2 * M * round8(K) * 2, 256) + round_up((size_t)2 * N * round8(K) * 2, 256);
+}
+int h3_splits(int64_t M, int64_t N, int64_t K, int nsm) {
+  return split_count(M, N, (int)((round8(K) + H3_BK - 1) / H3_BK), nsm);
+}
+size_t h3_partial_bound(int64_t M, int64_t N, int64_t K) {
+  const int sp = h3_splits(M, N, K, 256);
+  return sp > 1 ? (size_t)sp * M * N * 4 : 0;
+}
+bool make_map_f16(CUtensorMap *tm, const __half *ptr, int64_t R, int64_t K8) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K8, (cuuint64_t)R};
+  cuuint64_t strides[1] = {(cuuint64_t)K8 * 2};
+  cuuint32_t box[2] = {H3_BK, (cuuint32_t)BM};
+  cuuint32_t es[2] = {1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)ptr, dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// C = A.B^T (+bias) for K-major A [M][lda] and B [N][ldb] through the split;
+// false in *done leaves the product to the caller's other paths.
+int gemm_h3_try(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N, int64_t K,
+                int64_t lda, int64_t ldb, int64_t ldc, int beta, void *ws, size_t ws_bytes, int *status,
+                cudaStream_t st, bool *done) {
+  *done = false;
+  const int64_t K8 = round8(K);
+  const int nsm = device_sms();
+  int splits = h3_splits(M, N, K, nsm);
+  const size_t scratch = h3_scratch(M, N, K);
+  size_t need = scratch + (splits > 1 ? (size_t)splits * M * N * 4 : 0);
+  if (!ws || !aligned(ws, 256)) return HS_OK;
+  if (ws_bytes < need) {
+    splits = 1;
+    need = scratch;
+    if (ws_bytes < need) return HS_OK;
+  }
+  char *w = static_cast<char *>(ws);
+  unsigned *absmax = reinterpret_cast<unsigned *>(w);
+  __half *ah = reinterpret_cast<__half *>(w + 256);
+  __half *al = ah + M * K8;
+  __half *bh = reinterpret_cast<__half *>(w + 256 + round_up((size_t)2 * M * K8 * 2, 256));
+  __half *bl = bh + N * K8;
+  float *partial = splits > 1 ? reinterpret_cast<float *>(w + scratch) : nullptr;
+  CUtensorMap tah, tal, tbh, tbl, tc;
+  if (!make_map_f16(&tah, ah, M, K8) || !make_map_f16(&tal, al, M, K8) || !make_map_f16(&tbh, bh, N, K8) ||
+      !make_map_f16(&tbl, bl, N, K8))
+    return HS_OK;
+  float *cdst = splits > 1 ? partial : C;
+  if (!make_out_map(&tc, cdst, splits, M, N, splits > 1 ? N : ldc)) return HS_OK;
+  const int nkb = (int)((K8 + H3_BK - 1) / H3_BK);
+  const int kbps = (nkb + splits - 1) / splits;
+  splits = (nkb + kbps - 1) / kbps;
+  const dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), (unsigned)splits);
+  if (grid.y > 65535) return HS_OK;
+  if (cudaMemsetAsync(absmax, 0, 8, st) != cudaSuccess) return check_launch("h3 memset");
+  absmax_kernel<<<4 * nsm, 256, 0, st>>>(A, M, K, lda, absmax);
+  absmax_kernel<<<nsm, 256, 0, st>>>(B, N, K, ldb, absmax + 1);
+  if (int e = check_launch("absmax_kernel")) return e;
+  split_h2_kernel<<<4 * nsm, 256, 0, st>>>(A, M, K, lda, absmax, ah, al, K8);
+  split_h2_kernel<<<nsm, 256, 0, st>>>(B, N, K, ldb, absmax + 1, bh, bl, K8);
+  if (int e = check_launch("split_h2_kernel")) return e;
+  TcArgs args;
+  args.C = C;
+  args.bias = bias;
+  args.partial = partial;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.ldc = ldc;
+  args.beta = beta;
+  args.kb_per_split = kbps;
+  args.nkb = nkb;
+  args.status = status;
+  static std::atomic<unsigned long long> attr_set{0};
+  if (int e = allow_dynamic_smem((const void *)gemm_h3_kernel, H3_SMEM_BYTES, &attr_set)) return e;
+  gemm_h3_kernel<<<grid, H3_THREADS, H3_SMEM_BYTES, st>>>(tah, tal, tbh, tbl, tc, args, absmax);
+  if (int e = check_launch("gemm_h3_kernel")) return e;
+  if (splits > 1) {
+    const int64_t n = M * N;
+    splitk_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(partial, C, bias, M, N, ldc, splits, beta);
+    if (int e = check_launch("splitk_reduce_kernel")) return e;
+  }
+  *done = true;
+  return HS_OK;
+}
+
 }  // namespace
 
 size_t gemm_tc_workspace(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K,
@@ -840,12 +1157,15 @@ size_t gemm_tc_workspace(const float *A, const float *B, float *C, int64_t M, in
   return pl.ok ? pl.ws : 0;
 }
 
-// Upper bound of the split-K scratch of one M x N x K product on any device
-// with up to 256 SMs (the split count only grows with the SM count).
-size_t gemm_tc_workspace_bound(int64_t M, int64_t N, int64_t K) {
+// Upper bound of the scratch of one M x N x K product on any device with up
+// to 256 SMs (the split count only grows with the SM count): split-K
+// partials, and for products with both operands K-major the fp16 split.
+size_t gemm_tc_workspace_bound(int64_t M, int64_t N, int64_t K, bool kmajor_both) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const int splits = split_count(M, N, (int)((K + BK - 1) / BK), 256);
-  return splits > 1 ? (size_t)splits * M * N * 4 : 0;
+  const size_t partial = splits > 1 ? (size_t)splits * M * N * 4 : 0;
+  if (!kmajor_both) return partial;
+  return std::max(partial, h3_scratch(M, N, K) + h3_partial_bound(M, N, K));
 }
 
 int gemm_tc_try(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
@@ -855,6 +1175,10 @@ int gemm_tc_try(const float *A, const float *B, float *C, const float *bias, int
   *done = false;
   TcPlan pl = plan_tc(A, B, C, M, N, K, lda, ldb, ldc, a_kc, b_kc);
   if (!pl.ok) return HS_OK;
+  if (a_kc && b_kc && h3_enabled()) {
+    if (int e = gemm_h3_try(A, B, C, bias, M, N, K, lda, ldb, ldc, beta, ws, ws_bytes, status, st, done)) return e;
+    if (*done) return HS_OK;
+  }
   if (pl.splits > 1 && (!ws || ws_bytes < pl.ws || !aligned(ws, 16))) {
     // not enough scratch for split-K: run unsplit (fewer CTAs, still exact)
     pl.splits = 1;
