@@ -86,9 +86,9 @@ HS_API int hs_selftest_activations(float *max_rel_err, int n, float lim, hs_stre
  *   weight gradients    dgates_flat.t() @ h / x    _torch.py:157-158, _triton.py:451-452
  *   bias gradient       dgates_flat.sum(dim=0)     _torch.py:159, _triton.py:453
  * ---------------------------------------------------------------------- */
-/* Scratch (bytes) any of the three products below may use for a split-K
- * reduction on these extents; pass at least this much, or NULL/0 (then the
- * product runs unsplit, slower on small outputs, same result). */
+/* Scratch (bytes) any of the products below may use on these extents (split-K
+ * partials, fp16 operand splits); pass at least this much, or NULL/0 (then
+ * the products take slower paths with the same accuracy). */
 HS_API size_t hs_linear_workspace_bytes(int64_t M, int64_t N, int64_t K);
 /* y[M,N] = x[M,K] . w[N,K]^T (+ bias[N] if bias != NULL) */
 HS_API int hs_linear_forward(const float *x, const float *w, const float *bias, float *y,
@@ -102,6 +102,14 @@ HS_API int hs_linear_dgrad(const float *dy, const float *w, float *dx, int64_t M
 HS_API int hs_linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t N,
                            int64_t K, int beta, void *workspace, size_t workspace_bytes,
                            int *dev_status, hs_stream_t stream);
+/* Both gradient products of y = x.w^T + b in one call: dx[M,K] = dy . w
+ * (skipped if dx is NULL) and dw[N,K] = beta * dw + dy^T . x.  Replaces the
+ * pair of products of the reference's backward (_torch.py:157-162,
+ * _triton.py:451-456); with enough workspace dy, x and w are converted once
+ * and shared by both products. */
+HS_API int hs_linear_backward(const float *dy, const float *x, const float *w, float *dx, float *dw,
+                              int64_t M, int64_t N, int64_t K, int beta, void *workspace,
+                              size_t workspace_bytes, int *dev_status, hs_stream_t stream);
 /* db[N] = beta * db + sum_m dy[m, N]   (beta is 0 or 1) */
 HS_API int hs_colsum(const float *dy, float *db, int64_t M, int64_t N, int beta,
               hs_stream_t stream);

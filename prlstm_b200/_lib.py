@@ -42,6 +42,7 @@ SIGNATURES = {
     "hs_linear_forward": (_i32, [_c_p] * 4 + [_i64] * 3 + [_c_p, _sz, _c_p, _c_p]),
     "hs_linear_dgrad": (_i32, [_c_p] * 3 + [_i64] * 3 + [_c_p, _sz, _c_p, _c_p]),
     "hs_linear_wgrad": (_i32, [_c_p] * 3 + [_i64] * 3 + [_i32, _c_p, _sz, _c_p, _c_p]),
+    "hs_linear_backward": (_i32, [_c_p] * 5 + [_i64] * 3 + [_i32, _c_p, _sz, _c_p, _c_p]),
     "hs_colsum": (_i32, [_c_p, _c_p, _i64, _i64, _i32, _c_p]),
     "hs_scan_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "hs_parallel_workspace_bytes": (_sz, [_i64] * 4),

@@ -35,6 +35,16 @@ int gemm_tc_try(const float *A, const float *B, float *C, const float *bias, int
                 int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kc, bool b_kc, int beta,
                 void *ws, size_t ws_bytes, int *status, cudaStream_t st, bool *done);
 size_t gemm_tc_workspace_bound(int64_t M, int64_t N, int64_t K, bool kmajor_both);
+bool gemm_h3_enabled();
+bool gemm_tc_size_ok(int64_t M, int64_t N, int64_t K);
+size_t gemm_h3_partial_bound(int64_t M, int64_t N, int64_t K);
+size_t h3_split_bytes(int64_t rows, int64_t cols);
+int h3_split(const float *x, int64_t rows, int64_t cols, int64_t ld, unsigned *absmax, void *dst,
+             cudaStream_t st);
+int gemm_h3_presplit(const void *a_split, const unsigned *a_absmax, bool a_mn, const void *b_split,
+                     const unsigned *b_absmax, bool b_mn, float *C, const float *bias, int64_t M, int64_t N,
+                     int64_t K, int64_t ldc, int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st,
+                     bool *done);
 size_t scan_workspace(int64_t T, int64_t B, int64_t H);
 int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st);
 int scan_forward(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
@@ -58,9 +68,17 @@ static int gemm(const float *A, const float *B, float *C, const float *bias, int
 }
 
 // Scratch any of the three linear-layer products of these extents may use.
+// Backward of one linear layer through the fp16 split: absmax words, then the
+// splits of dy [M][N], x [M][K] and w [N][K], then split-K partials.
+static size_t h3_bwd_scratch(int64_t M, int64_t N, int64_t K) {
+  return 256 + h3_split_bytes(M, N) + h3_split_bytes(M, K) + h3_split_bytes(N, K);
+}
+
 size_t linear_ws_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
   return std::max({gemm_tc_workspace_bound(M, N, K, true), gemm_tc_workspace_bound(M, K, N, false),
-                   gemm_tc_workspace_bound(N, K, M, false)});
+                   gemm_tc_workspace_bound(N, K, M, false),
+                   h3_bwd_scratch(M, N, K) + std::max(gemm_h3_partial_bound(M, K, N), gemm_h3_partial_bound(N, K, M))});
 }
 
 static int check_gemm(const void *a, const void *b, const void *c, int64_t M, int64_t N, int64_t K) {
@@ -88,6 +106,43 @@ int linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t 
   return gemm(dy, x, dw, nullptr, N, K, M, N, K, K, false, false, beta, ws, ws_bytes, status, st);
 }
 
+// Both gradient products of y = x.w^T + b: dx[M,K] = dy.w (dx may be null)
+// and dw[N,K] = beta*dw + dy^T.x.  Through the fp16 split, dy, x and w are
+// each split once and shared by the two products (dy K-major for dx,
+// M/N-major for dw); otherwise the two products run separately.
+int linear_backward(const float *dy, const float *x, const float *w, float *dx, float *dw, int64_t M, int64_t N,
+                    int64_t K, int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st) {
+  if (int e = check_gemm(dy, x, dw, N, K, M)) return e;
+  bool ddx = dx == nullptr, ddw = false;
+  const size_t sc = h3_bwd_scratch(M, N, K);
+  if (gemm_h3_enabled() && status && gemm_tc_size_ok(M, N, K) && ws && aligned(ws, 256) && ws_bytes >= sc &&
+      aligned(dw, 16) && K % 4 == 0 && (!dx || aligned(dx, 16))) {
+    char *w8 = static_cast<char *>(ws);
+    unsigned *am = reinterpret_cast<unsigned *>(w8);
+    char *dys = w8 + 256;
+    char *xs = dys + h3_split_bytes(M, N);
+    char *wsp = xs + h3_split_bytes(M, K);
+    char *tail = wsp + h3_split_bytes(N, K);
+    const size_t tb = ws_bytes - sc;
+    if (int e = h3_split(dy, M, N, N, am, dys, st)) return e;
+    if (dx) {
+      if (int e = h3_split(w, N, K, K, am + 2, wsp, st)) return e;
+      if (int e = gemm_h3_presplit(dys, am, false, wsp, am + 2, true, dx, nullptr, M, K, N, K, 0, tail, tb, status,
+                                   st, &ddx))
+        return e;
+    }
+    if (int e = h3_split(x, M, K, K, am + 1, xs, st)) return e;
+    if (int e = gemm_h3_presplit(dys, am, true, xs, am + 1, true, dw, nullptr, N, K, M, K, beta, tail, tb, status,
+                                 st, &ddw))
+      return e;
+  }
+  if (!ddx)
+    if (int e = linear_dgrad(dy, w, dx, M, N, K, ws, ws_bytes, status, st)) return e;
+  if (!ddw)
+    if (int e = linear_wgrad(dy, x, dw, M, N, K, beta, ws, ws_bytes, status, st)) return e;
+  return HS_OK;
+}
+
 size_t parallel_ws_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
   return std::max(scan_workspace(T, B, H), linear_ws_bytes(T * B, 4 * H, D));
 }
@@ -110,9 +165,7 @@ int parallel_backward(const float *x, const float *w_ih, float *z, const float *
   if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return fail(HS_ERR_INVALID_ARG, "T, B, D, H must be positive");
   if (!x || !w_ih || !z || !dw_ih || !db_ih) return fail(HS_ERR_INVALID_ARG, "parallel_backward: null x/w_ih/z/dw_ih/db_ih");
   if (int e = scan_backward(z, c, c0, dout, dh_n, dc_n, z, dc0, db_ih, T, B, H, eps, ws, ws_bytes, status, st)) return e;
-  if (dx)
-    if (int e = linear_dgrad(z, w_ih, dx, T * B, 4 * H, D, ws, ws_bytes, status, st)) return e;
-  return linear_wgrad(z, x, dw_ih, T * B, 4 * H, D, 0, ws, ws_bytes, status, st);
+  return linear_backward(z, x, w_ih, dx, dw_ih, T * B, 4 * H, D, 0, ws, ws_bytes, status, st);
 }
 
 namespace {
@@ -211,6 +264,13 @@ int hs_linear_dgrad(const float *dy, const float *w, float *dx, int64_t M, int64
   return hs::linear_dgrad(dy, w, dx, M, N, K, workspace, workspace_bytes, dev_status,
                           (cudaStream_t)stream);
 }
+int hs_linear_backward(const float *dy, const float *x, const float *w, float *dx, float *dw, int64_t M,
+                       int64_t N, int64_t K, int beta, void *workspace, size_t workspace_bytes, int *dev_status,
+                       hs_stream_t stream) {
+  return hs::linear_backward(dy, x, w, dx, dw, M, N, K, beta, workspace, workspace_bytes, dev_status,
+                             (cudaStream_t)stream);
+}
+
 int hs_linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t N, int64_t K,
                     int beta, void *workspace, size_t workspace_bytes, int *dev_status,
                     hs_stream_t stream) {

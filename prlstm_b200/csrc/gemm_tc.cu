@@ -767,15 +767,24 @@ constexpr int H3_BK = 64;                        // fp16 k per block: one 128-by
 constexpr int H3_TILE = 128 * H3_BK * 2;         // 16 KB per operand part
 constexpr int H3_STAGE = 4 * H3_TILE;            // Ah, Al, Bh, Bl
 constexpr int H3_STAGES = 3;
-constexpr int H3_PROMOTE = 4;
+#ifndef HS_H3_PROMOTE
+#define HS_H3_PROMOTE 4
+#endif
+constexpr int H3_PROMOTE = HS_H3_PROMOTE;         // k-blocks per accumulator group
 constexpr int H3_THREADS = 192;                  // producer, MMA, 4 fold/epilogue warps
 constexpr int H3_SMEM_BYTES = H3_STAGES * H3_STAGE + 1024 + 256;
 static_assert(H3_SMEM_BYTES <= 232448, "shared memory per block");
 
+// An operand part in shared memory is 16 KB either way: K-major, 128 rows of
+// 64 k (one 128-byte swizzled row each); MN-major, two 8 KB blocks of 64 M/N
+// elements x 64 k rows (canonical SW128 MN-major layout: 8-row atoms 1 KB
+// apart, blocks 8 KB apart).
+template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(H3_THREADS, 1)
 gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
-               const __grid_constant__ CUtensorMap tmC, TcArgs p, const unsigned *absmax) {
+               const __grid_constant__ CUtensorMap tmC, TcArgs p, const unsigned *absmax_a,
+               const unsigned *absmax_b) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + H3_STAGES * H3_STAGE);
@@ -827,10 +836,26 @@ gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__
         unsigned char *st = smem + s * H3_STAGE;
         mbar_expect_tx(&full[s], H3_STAGE);
         const int k0 = (kb0 + i) * H3_BK;
-        tma_2d(st, &tmAh, &full[s], k0, (int)m0);
-        tma_2d(st + H3_TILE, &tmAl, &full[s], k0, (int)m0);
-        tma_2d(st + 2 * H3_TILE, &tmBh, &full[s], k0, (int)n0);
-        tma_2d(st + 3 * H3_TILE, &tmBl, &full[s], k0, (int)n0);
+        if (A_MN) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            tma_2d(st + j * 8192, &tmAh, &full[s], (int)m0 + 64 * j, k0);
+            tma_2d(st + H3_TILE + j * 8192, &tmAl, &full[s], (int)m0 + 64 * j, k0);
+          }
+        } else {
+          tma_2d(st, &tmAh, &full[s], k0, (int)m0);
+          tma_2d(st + H3_TILE, &tmAl, &full[s], k0, (int)m0);
+        }
+        if (B_MN) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            tma_2d(st + 2 * H3_TILE + j * 8192, &tmBh, &full[s], (int)n0 + 64 * j, k0);
+            tma_2d(st + 3 * H3_TILE + j * 8192, &tmBl, &full[s], (int)n0 + 64 * j, k0);
+          }
+        } else {
+          tma_2d(st + 2 * H3_TILE, &tmBh, &full[s], k0, (int)n0);
+          tma_2d(st + 3 * H3_TILE, &tmBl, &full[s], k0, (int)n0);
+        }
       }
       for (int i = std::max(0, issued - H3_STAGES); i < issued; ++i) {
         if (ld_status(p.status)) mbar_drain(&full[i % H3_STAGES], (i / H3_STAGES) & 1);
@@ -839,7 +864,7 @@ gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__
     }
   } else if (!skip && warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(BM, BN);
+      constexpr uint32_t idesc = idesc_f16(BM, BN) | ((A_MN ? 1u : 0u) << 15) | ((B_MN ? 1u : 0u) << 16);
       for (int i = 0; i < nk; ++i) {
         const int s = i % H3_STAGES;
         const uint32_t ph = (i / H3_STAGES) & 1;
@@ -854,10 +879,12 @@ gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__
         const uint32_t t_corr = t_main + BN;
 #pragma unroll
         for (int kk = 0; kk < H3_BK / 16; ++kk) {
-          // 16 fp16 = 32 bytes of each 128-byte K-major row per k-step
-          const uint32_t o = kk * 32;
-          const uint64_t dAh = sdesc(ah + o, 16, 1024, 2), dAl = sdesc(al + o, 16, 1024, 2);
-          const uint64_t dBh = sdesc(bh + o, 16, 1024, 2), dBl = sdesc(bl + o, 16, 1024, 2);
+          // K-major: 16 fp16 = 32 bytes into each 128-byte row; MN-major: the
+          // next 16 k rows (2 KB), LBO = 8 KB between 64-element blocks.
+          const uint32_t oa = A_MN ? kk * 2048 : kk * 32, ob = B_MN ? kk * 2048 : kk * 32;
+          const uint32_t la = A_MN ? 8192 : 16, lb = B_MN ? 8192 : 16;
+          const uint64_t dAh = sdesc(ah + oa, la, 1024, 2), dAl = sdesc(al + oa, la, 1024, 2);
+          const uint64_t dBh = sdesc(bh + ob, lb, 1024, 2), dBl = sdesc(bl + ob, lb, 1024, 2);
           const uint32_t acc = (gstart && kk == 0) ? 0u : 1u;
           mma_f16(t_main, dAh, dBh, idesc, acc);
           mma_f16(t_corr, dAh, dBl, idesc, acc);
@@ -892,7 +919,7 @@ gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__
       if (lane == 0) mbar_arrive(&pempty[b]);
     }
     if (ok) {
-      const float inv = 1.0f / (pow2_scale(absmax[0]) * pow2_scale(absmax[1]));  // exact: a power of two
+      const float inv = 1.0f / (pow2_scale(*absmax_a) * pow2_scale(*absmax_b));  // exact: a power of two
 #pragma unroll
       for (int j = 0; j < BN; ++j) tot[j] *= inv;
       store_tile(tot, smem, &tmC, p, q, lane, t, m0, n0);
@@ -1067,63 +1094,78 @@ int h3_splits(int64_t M, int64_t N, int64_t K, int nsm) {
   return split_count(M, N, (int)((round8(K) + H3_BK - 1) / H3_BK), nsm);
 }
 size_t h3_partial_bound(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
   const int sp = h3_splits(M, N, K, 256);
   return sp > 1 ? (size_t)sp * M * N * 4 : 0;
 }
-bool make_map_f16(CUtensorMap *tm, const __half *ptr, int64_t R, int64_t K8) {
+// Map of a split operand stored [rows][ld] fp16.  K-major use (rows = M or
+// N, columns = K): box {64 k, 128 rows}.  MN-major use (rows = K, columns =
+// M or N): box {64 columns, 64 k rows}.
+bool make_map_f16(CUtensorMap *tm, const __half *ptr, int64_t rows, int64_t ld, bool mn) {
   auto enc = encode_fn();
   if (!enc) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)K8, (cuuint64_t)R};
-  cuuint64_t strides[1] = {(cuuint64_t)K8 * 2};
-  cuuint32_t box[2] = {H3_BK, (cuuint32_t)BM};
+  cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {H3_BK, mn ? 64u : (cuuint32_t)BM};
   cuuint32_t es[2] = {1, 1};
   return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)ptr, dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// C = A.B^T (+bias) for K-major A [M][lda] and B [N][ldb] through the split;
-// false in *done leaves the product to the caller's other paths.
-int gemm_h3_try(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N, int64_t K,
-                int64_t lda, int64_t ldb, int64_t ldc, int beta, void *ws, size_t ws_bytes, int *status,
-                cudaStream_t st, bool *done) {
-  *done = false;
-  const int64_t K8 = round8(K);
+}  // namespace
+
+size_t h3_split_bytes(int64_t rows, int64_t cols) { return round_up((size_t)4 * rows * round8(cols), 256); }
+
+// hi/lo fp16 [rows][round8(cols)] of a float32 [rows][ld] matrix, scaled by
+// the power of two its absmax selects; *absmax (in device memory) is written.
+int h3_split(const float *x, int64_t rows, int64_t cols, int64_t ld, unsigned *absmax, void *dst,
+             cudaStream_t st) {
   const int nsm = device_sms();
-  int splits = h3_splits(M, N, K, nsm);
-  const size_t scratch = h3_scratch(M, N, K);
-  size_t need = scratch + (splits > 1 ? (size_t)splits * M * N * 4 : 0);
-  if (!ws || !aligned(ws, 256)) return HS_OK;
-  if (ws_bytes < need) {
-    splits = 1;
-    need = scratch;
-    if (ws_bytes < need) return HS_OK;
-  }
-  char *w = static_cast<char *>(ws);
-  unsigned *absmax = reinterpret_cast<unsigned *>(w);
-  __half *ah = reinterpret_cast<__half *>(w + 256);
-  __half *al = ah + M * K8;
-  __half *bh = reinterpret_cast<__half *>(w + 256 + round_up((size_t)2 * M * K8 * 2, 256));
-  __half *bl = bh + N * K8;
-  float *partial = splits > 1 ? reinterpret_cast<float *>(w + scratch) : nullptr;
+  const int64_t ldo = round8(cols);
+  __half *hi = static_cast<__half *>(dst);
+  __half *lo = hi + rows * ldo;
+  if (cudaMemsetAsync(absmax, 0, 4, st) != cudaSuccess) return check_launch("h3 memset");
+  const int grid = (int)std::min<int64_t>(8 * nsm, (rows + 7) / 8);
+  absmax_kernel<<<grid, 256, 0, st>>>(x, rows, cols, ld, absmax);
+  if (int e = check_launch("absmax_kernel")) return e;
+  split_h2_kernel<<<grid, 256, 0, st>>>(x, rows, cols, ld, absmax, hi, lo, ldo);
+  return check_launch("split_h2_kernel");
+}
+
+// C[M,N] = A.B^T over K (+bias, beta) from split operands.  A is stored
+// [M][.] (a_mn false, K-major) or [K][.] (a_mn true); B likewise with N.
+// Scratch (split-K partials, if any) from ws; *done = false if the shape or
+// the scratch does not suit (the caller then takes another path).
+int gemm_h3_presplit(const void *a_split, const unsigned *a_absmax, bool a_mn, const void *b_split,
+                     const unsigned *b_absmax, bool b_mn, float *C, const float *bias, int64_t M, int64_t N,
+                     int64_t K, int64_t ldc, int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st,
+                     bool *done) {
+  *done = false;
+  if (!status || M <= 0 || N <= 0 || K <= 0) return HS_OK;
+  if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) return HS_OK;
+  if (!aligned(C, 16) || ldc % 4 || N % 4) return HS_OK;
+  const int nsm = device_sms();
+  const int64_t K8 = round8(K), M8 = round8(M), N8 = round8(N);
+  int splits = split_count(M, N, (int)((K8 + H3_BK - 1) / H3_BK), nsm);
+  if (splits > 1 && (!ws || !aligned(ws, 256) || ws_bytes < (size_t)splits * M * N * 4)) splits = 1;
+  const __half *ah = static_cast<const __half *>(a_split);
+  const __half *bh = static_cast<const __half *>(b_split);
+  const int64_t a_rows = a_mn ? K : M, a_ld = a_mn ? M8 : K8;
+  const int64_t b_rows = b_mn ? K : N, b_ld = b_mn ? N8 : K8;
+  const __half *al = ah + a_rows * a_ld;
+  const __half *bl = bh + b_rows * b_ld;
+  float *partial = splits > 1 ? static_cast<float *>(ws) : nullptr;
   CUtensorMap tah, tal, tbh, tbl, tc;
-  if (!make_map_f16(&tah, ah, M, K8) || !make_map_f16(&tal, al, M, K8) || !make_map_f16(&tbh, bh, N, K8) ||
-      !make_map_f16(&tbl, bl, N, K8))
+  if (!make_map_f16(&tah, ah, a_rows, a_ld, a_mn) || !make_map_f16(&tal, al, a_rows, a_ld, a_mn) ||
+      !make_map_f16(&tbh, bh, b_rows, b_ld, b_mn) || !make_map_f16(&tbl, bl, b_rows, b_ld, b_mn))
     return HS_OK;
-  float *cdst = splits > 1 ? partial : C;
-  if (!make_out_map(&tc, cdst, splits, M, N, splits > 1 ? N : ldc)) return HS_OK;
+  if (!make_out_map(&tc, splits > 1 ? partial : C, splits, M, N, splits > 1 ? N : ldc)) return HS_OK;
   const int nkb = (int)((K8 + H3_BK - 1) / H3_BK);
   const int kbps = (nkb + splits - 1) / splits;
   splits = (nkb + kbps - 1) / kbps;
   const dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), (unsigned)splits);
   if (grid.y > 65535) return HS_OK;
-  if (cudaMemsetAsync(absmax, 0, 8, st) != cudaSuccess) return check_launch("h3 memset");
-  absmax_kernel<<<4 * nsm, 256, 0, st>>>(A, M, K, lda, absmax);
-  absmax_kernel<<<nsm, 256, 0, st>>>(B, N, K, ldb, absmax + 1);
-  if (int e = check_launch("absmax_kernel")) return e;
-  split_h2_kernel<<<4 * nsm, 256, 0, st>>>(A, M, K, lda, absmax, ah, al, K8);
-  split_h2_kernel<<<nsm, 256, 0, st>>>(B, N, K, ldb, absmax + 1, bh, bl, K8);
-  if (int e = check_launch("split_h2_kernel")) return e;
   TcArgs args;
   args.C = C;
   args.bias = bias;
@@ -1136,9 +1178,13 @@ int gemm_h3_try(const float *A, const float *B, float *C, const float *bias, int
   args.kb_per_split = kbps;
   args.nkb = nkb;
   args.status = status;
-  static std::atomic<unsigned long long> attr_set{0};
-  if (int e = allow_dynamic_smem((const void *)gemm_h3_kernel, H3_SMEM_BYTES, &attr_set)) return e;
-  gemm_h3_kernel<<<grid, H3_THREADS, H3_SMEM_BYTES, st>>>(tah, tal, tbh, tbl, tc, args, absmax);
+  void (*fn)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs,
+             const unsigned *, const unsigned *);
+  if (a_mn) fn = b_mn ? gemm_h3_kernel<true, true> : gemm_h3_kernel<true, false>;
+  else fn = b_mn ? gemm_h3_kernel<false, true> : gemm_h3_kernel<false, false>;
+  static std::atomic<unsigned long long> attr_set[4];
+  if (int e = allow_dynamic_smem((const void *)fn, H3_SMEM_BYTES, &attr_set[(a_mn ? 2 : 0) + (b_mn ? 1 : 0)])) return e;
+  fn<<<grid, H3_THREADS, H3_SMEM_BYTES, st>>>(tah, tal, tbh, tbl, tc, args, a_absmax, b_absmax);
   if (int e = check_launch("gemm_h3_kernel")) return e;
   if (splits > 1) {
     const int64_t n = M * N;
@@ -1149,7 +1195,30 @@ int gemm_h3_try(const float *A, const float *B, float *C, const float *bias, int
   return HS_OK;
 }
 
+namespace {
+
+// K-major product from float32 operands: split both into ws, then multiply.
+int gemm_h3_try(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N, int64_t K,
+                int64_t lda, int64_t ldb, int64_t ldc, int beta, void *ws, size_t ws_bytes, int *status,
+                cudaStream_t st, bool *done) {
+  *done = false;
+  const size_t scratch = h3_scratch(M, N, K);
+  if (!ws || !aligned(ws, 256) || ws_bytes < scratch) return HS_OK;
+  char *w = static_cast<char *>(ws);
+  unsigned *absmax = reinterpret_cast<unsigned *>(w);
+  void *as = w + 256;
+  void *bs = w + 256 + h3_split_bytes(M, K);
+  if (int e = h3_split(A, M, K, lda, absmax, as, st)) return e;
+  if (int e = h3_split(B, N, K, ldb, absmax + 1, bs, st)) return e;
+  return gemm_h3_presplit(as, absmax, false, bs, absmax + 1, false, C, bias, M, N, K, ldc, beta, w + scratch,
+                          ws_bytes - scratch, status, st, done);
+}
+
 }  // namespace
+
+bool gemm_h3_enabled() { return tc_enabled() && h3_enabled(); }
+bool gemm_tc_size_ok(int64_t M, int64_t N, int64_t K) { return (double)M * N * K >= tc_min_mnk(); }
+size_t gemm_h3_partial_bound(int64_t M, int64_t N, int64_t K) { return h3_partial_bound(M, N, K); }
 
 size_t gemm_tc_workspace(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K,
                          int64_t lda, int64_t ldb, int64_t ldc, bool a_kc, bool b_kc) {

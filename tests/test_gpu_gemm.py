@@ -150,3 +150,29 @@ print(f"{ey:.3e} {ex:.3e}")
         print(f"GEMMERR HS_TC_TMEM_A={v}: forward {errs[v][0]:.3e} dgrad {errs[v][1]:.3e}")
     for v, (ey, ex) in errs.items():
         assert ey < TOL and ex < TOL, (v, ey, ex)
+
+
+@pytest.mark.parametrize("M,N,K,beta,with_dx", [(8192, 1024, 256, 0, True), (4096, 2048, 512, 1, True),
+                                               (3000, 520, 132, 0, False), (5000, 520, 40, 1, True)])
+def test_linear_backward(M, N, K, beta, with_dx):
+    """dx = dy.w and dw = beta*dw + dy^T.x in one call (the fp16-split path
+    shares one conversion of dy between the two products)."""
+    L = _lib()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(M + N + K + beta)
+    dy = torch.randn(M, N, device=dev, generator=g)
+    x = torch.randn(M, K, device=dev, generator=g)
+    w = torch.randn(N, K, device=dev, generator=g) / K ** 0.5
+    dx = torch.empty(M, K, device=dev) if with_dx else None
+    dw0 = torch.randn(N, K, device=dev, generator=g)
+    dw = dw0.clone()
+    ws, n = _ws(L, M, N, K, dev)
+    P = L.ptr
+    L.call("hs_linear_backward", P(dy), P(x), P(w), P(dx), P(dw), M, N, K, beta, P(ws), n,
+           P(L.status_word(dev)), L.stream_ptr(dev))
+    dy64, x64, w64 = dy.double().cpu(), x.double().cpu(), w.double().cpu()
+    ref_dw = dy64.t() @ x64 + (dw0.double().cpu() if beta else 0)
+    assert _rel(dw, ref_dw) < TOL
+    if with_dx:
+        assert _rel(dx, dy64 @ w64) < TOL
+    L.check_device_status(dev)
