@@ -68,17 +68,13 @@ static int gemm(const float *A, const float *B, float *C, const float *bias, int
 }
 
 // Scratch any of the three linear-layer products of these extents may use.
-// Backward of one linear layer through the fp16 split: absmax words, then the
-// splits of dy [M][N], x [M][K] and w [N][K], then split-K partials.
-static size_t h3_bwd_scratch(int64_t M, int64_t N, int64_t K) {
-  return 256 + h3_split_bytes(M, N) + h3_split_bytes(M, K) + h3_split_bytes(N, K);
-}
+size_t linear_backward_ws(int64_t M, int64_t N, int64_t K, int64_t K2);
 
 size_t linear_ws_bytes(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   return std::max({gemm_tc_workspace_bound(M, N, K, true), gemm_tc_workspace_bound(M, K, N, false),
                    gemm_tc_workspace_bound(N, K, M, false),
-                   h3_bwd_scratch(M, N, K) + std::max(gemm_h3_partial_bound(M, K, N), gemm_h3_partial_bound(N, K, M))});
+                   linear_backward_ws(M, N, K, 0)});
 }
 
 static int check_gemm(const void *a, const void *b, const void *c, int64_t M, int64_t N, int64_t K) {
@@ -106,23 +102,40 @@ int linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t 
   return gemm(dy, x, dw, nullptr, N, K, M, N, K, K, false, false, beta, ws, ws_bytes, status, st);
 }
 
-// Both gradient products of y = x.w^T + b: dx[M,K] = dy.w (dx may be null)
-// and dw[N,K] = beta*dw + dy^T.x.  Through the fp16 split, dy, x and w are
-// each split once and shared by the two products (dy K-major for dx,
-// M/N-major for dw); otherwise the two products run separately.
-int linear_backward(const float *dy, const float *x, const float *w, float *dx, float *dw, int64_t M, int64_t N,
-                    int64_t K, int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st) {
+// Gradient products of y = x.w^T (+ x2.w2^T): dx[M,K] = dy.w (dx may be
+// null), dw[N,K] = beta*dw + dy^T.x and, if x2 is given, dw2[N,K2] =
+// beta*dw2 + dy^T.x2.  Through the fp16 split, dy is split once and shared
+// by all products (K-major for dx, M/N-major for the weight gradients);
+// otherwise each product runs on its own.
+size_t linear_backward_ws(int64_t M, int64_t N, int64_t K, int64_t K2) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  size_t sc = 256 + h3_split_bytes(M, N) + h3_split_bytes(M, K) + h3_split_bytes(N, K);
+  size_t part = std::max(gemm_h3_partial_bound(M, K, N), gemm_h3_partial_bound(N, K, M));
+  if (K2 > 0) {
+    sc += h3_split_bytes(M, K2);
+    part = std::max(part, gemm_h3_partial_bound(N, K2, M));
+  }
+  return sc + part;
+}
+
+int linear_backward_ex(const float *dy, const float *w, float *dx, const float *x, float *dw, const float *x2,
+                       float *dw2, int64_t M, int64_t N, int64_t K, int64_t K2, int beta, void *ws, size_t ws_bytes,
+                       int *status, cudaStream_t st) {
   if (int e = check_gemm(dy, x, dw, N, K, M)) return e;
-  bool ddx = dx == nullptr, ddw = false;
-  const size_t sc = h3_bwd_scratch(M, N, K);
+  if (x2)
+    if (int e = check_gemm(dy, x2, dw2, N, K2, M)) return e;
+  bool ddx = dx == nullptr, ddw = false, ddw2 = x2 == nullptr;
+  size_t sc = 256 + h3_split_bytes(M, N) + h3_split_bytes(M, K) + h3_split_bytes(N, K);
+  if (x2) sc += h3_split_bytes(M, K2);
   if (gemm_h3_enabled() && status && gemm_tc_size_ok(M, N, K) && ws && aligned(ws, 256) && ws_bytes >= sc &&
-      aligned(dw, 16) && K % 4 == 0 && (!dx || aligned(dx, 16))) {
+      aligned(dw, 16) && K % 4 == 0 && (!dx || aligned(dx, 16)) && (!x2 || (aligned(dw2, 16) && K2 % 4 == 0))) {
     char *w8 = static_cast<char *>(ws);
     unsigned *am = reinterpret_cast<unsigned *>(w8);
     char *dys = w8 + 256;
     char *xs = dys + h3_split_bytes(M, N);
     char *wsp = xs + h3_split_bytes(M, K);
-    char *tail = wsp + h3_split_bytes(N, K);
+    char *x2s = wsp + h3_split_bytes(N, K);
+    char *tail = w8 + sc;
     const size_t tb = ws_bytes - sc;
     if (int e = h3_split(dy, M, N, N, am, dys, st)) return e;
     if (dx) {
@@ -135,12 +148,25 @@ int linear_backward(const float *dy, const float *x, const float *w, float *dx, 
     if (int e = gemm_h3_presplit(dys, am, true, xs, am + 1, true, dw, nullptr, N, K, M, K, beta, tail, tb, status,
                                  st, &ddw))
       return e;
+    if (x2) {
+      if (int e = h3_split(x2, M, K2, K2, am + 3, x2s, st)) return e;
+      if (int e = gemm_h3_presplit(dys, am, true, x2s, am + 3, true, dw2, nullptr, N, K2, M, K2, beta, tail, tb,
+                                   status, st, &ddw2))
+        return e;
+    }
   }
   if (!ddx)
     if (int e = linear_dgrad(dy, w, dx, M, N, K, ws, ws_bytes, status, st)) return e;
   if (!ddw)
     if (int e = linear_wgrad(dy, x, dw, M, N, K, beta, ws, ws_bytes, status, st)) return e;
+  if (!ddw2)
+    if (int e = linear_wgrad(dy, x2, dw2, M, N, K2, beta, ws, ws_bytes, status, st)) return e;
   return HS_OK;
+}
+
+int linear_backward(const float *dy, const float *x, const float *w, float *dx, float *dw, int64_t M, int64_t N,
+                    int64_t K, int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st) {
+  return linear_backward_ex(dy, w, dx, x, dw, nullptr, nullptr, M, N, K, 0, beta, ws, ws_bytes, status, st);
 }
 
 size_t parallel_ws_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {

@@ -25,6 +25,8 @@
 // HS_ERR_DEVICE_TIMEOUT in the caller's status word and leaves.
 #include <cooperative_groups.h>
 
+#include <algorithm>
+
 #include "hs_common.cuh"
 
 namespace hs {
@@ -39,6 +41,10 @@ int linear_dgrad(const float *dy, const float *w, float *dx, int64_t M, int64_t 
 int linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t N, int64_t K,
                  int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st);
 size_t linear_ws_bytes(int64_t M, int64_t N, int64_t K);
+size_t linear_backward_ws(int64_t M, int64_t N, int64_t K, int64_t K2);
+int linear_backward_ex(const float *dy, const float *w, float *dx, const float *x, float *dw, const float *x2,
+                       float *dw2, int64_t M, int64_t N, int64_t K, int64_t K2, int beta, void *ws, size_t ws_bytes,
+                       int *status, cudaStream_t st);
 int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st);
 
 namespace {
@@ -593,7 +599,8 @@ size_t rec_ws_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
   if (!make_plan(p, B, H, nsm > 0 ? nsm : 148)) return 0;
   // the GEMMs run before the persistent kernels (forward) or after them
   // (backward), so they reuse the same scratch
-  return std::max(p.total, std::max(linear_ws_bytes(T * B, 4 * H, D), linear_ws_bytes(T * B, 4 * H, H)));
+  return std::max<size_t>({p.total, linear_ws_bytes(T * B, 4 * H, D), linear_ws_bytes(T * B, 4 * H, H),
+                   linear_backward_ws(T * B, 4 * H, D, H)});
 }
 
 int rec_forward(const float *x, const float *h0, const float *c0, const float *w_ih,
@@ -695,12 +702,12 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
     if (int e = launch_persistent(fn, pl, pl.bwd, args, st)) return e;
   }
   // Batched parameter gradients (_torch.py:153-162); acts now holds dgates.
+  // dX = dG.W_ih, dW_ih = dG^T.x and dW_hh_s = dG^T.h_{t-1} share one
+  // conversion of dG (h_save rows 0..T-1 are the h_{t-1} of steps 0..T-1).
   const int64_t M = T * B, N = 4 * H;
-  if (int e = linear_wgrad(acts, h_save, dw_hh, M, N, H, 0, ws, ws_bytes, status, st)) return e;  // dW_hh_s
-  if (int e = linear_wgrad(acts, x, dw_ih, M, N, D, 0, ws, ws_bytes, status, st)) return e;
+  if (int e = linear_backward_ex(acts, w_ih, dx, x, dw_ih, h_save, dw_hh, M, N, D, H, 0, ws, ws_bytes, status, st))
+    return e;
   if (int e = colsum(acts, db_ih, M, N, 0, st)) return e;
-  if (dx)
-    if (int e = linear_dgrad(acts, w_ih, dx, M, N, D, ws, ws_bytes, status, st)) return e;
   // partial sums of da in the (now free) workspace
   float *part = reinterpret_cast<float *>(w);
   rec_unscale_kernel<<<dim3(kUnscaleParts, 4), 256, 0, st>>>(w_hh, b_hh, a, dw_hh, db_ih, db_hh, part, H);
