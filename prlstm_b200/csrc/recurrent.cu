@@ -57,7 +57,11 @@ constexpr int NW = 8;          // warps per CTA
 constexpr int NT = NW * 32;
 constexpr int kMaxPairs = 4;   // (unit, batch) pairs per thread in the epilogue
 constexpr int kMaxBatch = 32;  // batch rows per launch (larger B: several launches)
-constexpr size_t kSmemBudget = 200 * 1024;
+constexpr size_t kSmemBudget = 216 * 1024;
+// Chunk buffers of the step matvec: chunks c+1 .. c+kStages-1 are in flight
+// (cp.async) while chunk c is multiplied, hiding the L2 latency of the
+// streamed operands (exchange rows, and weights when not resident).
+constexpr int kStages = 4;
 
 // ------------------------------------------------------------------ plan
 struct Dir {
@@ -91,7 +95,7 @@ void size_dir(Dir &d, int BP) {
   for (int kc : {256, 128, 64, 32}) {
     d.KC = kc;
     d.K_pad = (d.K + kc - 1) / kc * kc;
-    const size_t xbuf = 2ull * kc * BP * 4;
+    const size_t xbuf = (size_t)kStages * kc * BP * 4;
     const size_t wres = (size_t)d.K_pad * d.rows_pad * 4;
     if (wres + xbuf + red <= kSmemBudget) { d.resident = true; d.smem = wres + xbuf + red; return; }
   }
@@ -99,7 +103,7 @@ void size_dir(Dir &d, int BP) {
   for (int kc : {128, 64, 32}) {
     d.KC = kc;
     d.K_pad = (d.K + kc - 1) / kc * kc;
-    d.smem = 2ull * kc * BP * 4 + 2ull * kc * d.rows_pad * 4 + red;
+    d.smem = (size_t)kStages * kc * (BP + d.rows_pad) * 4 + red;
     if (d.smem <= kSmemBudget) return;
   }
 }
@@ -177,14 +181,48 @@ __global__ void rec_prep_kernel(const float *__restrict__ w_hh, const float *__r
   }
 }
 
+// Forward slices as a tiled transpose: block (c, k-tile) reads the CTA's
+// weight rows {g*H + u} for 32 consecutive k (coalesced along k) into shared
+// memory and writes wf[c][k][ri] for those k (coalesced along ri).  Rows of
+// the slice beyond 4U, units beyond H and k beyond H are written as zero.
+__global__ void __launch_bounds__(256) rec_prep_fwd_kernel(const float *__restrict__ w_hh,
+                                                           const float *__restrict__ b_hh,
+                                                           const float *__restrict__ a, float *__restrict__ wf,
+                                                           float *__restrict__ bf, int64_t H, int U, int rpf,
+                                                           int64_t kpf) {
+  __shared__ float tile[256][33];  // [ri][k] (rpf <= 256)
+  const int c = blockIdx.y;
+  const int64_t k0 = (int64_t)blockIdx.x * 32;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int ri = w; ri < rpf; ri += 8) {
+    const int ul = ri / 4, g = ri % 4;
+    const int64_t u = (int64_t)c * U + ul, k = k0 + lane;
+    float v = 0.f;
+    if (ul < U && u < H && k < H) v = a[g] * w_hh[(g * H + u) * H + k];
+    tile[ri][lane] = v;
+  }
+  __syncthreads();
+  float *dst = wf + ((int64_t)c * kpf + k0) * rpf;
+  for (int i = threadIdx.x; i < 32 * rpf; i += 256) {
+    const int kk = i / rpf, ri = i - kk * rpf;
+    if (k0 + kk < kpf) dst[(int64_t)kk * rpf + ri] = tile[ri][kk];
+  }
+  if (blockIdx.x == 0) {
+    for (int ri = threadIdx.x; ri < rpf; ri += 256) {
+      const int ul = ri / 4, g = ri % 4;
+      const int64_t u = (int64_t)c * U + ul;
+      bf[(int64_t)c * rpf + ri] = (ul < U && u < H) ? a[g] * b_hh[g * H + u] : 0.f;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ device pieces
 HS_DEV void cp_async16(void *smem, const void *gmem) {
   const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
 }
 HS_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-HS_DEV void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-HS_DEV void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+template <int N> HS_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 HS_DEV void copy_chunk(float *dst, const float *src, int nfloat) {
   for (int i = threadIdx.x; i < nfloat / 4; i += NT) cp_async16(dst + 4 * i, src + 4 * i);
@@ -240,19 +278,27 @@ HS_DEV void step_matvec(const float *wres, const float *wsrc, const float *xsrc,
 
   const int nchunk = (int)(d.K_pad / d.KC);
   const int xfl = d.KC * BP, wfl = d.KC * rp;
-  copy_chunk(xbuf, xsrc, xfl);
-  if (!wres) copy_chunk(wbuf, wsrc, wfl);
-  cp_async_commit();
-  for (int c = 0; c < nchunk; ++c) {
-    const int cur = c & 1;
-    if (c + 1 < nchunk) {
-      copy_chunk(xbuf + (cur ^ 1) * xfl, xsrc + (int64_t)(c + 1) * xfl, xfl);
-      if (!wres) copy_chunk(wbuf + (cur ^ 1) * wfl, wsrc + (int64_t)(c + 1) * wfl, wfl);
-      cp_async_commit();
-      cp_async_wait_1();
-    } else {
-      cp_async_wait_0();
+  // prologue: chunks 0 .. kStages-2 (one commit group each, empty past the end)
+#pragma unroll
+  for (int c = 0; c < kStages - 1; ++c) {
+    if (c < nchunk) {
+      copy_chunk(xbuf + c * xfl, xsrc + (int64_t)c * xfl, xfl);
+      if (!wres) copy_chunk(wbuf + c * wfl, wsrc + (int64_t)c * wfl, wfl);
     }
+    cp_async_commit();
+  }
+  for (int c = 0; c < nchunk; ++c) {
+    const int cur = c % kStages;
+    // refill the buffer that chunk c-1 used (every thread left it at the
+    // barrier closing iteration c-1) with chunk c + kStages - 1
+    const int nxt = c + kStages - 1;
+    if (nxt < nchunk) {
+      const int b = nxt % kStages;
+      copy_chunk(xbuf + b * xfl, xsrc + (int64_t)nxt * xfl, xfl);
+      if (!wres) copy_chunk(wbuf + b * wfl, wsrc + (int64_t)nxt * wfl, wfl);
+    }
+    cp_async_commit();
+    cp_async_wait<kStages - 1>();  // chunk c has landed
     __syncthreads();
     const float *X = xbuf + cur * xfl;
     const float *W = wres ? wres + (int64_t)c * wfl : wbuf + cur * wfl;
@@ -329,8 +375,8 @@ __global__ void __launch_bounds__(NT, 1) rec_fwd_kernel(RecArgs p) {
   const int cta = blockIdx.x;
   float *wres = d.resident ? smem : nullptr;
   float *xbuf = smem + (d.resident ? d.K_pad * rp : 0);
-  float *wbuf = xbuf + 2 * d.KC * BP;
-  float *red = wbuf + (d.resident ? 0 : 2 * d.KC * rp);
+  float *wbuf = xbuf + kStages * d.KC * BP;
+  float *red = wbuf + (d.resident ? 0 : kStages * d.KC * rp);
   const float *wsrc = p.wf + (int64_t)cta * d.K_pad * rp;
   const int64_t H = p.H, Bt = p.Bt;
   const int u0 = cta * p.U;
@@ -417,8 +463,8 @@ __global__ void __launch_bounds__(NT, 1) rec_bwd_kernel(RecArgs p) {
   const int cta = blockIdx.x;
   float *wres = d.resident ? smem : nullptr;
   float *xbuf = smem + (d.resident ? d.K_pad * rp : 0);
-  float *wbuf = xbuf + 2 * d.KC * BP;
-  float *red = wbuf + (d.resident ? 0 : 2 * d.KC * rp);
+  float *wbuf = xbuf + kStages * d.KC * BP;
+  float *red = wbuf + (d.resident ? 0 : kStages * d.KC * rp);
   const float *wsrc = p.wb + (int64_t)cta * d.K_pad * rp;
   const int64_t H = p.H, Bt = p.Bt;
   const int u0 = cta * p.U;
@@ -619,10 +665,10 @@ int rec_forward(const float *x, const float *h0, const float *c0, const float *w
   char *w = static_cast<char *>(ws);
   // Z = x W_ih^T + b_ih, written into acts (_torch.py:96)
   if (int e = linear_forward(x, w_ih, b_ih, acts, T * B, 4 * H, D, ws, ws_bytes, status, st)) return e;
-  rec_prep_kernel<<<4 * nsm, 256, 0, st>>>(w_hh, b_hh, a, (float *)(w + pl.o_wf), (float *)(w + pl.o_bf),
-                                           nullptr, H, pl.U, pl.ncta, pl.fwd.rows_pad,
-                                           pl.fwd.K_pad, pl.bwd.rows_pad, pl.bwd.K_pad);
-  if (int e = check_launch("rec_prep_kernel")) return e;
+  if (pl.fwd.rows_pad > 256) return fail(HS_ERR_UNSUPPORTED, "recurrent: slice of %d rows", pl.fwd.rows_pad);
+  rec_prep_fwd_kernel<<<dim3((unsigned)((pl.fwd.K_pad + 31) / 32), (unsigned)pl.ncta), 256, 0, st>>>(
+      w_hh, b_hh, a, (float *)(w + pl.o_wf), (float *)(w + pl.o_bf), H, pl.U, pl.fwd.rows_pad, pl.fwd.K_pad);
+  if (int e = check_launch("rec_prep_fwd_kernel")) return e;
   KernelFn fn = pick_fwd(pl.BG, pl.fwd.RG);
   if (!fn) return fail(HS_ERR_UNSUPPORTED, "recurrent_forward: no kernel for BG=%d RG=%d", pl.BG, pl.fwd.RG);
   for (int64_t b0 = 0; b0 < B; b0 += kMaxBatch) {
