@@ -731,7 +731,9 @@ __global__ void absmax_kernel(const float *__restrict__ x, int64_t rows, int64_t
   if (lane == 0) atomicMax(out, __float_as_uint(m));
 }
 
-// hi/lo [rows][ldo] fp16, ldo = cols rounded up to 8 (zero padding).
+// hi/lo [rows][ldo] fp16, ldo = cols rounded up to 8 (zero padding).  Lanes
+// take 4 consecutive columns (one float4 load when the row allows it, one
+// 8-byte store per part).
 __global__ void split_h2_kernel(const float *__restrict__ x, int64_t rows, int64_t cols, int64_t ld,
                                 const unsigned *__restrict__ absmax, __half *__restrict__ hi,
                                 __half *__restrict__ lo, int64_t ldo) {
@@ -739,14 +741,28 @@ __global__ void split_h2_kernel(const float *__restrict__ x, int64_t rows, int64
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarp = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const bool vec = (cols % 4 == 0) && (ld % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
   for (int64_t r = warp; r < rows; r += nwarp) {
     const float *row = x + r * ld;
     __half *hr = hi + r * ldo, *lr = lo + r * ldo;
-    for (int64_t c = lane; c < ldo; c += 32) {
-      const float v = c < cols ? row[c] * s : 0.f;
-      const __half h = __float2half_rn(v);
-      hr[c] = h;
-      lr[c] = __float2half_rn((v - __half2float(h)) * 2048.0f);
+    for (int64_t c = 4 * lane; c < ldo; c += 128) {  // ldo is a multiple of 8, so c+3 < ldo
+      float v[4];
+      if (vec && c + 3 < cols) {
+        const float4 q = *reinterpret_cast<const float4 *>(row + c);
+        v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = c + j < cols ? row[c + j] : 0.f;
+      }
+      __half h[4], l[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float y = v[j] * s;
+        h[j] = __float2half_rn(y);
+        l[j] = __float2half_rn((y - __half2float(h[j])) * 2048.0f);
+      }
+      *reinterpret_cast<uint2 *>(hr + c) = *reinterpret_cast<const uint2 *>(h);
+      *reinterpret_cast<uint2 *>(lr + c) = *reinterpret_cast<const uint2 *>(l);
     }
   }
 }
@@ -779,15 +795,63 @@ static_assert(H3_SMEM_BYTES <= 232448, "shared memory per block");
 // 64 k (one 128-byte swizzled row each); MN-major, two 8 KB blocks of 64 M/N
 // elements x 64 k rows (canonical SW128 MN-major layout: 8-row atoms 1 KB
 // apart, blocks 8 KB apart).
+//
+// Persistent: one CTA per SM walks the output tiles (n fastest, then m,
+// then the split), the load ring and the accumulator groups continuing from
+// tile to tile, so the MMAs of the next tile run while the fold warps finish
+// the last groups and the epilogue of the previous one.  The epilogue stages
+// one 128 x 32 box at a time in its own 16 KB buffer (the operand stages
+// belong to the next tile's loads by then).
+constexpr int H3_EPI = BM * 32 * 4;              // 16 KB staging box
+constexpr int H3_SMEM_P = H3_STAGES * H3_STAGE + H3_EPI + 1024 + 256;
+static_assert(H3_SMEM_P <= 232448, "shared memory per block");
+
+HS_DEV void store_tile_boxes(const float (&tot)[BN], float *box, const CUtensorMap *tmC_, const TcArgs &p, int q,
+                             int lane, int t, int64_t m0, int64_t n0, int zc) {
+  const CUtensorMap &tmC = *tmC_;
+  const int r = q * 32 + lane;
+  const bool direct = p.partial == nullptr;
+#pragma unroll
+  for (int c = 0; c < BN / 32; ++c) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 o = make_float4(tot[c * 32 + 4 * j], tot[c * 32 + 4 * j + 1], tot[c * 32 + 4 * j + 2],
+                             tot[c * 32 + 4 * j + 3]);
+      if (direct && p.bias) {
+        const int64_t n = n0 + c * 32 + 4 * j;
+        if (n + 3 < p.N) {
+          const float4 bb = *reinterpret_cast<const float4 *>(p.bias + n);
+          o.x += bb.x; o.y += bb.y; o.z += bb.z; o.w += bb.w;
+        } else {
+          if (n < p.N) o.x += p.bias[n];
+          if (n + 1 < p.N) o.y += p.bias[n + 1];
+          if (n + 2 < p.N) o.z += p.bias[n + 2];
+        }
+      }
+      *reinterpret_cast<float4 *>(box + r * 32 + ((j ^ (r & 7)) * 4)) = o;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (t == 0) {
+      if (direct && p.beta) tma_reduce_add_3d(&tmC, box, (int)n0 + 32 * c, (int)m0, zc);
+      else tma_store_3d(&tmC, box, (int)n0 + 32 * c, (int)m0, zc);
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // box free again
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+  }
+}
+
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(H3_THREADS, 1)
 gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
                const __grid_constant__ CUtensorMap tmC, TcArgs p, const unsigned *absmax_a,
-               const unsigned *absmax_b) {
+               const unsigned *absmax_b, int mtiles, int ntiles, int ntiles_total) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + H3_STAGES * H3_STAGE);
+  float *epi = reinterpret_cast<float *>(smem + H3_STAGES * H3_STAGE);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + H3_STAGES * H3_STAGE + H3_EPI);
   uint64_t *empty = full + H3_STAGES;
   uint64_t *pfull = empty + H3_STAGES;
   uint64_t *pempty = pfull + 2;
@@ -795,11 +859,15 @@ gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__
   int *abort_flag = reinterpret_cast<int *>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
-  const int kb0 = blockIdx.z * p.kb_per_split;
-  const int kb1 = min(p.nkb, kb0 + p.kb_per_split);
-  const int nk = kb1 - kb0;
-  const int ngroups = (nk + H3_PROMOTE - 1) / H3_PROMOTE;
+  auto tile_of = [&](int tl, int64_t &m0, int64_t &n0, int &z, int &nk) {
+    const int per = mtiles * ntiles;
+    z = tl / per;
+    const int rem = tl - z * per;
+    m0 = (int64_t)(rem / ntiles) * BM;
+    n0 = (int64_t)(rem % ntiles) * BN;
+    const int kb0 = z * p.kb_per_split;
+    nk = min(p.nkb, kb0 + p.kb_per_split) - kb0;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < H3_STAGES; ++s) {
@@ -823,106 +891,132 @@ gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_holder;
-  const bool skip = *abort_flag != 0 || nk <= 0;
+  const bool skip = *abort_flag != 0;
 
   if (!skip && warp == 0) {
+    // ---------------- TMA producer: the k-blocks of every tile of this CTA
     if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % H3_STAGES;
-        const uint32_t ph = (i / H3_STAGES) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, p.status)) break;
-        ++issued;
-        unsigned char *st = smem + s * H3_STAGE;
-        mbar_expect_tx(&full[s], H3_STAGE);
-        const int k0 = (kb0 + i) * H3_BK;
-        if (A_MN) {
+      int it = 0, issued = 0;
+      bool ok = true;
+      for (int tl = blockIdx.x; tl < ntiles_total && ok; tl += gridDim.x) {
+        int64_t m0, n0;
+        int z, nk;
+        tile_of(tl, m0, n0, z, nk);
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int s = it % H3_STAGES;
+          const uint32_t ph = (it / H3_STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.status)) { ok = false; break; }
+          ++issued;
+          unsigned char *st = smem + s * H3_STAGE;
+          mbar_expect_tx(&full[s], H3_STAGE);
+          const int k0 = (z * p.kb_per_split + i) * H3_BK;
+          if (A_MN) {
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            tma_2d(st + j * 8192, &tmAh, &full[s], (int)m0 + 64 * j, k0);
-            tma_2d(st + H3_TILE + j * 8192, &tmAl, &full[s], (int)m0 + 64 * j, k0);
+            for (int j = 0; j < 2; ++j) {
+              tma_2d(st + j * 8192, &tmAh, &full[s], (int)m0 + 64 * j, k0);
+              tma_2d(st + H3_TILE + j * 8192, &tmAl, &full[s], (int)m0 + 64 * j, k0);
+            }
+          } else {
+            tma_2d(st, &tmAh, &full[s], k0, (int)m0);
+            tma_2d(st + H3_TILE, &tmAl, &full[s], k0, (int)m0);
           }
-        } else {
-          tma_2d(st, &tmAh, &full[s], k0, (int)m0);
-          tma_2d(st + H3_TILE, &tmAl, &full[s], k0, (int)m0);
-        }
-        if (B_MN) {
+          if (B_MN) {
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            tma_2d(st + 2 * H3_TILE + j * 8192, &tmBh, &full[s], (int)n0 + 64 * j, k0);
-            tma_2d(st + 3 * H3_TILE + j * 8192, &tmBl, &full[s], (int)n0 + 64 * j, k0);
+            for (int j = 0; j < 2; ++j) {
+              tma_2d(st + 2 * H3_TILE + j * 8192, &tmBh, &full[s], (int)n0 + 64 * j, k0);
+              tma_2d(st + 3 * H3_TILE + j * 8192, &tmBl, &full[s], (int)n0 + 64 * j, k0);
+            }
+          } else {
+            tma_2d(st + 2 * H3_TILE, &tmBh, &full[s], k0, (int)n0);
+            tma_2d(st + 3 * H3_TILE, &tmBl, &full[s], k0, (int)n0);
           }
-        } else {
-          tma_2d(st + 2 * H3_TILE, &tmBh, &full[s], k0, (int)n0);
-          tma_2d(st + 3 * H3_TILE, &tmBl, &full[s], k0, (int)n0);
         }
       }
-      for (int i = std::max(0, issued - H3_STAGES); i < issued; ++i) {
-        if (ld_status(p.status)) mbar_drain(&full[i % H3_STAGES], (i / H3_STAGES) & 1);
-        else (void)mbar_wait(&full[i % H3_STAGES], (i / H3_STAGES) & 1, p.status);
+      // never leave while a copy into this CTA's shared memory is in flight
+      for (int j = std::max(0, issued - H3_STAGES); j < issued; ++j) {
+        if (ld_status(p.status)) mbar_drain(&full[j % H3_STAGES], (j / H3_STAGES) & 1);
+        else (void)mbar_wait(&full[j % H3_STAGES], (j / H3_STAGES) & 1, p.status);
       }
     }
   } else if (!skip && warp == 1) {
+    // ---------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16(BM, BN) | ((A_MN ? 1u : 0u) << 15) | ((B_MN ? 1u : 0u) << 16);
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % H3_STAGES;
-        const uint32_t ph = (i / H3_STAGES) & 1;
-        const int g = i / H3_PROMOTE, b = g & 1;
-        const bool gstart = (i % H3_PROMOTE) == 0;
-        if (gstart && !mbar_wait(&pempty[b], ((g >> 1) & 1) ^ 1, p.status)) break;
-        if (!mbar_wait(&full[s], ph, p.status)) break;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t ah = su32(smem + s * H3_STAGE);
-        const uint32_t al = ah + H3_TILE, bh = ah + 2 * H3_TILE, bl = ah + 3 * H3_TILE;
-        const uint32_t t_main = tmem + (uint32_t)(b * 2 * BN);
-        const uint32_t t_corr = t_main + BN;
+      int it = 0, gg = 0;
+      bool ok = true;
+      for (int tl = blockIdx.x; tl < ntiles_total && ok; tl += gridDim.x) {
+        int64_t m0, n0;
+        int z, nk;
+        tile_of(tl, m0, n0, z, nk);
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int s = it % H3_STAGES;
+          const uint32_t ph = (it / H3_STAGES) & 1;
+          const bool gstart = (i % H3_PROMOTE) == 0;
+          const int b = gg & 1;
+          if (gstart && !mbar_wait(&pempty[b], ((gg >> 1) & 1) ^ 1, p.status)) { ok = false; break; }
+          if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t ah = su32(smem + s * H3_STAGE);
+          const uint32_t al = ah + H3_TILE, bh = ah + 2 * H3_TILE, bl = ah + 3 * H3_TILE;
+          const uint32_t t_main = tmem + (uint32_t)(b * 2 * BN);
+          const uint32_t t_corr = t_main + BN;
 #pragma unroll
-        for (int kk = 0; kk < H3_BK / 16; ++kk) {
-          // K-major: 16 fp16 = 32 bytes into each 128-byte row; MN-major: the
-          // next 16 k rows (2 KB), LBO = 8 KB between 64-element blocks.
-          const uint32_t oa = A_MN ? kk * 2048 : kk * 32, ob = B_MN ? kk * 2048 : kk * 32;
-          const uint32_t la = A_MN ? 8192 : 16, lb = B_MN ? 8192 : 16;
-          const uint64_t dAh = sdesc(ah + oa, la, 1024, 2), dAl = sdesc(al + oa, la, 1024, 2);
-          const uint64_t dBh = sdesc(bh + ob, lb, 1024, 2), dBl = sdesc(bl + ob, lb, 1024, 2);
-          const uint32_t acc = (gstart && kk == 0) ? 0u : 1u;
-          mma_f16(t_main, dAh, dBh, idesc, acc);
-          mma_f16(t_corr, dAh, dBl, idesc, acc);
-          mma_f16(t_corr, dAl, dBh, idesc, 1u);
+          for (int kk = 0; kk < H3_BK / 16; ++kk) {
+            // K-major: 16 fp16 = 32 bytes into each 128-byte row; MN-major: the
+            // next 16 k rows (2 KB), LBO = 8 KB between 64-element blocks.
+            const uint32_t oa = A_MN ? kk * 2048 : kk * 32, ob = B_MN ? kk * 2048 : kk * 32;
+            const uint32_t la = A_MN ? 8192 : 16, lb = B_MN ? 8192 : 16;
+            const uint64_t dAh = sdesc(ah + oa, la, 1024, 2), dAl = sdesc(al + oa, la, 1024, 2);
+            const uint64_t dBh = sdesc(bh + ob, lb, 1024, 2), dBl = sdesc(bl + ob, lb, 1024, 2);
+            const uint32_t acc = (gstart && kk == 0) ? 0u : 1u;
+            mma_f16(t_main, dAh, dBh, idesc, acc);
+            mma_f16(t_corr, dAh, dBl, idesc, acc);
+            mma_f16(t_corr, dAl, dBh, idesc, 1u);
+          }
+          mma_commit(&empty[s]);
+          if ((i % H3_PROMOTE) == H3_PROMOTE - 1 || i == nk - 1) {
+            mma_commit(&pfull[b]);
+            ++gg;
+          }
         }
-        mma_commit(&empty[s]);
-        if ((i % H3_PROMOTE) == H3_PROMOTE - 1 || i == nk - 1) mma_commit(&pfull[b]);
       }
     }
   } else if (!skip) {
+    // ---------------- fold finished groups, epilogue per tile
     const int t = threadIdx.x - 64;  // 0..127
     const int q = warp & 3;
-    float tot[BN];
-#pragma unroll
-    for (int j = 0; j < BN; ++j) tot[j] = 0.f;
+    const float inv = 1.0f / (pow2_scale(*absmax_a) * pow2_scale(*absmax_b));  // exact: a power of two
+    int gg = 0;
     bool ok = true;
-    for (int g = 0; g < ngroups; ++g) {
-      const int b = g & 1;
-      if (!mbar_wait(&pfull[b], (g >> 1) & 1, p.status)) { ok = false; break; }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 2 * BN);
+    for (int tl = blockIdx.x; tl < ntiles_total && ok; tl += gridDim.x) {
+      int64_t m0, n0;
+      int z, nk;
+      tile_of(tl, m0, n0, z, nk);
+      const int ngroups = (nk + H3_PROMOTE - 1) / H3_PROMOTE;
+      float tot[BN];
 #pragma unroll
-      for (int c = 0; c < BN; c += 32) {
-        float v[32], w[32];
-        tmem_ld32(base + BN + c, w);
-        tmem_ld32(base + c, v);
+      for (int j = 0; j < BN; ++j) tot[j] = 0.f;
+      for (int g = 0; g < ngroups; ++g, ++gg) {
+        const int b = gg & 1;
+        if (!mbar_wait(&pfull[b], (gg >> 1) & 1, p.status)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 2 * BN);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) tot[c + j] += fmaf(w[j], 1.0f / 2048.0f, v[j]);
+        for (int c = 0; c < BN; c += 32) {
+          float v[32], w[32];
+          tmem_ld32(base + BN + c, w);
+          tmem_ld32(base + c, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) tot[c + j] += fmaf(w[j], 1.0f / 2048.0f, v[j]);
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pempty[b]);
       }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&pempty[b]);
-    }
-    if (ok) {
-      const float inv = 1.0f / (pow2_scale(*absmax_a) * pow2_scale(*absmax_b));  // exact: a power of two
+      if (!ok) break;
 #pragma unroll
       for (int j = 0; j < BN; ++j) tot[j] *= inv;
-      store_tile(tot, smem, &tmC, p, q, lane, t, m0, n0);
+      store_tile_boxes(tot, epi, &tmC, p, q, lane, t, m0, n0, p.partial ? z : 0);
     }
   }
 
@@ -1164,8 +1258,10 @@ int gemm_h3_presplit(const void *a_split, const unsigned *a_absmax, bool a_mn, c
   const int nkb = (int)((K8 + H3_BK - 1) / H3_BK);
   const int kbps = (nkb + splits - 1) / splits;
   splits = (nkb + kbps - 1) / kbps;
-  const dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), (unsigned)splits);
-  if (grid.y > 65535) return HS_OK;
+  const int64_t mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
+  const int64_t ntot = mt * nt * splits;
+  if (ntot >= (1ll << 31)) return HS_OK;
+  const unsigned grid = (unsigned)std::min<int64_t>(ntot, nsm);
   TcArgs args;
   args.C = C;
   args.bias = bias;
@@ -1179,12 +1275,13 @@ int gemm_h3_presplit(const void *a_split, const unsigned *a_absmax, bool a_mn, c
   args.nkb = nkb;
   args.status = status;
   void (*fn)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs,
-             const unsigned *, const unsigned *);
+             const unsigned *, const unsigned *, int, int, int);
   if (a_mn) fn = b_mn ? gemm_h3_kernel<true, true> : gemm_h3_kernel<true, false>;
   else fn = b_mn ? gemm_h3_kernel<false, true> : gemm_h3_kernel<false, false>;
   static std::atomic<unsigned long long> attr_set[4];
-  if (int e = allow_dynamic_smem((const void *)fn, H3_SMEM_BYTES, &attr_set[(a_mn ? 2 : 0) + (b_mn ? 1 : 0)])) return e;
-  fn<<<grid, H3_THREADS, H3_SMEM_BYTES, st>>>(tah, tal, tbh, tbl, tc, args, a_absmax, b_absmax);
+  if (int e = allow_dynamic_smem((const void *)fn, H3_SMEM_P, &attr_set[(a_mn ? 2 : 0) + (b_mn ? 1 : 0)])) return e;
+  fn<<<grid, H3_THREADS, H3_SMEM_P, st>>>(tah, tal, tbh, tbl, tc, args, a_absmax, b_absmax, (int)mt, (int)nt,
+                                           (int)ntot);
   if (int e = check_launch("gemm_h3_kernel")) return e;
   if (splits > 1) {
     const int64_t n = M * N;
