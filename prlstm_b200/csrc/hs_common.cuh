@@ -74,6 +74,30 @@ HS_DEV float tanh_pos(float c) {
   return __fdividef(1.0f - e, 1.0f + e);
 }
 
+// sigma(x) * sigma(y) with one reciprocal: 1 / ((1 + e^-x)(1 + e^-y)).  An
+// infinite denominator gives 0, a NaN stays NaN.
+HS_DEV float sig2(float x, float y) { return rcp_nr((1.0f + __expf(-x)) * (1.0f + __expf(-y))); }
+
+// sigma(z) * tanh(c) for c >= 0 from eo = e^-z, with one reciprocal:
+// poly(c) / (1 + eo) below 0.25 (odd Taylor series of tanh, as tanh_pos) and
+// (1 - e^-2c) / ((1 + e^-2c)(1 + eo)) above.
+HS_DEV float sig_tanh_pos(float eo, float c) {
+  float num, den;
+  if (c < 0.25f) {
+    const float u = c * c;
+    float p = fmaf(u, 62.0f / 2835.0f, -17.0f / 315.0f);
+    p = fmaf(p, u, 2.0f / 15.0f);
+    p = fmaf(p, u, -1.0f / 3.0f);
+    num = fmaf(p * u, c, c);
+    den = 1.0f + eo;
+  } else {
+    const float e = __expf(-2.0f * c);
+    num = 1.0f - e;
+    den = (1.0f + e) * (1.0f + eo);
+  }
+  return num * rcp_nr(den);
+}
+
 // ---------------------------------------------------------------- memory model
 HS_DEV uint64_t globaltimer() {
   uint64_t t;

@@ -242,7 +242,7 @@ scan_fwd_kernel(const float *__restrict__ z, const float *__restrict__ c0, float
   cp_async_wait_all();
   __syncwarp();
 
-  // Pass 1: activations (kept in place: slot i <- b', f <- f', o <- sigma(z_o))
+  // Pass 1: activations (kept in place: slot i <- b', f <- f', o <- e^-z_o)
   // and the tile's map.
   float A = 1.f, C = 0.f;
   if (hv) {
@@ -251,10 +251,10 @@ scan_fwd_kernel(const float *__restrict__ z, const float *__restrict__ c0, float
       if (s < nst) {
         float *r = zs + s * kFwdRow + lane;
         const float fp = fmaxf(sigf(r[32]), eps);
-        const float bp = fmaxf(sigf(r[0]) * sigf(r[64]), eps);
+        const float bp = fmaxf(sig2(r[0], r[64]), eps);
         r[0] = bp;
         r[32] = fp;
-        r[96] = sigf(r[96]);
+        r[96] = __expf(-r[96]);  // e^-z_o; sigma(z_o) is folded into pass 2
         C = fmaf(fp, C, bp);
         A *= fp;
       }
@@ -275,7 +275,7 @@ scan_fwd_kernel(const float *__restrict__ z, const float *__restrict__ c0, float
     if (s < nst) {
       const float *r = zs + s * kFwdRow + lane;
       c = fmaf(r[32], c, r[0]);
-      const float o = r[96] * tanh_pos(c);
+      const float o = sig_tanh_pos(r[96], c);
       __stcs(cb + s * os, c);
       __stcs(ob + s * os, o);
       if (t0 + s == T - 1) {

@@ -164,18 +164,18 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
     __syncwarp();
     const int64_t t0 = c * kFL;
     const int n = (int)min((int64_t)kFL, T - t0);
-    float fp[kFL], bp[kFL], og[kFL];
+    float fp[kFL], bp[kFL], eo[kFL];  // f', b', e^-z_o
     float A = 1.f, C = 0.f;
 #pragma unroll
     for (int s = 0; s < kFL; ++s) {
       fp[s] = 1.f;
       bp[s] = 0.f;
-      og[s] = 0.f;
+      eo[s] = 0.f;
       if (s < n && hv) {
         const float *r = buf + s * kFRow + lane;
         fp[s] = fmaxf(sigf(r[32]), eps);
-        bp[s] = fmaxf(sigf(r[0]) * sigf(r[64]), eps);
-        og[s] = sigf(r[96]);
+        bp[s] = fmaxf(sig2(r[0], r[64]), eps);
+        eo[s] = __expf(-r[96]);
         C = fmaf(fp[s], C, bp[s]);
         A *= fp[s];
       }
@@ -195,7 +195,7 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
       for (int s = 0; s < kFL; ++s) {
         if (s < n) {
           cc = fmaf(fp[s], cc, bp[s]);
-          o = og[s] * tanh_pos(cc);
+          o = sig_tanh_pos(eo[s], cc);
           __stcs(cb, cc);
           __stcs(ob, o);
           cb += ostep;
