@@ -104,7 +104,8 @@ class ParallelFn(torch.autograd.Function):
         h_n = torch.empty(B, H, device=dev)
         c_n = torch.empty(B, H, device=dev)
         lib = _lib.load()
-        ws = _lib.workspace(lib.hs_parallel_workspace_bytes(T, B, D, H), dev)
+        ws = _lib.workspace(lib.hs_parallel_workspace_bytes(T, B, D, H), dev,
+                            min_bytes=lib.hs_scan_workspace_bytes(T, B, H))
         P = _lib.ptr
         _lib.call("hs_parallel_forward", P(x), P(c0), P(W_ih), P(b_ih), P(z), P(out), P(c),
                   P(h_n), P(c_n), T, B, D, H, float(eps), P(ws), ws.numel(),
@@ -132,7 +133,8 @@ class ParallelFn(torch.autograd.Function):
         dW_ih = torch.empty_like(W_ih)
         db_ih = torch.empty(4 * H, device=dev)
         lib = _lib.load()
-        ws = _lib.workspace(lib.hs_parallel_workspace_bytes(T, B, D, H), dev)
+        ws = _lib.workspace(lib.hs_parallel_workspace_bytes(T, B, D, H), dev,
+                            min_bytes=lib.hs_scan_workspace_bytes(T, B, H))
         P = _lib.ptr
         _lib.call("hs_parallel_backward", P(x), P(W_ih), P(z), P(c), P(c0), P(dout), P(dh_n),
                   P(dc_n), P(dx), P(dW_ih), P(db_ih), P(dc0), T, B, D, H, ctx.eps, P(ws),

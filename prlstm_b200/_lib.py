@@ -162,7 +162,16 @@ def clear_device_status(device=None):
     _pending.pop(idx, None)
 
 
-def workspace(nbytes: int, device) -> torch.Tensor:
+def workspace(nbytes: int, device, min_bytes: int = 0) -> torch.Tensor:
     """Caller-owned scratch (the library never allocates); 256-byte aligned
-    by the caching allocator."""
-    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+    by the caching allocator.  If the full size does not fit in device
+    memory and ``min_bytes`` is given, the smaller size is allocated instead:
+    the library then takes the paths that need less scratch (same results,
+    slower GEMMs)."""
+    try:
+        return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+    except torch.cuda.OutOfMemoryError:
+        if not min_bytes or min_bytes >= nbytes:
+            raise
+        torch.cuda.empty_cache()
+        return torch.empty(max(int(min_bytes), 256), dtype=torch.uint8, device=device)
