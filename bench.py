@@ -190,6 +190,7 @@ class ParallelStep:
         lib = _lib.load()
         self.ws = _lib.workspace(lib.hs_parallel_workspace_bytes(T, mb, D, H), dev)
         self.status = _lib.status_word(dev)
+        self.dz_absmax = torch.zeros(64, dtype=torch.int32, device=dev)  # max |dz| bits, word 0
         self.names = ("proj_gemm", "scan_fwd", "scan_bwd", "linear_bwd")
         self.ms = {n: 0.0 for n in self.names}
         self.launches = 0
@@ -214,20 +215,21 @@ class ParallelStep:
                    P(self.c_n), T, mb, H, 1e-6, P(self.ws), self.ws.numel(), P(self.status), st)
             if record:
                 e[2].record()
-            L.call("hs_scan_backward", P(self.z), P(self.c), P(self.c0), P(Gs), None, None,
+            # the scan backward also yields max |dz| for the split of dz below
+            L.call("hs_scan_backward_absmax", P(self.z), P(self.c), P(self.c0), P(Gs), None, None,
                    P(self.z), None, P(self.db_mb), T, mb, H, 1e-6, P(self.ws), self.ws.numel(),
-                   P(self.status), st)
+                   P(self.dz_absmax), P(self.status), st)
             if record:
                 e[3].record()
             # dX and dW_ih (accumulated over micro-batches) in one call
-            L.call("hs_linear_backward", P(self.z), P(xs), P(self.W_ih), P(self.dx), P(self.dW), M, 4 * H,
-                   D, 1 if i else 0, P(self.ws), self.ws.numel(), P(self.status), st)
+            L.call("hs_linear_backward_absmax", P(self.z), P(xs), P(self.W_ih), P(self.dx), P(self.dW), M,
+                   4 * H, D, 1 if i else 0, P(self.dz_absmax), P(self.ws), self.ws.numel(), P(self.status), st)
             if record:
                 e[4].record()
             self.db.add_(self.db_mb) if i else self.db.copy_(self.db_mb)
             # projection: 2 absmax + 2 split + GEMM; scans: 2 + rowsum; backward:
-            # 3 absmax + 3 split + 2 GEMMs
-            self.launches += 5 + 3 + 8
+            # 2 absmax + 3 split + 2 GEMMs
+            self.launches += 5 + 3 + 7
             if record:
                 evs.append(e)
         return evs

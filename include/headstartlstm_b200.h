@@ -110,6 +110,16 @@ HS_API int hs_linear_wgrad(const float *dy, const float *x, float *dw, int64_t M
 HS_API int hs_linear_backward(const float *dy, const float *x, const float *w, float *dx, float *dw,
                               int64_t M, int64_t N, int64_t K, int beta, void *workspace,
                               size_t workspace_bytes, int *dev_status, hs_stream_t stream);
+/* hs_linear_backward with max |dy| already known: *dy_absmax (device
+ * memory) is an upper bound of max |dy| as float32 bits, for example the
+ * word hs_scan_backward_absmax writes for its dz.  The fp16 split of dy then
+ * skips its own pass over dy.  A bound below the true maximum overflows the
+ * split; the exact maximum keeps the most precision.  Same replacement as
+ * hs_linear_backward (_torch.py:157-162, _triton.py:451-456). */
+HS_API int hs_linear_backward_absmax(const float *dy, const float *x, const float *w, float *dx,
+                                     float *dw, int64_t M, int64_t N, int64_t K, int beta,
+                                     const unsigned *dy_absmax, void *workspace,
+                                     size_t workspace_bytes, int *dev_status, hs_stream_t stream);
 /* db[N] = beta * db + sum_m dy[m, N]   (beta is 0 or 1) */
 HS_API int hs_colsum(const float *dy, float *db, int64_t M, int64_t N, int beta,
               hs_stream_t stream);
@@ -143,6 +153,16 @@ HS_API int hs_scan_backward(const float *z, const float *c, const float *c0, con
                      float *db, int64_t T, int64_t B, int64_t H, float eps,
                      void *workspace, size_t workspace_bytes, int *dev_status,
                      hs_stream_t stream);
+/* hs_scan_backward that also writes *dz_absmax (device memory, 4-byte
+ * aligned) = max |dz| over all written elements as float32 bits (NaN
+ * ignored), for hs_linear_backward_absmax: the gradient GEMMs that follow
+ * the scan in the reference's backward (_parallel.py:38-74 traced by
+ * autograd) then read dz once.  The word is zeroed by this call. */
+HS_API int hs_scan_backward_absmax(const float *z, const float *c, const float *c0,
+                                   const float *dout, const float *dh_n, const float *dc_n,
+                                   float *dz, float *dc0, float *db, int64_t T, int64_t B,
+                                   int64_t H, float eps, void *workspace, size_t workspace_bytes,
+                                   unsigned *dz_absmax, int *dev_status, hs_stream_t stream);
 
 /* hs_scan_forward without a workspace argument, for callers that cannot
  * allocate device memory (for example a host framework that passes the

@@ -41,6 +41,8 @@ size_t gemm_h3_partial_bound(int64_t M, int64_t N, int64_t K);
 size_t h3_split_bytes(int64_t rows, int64_t cols);
 int h3_split(const float *x, int64_t rows, int64_t cols, int64_t ld, unsigned *absmax, void *dst,
              cudaStream_t st);
+int h3_split_known(const float *x, int64_t rows, int64_t cols, int64_t ld, const unsigned *absmax, void *dst,
+                   cudaStream_t st);
 int gemm_h3_presplit(const void *a_split, const unsigned *a_absmax, bool a_mn, const void *b_split,
                      const unsigned *b_absmax, bool b_mn, float *C, const float *bias, int64_t M, int64_t N,
                      int64_t K, int64_t ldc, int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st,
@@ -53,7 +55,7 @@ int scan_forward(const float *z, const float *c0, float *out, float *c, float *h
 int scan_backward(const float *z, const float *c, const float *c0, const float *dout,
                   const float *dh_n, const float *dc_n, float *dz, float *dc0, float *db,
                   int64_t T, int64_t B, int64_t H, float eps, void *ws, size_t ws_bytes,
-                  int *status, cudaStream_t st);
+                  int *status, cudaStream_t st, unsigned *dz_absmax);
 
 // One GEMM: tensor-core path when it takes the shape, FFMA path otherwise.
 static int gemm(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
@@ -106,7 +108,9 @@ int linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t 
 // null), dw[N,K] = beta*dw + dy^T.x and, if x2 is given, dw2[N,K2] =
 // beta*dw2 + dy^T.x2.  Through the fp16 split, dy is split once and shared
 // by all products (K-major for dx, M/N-major for the weight gradients);
-// otherwise each product runs on its own.
+// otherwise each product runs on its own.  dy_absmax (device memory, may be
+// null) holds an upper bound of max |dy| as float bits, computed by the
+// producer of dy; the split then skips its own pass over dy.
 size_t linear_backward_ws(int64_t M, int64_t N, int64_t K, int64_t K2) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   size_t sc = 256 + h3_split_bytes(M, N) + h3_split_bytes(M, K) + h3_split_bytes(N, K);
@@ -120,7 +124,7 @@ size_t linear_backward_ws(int64_t M, int64_t N, int64_t K, int64_t K2) {
 
 int linear_backward_ex(const float *dy, const float *w, float *dx, const float *x, float *dw, const float *x2,
                        float *dw2, int64_t M, int64_t N, int64_t K, int64_t K2, int beta, void *ws, size_t ws_bytes,
-                       int *status, cudaStream_t st) {
+                       int *status, cudaStream_t st, const unsigned *dy_absmax) {
   if (int e = check_gemm(dy, x, dw, N, K, M)) return e;
   if (x2)
     if (int e = check_gemm(dy, x2, dw2, N, K2, M)) return e;
@@ -137,20 +141,25 @@ int linear_backward_ex(const float *dy, const float *w, float *dx, const float *
     char *x2s = wsp + h3_split_bytes(N, K);
     char *tail = w8 + sc;
     const size_t tb = ws_bytes - sc;
-    if (int e = h3_split(dy, M, N, N, am, dys, st)) return e;
+    const unsigned *dam = dy_absmax ? dy_absmax : am;
+    if (dy_absmax) {
+      if (int e = h3_split_known(dy, M, N, N, dy_absmax, dys, st)) return e;
+    } else if (int e = h3_split(dy, M, N, N, am, dys, st)) {
+      return e;
+    }
     if (dx) {
       if (int e = h3_split(w, N, K, K, am + 2, wsp, st)) return e;
-      if (int e = gemm_h3_presplit(dys, am, false, wsp, am + 2, true, dx, nullptr, M, K, N, K, 0, tail, tb, status,
+      if (int e = gemm_h3_presplit(dys, dam, false, wsp, am + 2, true, dx, nullptr, M, K, N, K, 0, tail, tb, status,
                                    st, &ddx))
         return e;
     }
     if (int e = h3_split(x, M, K, K, am + 1, xs, st)) return e;
-    if (int e = gemm_h3_presplit(dys, am, true, xs, am + 1, true, dw, nullptr, N, K, M, K, beta, tail, tb, status,
+    if (int e = gemm_h3_presplit(dys, dam, true, xs, am + 1, true, dw, nullptr, N, K, M, K, beta, tail, tb, status,
                                  st, &ddw))
       return e;
     if (x2) {
       if (int e = h3_split(x2, M, K2, K2, am + 3, x2s, st)) return e;
-      if (int e = gemm_h3_presplit(dys, am, true, x2s, am + 3, true, dw2, nullptr, N, K2, M, K2, beta, tail, tb,
+      if (int e = gemm_h3_presplit(dys, dam, true, x2s, am + 3, true, dw2, nullptr, N, K2, M, K2, beta, tail, tb,
                                    status, st, &ddw2))
         return e;
     }
@@ -166,11 +175,15 @@ int linear_backward_ex(const float *dy, const float *w, float *dx, const float *
 
 int linear_backward(const float *dy, const float *x, const float *w, float *dx, float *dw, int64_t M, int64_t N,
                     int64_t K, int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st) {
-  return linear_backward_ex(dy, w, dx, x, dw, nullptr, nullptr, M, N, K, 0, beta, ws, ws_bytes, status, st);
+  return linear_backward_ex(dy, w, dx, x, dw, nullptr, nullptr, M, N, K, 0, beta, ws, ws_bytes, status, st,
+                            nullptr);
 }
 
+// The scan's and the linear layer's scratch overlap (they run one after the
+// other); the last 256 bytes hold max |dz|, which the scan backward writes
+// and the gradient GEMMs' split reads.
 size_t parallel_ws_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
-  return std::max(scan_workspace(T, B, H), linear_ws_bytes(T * B, 4 * H, D));
+  return std::max(scan_workspace(T, B, H), linear_ws_bytes(T * B, 4 * H, D)) + 256;
 }
 
 int parallel_forward(const float *x, const float *c0, const float *w_ih, const float *b_ih,
@@ -190,8 +203,20 @@ int parallel_backward(const float *x, const float *w_ih, float *z, const float *
                       cudaStream_t st) {
   if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return fail(HS_ERR_INVALID_ARG, "T, B, D, H must be positive");
   if (!x || !w_ih || !z || !dw_ih || !db_ih) return fail(HS_ERR_INVALID_ARG, "parallel_backward: null x/w_ih/z/dw_ih/db_ih");
-  if (int e = scan_backward(z, c, c0, dout, dh_n, dc_n, z, dc0, db_ih, T, B, H, eps, ws, ws_bytes, status, st)) return e;
-  return linear_backward(z, x, w_ih, dx, dw_ih, T * B, 4 * H, D, 0, ws, ws_bytes, status, st);
+  // With room for it, max |dz| comes out of the scan (the split then reads dz once, not twice).
+  unsigned *dz_absmax = nullptr;
+  size_t wsb = ws_bytes & ~(size_t)255;
+  if (ws && aligned(ws, 256) && wsb >= scan_workspace(T, B, H) + 256) {
+    wsb -= 256;
+    dz_absmax = reinterpret_cast<unsigned *>(static_cast<char *>(ws) + wsb);
+    if (cudaMemsetAsync(dz_absmax, 0, 4, st) != cudaSuccess) return check_launch("parallel_backward memset");
+  } else {
+    wsb = ws_bytes;
+  }
+  if (int e = scan_backward(z, c, c0, dout, dh_n, dc_n, z, dc0, db_ih, T, B, H, eps, ws, wsb, status, st, dz_absmax))
+    return e;
+  return linear_backward_ex(z, w_ih, dx, x, dw_ih, nullptr, nullptr, T * B, 4 * H, D, 0, 0, ws, wsb, status, st,
+                            dz_absmax);
 }
 
 namespace {
@@ -295,6 +320,15 @@ int hs_linear_backward(const float *dy, const float *x, const float *w, float *d
                        hs_stream_t stream) {
   return hs::linear_backward(dy, x, w, dx, dw, M, N, K, beta, workspace, workspace_bytes, dev_status,
                              (cudaStream_t)stream);
+}
+
+int hs_linear_backward_absmax(const float *dy, const float *x, const float *w, float *dx, float *dw, int64_t M,
+                              int64_t N, int64_t K, int beta, const unsigned *dy_absmax, void *workspace,
+                              size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
+  if (!dy_absmax || !hs::aligned(dy_absmax, 4))
+    return hs::fail(HS_ERR_INVALID_ARG, "hs_linear_backward_absmax: null or misaligned dy_absmax");
+  return hs::linear_backward_ex(dy, w, dx, x, dw, nullptr, nullptr, M, N, K, 0, beta, workspace, workspace_bytes,
+                                dev_status, (cudaStream_t)stream, dy_absmax);
 }
 
 int hs_linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t N, int64_t K,

@@ -1227,6 +1227,20 @@ int h3_split(const float *x, int64_t rows, int64_t cols, int64_t ld, unsigned *a
   return check_launch("split_h2_kernel");
 }
 
+// The same split with *absmax already known: an upper bound of max |x| as
+// float bits (the exact maximum keeps the most precision; anything below it
+// overflows fp16).
+int h3_split_known(const float *x, int64_t rows, int64_t cols, int64_t ld, const unsigned *absmax, void *dst,
+                   cudaStream_t st) {
+  const int nsm = device_sms();
+  const int64_t ldo = round8(cols);
+  __half *hi = static_cast<__half *>(dst);
+  __half *lo = hi + rows * ldo;
+  const int grid = (int)std::min<int64_t>(8 * nsm, (rows + 7) / 8);
+  split_h2_kernel<<<grid, 256, 0, st>>>(x, rows, cols, ld, absmax, hi, lo, ldo);
+  return check_launch("split_h2_kernel");
+}
+
 // C[M,N] = A.B^T over K (+bias, beta) from split operands.  A is stored
 // [M][.] (a_mn false, K-major) or [K][.] (a_mn true); B likewise with N.
 // Scratch (split-K partials, if any) from ws; *done = false if the shape or

@@ -44,7 +44,7 @@ size_t linear_ws_bytes(int64_t M, int64_t N, int64_t K);
 size_t linear_backward_ws(int64_t M, int64_t N, int64_t K, int64_t K2);
 int linear_backward_ex(const float *dy, const float *w, float *dx, const float *x, float *dw, const float *x2,
                        float *dw2, int64_t M, int64_t N, int64_t K, int64_t K2, int beta, void *ws, size_t ws_bytes,
-                       int *status, cudaStream_t st);
+                       int *status, cudaStream_t st, const unsigned *dy_absmax);
 int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st);
 
 namespace {
@@ -751,7 +751,8 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
   // dX = dG.W_ih, dW_ih = dG^T.x and dW_hh_s = dG^T.h_{t-1} share one
   // conversion of dG (h_save rows 0..T-1 are the h_{t-1} of steps 0..T-1).
   const int64_t M = T * B, N = 4 * H;
-  if (int e = linear_backward_ex(acts, w_ih, dx, x, dw_ih, h_save, dw_hh, M, N, D, H, 0, ws, ws_bytes, status, st))
+  if (int e = linear_backward_ex(acts, w_ih, dx, x, dw_ih, h_save, dw_hh, M, N, D, H, 0, ws, ws_bytes, status, st,
+                                  nullptr))
     return e;
   if (int e = colsum(acts, db_ih, M, N, 0, st)) return e;
   // partial sums of da in the (now free) workspace

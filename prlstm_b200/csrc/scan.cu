@@ -49,7 +49,8 @@ int scan_fwd_chain_launch(const float *z, const float *c0, float *out, float *c,
                           int64_t T, int64_t B, int64_t H, float eps, int *status, cudaStream_t st);
 int scan_bwd_chain_launch(const float *z, const float *c, const float *c0, const float *dout,
                           const float *dh_n, const float *dc_n, float *dz, float *dc0, float *db_part,
-                          int64_t T, int64_t B, int64_t H, float eps, int *status, cudaStream_t st);
+                          int64_t T, int64_t B, int64_t H, float eps, unsigned *dz_absmax, int *status,
+                          cudaStream_t st);
 
 namespace {
 
@@ -291,7 +292,8 @@ template <bool V16>
 __global__ void __launch_bounds__(kBwdWPC * 32)
 scan_bwd_kernel(const float *z, const float *__restrict__ cbuf, const float *__restrict__ c0,
                 const float *__restrict__ dout, const float *__restrict__ dh_n, const float *__restrict__ dc_n,
-                float *dz, float *__restrict__ dc0, ScanShape sh, float eps, ScanWs ws, int *status) {
+                float *dz, float *__restrict__ dc0, ScanShape sh, float eps, ScanWs ws, unsigned *dz_absmax,
+                int *status) {
   constexpr int L = kBwdL;
   extern __shared__ float4 smem_f4[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -312,6 +314,7 @@ scan_bwd_kernel(const float *z, const float *__restrict__ cbuf, const float *__r
   const int nst = active ? (int)min((int64_t)L, T - t0) : 0;
   const int64_t zstep = B * 4 * H, sstep = B * H;
   float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+  float amax = 0.f;  // max |dz| of this lane (NaN ignored), if dz_absmax is wanted
 
   if (active) {
     // Stage z (4 rows), c and dout of each step, and c_{t0-1}.
@@ -368,6 +371,7 @@ scan_bwd_kernel(const float *z, const float *__restrict__ cbuf, const float *__r
           const float dzo = d * th * o * (1.f - o);
           __stcs(dz + (t * B + b) * 4 * H + 3 * H + h, dzo);
           acc3 += dzo;
+          amax = fmaxf(amax, fabsf(dzo));
           r[0] = g * i * (1.f - i) * mb;
           r[32] = cp * f * (1.f - f) * mf;
           r[64] = i * g * (1.f - g) * mb;
@@ -398,10 +402,16 @@ scan_bwd_kernel(const float *z, const float *__restrict__ cbuf, const float *__r
           acc0 += di;
           acc1 += df;
           acc2 += dg;
+          amax = fmaxf(amax, fmaxf(fabsf(di), fmaxf(fabsf(df), fabsf(dg))));
         }
       }
       if (t0 == 0 && dc0) dc0[b * H + h] = (c0 && c0[b * H + h] >= eps) ? e : 0.f;
     }
+  }
+  if (dz_absmax) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) atomicMax(dz_absmax, __float_as_uint(amax));
   }
 
   // Bias-gradient sums of this CTA's WPC tiles, added in a fixed order.
@@ -507,7 +517,7 @@ int scan_forward(const float *z, const float *c0, float *out, float *c, float *h
 
 int scan_backward(const float *z, const float *c, const float *c0, const float *dout, const float *dh_n,
                   const float *dc_n, float *dz, float *dc0, float *db, int64_t T, int64_t B, int64_t H, float eps,
-                  void *ws_base, size_t ws_bytes, int *status, cudaStream_t st) {
+                  void *ws_base, size_t ws_bytes, int *status, cudaStream_t st, unsigned *dz_absmax) {
   if (int e = check_scan_args(T, B, H)) return e;
   if (!z || !c || !dout || !dz || !status) return fail(HS_ERR_INVALID_ARG, "scan_backward: null z/c/dout/dz/status");
   if (!ws_base || !aligned(ws_base, 256))
@@ -521,7 +531,7 @@ int scan_backward(const float *z, const float *c, const float *c0, const float *
   if (scan_chain_wanted(T, B, H)) {
     // one CTA per column; bias sums per sequence
     if (int e = scan_bwd_chain_launch(z, c, c0, dout, dh_n, dc_n, dz, dc0, db ? ws.db_part : nullptr, T, B, H, eps,
-                                      status, st))
+                                      dz_absmax, status, st))
       return e;
     if (db) {
       rowsum_kernel<<<(unsigned)((N + 31) / 32), 256, 0, st>>>(ws.db_part, db, B, N, 0);
@@ -535,10 +545,10 @@ int scan_backward(const float *z, const float *c, const float *c0, const float *
   const unsigned grid = (unsigned)((int64_t)sh.ngroup * B * sh.ncol);
   if (v16)
     scan_bwd_kernel<true><<<grid, kBwdWPC * 32, kBwdSmem, st>>>(z, c, c0, dout, dh_n, dc_n, dz, dc0, sh, eps, ws,
-                                                                status);
+                                                                dz_absmax, status);
   else
     scan_bwd_kernel<false><<<grid, kBwdWPC * 32, kBwdSmem, st>>>(z, c, c0, dout, dh_n, dc_n, dz, dc0, sh, eps, ws,
-                                                                 status);
+                                                                 dz_absmax, status);
   if (int e = check_launch("scan_bwd_kernel")) return e;
   if (db) {
     rowsum_kernel<<<(unsigned)((N + 31) / 32), 256, 0, st>>>(ws.db_part, db, (int64_t)sh.ngroup * B, N, 0);
@@ -634,7 +644,19 @@ int hs_scan_backward(const float *z, const float *c, const float *c0, const floa
                      int64_t T, int64_t B, int64_t H, float eps, void *workspace,
                      size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
   return hs::scan_backward(z, c, c0, dout, dh_n, dc_n, dz, dc0, db, T, B, H, eps, workspace,
-                           workspace_bytes, dev_status, (cudaStream_t)stream);
+                           workspace_bytes, dev_status, (cudaStream_t)stream, nullptr);
+}
+
+int hs_scan_backward_absmax(const float *z, const float *c, const float *c0, const float *dout,
+                            const float *dh_n, const float *dc_n, float *dz, float *dc0, float *db, int64_t T,
+                            int64_t B, int64_t H, float eps, void *workspace, size_t workspace_bytes,
+                            unsigned *dz_absmax, int *dev_status, hs_stream_t stream) {
+  if (!dz_absmax || !hs::aligned(dz_absmax, 4))
+    return hs::fail(HS_ERR_INVALID_ARG, "hs_scan_backward_absmax: null or misaligned dz_absmax");
+  if (cudaMemsetAsync(dz_absmax, 0, 4, (cudaStream_t)stream) != cudaSuccess)
+    return hs::check_launch("hs_scan_backward_absmax memset");
+  return hs::scan_backward(z, c, c0, dout, dh_n, dc_n, dz, dc0, db, T, B, H, eps, workspace, workspace_bytes,
+                           dev_status, (cudaStream_t)stream, dz_absmax);
 }
 
 int hs_scan_forward_noalloc(const float *z, const float *c0, float *out, float *c, float *h_n,

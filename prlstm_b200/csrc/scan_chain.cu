@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(kBNW * 32, V16 ? kMinCtas : kMinCtas - 2)
 scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float *__restrict__ c0,
                     const float *__restrict__ dout, const float *__restrict__ dh_n, const float *__restrict__ dc_n,
                     float *dz, float *__restrict__ dc0, float *__restrict__ db_part, int64_t T, int64_t B,
-                    int64_t H, float eps, int *status) {
+                    int64_t H, float eps, unsigned *dz_absmax, int *status) {
   extern __shared__ float4 smem_f4[];
   float *sm = reinterpret_cast<float *>(smem_f4);
   unsigned long long *slots = reinterpret_cast<unsigned long long *>(sm + kBNW * 2 * kBBuf);  // [NW][32]
@@ -271,6 +271,7 @@ scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float 
   };
 
   float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+  float amax = 0.f;  // max |dz| of this lane (NaN ignored), if dz_absmax is wanted
   int64_t q = warp;
   if (q < nchunk) stage(q, buf0);
   commit();
@@ -306,6 +307,7 @@ scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float 
         const float dzo = d * th * o * (1.f - o);
         __stcs(dzs + s * zstep + 3 * H, dzo);
         acc3 += dzo;
+        amax = fmaxf(amax, fabsf(dzo));
         FP[s] = fmaxf(f, eps);
         DCD[s] = dcd;
         KI[s] = g * ig * (1.f - ig) * mb;
@@ -336,12 +338,18 @@ scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float 
           acc0 += di;
           acc1 += df;
           acc2 += dg;
+          amax = fmaxf(amax, fmaxf(fabsf(di), fmaxf(fabsf(df), fabsf(dg))));
         }
       }
       if (t0 == 0 && dc0) dc0[b * H + h] = (c0 && c0[b * H + h] >= eps) ? e : 0.f;
     }
   }
   wait_group<0>();
+  if (dz_absmax) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) atomicMax(dz_absmax, __float_as_uint(amax));
+  }
   if (db_part) {
     __syncthreads();  // every warp is done with its buffers
     float *red = sm;  // [NW][4][32]
@@ -416,7 +424,7 @@ int scan_fwd_chain_launch(const float *z, const float *c0, float *out, float *c,
 
 int scan_bwd_chain_launch(const float *z, const float *c, const float *c0, const float *dout, const float *dh_n,
                           const float *dc_n, float *dz, float *dc0, float *db_part, int64_t T, int64_t B, int64_t H,
-                          float eps, int *status, cudaStream_t st) {
+                          float eps, unsigned *dz_absmax, int *status, cudaStream_t st) {
   const int64_t grid = B * ((H + 31) / 32);
   if (grid >= (1ll << 31)) return fail(HS_ERR_UNSUPPORTED, "scan: too many columns");
   if ((T + kBL - 1) / kBL >= (1ll << 32)) return fail(HS_ERR_UNSUPPORTED, "scan: T too large");
@@ -425,10 +433,10 @@ int scan_bwd_chain_launch(const float *z, const float *c, const float *c0, const
   if (int e = allow_dynamic_smem(fn, kBSmem, &g_bwd_attr[v16])) return e;
   if (v16)
     scan_bwd_col_kernel<true><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(z, c, c0, dout, dh_n, dc_n, dz, dc0,
-                                                                       db_part, T, B, H, eps, status);
+                                                                       db_part, T, B, H, eps, dz_absmax, status);
   else
     scan_bwd_col_kernel<false><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(z, c, c0, dout, dh_n, dc_n, dz, dc0,
-                                                                        db_part, T, B, H, eps, status);
+                                                                        db_part, T, B, H, eps, dz_absmax, status);
   return check_launch("scan_bwd_col_kernel");
 }
 

@@ -176,3 +176,37 @@ def test_linear_backward(M, N, K, beta, with_dx):
     if with_dx:
         assert _rel(dx, dy64 @ w64) < TOL
     L.check_device_status(dev)
+
+
+@pytest.mark.parametrize("M,N,K,beta", [(8192, 1024, 256, 0), (3000, 520, 132, 1)])
+def test_linear_backward_with_known_absmax(M, N, K, beta):
+    """hs_linear_backward_absmax with the exact max |dy| gives the same bits
+    as hs_linear_backward (which measures it itself); a looser upper bound
+    (4x) still meets the tolerance."""
+    L = _lib()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(M + K)
+    dy = torch.randn(M, N, device=dev, generator=g)
+    x = torch.randn(M, K, device=dev, generator=g)
+    w = torch.randn(N, K, device=dev, generator=g) / K ** 0.5
+    dw0 = torch.randn(N, K, device=dev, generator=g)
+    ws, n = _ws(L, M, N, K, dev)
+    P, st, status = L.ptr, L.stream_ptr(dev), L.status_word(dev)
+    res = {}
+    for name, bound in (("own", None), ("exact", 1.0), ("loose", 4.0)):
+        dx = torch.empty(M, K, device=dev)
+        dw = dw0.clone()
+        if bound is None:
+            L.call("hs_linear_backward", P(dy), P(x), P(w), P(dx), P(dw), M, N, K, beta, P(ws), n, P(status), st)
+        else:
+            am = (dy.abs().max() * bound).reshape(1).view(torch.int32).clone()
+            L.call("hs_linear_backward_absmax", P(dy), P(x), P(w), P(dx), P(dw), M, N, K, beta, P(am), P(ws), n,
+                   P(status), st)
+        res[name] = (dx, dw)
+    torch.cuda.synchronize(dev)
+    L.check_device_status(dev)
+    assert torch.equal(res["own"][0], res["exact"][0]) and torch.equal(res["own"][1], res["exact"][1])
+    dy64, x64, w64 = dy.double().cpu(), x.double().cpu(), w.double().cpu()
+    ref_dw = dy64.t() @ x64 + (dw0.double().cpu() if beta else 0)
+    assert _rel(res["loose"][1], ref_dw) < TOL
+    assert _rel(res["loose"][0], dy64 @ w64) < TOL

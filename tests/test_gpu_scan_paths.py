@@ -96,3 +96,48 @@ def test_scan_paths_match_float64(T, B, H):
             assert e < TOL, f"{p}:{k} rel err {e:.3e}"
     for k in truth:
         assert _rel(res["chain"][k], res["lookback"][k]) < TOL
+
+
+@pytest.mark.parametrize("path", ["chain", "lookback"])
+def test_scan_backward_absmax(path):
+    """hs_scan_backward_absmax writes the same dz as hs_scan_backward (the
+    same bits on the column-chain path; the look-back path may combine a
+    carry from a tile's aggregate or from its inclusive prefix, whichever is
+    published first, so its bits may differ in rounding) and the exact
+    max |dz| of its own dz (as float bits) into its word."""
+    from prlstm_b200 import _lib as L
+
+    T, B, H = 512, 4, 100
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(11)
+    z = 2.0 * torch.randn(T, B, 4 * H, device=dev, generator=g)
+    c0 = torch.rand(B, H, device=dev, generator=g)
+    G = torch.randn(T, B, H, device=dev, generator=g)
+    dh_n = torch.randn(B, H, device=dev, generator=g)
+    dc_n = torch.randn(B, H, device=dev, generator=g)
+    ref = _run(path, z, c0, G, dh_n, dc_n)
+    old = os.environ.get("HS_SCAN_PATH")
+    os.environ["HS_SCAN_PATH"] = path
+    try:
+        lib = L.load()
+        ws = L.workspace(lib.hs_scan_workspace_bytes(T, B, H), dev)
+        P, st = L.ptr, L.stream_ptr(dev)
+        dz = torch.empty_like(z)
+        dc0 = torch.empty(B, H, device=dev)
+        db = torch.empty(4 * H, device=dev)
+        am = torch.full((4,), -1, dtype=torch.int32, device=dev)  # the call zeroes it first
+        L.call("hs_scan_backward_absmax", P(z), P(ref["c"]), P(c0), P(G), P(dh_n), P(dc_n), P(dz), P(dc0),
+               P(db), T, B, H, 1e-6, P(ws), ws.numel(), P(am), P(L.status_word(dev)), st)
+        torch.cuda.synchronize(dev)
+        L.check_device_status(dev)
+    finally:
+        if old is None:
+            del os.environ["HS_SCAN_PATH"]
+        else:
+            os.environ["HS_SCAN_PATH"] = old
+    for k, v in (("dz", dz), ("db", db), ("dc0", dc0)):
+        if path == "chain":
+            assert torch.equal(v, ref[k]), k
+        else:
+            assert _rel(v, ref[k]) < TOL, k
+    assert am[0].item() == dz.abs().max().reshape(1).view(torch.int32).item()
