@@ -195,6 +195,18 @@ HS_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+HS_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 struct TcArgs {
   float *C;
   const float *bias;
@@ -696,13 +708,15 @@ gemm_ta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // which runs at twice the tf32 rate and reads half the operand bytes.  Each
 // operand is scaled by a power of two s (so that max|x s| lies in
 // [2^14, 2^15)) and split into two fp16 words,
-//     hi = fp16(x s),   lo = fp16((x s - hi) * 2^11),
+//     hi = fp16(x s),   lo = fp16(x s - hi),
 // which keep 22 significand bits together (as tf32 hi + lo do), and
-//     A.B ~= [Ah.Bh + 2^-11 (Ah.Bl + Al.Bh)] / (s_A s_B)
-// in three MMAs per k-step, with the same two-accumulator promotion scheme
-// as the tf32 kernel.  Elements far below the tensor's maximum lose relative
-// precision in fp16's subnormal range; their absolute error stays below
-// 2^-38 of the largest element, far under the float32 result's own rounding.
+//     A.B ~= [Ah.Bh + Ah.Bl + Al.Bh] / (s_A s_B)
+// in three MMAs per k-step; the tensor core's float32 sums run over a few
+// k-blocks at a time and are then added in float32 registers (promotion),
+// as in the tf32 kernel.  Elements far below the tensor's maximum lose
+// relative precision in fp16's subnormal range (lo below 2^-14, i.e.
+// |x s| < 2^-4); their absolute error stays below 2^-25 in scaled units,
+// 2^-39 of the largest element, far under the float32 result's own rounding.
 // The split runs as a separate pass over each operand (absmax, then split),
 // into caller workspace.
 HS_DEV float pow2_scale(unsigned absmax_bits) {
@@ -759,7 +773,7 @@ __global__ void split_h2_kernel(const float *__restrict__ x, int64_t rows, int64
       for (int j = 0; j < 4; ++j) {
         const float y = v[j] * s;
         h[j] = __float2half_rn(y);
-        l[j] = __float2half_rn((y - __half2float(h[j])) * 2048.0f);
+        l[j] = __float2half_rn(y - __half2float(h[j]));
       }
       *reinterpret_cast<uint2 *>(hr + c) = *reinterpret_cast<const uint2 *>(h);
       *reinterpret_cast<uint2 *>(lr + c) = *reinterpret_cast<const uint2 *>(l);
@@ -787,6 +801,12 @@ constexpr int H3_STAGES = 3;
 #define HS_H3_PROMOTE 4
 #endif
 constexpr int H3_PROMOTE = HS_H3_PROMOTE;         // k-blocks per accumulator group
+// 1: Ah.Bh and Ah.Bl as one N = 256 MMA (Bh and Bl are adjacent in shared
+// memory, main and correction accumulators adjacent in TMEM), so A_hi is
+// read once per k-step for both; 0: three N = 128 MMAs.
+#ifndef HS_H3_WIDE
+#define HS_H3_WIDE 1
+#endif
 constexpr int H3_THREADS = 192;                  // producer, MMA, 4 fold/epilogue warps
 constexpr int H3_SMEM_BYTES = H3_STAGES * H3_STAGE + 1024 + 256;
 static_assert(H3_SMEM_BYTES <= 232448, "shared memory per block");
@@ -806,8 +826,12 @@ constexpr int H3_EPI = BM * 32 * 4;              // 16 KB staging box
 constexpr int H3_SMEM_P = H3_STAGES * H3_STAGE + H3_EPI + 1024 + 256;
 static_assert(H3_SMEM_P <= 232448, "shared memory per block");
 
+HS_DEV void named_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+
+// bar_id: the named barrier of these 128 threads (1 unless several groups
+// store at once).
 HS_DEV void store_tile_boxes(const float (&tot)[BN], float *box, const CUtensorMap *tmC_, const TcArgs &p, int q,
-                             int lane, int t, int64_t m0, int64_t n0, int zc) {
+                             int lane, int t, int64_t m0, int64_t n0, int zc, int bar_id = 1) {
   const CUtensorMap &tmC = *tmC_;
   const int r = q * 32 + lane;
   const bool direct = p.partial == nullptr;
@@ -831,14 +855,14 @@ HS_DEV void store_tile_boxes(const float (&tot)[BN], float *box, const CUtensorM
       *reinterpret_cast<float4 *>(box + r * 32 + ((j ^ (r & 7)) * 4)) = o;
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    named_sync(bar_id);
     if (t == 0) {
       if (direct && p.beta) tma_reduce_add_3d(&tmC, box, (int)n0 + 32 * c, (int)m0, zc);
       else tma_store_3d(&tmC, box, (int)n0 + 32 * c, (int)m0, zc);
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // box free again
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    named_sync(bar_id);
   }
 }
 
@@ -941,7 +965,10 @@ gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__
   } else if (!skip && warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(BM, BN) | ((A_MN ? 1u : 0u) << 15) | ((B_MN ? 1u : 0u) << 16);
+      constexpr uint32_t majors = ((A_MN ? 1u : 0u) << 15) | ((B_MN ? 1u : 0u) << 16);
+      constexpr uint32_t idesc = idesc_f16(BM, BN) | majors;
+      constexpr uint32_t idesc2 = idesc_f16(BM, 2 * BN) | majors;
+      (void)idesc2;
       int it = 0, gg = 0;
       bool ok = true;
       for (int tl = blockIdx.x; tl < ntiles_total && ok; tl += gridDim.x) {
@@ -969,8 +996,13 @@ gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__
             const uint64_t dAh = sdesc(ah + oa, la, 1024, 2), dAl = sdesc(al + oa, la, 1024, 2);
             const uint64_t dBh = sdesc(bh + ob, lb, 1024, 2), dBl = sdesc(bl + ob, lb, 1024, 2);
             const uint32_t acc = (gstart && kk == 0) ? 0u : 1u;
+#if HS_H3_WIDE
+            (void)dBl;
+            mma_f16(t_main, dAh, dBh, idesc2, acc);  // [main | corr] = Ah.[Bh | Bl]
+#else
             mma_f16(t_main, dAh, dBh, idesc, acc);
             mma_f16(t_corr, dAh, dBl, idesc, acc);
+#endif
             mma_f16(t_corr, dAl, dBh, idesc, 1u);
           }
           mma_commit(&empty[s]);
@@ -1007,7 +1039,7 @@ gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__
           tmem_ld32(base + BN + c, w);
           tmem_ld32(base + c, v);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) tot[c + j] += fmaf(w[j], 1.0f / 2048.0f, v[j]);
+          for (int j = 0; j < 32; ++j) tot[c + j] += w[j] + v[j];
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
@@ -1024,6 +1056,284 @@ gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------- 2-SM pairs
+// The same 3 x fp16 product with the pair MMA (tcgen05 cta_group::2): a
+// cluster of two CTAs on two SMs computes a 256 x 256 output tile, each CTA
+// holding 128 rows of A and 128 rows (N) of B per stage in its own shared
+// memory, and the MMA reads both halves of B across the pair.  Per SM and
+// k-step of 16 this reads 4 KB of A and 4 KB of B per product (half what a
+// one-SM 128 x 256 tile reads for the same work), which keeps the three
+// products per k-step below the shared-memory bandwidth.  The three products
+// go into ONE accumulator (lo parts are unscaled), 256 TMEM columns, so two
+// accumulator buffers fit the 512 columns.
+//
+// Roles: warp 0 loads (both CTAs, each its own rows; the completion bytes of
+// both land on the first CTA's barrier), warp 1 of the first CTA issues the
+// MMAs, warps 2-9 of both CTAs fold the groups and store the tile (two
+// groups of four warps, one per 128-column half, thread = row).
+//
+// Cross-CTA signals without multicast: the first CTA's producer, having seen
+// a stage freed by the MMAs (one commit covers both CTAs' operands), passes
+// the release on to the second CTA's barrier; the first CTA's fold thread
+// passes on "accumulator ready" likewise; every fold warp of both CTAs
+// arrives on the first CTA's "accumulator free" barrier.  Every wait is
+// bounded.
+constexpr int P_STAGES = 3;
+constexpr int P_THREADS = 320;                       // producer, MMA, 8 fold/epilogue warps
+constexpr int P_SMEM = P_STAGES * H3_STAGE + 2 * H3_EPI + 1024 + 256;
+static_assert(P_SMEM <= 232448, "shared memory per block");
+constexpr int P_BM = 256, P_BN = 256;                // pair tile
+constexpr uint32_t P_ACC_COLS = 256;                 // one accumulator buffer
+
+HS_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+HS_DEV uint32_t cluster_addr(const void *p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(su32(p)), "r"(rank));
+  return r;
+}
+// Arrive on a barrier of either CTA of the cluster (default semantics:
+// release at CTA scope, no cluster-wide fence).
+HS_DEV void mbar_arrive_cluster(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+HS_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Load into this CTA's shared memory; completion bytes counted on the
+// barrier at cluster address bar (the first CTA's).
+HS_DEV void tma_2d_pair(void *dst, const CUtensorMap *tm, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(su32(dst)),
+      "l"(tm), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+HS_DEV void mma_f16_pair(uint32_t dt, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dt),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+HS_DEV void mma_commit_pair(uint64_t *b) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b))
+               : "memory");
+}
+
+template <bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
+gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+                    const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
+                    const __grid_constant__ CUtensorMap tmC, TcArgs p, const unsigned *absmax_a,
+                    const unsigned *absmax_b, int mtiles, int ntiles, int ntiles_total) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float *epi = reinterpret_cast<float *>(smem + P_STAGES * H3_STAGE);  // two 16 KB boxes
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + P_STAGES * H3_STAGE + 2 * H3_EPI);
+  uint64_t *empty = full + P_STAGES;
+  uint64_t *pfull = empty + P_STAGES;
+  uint64_t *pempty = pfull + 2;
+  uint64_t *mdone = pempty + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(mdone + 1);
+  int *abort_flag = reinterpret_cast<int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  auto tile_of = [&](int tl, int64_t &m0, int64_t &n0, int &z, int &nk) {
+    const int per = mtiles * ntiles;
+    z = tl / per;
+    const int rem = tl - z * per;
+    m0 = (int64_t)(rem / ntiles) * P_BM;
+    n0 = (int64_t)(rem % ntiles) * P_BN;
+    const int kb0 = z * p.kb_per_split;
+    nk = min(p.nkb, kb0 + p.kb_per_split) - kb0;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pfull[b], 1);
+      mbar_init(&pempty[b], 16);  // 8 fold warps x 2 CTAs (used in the first CTA)
+    }
+    mbar_init(mdone, 1);
+    *abort_flag = ld_status(p.status) != 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_holder)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync_all();  // barriers and TMEM of both CTAs ready before any cross-CTA use
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_holder;
+  const bool skip = *abort_flag != 0;
+
+  if (!skip && warp == 0) {
+    // ---------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      int it = 0, issued = 0;
+      bool ok = true;
+      for (int tl = pair; tl < ntiles_total && ok; tl += npairs) {
+        int64_t m0, n0;
+        int z, nk;
+        tile_of(tl, m0, n0, z, nk);
+        const int mr = (int)m0 + 128 * (int)rank, nr = (int)n0 + 128 * (int)rank;
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int s = it % P_STAGES;
+          const uint32_t ph = (it / P_STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.status)) { ok = false; break; }
+          // pass a real release (not the first use of a stage) on to the
+          // second CTA first, so that its loads start with this CTA's
+          if (rank == 0 && it >= P_STAGES) mbar_arrive_cluster(cluster_addr(&empty[s], 1));
+          const uint32_t fb = cluster_addr(&full[s], 0);
+          unsigned char *st = smem + s * H3_STAGE;
+          if (rank == 0) mbar_expect_tx(&full[s], 2 * H3_STAGE);  // both CTAs' bytes
+          const int k0 = (z * p.kb_per_split + i) * H3_BK;
+          if (A_MN) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              tma_2d_pair(st + j * 8192, &tmAh, fb, mr + 64 * j, k0);
+              tma_2d_pair(st + H3_TILE + j * 8192, &tmAl, fb, mr + 64 * j, k0);
+            }
+          } else {
+            tma_2d_pair(st, &tmAh, fb, k0, mr);
+            tma_2d_pair(st + H3_TILE, &tmAl, fb, k0, mr);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              tma_2d_pair(st + 2 * H3_TILE + j * 8192, &tmBh, fb, nr + 64 * j, k0);
+              tma_2d_pair(st + 3 * H3_TILE + j * 8192, &tmBl, fb, nr + 64 * j, k0);
+            }
+          } else {
+            tma_2d_pair(st + 2 * H3_TILE, &tmBh, fb, k0, nr);
+            tma_2d_pair(st + 3 * H3_TILE, &tmBl, fb, k0, nr);
+          }
+          ++issued;
+        }
+      }
+      // The first CTA's barrier counts both CTAs' bytes: never leave while a
+      // copy into either CTA's shared memory is in flight.
+      if (rank == 0) {
+        for (int j = std::max(0, issued - P_STAGES); j < issued; ++j) {
+          if (ld_status(p.status)) mbar_drain(&full[j % P_STAGES], (j / P_STAGES) & 1);
+          else (void)mbar_wait(&full[j % P_STAGES], (j / P_STAGES) & 1, p.status);
+        }
+      }
+    }
+  } else if (!skip && warp == 1) {
+    // ---------------- MMA issuer (first CTA only)
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t idesc =
+          idesc_f16(P_BM, P_BN) | ((A_MN ? 1u : 0u) << 15) | ((B_MN ? 1u : 0u) << 16);
+      int it = 0, gg = 0;
+      bool ok = true;
+      for (int tl = pair; tl < ntiles_total && ok; tl += npairs) {
+        int64_t m0, n0;
+        int z, nk;
+        tile_of(tl, m0, n0, z, nk);
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int s = it % P_STAGES;
+          const uint32_t ph = (it / P_STAGES) & 1;
+          const bool gstart = (i % H3_PROMOTE) == 0;
+          const int b = gg & 1;
+          if (gstart && !mbar_wait(&pempty[b], ((gg >> 1) & 1) ^ 1, p.status)) { ok = false; break; }
+          if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t ah = su32(smem + s * H3_STAGE);
+          const uint32_t al = ah + H3_TILE, bh = ah + 2 * H3_TILE, bl = ah + 3 * H3_TILE;
+          const uint32_t t_acc = tmem + (uint32_t)(b * P_ACC_COLS);
+#pragma unroll
+          for (int kk = 0; kk < H3_BK / 16; ++kk) {
+            const uint32_t oa = A_MN ? kk * 2048 : kk * 32, ob = B_MN ? kk * 2048 : kk * 32;
+            const uint32_t la = A_MN ? 8192 : 16, lb = B_MN ? 8192 : 16;
+            const uint64_t dAh = sdesc(ah + oa, la, 1024, 2), dAl = sdesc(al + oa, la, 1024, 2);
+            const uint64_t dBh = sdesc(bh + ob, lb, 1024, 2), dBl = sdesc(bl + ob, lb, 1024, 2);
+            const uint32_t acc = (gstart && kk == 0) ? 0u : 1u;
+            mma_f16_pair(t_acc, dAh, dBh, idesc, acc);
+            mma_f16_pair(t_acc, dAh, dBl, idesc, 1u);
+            mma_f16_pair(t_acc, dAl, dBh, idesc, 1u);
+          }
+          mma_commit_pair(&empty[s]);
+          if ((i % H3_PROMOTE) == H3_PROMOTE - 1 || i == nk - 1) {
+            mma_commit_pair(&pfull[b]);
+            ++gg;
+          }
+        }
+      }
+      // all issued MMAs complete before the CTAs may leave
+      mma_commit_pair(mdone);
+      if (ld_status(p.status)) mbar_drain(mdone, 0);
+      else (void)mbar_wait(mdone, 0, p.status);
+    }
+  } else if (!skip) {
+    // ---------------- fold finished groups, epilogue per tile (both CTAs)
+    const int e = warp - 2;            // 0..7
+    const int half = e >> 2;           // 128-column half of the tile
+    const int q = warp & 3;            // TMEM lane quarter of this warp
+    const int t = (e & 3) * 32 + lane;  // 0..127 within the half's group
+    const float inv = 1.0f / (pow2_scale(*absmax_a) * pow2_scale(*absmax_b));  // exact: a power of two
+    const uint32_t pe0 = cluster_addr(&pempty[0], 0), pe1 = cluster_addr(&pempty[1], 0);
+    const uint32_t pf0 = cluster_addr(&pfull[0], 1), pf1 = cluster_addr(&pfull[1], 1);
+    int gg = 0;
+    bool ok = true;
+    for (int tl = pair; tl < ntiles_total && ok; tl += npairs) {
+      int64_t m0, n0;
+      int z, nk;
+      tile_of(tl, m0, n0, z, nk);
+      const int ngroups = (nk + H3_PROMOTE - 1) / H3_PROMOTE;
+      float tot[BN];
+#pragma unroll
+      for (int j = 0; j < BN; ++j) tot[j] = 0.f;
+      for (int g = 0; g < ngroups; ++g, ++gg) {
+        const int b = gg & 1;
+        if (!mbar_wait(&pfull[b], (gg >> 1) & 1, p.status)) { ok = false; break; }
+        if (rank == 0 && e == 0 && lane == 0) mbar_arrive_cluster(b ? pf1 : pf0);  // tell the second CTA
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t base =
+            tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * P_ACC_COLS) + (uint32_t)(half * BN);
+#pragma unroll
+        for (int c = 0; c < BN; c += 16) {
+          float v[16];
+          tmem_ld16(base + c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) tot[c + j] += v[j];
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(b ? pe1 : pe0);
+      }
+      if (!ok) break;
+#pragma unroll
+      for (int j = 0; j < BN; ++j) tot[j] *= inv;
+      store_tile_boxes(tot, epi + half * (H3_EPI / 4), &tmC, p, q, lane, t, m0 + 128 * (int64_t)rank,
+                       n0 + (int64_t)half * BN, p.partial ? z : 0, 1 + half);
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncwarp();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA frees TMEM or leaves while the pair's work may touch it
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
 }
 
@@ -1187,10 +1497,43 @@ size_t h3_scratch(int64_t M, int64_t N, int64_t K) {
 int h3_splits(int64_t M, int64_t N, int64_t K, int nsm) {
   return split_count(M, N, (int)((round8(K) + H3_BK - 1) / H3_BK), nsm);
 }
+// 2-SM pair path (HS_H3_PAIR=0 turns it off).
+bool h3_pair_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char *e = getenv("HS_H3_PAIR");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+constexpr int kPairMaxSplits = 16;
+// Split-K count for pair tiles: none when the tiles fill the pairs; else the
+// smallest count whose work units fill whole waves of the pairs to >= 90%
+// (the best one if none does), each split keeping >= 8 k-blocks.
+int pair_split_count(int64_t tiles, int nkb, int npairs) {
+  if (tiles >= npairs || nkb < 16) return 1;
+  const int smax = std::max(1, std::min(kPairMaxSplits, nkb / 8));
+  int best = 1;
+  double best_eff = 0.0;
+  for (int sp = 1; sp <= smax; ++sp) {
+    const int64_t units = tiles * sp;
+    const int64_t waves = (units + npairs - 1) / npairs;
+    const double eff = (double)units / (double)(waves * npairs);
+    if (eff >= 0.9) { best = sp; break; }
+    if (eff > best_eff + 1e-9) { best_eff = eff; best = sp; }
+  }
+  const int kbps = (nkb + best - 1) / best;
+  return (nkb + kbps - 1) / kbps;
+}
 size_t h3_partial_bound(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const int sp = h3_splits(M, N, K, 256);
-  return sp > 1 ? (size_t)sp * M * N * 4 : 0;
+  size_t b = sp > 1 ? (size_t)sp * M * N * 4 : 0;
+  const int nkb = (int)((round8(K) + H3_BK - 1) / H3_BK);
+  const int64_t ptiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
+  if (ptiles < 128 && nkb >= 16)  // any pair count up to 128 (256 SMs)
+    b = std::max(b, (size_t)std::min(kPairMaxSplits, std::max(1, nkb / 8)) * M * N * 4);
+  return b;
 }
 // Map of a split operand stored [rows][ld] fp16.  K-major use (rows = M or
 // N, columns = K): box {64 k, 128 rows}.  MN-major use (rows = K, columns =
@@ -1241,6 +1584,79 @@ int h3_split_known(const float *x, int64_t rows, int64_t cols, int64_t ld, const
   return check_launch("split_h2_kernel");
 }
 
+// Largest number of pairs (clusters of two CTAs) of this kernel variant
+// resident at once on the current device; 0 if none.
+int pair_capacity(const void *fn, int variant) {
+  static std::atomic<int> cached[64][4];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::atomic<int> &c = cached[dev & 63][variant & 3];
+  int v = c.load(std::memory_order_relaxed);
+  if (v > 0) return v - 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (unsigned)device_sms(), 1, 1);
+  cfg.blockDim = dim3(P_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = P_SMEM;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = 0;
+  }
+  c.store(n + 1, std::memory_order_relaxed);
+  return n;
+}
+
+// The pair kernel on already encoded operand maps; *done = false if it does
+// not apply (no pair fits, or a split-K partial would not fit ws).
+int gemm_h3_pair(const CUtensorMap &tah, const CUtensorMap &tal, const CUtensorMap &tbh, const CUtensorMap &tbl,
+                 bool a_mn, bool b_mn, const unsigned *a_absmax, const unsigned *b_absmax, float *C,
+                 const float *bias, int64_t M, int64_t N, int64_t K, int64_t ldc, int beta, void *ws,
+                 size_t ws_bytes, int *status, cudaStream_t st, bool *done) {
+  *done = false;
+  void (*fn)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs,
+             const unsigned *, const unsigned *, int, int, int);
+  if (a_mn) fn = b_mn ? gemm_h3_pair_kernel<true, true> : gemm_h3_pair_kernel<true, false>;
+  else fn = b_mn ? gemm_h3_pair_kernel<false, true> : gemm_h3_pair_kernel<false, false>;
+  const int variant = (a_mn ? 2 : 0) + (b_mn ? 1 : 0);
+  static std::atomic<unsigned long long> attr_set[4];
+  if (int e = allow_dynamic_smem((const void *)fn, P_SMEM, &attr_set[variant])) return e;
+  const int npairs = pair_capacity((const void *)fn, variant);
+  if (npairs < 1) return HS_OK;
+  const int nkb = (int)((round8(K) + H3_BK - 1) / H3_BK);
+  const int64_t mt = (M + P_BM - 1) / P_BM, nt = (N + P_BN - 1) / P_BN;
+  int splits = pair_split_count(mt * nt, nkb, npairs);
+  if (splits > 1 && (!ws || !aligned(ws, 256) || ws_bytes < (size_t)splits * M * N * 4)) splits = 1;
+  const int kbps = (nkb + splits - 1) / splits;
+  splits = (nkb + kbps - 1) / kbps;
+  float *partial = splits > 1 ? static_cast<float *>(ws) : nullptr;
+  CUtensorMap tc;
+  if (!make_out_map(&tc, splits > 1 ? partial : C, splits, M, N, splits > 1 ? N : ldc)) return HS_OK;
+  const int64_t ntot = mt * nt * splits;
+  if (ntot >= (1ll << 30)) return HS_OK;
+  const unsigned grid = 2u * (unsigned)std::min<int64_t>(ntot, npairs);
+  TcArgs args;
+  args.C = C;
+  args.bias = bias;
+  args.partial = partial;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.ldc = ldc;
+  args.beta = beta;
+  args.kb_per_split = kbps;
+  args.nkb = nkb;
+  args.status = status;
+  fn<<<grid, P_THREADS, P_SMEM, st>>>(tah, tal, tbh, tbl, tc, args, a_absmax, b_absmax, (int)mt, (int)nt, (int)ntot);
+  if (int e = check_launch("gemm_h3_pair_kernel")) return e;
+  if (splits > 1) {
+    const int64_t n = M * N;
+    splitk_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(partial, C, bias, M, N, ldc, splits, beta);
+    if (int e = check_launch("splitk_reduce_kernel")) return e;
+  }
+  *done = true;
+  return HS_OK;
+}
+
 // C[M,N] = A.B^T over K (+bias, beta) from split operands.  A is stored
 // [M][.] (a_mn false, K-major) or [K][.] (a_mn true); B likewise with N.
 // Scratch (split-K partials, if any) from ws; *done = false if the shape or
@@ -1263,11 +1679,21 @@ int gemm_h3_presplit(const void *a_split, const unsigned *a_absmax, bool a_mn, c
   const int64_t b_rows = b_mn ? K : N, b_ld = b_mn ? N8 : K8;
   const __half *al = ah + a_rows * a_ld;
   const __half *bl = bh + b_rows * b_ld;
-  float *partial = splits > 1 ? static_cast<float *>(ws) : nullptr;
   CUtensorMap tah, tal, tbh, tbl, tc;
   if (!make_map_f16(&tah, ah, a_rows, a_ld, a_mn) || !make_map_f16(&tal, al, a_rows, a_ld, a_mn) ||
       !make_map_f16(&tbh, bh, b_rows, b_ld, b_mn) || !make_map_f16(&tbl, bl, b_rows, b_ld, b_mn))
     return HS_OK;
+  if (h3_pair_enabled()) {
+    bool pdone = false;
+    if (int e = gemm_h3_pair(tah, tal, tbh, tbl, a_mn, b_mn, a_absmax, b_absmax, C, bias, M, N, K, ldc, beta, ws,
+                             ws_bytes, status, st, &pdone))
+      return e;
+    if (pdone) {
+      *done = true;
+      return HS_OK;
+    }
+  }
+  float *partial = splits > 1 ? static_cast<float *>(ws) : nullptr;
   if (!make_out_map(&tc, splits > 1 ? partial : C, splits, M, N, splits > 1 ? N : ldc)) return HS_OK;
   const int nkb = (int)((K8 + H3_BK - 1) / H3_BK);
   const int kbps = (nkb + splits - 1) / splits;
