@@ -1081,9 +1081,26 @@ gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__
 // passes on "accumulator ready" likewise; every fold warp of both CTAs
 // arrives on the first CTA's "accumulator free" barrier.  Every wait is
 // bounded.
-constexpr int P_STAGES = 3;
+// k-block depth: 64 fp16 (128-byte rows, 128-byte swizzle, 3 stages) or 32
+// (64-byte rows and swizzle, 6 stages: the same ring bytes in finer steps).
+#ifndef HS_P_BK
+#define HS_P_BK 64
+#endif
+constexpr int P_BK = HS_P_BK;
+static_assert(P_BK == 64 || P_BK == 32, "pair k-block depth");
+constexpr int P_ROWB = P_BK * 2;                     // bytes per operand row (K-major)
+constexpr int P_TILE = 128 * P_BK * 2;               // bytes per operand part per CTA
+constexpr int P_STAGE = 4 * P_TILE;                  // Ah, Al, Bh, Bl
+constexpr int P_STAGES = P_BK == 64 ? 3 : 6;
+constexpr int P_PROMOTE = H3_PROMOTE * 64 / P_BK;    // same k per accumulator group
+constexpr uint32_t P_LAYOUT = P_BK == 64 ? 2u : 4u;  // descriptor swizzle: 128 B or 64 B
+constexpr uint32_t P_SBO = 8 * P_ROWB;               // 8-row core-matrix groups
+// MN-major parts: boxes of P_BK M/N elements (one swizzle row) x P_BK k rows,
+// 128 / P_BK of them side by side.
+constexpr int P_MN_BOX = P_BK * P_BK * 2;
+constexpr int P_MN_NBOX = 128 / P_BK;
 constexpr int P_THREADS = 320;                       // producer, MMA, 8 fold/epilogue warps
-constexpr int P_SMEM = P_STAGES * H3_STAGE + 2 * H3_EPI + 1024 + 256;
+constexpr int P_SMEM = P_STAGES * P_STAGE + 2 * H3_EPI + 1024 + 256;
 static_assert(P_SMEM <= 232448, "shared memory per block");
 constexpr int P_BM = 256, P_BN = 256;                // pair tile
 constexpr uint32_t P_ACC_COLS = 256;                 // one accumulator buffer
@@ -1136,8 +1153,8 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
                     const unsigned *absmax_b, int mtiles, int ntiles, int ntiles_total) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float *epi = reinterpret_cast<float *>(smem + P_STAGES * H3_STAGE);  // two 16 KB boxes
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + P_STAGES * H3_STAGE + 2 * H3_EPI);
+  float *epi = reinterpret_cast<float *>(smem + P_STAGES * P_STAGE);  // two 16 KB boxes
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE + 2 * H3_EPI);
   uint64_t *empty = full + P_STAGES;
   uint64_t *pfull = empty + P_STAGES;
   uint64_t *pempty = pfull + 2;
@@ -1202,28 +1219,28 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
           // second CTA first, so that its loads start with this CTA's
           if (rank == 0 && it >= P_STAGES) mbar_arrive_cluster(cluster_addr(&empty[s], 1));
           const uint32_t fb = cluster_addr(&full[s], 0);
-          unsigned char *st = smem + s * H3_STAGE;
-          if (rank == 0) mbar_expect_tx(&full[s], 2 * H3_STAGE);  // both CTAs' bytes
-          const int k0 = (z * p.kb_per_split + i) * H3_BK;
+          unsigned char *st = smem + s * P_STAGE;
+          if (rank == 0) mbar_expect_tx(&full[s], 2 * P_STAGE);  // both CTAs' bytes
+          const int k0 = (z * p.kb_per_split + i) * P_BK;
           if (A_MN) {
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              tma_2d_pair(st + j * 8192, &tmAh, fb, mr + 64 * j, k0);
-              tma_2d_pair(st + H3_TILE + j * 8192, &tmAl, fb, mr + 64 * j, k0);
+            for (int j = 0; j < P_MN_NBOX; ++j) {
+              tma_2d_pair(st + j * P_MN_BOX, &tmAh, fb, mr + P_BK * j, k0);
+              tma_2d_pair(st + P_TILE + j * P_MN_BOX, &tmAl, fb, mr + P_BK * j, k0);
             }
           } else {
             tma_2d_pair(st, &tmAh, fb, k0, mr);
-            tma_2d_pair(st + H3_TILE, &tmAl, fb, k0, mr);
+            tma_2d_pair(st + P_TILE, &tmAl, fb, k0, mr);
           }
           if (B_MN) {
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              tma_2d_pair(st + 2 * H3_TILE + j * 8192, &tmBh, fb, nr + 64 * j, k0);
-              tma_2d_pair(st + 3 * H3_TILE + j * 8192, &tmBl, fb, nr + 64 * j, k0);
+            for (int j = 0; j < P_MN_NBOX; ++j) {
+              tma_2d_pair(st + 2 * P_TILE + j * P_MN_BOX, &tmBh, fb, nr + P_BK * j, k0);
+              tma_2d_pair(st + 3 * P_TILE + j * P_MN_BOX, &tmBl, fb, nr + P_BK * j, k0);
             }
           } else {
-            tma_2d_pair(st + 2 * H3_TILE, &tmBh, fb, k0, nr);
-            tma_2d_pair(st + 3 * H3_TILE, &tmBl, fb, k0, nr);
+            tma_2d_pair(st + 2 * P_TILE, &tmBh, fb, k0, nr);
+            tma_2d_pair(st + 3 * P_TILE, &tmBl, fb, k0, nr);
           }
           ++issued;
         }
@@ -1251,27 +1268,29 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
         for (int i = 0; i < nk; ++i, ++it) {
           const int s = it % P_STAGES;
           const uint32_t ph = (it / P_STAGES) & 1;
-          const bool gstart = (i % H3_PROMOTE) == 0;
+          const bool gstart = (i % P_PROMOTE) == 0;
           const int b = gg & 1;
           if (gstart && !mbar_wait(&pempty[b], ((gg >> 1) & 1) ^ 1, p.status)) { ok = false; break; }
           if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t ah = su32(smem + s * H3_STAGE);
-          const uint32_t al = ah + H3_TILE, bh = ah + 2 * H3_TILE, bl = ah + 3 * H3_TILE;
+          const uint32_t ah = su32(smem + s * P_STAGE);
+          const uint32_t al = ah + P_TILE, bh = ah + 2 * P_TILE, bl = ah + 3 * P_TILE;
           const uint32_t t_acc = tmem + (uint32_t)(b * P_ACC_COLS);
 #pragma unroll
-          for (int kk = 0; kk < H3_BK / 16; ++kk) {
-            const uint32_t oa = A_MN ? kk * 2048 : kk * 32, ob = B_MN ? kk * 2048 : kk * 32;
-            const uint32_t la = A_MN ? 8192 : 16, lb = B_MN ? 8192 : 16;
-            const uint64_t dAh = sdesc(ah + oa, la, 1024, 2), dAl = sdesc(al + oa, la, 1024, 2);
-            const uint64_t dBh = sdesc(bh + ob, lb, 1024, 2), dBl = sdesc(bl + ob, lb, 1024, 2);
+          for (int kk = 0; kk < P_BK / 16; ++kk) {
+            // K-major: 16 fp16 = 32 bytes into each row; MN-major: the next 16
+            // k rows; LBO = one box between M/N blocks.
+            const uint32_t oa = A_MN ? kk * 16 * P_ROWB : kk * 32, ob = B_MN ? kk * 16 * P_ROWB : kk * 32;
+            const uint32_t la = A_MN ? P_MN_BOX : 16, lb = B_MN ? P_MN_BOX : 16;
+            const uint64_t dAh = sdesc(ah + oa, la, P_SBO, P_LAYOUT), dAl = sdesc(al + oa, la, P_SBO, P_LAYOUT);
+            const uint64_t dBh = sdesc(bh + ob, lb, P_SBO, P_LAYOUT), dBl = sdesc(bl + ob, lb, P_SBO, P_LAYOUT);
             const uint32_t acc = (gstart && kk == 0) ? 0u : 1u;
             mma_f16_pair(t_acc, dAh, dBh, idesc, acc);
             mma_f16_pair(t_acc, dAh, dBl, idesc, 1u);
             mma_f16_pair(t_acc, dAl, dBh, idesc, 1u);
           }
           mma_commit_pair(&empty[s]);
-          if ((i % H3_PROMOTE) == H3_PROMOTE - 1 || i == nk - 1) {
+          if ((i % P_PROMOTE) == P_PROMOTE - 1 || i == nk - 1) {
             mma_commit_pair(&pfull[b]);
             ++gg;
           }
@@ -1297,7 +1316,7 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
       int64_t m0, n0;
       int z, nk;
       tile_of(tl, m0, n0, z, nk);
-      const int ngroups = (nk + H3_PROMOTE - 1) / H3_PROMOTE;
+      const int ngroups = (nk + P_PROMOTE - 1) / P_PROMOTE;
       float tot[BN];
 #pragma unroll
       for (int j = 0; j < BN; ++j) tot[j] = 0.f;
@@ -1529,7 +1548,7 @@ size_t h3_partial_bound(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const int sp = h3_splits(M, N, K, 256);
   size_t b = sp > 1 ? (size_t)sp * M * N * 4 : 0;
-  const int nkb = (int)((round8(K) + H3_BK - 1) / H3_BK);
+  const int nkb = (int)((round8(K) + P_BK - 1) / P_BK);
   const int64_t ptiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
   if (ptiles < 128 && nkb >= 16)  // any pair count up to 128 (256 SMs)
     b = std::max(b, (size_t)std::min(kPairMaxSplits, std::max(1, nkb / 8)) * M * N * 4);
@@ -1548,6 +1567,20 @@ bool make_map_f16(CUtensorMap *tm, const __half *ptr, int64_t rows, int64_t ld, 
   return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)ptr, dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The pair kernel's maps: K-major box {P_BK k, 128 rows}, MN-major box
+// {P_BK columns, P_BK k rows}, swizzled to the row width (128 or 64 bytes).
+bool make_map_f16_pair(CUtensorMap *tm, const __half *ptr, int64_t rows, int64_t ld, bool mn) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)P_BK, mn ? (cuuint32_t)P_BK : 128u};
+  cuuint32_t es[2] = {1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)ptr, dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, P_BK == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -1608,11 +1641,15 @@ int pair_capacity(const void *fn, int variant) {
 
 // The pair kernel on already encoded operand maps; *done = false if it does
 // not apply (no pair fits, or a split-K partial would not fit ws).
-int gemm_h3_pair(const CUtensorMap &tah, const CUtensorMap &tal, const CUtensorMap &tbh, const CUtensorMap &tbl,
-                 bool a_mn, bool b_mn, const unsigned *a_absmax, const unsigned *b_absmax, float *C,
-                 const float *bias, int64_t M, int64_t N, int64_t K, int64_t ldc, int beta, void *ws,
-                 size_t ws_bytes, int *status, cudaStream_t st, bool *done) {
+int gemm_h3_pair(const __half *ah, const __half *al, int64_t a_rows, int64_t a_ld, bool a_mn, const __half *bh,
+                 const __half *bl, int64_t b_rows, int64_t b_ld, bool b_mn, const unsigned *a_absmax,
+                 const unsigned *b_absmax, float *C, const float *bias, int64_t M, int64_t N, int64_t K, int64_t ldc,
+                 int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st, bool *done) {
   *done = false;
+  CUtensorMap tah, tal, tbh, tbl;
+  if (!make_map_f16_pair(&tah, ah, a_rows, a_ld, a_mn) || !make_map_f16_pair(&tal, al, a_rows, a_ld, a_mn) ||
+      !make_map_f16_pair(&tbh, bh, b_rows, b_ld, b_mn) || !make_map_f16_pair(&tbl, bl, b_rows, b_ld, b_mn))
+    return HS_OK;
   void (*fn)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs,
              const unsigned *, const unsigned *, int, int, int);
   if (a_mn) fn = b_mn ? gemm_h3_pair_kernel<true, true> : gemm_h3_pair_kernel<true, false>;
@@ -1622,7 +1659,7 @@ int gemm_h3_pair(const CUtensorMap &tah, const CUtensorMap &tal, const CUtensorM
   if (int e = allow_dynamic_smem((const void *)fn, P_SMEM, &attr_set[variant])) return e;
   const int npairs = pair_capacity((const void *)fn, variant);
   if (npairs < 1) return HS_OK;
-  const int nkb = (int)((round8(K) + H3_BK - 1) / H3_BK);
+  const int nkb = (int)((round8(K) + P_BK - 1) / P_BK);
   const int64_t mt = (M + P_BM - 1) / P_BM, nt = (N + P_BN - 1) / P_BN;
   int splits = pair_split_count(mt * nt, nkb, npairs);
   if (splits > 1 && (!ws || !aligned(ws, 256) || ws_bytes < (size_t)splits * M * N * 4)) splits = 1;
@@ -1685,8 +1722,8 @@ int gemm_h3_presplit(const void *a_split, const unsigned *a_absmax, bool a_mn, c
     return HS_OK;
   if (h3_pair_enabled()) {
     bool pdone = false;
-    if (int e = gemm_h3_pair(tah, tal, tbh, tbl, a_mn, b_mn, a_absmax, b_absmax, C, bias, M, N, K, ldc, beta, ws,
-                             ws_bytes, status, st, &pdone))
+    if (int e = gemm_h3_pair(ah, al, a_rows, a_ld, a_mn, bh, bl, b_rows, b_ld, b_mn, a_absmax, b_absmax, C, bias, M,
+                             N, K, ldc, beta, ws, ws_bytes, status, st, &pdone))
       return e;
     if (pdone) {
       *done = true;

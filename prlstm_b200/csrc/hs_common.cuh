@@ -74,9 +74,20 @@ HS_DEV float tanh_pos(float c) {
   return __fdividef(1.0f - e, 1.0f + e);
 }
 
+// The hardware reciprocal alone (about 1 ulp; +inf gives 0).  Enough where
+// a value's rounding does not compound over time steps: the input and output
+// gates and i*g enter each cell state once, while the forget gate multiplies
+// every later state and keeps the refined reciprocal (sigf).
+HS_DEV float rcp_fast(float d) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  return r;
+}
+HS_DEV float sig_fast(float x) { return rcp_fast(1.0f + __expf(-x)); }
+
 // sigma(x) * sigma(y) with one reciprocal: 1 / ((1 + e^-x)(1 + e^-y)).  An
 // infinite denominator gives 0, a NaN stays NaN.
-HS_DEV float sig2(float x, float y) { return rcp_nr((1.0f + __expf(-x)) * (1.0f + __expf(-y))); }
+HS_DEV float sig2(float x, float y) { return rcp_fast((1.0f + __expf(-x)) * (1.0f + __expf(-y))); }
 
 // sigma(z) * tanh(c) for c >= 0 from eo = e^-z, with one reciprocal:
 // poly(c) / (1 + eo) below 0.25 (odd Taylor series of tanh, as tanh_pos) and
@@ -95,7 +106,7 @@ HS_DEV float sig_tanh_pos(float eo, float c) {
     num = 1.0f - e;
     den = (1.0f + e) * (1.0f + eo);
   }
-  return num * rcp_nr(den);
+  return num * rcp_fast(den);
 }
 
 // ---------------------------------------------------------------- memory model

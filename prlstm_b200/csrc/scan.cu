@@ -361,7 +361,7 @@ scan_bwd_kernel(const float *z, const float *__restrict__ cbuf, const float *__r
           float d = r[160];
           if (t == T - 1 && dh_n) d += dh_n[b * H + h];
           const float cp = s > 0 ? r[128 - kBwdRow] : c_init;
-          const float i = sigf(r[0]), f = sigf(r[32]), g = sigf(r[64]), o = sigf(r[96]);
+          const float i = sig_fast(r[0]), f = sigf(r[32]), g = sig_fast(r[64]), o = sig_fast(r[96]);
           const float th = tanh_pos(r[128]);
           const float mb = (i * g >= eps) ? 1.f : 0.f;
           const float mf = (f >= eps) ? 1.f : 0.f;

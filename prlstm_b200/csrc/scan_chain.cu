@@ -21,6 +21,8 @@
 // floats are 128-byte aligned segments: every warp access is one full line.
 // Per (t,b,h) element the forward moves its 24 algorithmic bytes and the
 // backward its 40, plus one c row per backward chunk (c_{t0-1}).
+#include <type_traits>
+
 #include "hs_common.cuh"
 
 namespace hs {
@@ -166,20 +168,28 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
     const int n = (int)min((int64_t)kFL, T - t0);
     float fp[kFL], bp[kFL], eo[kFL];  // f', b', e^-z_o
     float A = 1.f, C = 0.f;
+    // Full chunks (all but a sequence's last one, every lane valid) take a
+    // copy of the step loops without per-step conditions.
+    const bool full = n == kFL && hv;
+    auto coeffs = [&](auto full_tag) {
 #pragma unroll
-    for (int s = 0; s < kFL; ++s) {
-      fp[s] = 1.f;
-      bp[s] = 0.f;
-      eo[s] = 0.f;
-      if (s < n && hv) {
-        const float *r = buf + s * kFRow + lane;
-        fp[s] = fmaxf(sigf(r[32]), eps);
-        bp[s] = fmaxf(sig2(r[0], r[64]), eps);
-        eo[s] = __expf(-r[96]);
-        C = fmaf(fp[s], C, bp[s]);
-        A *= fp[s];
+      for (int s = 0; s < kFL; ++s) {
+        if (decltype(full_tag)::value || (s < n && hv)) {
+          const float *r = buf + s * kFRow + lane;
+          fp[s] = fmaxf(sigf(r[32]), eps);
+          bp[s] = fmaxf(sig2(r[0], r[64]), eps);
+          eo[s] = __expf(-r[96]);
+          C = fmaf(fp[s], C, bp[s]);
+          A *= fp[s];
+        } else {
+          fp[s] = 1.f;
+          bp[s] = 0.f;
+          eo[s] = 0.f;
+        }
       }
-    }
+    };
+    if (full) coeffs(std::true_type{});
+    else coeffs(std::false_type{});
     __syncwarp();  // every lane has read the buffer before it is refilled
     if (c + 2 * kFNW < nchunk) stage(c + 2 * kFNW, buf);
     commit();
@@ -191,17 +201,19 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
       float cc = cin, o = 0.f;
       float *ob = out + (t0 * B + b) * H + h;
       float *cb = cbuf + (t0 * B + b) * H + h;
+      auto emit = [&](auto full_tag) {
 #pragma unroll
-      for (int s = 0; s < kFL; ++s) {
-        if (s < n) {
-          cc = fmaf(fp[s], cc, bp[s]);
-          o = sig_tanh_pos(eo[s], cc);
-          __stcs(cb, cc);
-          __stcs(ob, o);
-          cb += ostep;
-          ob += ostep;
+        for (int s = 0; s < kFL; ++s) {
+          if (decltype(full_tag)::value || s < n) {
+            cc = fmaf(fp[s], cc, bp[s]);
+            o = sig_tanh_pos(eo[s], cc);
+            __stcs(cb + s * ostep, cc);
+            __stcs(ob + s * ostep, o);
+          }
         }
-      }
+      };
+      if (full) emit(std::true_type{});
+      else emit(std::false_type{});
       if (t0 + n == T) {  // the chunk that ends the sequence
         if (c_n) c_n[b * H + h] = cc;
         if (h_n) h_n[b * H + h] = o;
@@ -291,6 +303,8 @@ scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float 
     float FP[kBL], DCD[kBL], KI[kBL], KF[kBL], KG[kBL];
     float A = 1.f, C = 0.f;
     float *dzs = dz + (t0 * B + b) * 4 * H + h;  // dz row of step t0, unit h
+    // (A condition-free copy of the step loops for full chunks, as in the
+    // forward, measured slower here.)
 #pragma unroll
     for (int s = kBL - 1; s >= 0; --s) {
       FP[s] = 1.f;
@@ -299,7 +313,7 @@ scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float 
         const float *r = buf + s * kBRow + lane;
         const float d = r[160];
         const float cp = s > 0 ? r[128 - kBRow] : (t0 > 0 ? buf[kBL * kBRow + lane] : c0p);
-        const float ig = sigf(r[0]), f = sigf(r[32]), g = sigf(r[64]), o = sigf(r[96]);
+        const float ig = sig_fast(r[0]), f = sigf(r[32]), g = sig_fast(r[64]), o = sig_fast(r[96]);
         const float th = tanh_pos(r[128]);
         const float mb = (ig * g >= eps) ? 1.f : 0.f;
         const float mf = (f >= eps) ? 1.f : 0.f;
