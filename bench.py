@@ -188,9 +188,16 @@ class ParallelStep:
         self.dW_mb = torch.empty(4 * H, D, device=dev)
         self.db_mb = torch.empty(4 * H, device=dev)
         lib = _lib.load()
-        self.ws = _lib.workspace(lib.hs_parallel_workspace_bytes(T, mb, D, H), dev)
+        M = T * mb
+        self.ws = _lib.workspace(max(lib.hs_parallel_workspace_bytes(T, mb, D, H),
+                                     lib.hs_scan_split_workspace_bytes(T, mb, H),
+                                     lib.hs_linear_presplit_workspace_bytes(M, 4 * H, D)), dev)
         self.status = _lib.status_word(dev)
-        self.dz_absmax = torch.zeros(64, dtype=torch.int32, device=dev)  # max |dz| bits, word 0
+        # dZ travels from the scan backward to the gradient GEMMs as its fp16
+        # split (hi, lo) with one scale word; the forward's max c feeds the
+        # split scale's bound
+        self.dz_split = torch.empty(lib.hs_split_bytes(M, 4 * H), dtype=torch.uint8, device=dev)
+        self.words = torch.zeros(64, dtype=torch.int32, device=dev)  # [0] max c, [16] dZ scale
         self.names = ("proj_gemm", "scan_fwd", "scan_bwd", "linear_bwd")
         self.ms = {n: 0.0 for n in self.names}
         self.launches = 0
@@ -211,25 +218,28 @@ class ParallelStep:
                    P(self.ws), self.ws.numel(), P(self.status), st)
             if record:
                 e[1].record()
-            L.call("hs_scan_forward", P(self.z), P(self.c0), P(self.out), P(self.c), P(self.h_n),
-                   P(self.c_n), T, mb, H, 1e-6, P(self.ws), self.ws.numel(), P(self.status), st)
+            cmax, dz_scale = P(self.words[0:]), P(self.words[16:])
+            L.call("hs_scan_forward_kf", P(self.z), P(self.c0), P(self.out), P(self.c), P(self.h_n),
+                   P(self.c_n), T, mb, H, 1e-6, P(self.ws), self.ws.numel(), cmax, P(self.status), st)
             if record:
                 e[2].record()
-            # the scan backward also yields max |dz| for the split of dz below
-            L.call("hs_scan_backward_absmax", P(self.z), P(self.c), P(self.c0), P(Gs), None, None,
-                   P(self.z), None, P(self.db_mb), T, mb, H, 1e-6, P(self.ws), self.ws.numel(),
-                   P(self.dz_absmax), P(self.status), st)
+            # the scan backward writes dZ as the fp16 split the GEMMs read
+            L.call("hs_scan_backward_split", P(self.z), P(self.c), P(self.c0), P(Gs), None, None, cmax,
+                   P(self.dz_split), dz_scale, None, P(self.db_mb), T, mb, H, 1e-6, P(self.ws),
+                   self.ws.numel(), P(self.status), st)
             if record:
                 e[3].record()
             # dX and dW_ih (accumulated over micro-batches) in one call
-            L.call("hs_linear_backward_absmax", P(self.z), P(xs), P(self.W_ih), P(self.dx), P(self.dW), M,
-                   4 * H, D, 1 if i else 0, P(self.dz_absmax), P(self.ws), self.ws.numel(), P(self.status), st)
+            L.call("hs_linear_backward_presplit", P(self.dz_split), dz_scale, P(xs), P(self.W_ih), P(self.dx),
+                   P(self.dW), M, 4 * H, D, 1 if i else 0, P(self.ws), self.ws.numel(), P(self.status), st)
             if record:
                 e[4].record()
             self.db.add_(self.db_mb) if i else self.db.copy_(self.db_mb)
-            # projection: 2 absmax + 2 split + GEMM; scans: 2 + rowsum; backward:
-            # 2 absmax + 3 split + 2 GEMMs
-            self.launches += 5 + 3 + 7
+            # projection: 2 absmax + 2 split + GEMM; scan forward 1; scan
+            # backward: bound (3), scan, rowsum, check, conditional re-run and
+            # split (2, return at once unless needed); backward GEMMs: 2
+            # absmax + 2 split + 2 GEMMs + split-K reduce
+            self.launches += 5 + 1 + 8 + 7
             if record:
                 evs.append(e)
         return evs

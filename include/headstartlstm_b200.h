@@ -120,6 +120,20 @@ HS_API int hs_linear_backward_absmax(const float *dy, const float *x, const floa
                                      float *dw, int64_t M, int64_t N, int64_t K, int beta,
                                      const unsigned *dy_absmax, void *workspace,
                                      size_t workspace_bytes, int *dev_status, hs_stream_t stream);
+/* Bytes of an fp16 split buffer of a [rows][cols] float32 matrix: hi then
+ * lo, each [rows][cols rounded up to 8] fp16. */
+HS_API size_t hs_split_bytes(int64_t rows, int64_t cols);
+/* hs_linear_backward with dy given only as its fp16 split (dy_split, as
+ * hs_scan_backward_split writes it; N % 8 == 0) and its scale word dy_scale
+ * (float32 bits of an upper bound of max |dy|).  No float32 dy is read, so
+ * there is no fallback: shapes the tensor-core path does not take, or a
+ * workspace below hs_linear_presplit_workspace_bytes(M, N, K), return an
+ * error.  Same replacement as hs_linear_backward (_torch.py:157-162). */
+HS_API size_t hs_linear_presplit_workspace_bytes(int64_t M, int64_t N, int64_t K);
+HS_API int hs_linear_backward_presplit(const void *dy_split, const unsigned *dy_scale, const float *x,
+                                       const float *w, float *dx, float *dw, int64_t M, int64_t N, int64_t K,
+                                       int beta, void *workspace, size_t workspace_bytes, int *dev_status,
+                                       hs_stream_t stream);
 /* db[N] = beta * db + sum_m dy[m, N]   (beta is 0 or 1) */
 HS_API int hs_colsum(const float *dy, float *db, int64_t M, int64_t N, int beta,
               hs_stream_t stream);
@@ -163,6 +177,33 @@ HS_API int hs_scan_backward_absmax(const float *z, const float *c, const float *
                                    float *dz, float *dc0, float *db, int64_t T, int64_t B,
                                    int64_t H, float eps, void *workspace, size_t workspace_bytes,
                                    unsigned *dz_absmax, int *dev_status, hs_stream_t stream);
+
+/* hs_scan_forward that also writes *kf_max (device memory) = the maximum
+ * over all steps of c_{t-1} f'_t (1 - f'_t) (c_{-1} = max(c0, eps),
+ * f' = max(sigmoid(z_f), eps)) as float32 bits: the forget-gate factor of
+ * the bound on |dZ| that hs_scan_backward_split uses.  Same replacement as
+ * hs_scan_forward. */
+HS_API int hs_scan_forward_kf(const float *z, const float *c0, float *out, float *c, float *h_n,
+                                  float *c_n, int64_t T, int64_t B, int64_t H, float eps,
+                                  void *workspace, size_t workspace_bytes, unsigned *kf_max,
+                                  int *dev_status, hs_stream_t stream);
+/* The scan backward with dZ delivered as its fp16 split for the gradient
+ * GEMMs (hs_linear_backward_presplit) instead of float32: dz_split (16-byte
+ * aligned, hs_split_bytes(T*B, 4H) bytes) receives hi then lo, *dz_scale the
+ * scale word.  The scale is chosen before the scan from an upper bound of
+ * max |dZ|: D x max(1/4, Kf), D the largest column sum of |dout| (with
+ * |dh_n| + |dc_n|) and Kf the forward's kf_max; the scan writes the split
+ * directly, so dZ is never stored in float32.  If the bound turns out more than 2^16 above the exact maximum
+ * (or anything is not finite), the scan runs again into float32 dZ in place
+ * of z and the split is made from the exact maximum (z is overwritten then).
+ * Replaces, with the GEMMs after it, the autograd backward of
+ * headstartlstm_parallel (_parallel.py:38-74). */
+HS_API size_t hs_scan_split_workspace_bytes(int64_t T, int64_t B, int64_t H);
+HS_API int hs_scan_backward_split(float *z, const float *c, const float *c0, const float *dout,
+                                  const float *dh_n, const float *dc_n, const unsigned *kf_max,
+                                  void *dz_split, unsigned *dz_scale, float *dc0, float *db, int64_t T,
+                                  int64_t B, int64_t H, float eps, void *workspace,
+                                  size_t workspace_bytes, int *dev_status, hs_stream_t stream);
 
 /* hs_scan_forward without a workspace argument, for callers that cannot
  * allocate device memory (for example a host framework that passes the

@@ -44,6 +44,9 @@ SIGNATURES = {
     "hs_linear_wgrad": (_i32, [_c_p] * 3 + [_i64] * 3 + [_i32, _c_p, _sz, _c_p, _c_p]),
     "hs_linear_backward": (_i32, [_c_p] * 5 + [_i64] * 3 + [_i32, _c_p, _sz, _c_p, _c_p]),
     "hs_linear_backward_absmax": (_i32, [_c_p] * 5 + [_i64] * 3 + [_i32, _c_p, _c_p, _sz, _c_p, _c_p]),
+    "hs_split_bytes": (_sz, [_i64] * 2),
+    "hs_linear_presplit_workspace_bytes": (_sz, [_i64] * 3),
+    "hs_linear_backward_presplit": (_i32, [_c_p] * 6 + [_i64] * 3 + [_i32, _c_p, _sz, _c_p, _c_p]),
     "hs_colsum": (_i32, [_c_p, _c_p, _i64, _i64, _i32, _c_p]),
     "hs_scan_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "hs_parallel_workspace_bytes": (_sz, [_i64] * 4),
@@ -51,6 +54,9 @@ SIGNATURES = {
     "hs_scan_forward_noalloc": (_i32, [_c_p] * 6 + [_i64] * 3 + [_f32, _c_p, _c_p]),
     "hs_scan_backward": (_i32, [_c_p] * 9 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_scan_backward_absmax": (_i32, [_c_p] * 9 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),
+    "hs_scan_forward_kf": (_i32, [_c_p] * 6 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),
+    "hs_scan_split_workspace_bytes": (_sz, [_i64] * 3),
+    "hs_scan_backward_split": (_i32, [_c_p] * 11 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_parallel_forward": (_i32, [_c_p] * 9 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_parallel_backward": (_i32, [_c_p] * 12 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_recurrent_workspace_bytes": (_sz, [_i64] * 4),

@@ -42,7 +42,7 @@ size_t h3_split_bytes(int64_t rows, int64_t cols);
 int h3_split(const float *x, int64_t rows, int64_t cols, int64_t ld, unsigned *absmax, void *dst,
              cudaStream_t st);
 int h3_split_known(const float *x, int64_t rows, int64_t cols, int64_t ld, const unsigned *absmax, void *dst,
-                   cudaStream_t st);
+                   cudaStream_t st, const int *gate = nullptr);
 int gemm_h3_presplit(const void *a_split, const unsigned *a_absmax, bool a_mn, const void *b_split,
                      const unsigned *b_absmax, bool b_mn, float *C, const float *bias, int64_t M, int64_t N,
                      int64_t K, int64_t ldc, int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st,
@@ -51,7 +51,7 @@ size_t scan_workspace(int64_t T, int64_t B, int64_t H);
 int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st);
 int scan_forward(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
                  int64_t T, int64_t B, int64_t H, float eps, void *ws, size_t ws_bytes,
-                 int *status, cudaStream_t st);
+                 int *status, cudaStream_t st, unsigned *kf_max = nullptr);
 int scan_backward(const float *z, const float *c, const float *c0, const float *dout,
                   const float *dh_n, const float *dc_n, float *dz, float *dc0, float *db,
                   int64_t T, int64_t B, int64_t H, float eps, void *ws, size_t ws_bytes,
@@ -171,6 +171,44 @@ int linear_backward_ex(const float *dy, const float *w, float *dx, const float *
   if (!ddw2)
     if (int e = linear_wgrad(dy, x2, dw2, M, N, K2, beta, ws, ws_bytes, status, st)) return e;
   return HS_OK;
+}
+
+// dx = dy.w and dw = beta*dw + dy^T.x from dy given only as its fp16 split
+// (hi, lo [M][N], N % 8 == 0, scale word dy_scale); *took = false if the
+// tensor-core path does not take the shape or the workspace (nothing can be
+// done without float32 dy).
+int linear_backward_split_only(const void *dy_split, const unsigned *dy_scale, const float *x, const float *w,
+                               float *dx, float *dw, int64_t M, int64_t N, int64_t K, int beta, void *ws,
+                               size_t ws_bytes, int *status, cudaStream_t st, bool *took) {
+  *took = false;
+  if (M <= 0 || N <= 0 || K <= 0 || !x || !w || !dw || !status) return fail(HS_ERR_INVALID_ARG, "linear backward: bad arguments");
+  const size_t sc = 256 + h3_split_bytes(M, K) + h3_split_bytes(N, K);
+  if (!ws || !aligned(ws, 256) || ws_bytes < sc || !aligned(dw, 16) || K % 4 || (dx && !aligned(dx, 16))) return HS_OK;
+  char *w8 = static_cast<char *>(ws);
+  unsigned *am = reinterpret_cast<unsigned *>(w8);
+  char *xs = w8 + 256;
+  char *wsp = xs + h3_split_bytes(M, K);
+  char *tail = w8 + sc;
+  const size_t tb = ws_bytes - sc;
+  bool ddx = dx == nullptr, ddw = false;
+  if (dx) {
+    if (int e = h3_split(w, N, K, K, am + 2, wsp, st)) return e;
+    if (int e = gemm_h3_presplit(dy_split, dy_scale, false, wsp, am + 2, true, dx, nullptr, M, K, N, K, 0, tail, tb,
+                                 status, st, &ddx))
+      return e;
+  }
+  if (int e = h3_split(x, M, K, K, am + 1, xs, st)) return e;
+  if (int e = gemm_h3_presplit(dy_split, dy_scale, true, xs, am + 1, true, dw, nullptr, N, K, M, K, beta, tail, tb,
+                               status, st, &ddw))
+    return e;
+  *took = ddx && ddw;
+  return HS_OK;
+}
+
+size_t linear_backward_split_ws(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  return 256 + h3_split_bytes(M, K) + h3_split_bytes(N, K) +
+         std::max(gemm_h3_partial_bound(M, K, N), gemm_h3_partial_bound(N, K, M));
 }
 
 int linear_backward(const float *dy, const float *x, const float *w, float *dx, float *dw, int64_t M, int64_t N,
@@ -329,6 +367,30 @@ int hs_linear_backward_absmax(const float *dy, const float *x, const float *w, f
     return hs::fail(HS_ERR_INVALID_ARG, "hs_linear_backward_absmax: null or misaligned dy_absmax");
   return hs::linear_backward_ex(dy, w, dx, x, dw, nullptr, nullptr, M, N, K, 0, beta, workspace, workspace_bytes,
                                 dev_status, (cudaStream_t)stream, dy_absmax);
+}
+
+int hs_linear_backward_presplit(const void *dy_split, const unsigned *dy_scale, const float *x, const float *w,
+                                float *dx, float *dw, int64_t M, int64_t N, int64_t K, int beta, void *workspace,
+                                size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
+  if (!dy_split || !dy_scale || !hs::aligned(dy_split, 16) || !hs::aligned(dy_scale, 4))
+    return hs::fail(HS_ERR_INVALID_ARG, "hs_linear_backward_presplit: null or misaligned dy_split/dy_scale");
+  if (N % 8) return hs::fail(HS_ERR_UNSUPPORTED, "hs_linear_backward_presplit: N must be a multiple of 8");
+  if (!hs::gemm_h3_enabled() || !hs::gemm_tc_size_ok(M, N, K))
+    return hs::fail(HS_ERR_UNSUPPORTED, "hs_linear_backward_presplit: the fp16-split GEMMs do not take this shape");
+  bool took = false;
+  if (int e = hs::linear_backward_split_only(dy_split, dy_scale, x, w, dx, dw, M, N, K, beta, workspace,
+                                             workspace_bytes, dev_status, (cudaStream_t)stream, &took))
+    return e;
+  return took ? HS_OK
+              : hs::fail(HS_ERR_WORKSPACE, "hs_linear_backward_presplit: workspace too small or operands unaligned");
+}
+
+size_t hs_linear_presplit_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  return hs::linear_backward_split_ws(M, N, K);
+}
+
+size_t hs_split_bytes(int64_t rows, int64_t cols) {
+  return (rows > 0 && cols > 0) ? hs::h3_split_bytes(rows, cols) : 0;
 }
 
 int hs_linear_wgrad(const float *dy, const float *x, float *dw, int64_t M, int64_t N, int64_t K,

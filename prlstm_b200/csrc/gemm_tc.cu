@@ -719,14 +719,7 @@ gemm_ta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // 2^-39 of the largest element, far under the float32 result's own rounding.
 // The split runs as a separate pass over each operand (absmax, then split),
 // into caller workspace.
-HS_DEV float pow2_scale(unsigned absmax_bits) {
-  const float m = __uint_as_float(absmax_bits);
-  if (!(m > 0.f) || !(m < 3.0e38f)) return 1.0f;  // zero, inf or NaN: no scaling
-  int e;
-  (void)frexpf(m, &e);            // m = f 2^e, f in [0.5, 1): floor(log2 m) = e - 1
-  const int k = max(e - 1, -100);
-  return ldexpf(1.0f, 14 - k);
-}
+// (pow2_scale: hs_common.cuh)
 
 // Rows are taken one warp at a time (warps of the whole grid round-robin),
 // lanes stride over the columns: coalesced, no per-element index division.
@@ -750,7 +743,8 @@ __global__ void absmax_kernel(const float *__restrict__ x, int64_t rows, int64_t
 // 8-byte store per part).
 __global__ void split_h2_kernel(const float *__restrict__ x, int64_t rows, int64_t cols, int64_t ld,
                                 const unsigned *__restrict__ absmax, __half *__restrict__ hi,
-                                __half *__restrict__ lo, int64_t ldo) {
+                                __half *__restrict__ lo, int64_t ldo, const int *gate = nullptr) {
+  if (gate && *gate == 0) return;  // a conditional split that is not needed this time
   const float s = pow2_scale(*absmax);
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -1606,15 +1600,25 @@ int h3_split(const float *x, int64_t rows, int64_t cols, int64_t ld, unsigned *a
 // The same split with *absmax already known: an upper bound of max |x| as
 // float bits (the exact maximum keeps the most precision; anything below it
 // overflows fp16).
+// gate (device memory, may be null): the split runs only if *gate != 0.
 int h3_split_known(const float *x, int64_t rows, int64_t cols, int64_t ld, const unsigned *absmax, void *dst,
-                   cudaStream_t st) {
+                   cudaStream_t st, const int *gate) {
   const int nsm = device_sms();
   const int64_t ldo = round8(cols);
   __half *hi = static_cast<__half *>(dst);
   __half *lo = hi + rows * ldo;
   const int grid = (int)std::min<int64_t>(8 * nsm, (rows + 7) / 8);
-  split_h2_kernel<<<grid, 256, 0, st>>>(x, rows, cols, ld, absmax, hi, lo, ldo);
+  split_h2_kernel<<<grid, 256, 0, st>>>(x, rows, cols, ld, absmax, hi, lo, ldo, gate);
   return check_launch("split_h2_kernel");
+}
+
+// *out = max |x| over a [rows][cols] float32 matrix with row stride ld, as
+// float bits (NaN ignored).
+int absmax_rows(const float *x, int64_t rows, int64_t cols, int64_t ld, unsigned *out, cudaStream_t st) {
+  if (cudaMemsetAsync(out, 0, 4, st) != cudaSuccess) return check_launch("absmax memset");
+  const int grid = (int)std::min<int64_t>(8 * device_sms(), (rows + 7) / 8);
+  absmax_kernel<<<grid, 256, 0, st>>>(x, rows, cols, ld, out);
+  return check_launch("absmax_kernel");
 }
 
 // Largest number of pairs (clusters of two CTAs) of this kernel variant

@@ -22,6 +22,18 @@ int check_launch(const char *what);
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 // ---------------------------------------------------------------- math
+// Power-of-two scale of the 3 x fp16 split: 2^(14 - floor(log2 m)) for
+// m = the float with bits absmax_bits, so that |x| <= m maps into [0, 2^15);
+// 1 for zero, infinite or NaN m.
+HS_DEV float pow2_scale(unsigned absmax_bits) {
+  const float m = __uint_as_float(absmax_bits);
+  if (!(m > 0.f) || !(m < 3.0e38f)) return 1.0f;
+  int e;
+  (void)frexpf(m, &e);  // m = f 2^e, f in [0.5, 1): floor(log2 m) = e - 1
+  const int k = max(e - 1, -100);
+  return ldexpf(1.0f, 14 - k);
+}
+
 // Logistic sigmoid from expf; 1/(1+inf) = 0 keeps the large-negative tail exact.
 HS_DEV float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
 #ifndef HS_SIGF_NR

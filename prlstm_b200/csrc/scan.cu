@@ -38,6 +38,8 @@
 // column kernels of scan_chain.cu run instead (see scan_chain_wanted): they
 // pass the carry between the warps of a CTA through shared memory and need
 // no look-back scratch.
+#include <cuda_fp16.h>
+
 #include <mutex>
 
 #include "hs_common.cuh"
@@ -46,11 +48,16 @@ namespace hs {
 
 bool scan_chain_wanted(int64_t T, int64_t B, int64_t H);
 int scan_fwd_chain_launch(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
-                          int64_t T, int64_t B, int64_t H, float eps, int *status, cudaStream_t st);
+                          int64_t T, int64_t B, int64_t H, float eps, unsigned *kf_max, int *status,
+                          cudaStream_t st);
 int scan_bwd_chain_launch(const float *z, const float *c, const float *c0, const float *dout,
                           const float *dh_n, const float *dc_n, float *dz, float *dc0, float *db_part,
                           int64_t T, int64_t B, int64_t H, float eps, unsigned *dz_absmax, int *status,
-                          cudaStream_t st);
+                          cudaStream_t st, __half *dzh = nullptr, __half *dzl = nullptr,
+                          const unsigned *dz_bound = nullptr, const int *gate = nullptr);
+int h3_split_known(const float *x, int64_t rows, int64_t cols, int64_t ld, const unsigned *absmax, void *dst,
+                   cudaStream_t st, const int *gate);
+size_t h3_split_bytes(int64_t rows, int64_t cols);
 
 namespace {
 
@@ -460,6 +467,25 @@ __global__ void __launch_bounds__(256) rowsum_kernel(const float *__restrict__ p
   }
 }
 
+// *out = max over (t, b, h) of c_{t-1} f'_t (1 - f'_t) (c_{-1} = max(c0, eps),
+// f' = max(sigma(z_f), eps)) as float bits, for the look-back forward (the
+// per-column forward folds it in).
+__global__ void kf_max_kernel(const float *__restrict__ z, const float *__restrict__ c,
+                              const float *__restrict__ c0, int64_t T, int64_t B, int64_t H, float eps,
+                              unsigned *out) {
+  float m = 0.f;
+  const int64_t n = T * B * H, BH = B * H;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / BH, r = i - t * BH, b = r / H, h = r - b * H;
+    const float cp = t > 0 ? c[i - BH] : fmaxf(c0 ? c0[r] : 0.f, eps);
+    const float f = fmaxf(sigf(z[(t * B + b) * 4 * H + H + h]), eps);
+    m = fmaxf(m, cp * f * (1.f - f));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
 bool all_aligned16(std::initializer_list<const void *> ptrs) {
   for (const void *p : ptrs)
     if (p && !aligned(p, 16)) return false;
@@ -492,11 +518,13 @@ size_t scan_workspace(int64_t T, int64_t B, int64_t H) { return scan_ws_bytes(T,
 
 // ------------------------------------------------------------------ host API
 int scan_forward(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n, int64_t T,
-                 int64_t B, int64_t H, float eps, void *ws_base, size_t ws_bytes, int *status, cudaStream_t st) {
+                 int64_t B, int64_t H, float eps, void *ws_base, size_t ws_bytes, int *status, cudaStream_t st,
+                 unsigned *kf_max = nullptr) {
   if (int e = check_scan_args(T, B, H)) return e;
   if (!z || !out || !c || !status) return fail(HS_ERR_INVALID_ARG, "scan_forward: null z/out/c/status");
+  if (kf_max && cudaMemsetAsync(kf_max, 0, 4, st) != cudaSuccess) return check_launch("kf_max memset");
   if (scan_chain_wanted(T, B, H))  // one CTA per column, no scratch
-    return scan_fwd_chain_launch(z, c0, out, c, h_n, c_n, T, B, H, eps, status, st);
+    return scan_fwd_chain_launch(z, c0, out, c, h_n, c_n, T, B, H, eps, kf_max, status, st);
   if (!ws_base || !aligned(ws_base, 256))
     return fail(HS_ERR_INVALID_ARG, "workspace must be non-null and 256-byte aligned");
   const ScanShape sh = make_shape(T, B, H, kFwdL, kFwdWPC);
@@ -512,7 +540,11 @@ int scan_forward(const float *z, const float *c0, float *out, float *c, float *h
     scan_fwd_kernel<true><<<grid, kFwdWPC * 32, kFwdSmem, st>>>(z, c0, out, c, h_n, c_n, sh, eps, ws, status);
   else
     scan_fwd_kernel<false><<<grid, kFwdWPC * 32, kFwdSmem, st>>>(z, c0, out, c, h_n, c_n, sh, eps, ws, status);
-  return check_launch("scan_fwd_kernel");
+  if (int e = check_launch("scan_fwd_kernel")) return e;
+  if (!kf_max) return HS_OK;
+  const int64_t n = T * B * H;
+  kf_max_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 8 * 1024), 256, 0, st>>>(z, c, c0, T, B, H, eps, kf_max);
+  return check_launch("kf_max_kernel");
 }
 
 int scan_backward(const float *z, const float *c, const float *c0, const float *dout, const float *dh_n,
@@ -554,6 +586,169 @@ int scan_backward(const float *z, const float *c, const float *c0, const float *
     rowsum_kernel<<<(unsigned)((N + 31) / 32), 256, 0, st>>>(ws.db_part, db, (int64_t)sh.ngroup * B, N, 0);
     return check_launch("rowsum_kernel");
   }
+  return HS_OK;
+}
+
+// ------------------------------------------------------------------ backward into the fp16 split
+// The gradient GEMMs after the scan take dZ as its 3 x fp16 split, scaled by
+// a power of two chosen from max |dZ|.  Writing the split from the scan
+// itself (instead of float32 dZ and a split pass reading it back) needs the
+// scale before the first element, so it comes from an upper bound:
+//   e_t = sum_{s>=t} (prod f') d_s o_s (1 - tanh^2 c_s)  + (prod f') dc_n,
+// with f' <= 1, so |e_t| <= D = max over columns of sum_t |dout| + |dh_n| +
+// |dc_n|.  The o, i and g components are at most D/4 (sigmoid derivatives
+// are <= 1/4, gates <= 1) and the forget component e c_{t-1} f'(1 - f') at
+// most D Kf, Kf being the forward's maximum of c_{t-1} f'(1 - f') (the cell
+// state is large only where f' is near 1, which that product accounts for).
+// After the scan the exact max |dZ| it
+// folded in is compared with the bound: if the bound was more than 2^16 too
+// large (the small elements would lose bits in fp16's subnormal range), or
+// anything is not finite, the scan runs again into float32 dZ (in place of
+// Z) and the split is made from the exact maximum.  Both re-run kernels
+// return at once when the flag says they are not needed.
+namespace {
+constexpr int kBoundSteps = 256;
+
+// part[j][i] = sum of |dout[t][i]| over steps t of block j (i = b*H + h).
+// V4: four columns per thread with 16-byte loads (BH % 4 == 0, aligned);
+// four steps in flight per thread either way.
+template <bool V4>
+__global__ void dout_colsum_kernel(const float *__restrict__ dout, int64_t T, int64_t BH, float *__restrict__ part) {
+  constexpr int W = V4 ? 4 : 1;
+  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * W;
+  if (i >= BH) return;
+  const int64_t t0 = (int64_t)blockIdx.y * kBoundSteps, t1 = min(T, t0 + kBoundSteps);
+  const float *p = dout + t0 * BH + i;
+  float acc[4][W];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int k = 0; k < W; ++k) acc[u][k] = 0.f;
+  auto add = [&](int u, const float *q) {
+    if constexpr (V4) {
+      const float4 v = __ldcs(reinterpret_cast<const float4 *>(q));
+      acc[u][0] += fabsf(v.x);
+      acc[u][1] += fabsf(v.y);
+      acc[u][2] += fabsf(v.z);
+      acc[u][3] += fabsf(v.w);
+    } else {
+      acc[u][0] += fabsf(__ldcs(q));
+    }
+  };
+  int64_t t = t0;
+  for (; t + 3 < t1; t += 4, p += 4 * BH) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) add(u, p + u * BH);
+  }
+  for (; t < t1; ++t, p += BH) add(0, p);
+#pragma unroll
+  for (int k = 0; k < W; ++k)
+    part[(int64_t)blockIdx.y * BH + i + k] = (acc[0][k] + acc[1][k]) + (acc[2][k] + acc[3][k]);
+}
+
+// words[1] = max over columns of the summed |dout| (+ |dh_n| + |dc_n|) as
+// float bits by atomicMax (zeroed before).  Sums over the step blocks in a
+// fixed order.
+__global__ void dout_bound_kernel(const float *__restrict__ part, int64_t nj, int64_t BH,
+                                  const float *__restrict__ dh_n, const float *__restrict__ dc_n, unsigned *words) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  float d = 0.f;
+  if (i < BH) {
+    for (int64_t j = 0; j < nj; ++j) d += part[j * BH + i];
+    if (dh_n) d += fabsf(dh_n[i]);
+    if (dc_n) d += fabsf(dc_n[i]);
+  }
+  // NaN stays visible: fmaxf would drop it, so it is mapped to +inf first
+  if (d != d) d = __int_as_float(0x7f800000);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) d = fmaxf(d, __shfl_xor_sync(0xffffffffu, d, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(&words[1], __float_as_uint(d));
+}
+
+// words[0] = the bound D x max(1/4, Kf), Kf = the forward's max of
+// c_{t-1} f' (1 - f').
+__global__ void dz_bound_final_kernel(unsigned *words, const unsigned *kf_max) {
+  const float D = __uint_as_float(words[1]);
+  words[0] = __float_as_uint(D * fmaxf(__uint_as_float(*kf_max), 0.25f));
+}
+
+// After the split scan: words[3] = exact max |dZ|.  Sets words[5] (re-run
+// flag) and words[4] (the scale word the GEMMs read: the bound, or the exact
+// maximum when re-running).
+__global__ void dz_check_kernel(unsigned *words) {
+  const float y = __uint_as_float(words[3]) * pow2_scale(words[0]);
+  const bool ok = y >= 0.25f && y < 32768.0f;  // bound at most 2^16 above the maximum, and above it
+  reinterpret_cast<int *>(words)[5] = ok ? 0 : 1;
+  words[4] = ok ? words[0] : words[3];
+}
+}  // namespace
+
+size_t scan_split_ws_bytes(int64_t T, int64_t B, int64_t H) {
+  const int64_t nj = (T + kBoundSteps - 1) / kBoundSteps;
+  return 256 + round_up(scan_ws_bytes(T, B, H), 256) + round_up((size_t)nj * B * H * 4, 256);
+}
+
+// dZ of the scan backward as its fp16 split (hi then lo, [T*B][4H] each) in
+// dz_split, the scale's float bits in *dz_scale; z may be overwritten (the
+// re-run).  kf_max: the forward's max of c_{t-1} f'(1 - f')
+// (hs_scan_forward_kf).
+int scan_backward_split(float *z, const float *c, const float *c0, const float *dout, const float *dh_n,
+                        const float *dc_n, const unsigned *kf_max, void *dz_split, unsigned *dz_scale, float *dc0,
+                        float *db, int64_t T, int64_t B, int64_t H, float eps, void *ws_base, size_t ws_bytes,
+                        int *status, cudaStream_t st) {
+  if (int e = check_scan_args(T, B, H)) return e;
+  if (!z || !c || !dout || !dz_split || !dz_scale || !status)
+    return fail(HS_ERR_INVALID_ARG, "scan_backward_split: null z/c/dout/dz_split/dz_scale/status");
+  if (!ws_base || !aligned(ws_base, 256) || !aligned(dz_split, 16))
+    return fail(HS_ERR_INVALID_ARG, "workspace must be 256-byte and dz_split 16-byte aligned");
+  if (ws_bytes < scan_split_ws_bytes(T, B, H))
+    return fail(HS_ERR_WORKSPACE, "scan_backward_split: workspace %zu < %zu bytes", ws_bytes,
+                scan_split_ws_bytes(T, B, H));
+  unsigned *words = static_cast<unsigned *>(ws_base);
+  char *sws = static_cast<char *>(ws_base) + 256;
+  const size_t sws_bytes = round_up(scan_ws_bytes(T, B, H), 256);
+  float *part = reinterpret_cast<float *>(sws + sws_bytes);
+  const int64_t M = T * B, N = 4 * H, BH = B * H;
+  const bool fused = kf_max && scan_chain_wanted(T, B, H) && H % 4 == 0 && all_aligned16({z, c, dout});
+  if (!fused) {  // float32 dZ in place, then the split from its exact maximum
+    if (cudaMemsetAsync(dz_scale, 0, 4, st) != cudaSuccess) return check_launch("dz_scale memset");
+    if (int e = scan_backward(z, c, c0, dout, dh_n, dc_n, z, dc0, db, T, B, H, eps, sws, sws_bytes, status, st,
+                              dz_scale))
+      return e;
+    return h3_split_known(z, M, N, N, dz_scale, dz_split, st, nullptr);
+  }
+  if (cudaMemsetAsync(words, 0, 256, st) != cudaSuccess) return check_launch("scan split memset");
+  const int64_t nj = (T + kBoundSteps - 1) / kBoundSteps;
+  if (BH % 4 == 0)  // dout is 16-byte aligned on this path
+    dout_colsum_kernel<true><<<dim3((unsigned)((BH / 4 + 255) / 256), (unsigned)nj), 256, 0, st>>>(dout, T, BH, part);
+  else
+    dout_colsum_kernel<false><<<dim3((unsigned)((BH + 255) / 256), (unsigned)nj), 256, 0, st>>>(dout, T, BH, part);
+  if (int e = check_launch("dout_colsum_kernel")) return e;
+  dout_bound_kernel<<<(unsigned)((BH + 255) / 256), 256, 0, st>>>(part, nj, BH, dh_n, dc_n, words);
+  if (int e = check_launch("dout_bound_kernel")) return e;
+  dz_bound_final_kernel<<<1, 1, 0, st>>>(words, kf_max);
+  if (int e = check_launch("dz_bound_final_kernel")) return e;
+  const ScanShape sh = make_shape(T, B, H, kBwdL, kBwdWPC);
+  ScanWs ws;
+  (void)ws_layout(sh, true, &ws, sws);
+  __half *hi = static_cast<__half *>(dz_split);
+  __half *lo = hi + M * N;
+  if (int e = scan_bwd_chain_launch(z, c, c0, dout, dh_n, dc_n, z, dc0, db ? ws.db_part : nullptr, T, B, H, eps,
+                                    &words[3], status, st, hi, lo, &words[0], nullptr))
+    return e;
+  if (db) {
+    rowsum_kernel<<<(unsigned)((N + 31) / 32), 256, 0, st>>>(ws.db_part, db, B, N, 0);
+    if (int e = check_launch("rowsum_kernel")) return e;
+  }
+  dz_check_kernel<<<1, 1, 0, st>>>(words);
+  if (int e = check_launch("dz_check_kernel")) return e;
+  const int *redo = reinterpret_cast<const int *>(&words[5]);
+  if (int e = scan_bwd_chain_launch(z, c, c0, dout, dh_n, dc_n, z, dc0, nullptr, T, B, H, eps, nullptr, status, st,
+                                    nullptr, nullptr, nullptr, redo))
+    return e;
+  if (int e = h3_split_known(z, M, N, N, &words[4], dz_split, st, redo)) return e;
+  if (cudaMemcpyAsync(dz_scale, &words[4], 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+    return check_launch("dz_scale copy");
   return HS_OK;
 }
 
@@ -657,6 +852,27 @@ int hs_scan_backward_absmax(const float *z, const float *c, const float *c0, con
     return hs::check_launch("hs_scan_backward_absmax memset");
   return hs::scan_backward(z, c, c0, dout, dh_n, dc_n, dz, dc0, db, T, B, H, eps, workspace, workspace_bytes,
                            dev_status, (cudaStream_t)stream, dz_absmax);
+}
+
+size_t hs_scan_split_workspace_bytes(int64_t T, int64_t B, int64_t H) {
+  return (T > 0 && B > 0 && H > 0) ? hs::scan_split_ws_bytes(T, B, H) : 0;
+}
+
+int hs_scan_forward_kf(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n, int64_t T,
+                           int64_t B, int64_t H, float eps, void *workspace, size_t workspace_bytes,
+                           unsigned *kf_max, int *dev_status, hs_stream_t stream) {
+  if (!kf_max || !hs::aligned(kf_max, 4))
+    return hs::fail(HS_ERR_INVALID_ARG, "hs_scan_forward_kf: null or misaligned kf_max");
+  return hs::scan_forward(z, c0, out, c, h_n, c_n, T, B, H, eps, workspace, workspace_bytes, dev_status,
+                          (cudaStream_t)stream, kf_max);
+}
+
+int hs_scan_backward_split(float *z, const float *c, const float *c0, const float *dout, const float *dh_n,
+                           const float *dc_n, const unsigned *kf_max, void *dz_split, unsigned *dz_scale,
+                           float *dc0, float *db, int64_t T, int64_t B, int64_t H, float eps, void *workspace,
+                           size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
+  return hs::scan_backward_split(z, c, c0, dout, dh_n, dc_n, kf_max, dz_split, dz_scale, dc0, db, T, B, H, eps,
+                                 workspace, workspace_bytes, dev_status, (cudaStream_t)stream);
 }
 
 int hs_scan_forward_noalloc(const float *z, const float *c0, float *out, float *c, float *h_n,

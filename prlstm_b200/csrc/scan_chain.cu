@@ -21,6 +21,8 @@
 // floats are 128-byte aligned segments: every warp access is one full line.
 // Per (t,b,h) element the forward moves its 24 algorithmic bytes and the
 // backward its 40, plus one c row per backward chunk (c_{t0-1}).
+#include <cuda_fp16.h>
+
 #include <type_traits>
 
 #include "hs_common.cuh"
@@ -116,7 +118,7 @@ template <bool V16>
 __global__ void __launch_bounds__(kFNW * 32, V16 ? kMinCtas : kMinCtas - 2)
 scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, float *__restrict__ out,
                     float *__restrict__ cbuf, float *__restrict__ h_n, float *__restrict__ c_n, int64_t T,
-                    int64_t B, int64_t H, float eps, int *status) {
+                    int64_t B, int64_t H, float eps, unsigned *kf_max, int *status) {
   extern __shared__ float4 smem_f4[];
   float *sm = reinterpret_cast<float *>(smem_f4);
   unsigned long long *slots = reinterpret_cast<unsigned long long *>(sm + kFNW * 2 * kFBuf);  // [NW][32]
@@ -155,6 +157,9 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
     }
   };
 
+  // max over this lane's steps of c_{t-1} f'_t (1 - f'_t), the forget-gate
+  // factor of the backward's bound on |dZ| (if kf_max is wanted)
+  float kmax = 0.f;
   int64_t c = warp;
   if (c < nchunk) stage(c, buf0);
   commit();
@@ -205,6 +210,7 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
 #pragma unroll
         for (int s = 0; s < kFL; ++s) {
           if (decltype(full_tag)::value || s < n) {
+            kmax = fmaxf(kmax, cc * fp[s] * (1.f - fp[s]));
             cc = fmaf(fp[s], cc, bp[s]);
             o = sig_tanh_pos(eo[s], cc);
             __stcs(cb + s * ostep, cc);
@@ -221,6 +227,11 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
     }
   }
   wait_group<0>();  // no copy is left in flight at exit
+  if (kf_max) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) kmax = fmaxf(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+    if (lane == 0) atomicMax(kf_max, __float_as_uint(kmax));
+  }
 }
 
 // ------------------------------------------------------------------ backward
@@ -229,12 +240,18 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
 // after in time.  Bias sums are kept per lane over all of a warp's chunks and
 // added over the CTA's warps in a fixed order at the end: one partial row per
 // sequence.
-template <bool V16>
+// SPLIT: dZ is written as its 3 x fp16 split (hi, lo [T*B][4H] fp16, scaled
+// by pow2_scale(*dz_bound), *dz_bound being an upper bound of max |dZ|)
+// instead of float32 into dz.  gate (may be null): the kernel does nothing
+// unless *gate != 0 (a conditional re-run).
+template <bool V16, bool SPLIT>
 __global__ void __launch_bounds__(kBNW * 32, V16 ? kMinCtas : kMinCtas - 2)
 scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float *__restrict__ c0,
                     const float *__restrict__ dout, const float *__restrict__ dh_n, const float *__restrict__ dc_n,
                     float *dz, float *__restrict__ dc0, float *__restrict__ db_part, int64_t T, int64_t B,
-                    int64_t H, float eps, unsigned *dz_absmax, int *status) {
+                    int64_t H, float eps, unsigned *dz_absmax, __half *__restrict__ dzh, __half *__restrict__ dzl,
+                    const unsigned *__restrict__ dz_bound, const int *gate, int *status) {
+  if (gate && *gate == 0) return;
   extern __shared__ float4 smem_f4[];
   float *sm = reinterpret_cast<float *>(smem_f4);
   unsigned long long *slots = reinterpret_cast<unsigned long long *>(sm + kBNW * 2 * kBBuf);  // [NW][32]
@@ -284,6 +301,18 @@ scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float 
 
   float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
   float amax = 0.f;  // max |dz| of this lane (NaN ignored), if dz_absmax is wanted
+  const float sc = SPLIT ? pow2_scale(*dz_bound) : 1.f;
+  // One dZ element at offset i of the [T*B][4H] layout.
+  auto put = [&](int64_t i, float v) {
+    if (SPLIT) {
+      const float y = v * sc;
+      const __half hv = __float2half_rn(y);
+      __stcs(dzh + i, hv);
+      __stcs(dzl + i, __float2half_rn(y - __half2float(hv)));
+    } else {
+      __stcs(dz + i, v);
+    }
+  };
   int64_t q = warp;
   if (q < nchunk) stage(q, buf0);
   commit();
@@ -302,7 +331,7 @@ scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float 
     // (final already) and the chunk's map of e.
     float FP[kBL], DCD[kBL], KI[kBL], KF[kBL], KG[kBL];
     float A = 1.f, C = 0.f;
-    float *dzs = dz + (t0 * B + b) * 4 * H + h;  // dz row of step t0, unit h
+    const int64_t dzs = (t0 * B + b) * 4 * H + h;  // dZ offset of step t0, unit h
     // (A condition-free copy of the step loops for full chunks, as in the
     // forward, measured slower here.)
 #pragma unroll
@@ -319,7 +348,7 @@ scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float 
         const float mf = (f >= eps) ? 1.f : 0.f;
         const float dcd = d * o * (1.f - th * th);
         const float dzo = d * th * o * (1.f - o);
-        __stcs(dzs + s * zstep + 3 * H, dzo);
+        put(dzs + s * zstep + 3 * H, dzo);
         acc3 += dzo;
         amax = fmaxf(amax, fabsf(dzo));
         FP[s] = fmaxf(f, eps);
@@ -345,10 +374,10 @@ scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float 
           const float dc = DCD[s] + e;
           e = FP[s] * dc;
           const float di = dc * KI[s], df = dc * KF[s], dg = dc * KG[s];
-          float *dzr = dzs + s * zstep;
-          __stcs(dzr, di);
-          __stcs(dzr + H, df);
-          __stcs(dzr + 2 * H, dg);
+          const int64_t dzr = dzs + s * zstep;
+          put(dzr, di);
+          put(dzr + H, df);
+          put(dzr + 2 * H, dg);
           acc0 += di;
           acc1 += df;
           acc2 += dg;
@@ -404,7 +433,7 @@ int sm_count() {
   return n;
 }
 
-std::atomic<unsigned long long> g_fwd_attr[2], g_bwd_attr[2];
+std::atomic<unsigned long long> g_fwd_attr[2], g_bwd_attr[3];
 
 }  // namespace
 
@@ -420,7 +449,8 @@ bool scan_chain_wanted(int64_t T, int64_t B, int64_t H) {
 }
 
 int scan_fwd_chain_launch(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
-                          int64_t T, int64_t B, int64_t H, float eps, int *status, cudaStream_t st) {
+                          int64_t T, int64_t B, int64_t H, float eps, unsigned *kf_max, int *status,
+                          cudaStream_t st) {
   const int64_t grid = B * ((H + 31) / 32);
   if (grid >= (1ll << 31)) return fail(HS_ERR_UNSUPPORTED, "scan: too many columns");
   if ((T + kFL - 1) / kFL >= (1ll << 32)) return fail(HS_ERR_UNSUPPORTED, "scan: T too large");
@@ -429,28 +459,38 @@ int scan_fwd_chain_launch(const float *z, const float *c0, float *out, float *c,
   if (int e = allow_dynamic_smem(fn, kFSmem, &g_fwd_attr[v16])) return e;
   if (v16)
     scan_fwd_col_kernel<true><<<(unsigned)grid, kFNW * 32, kFSmem, st>>>(z, c0, out, c, h_n, c_n, T, B, H, eps,
-                                                                       status);
+                                                                       kf_max, status);
   else
     scan_fwd_col_kernel<false><<<(unsigned)grid, kFNW * 32, kFSmem, st>>>(z, c0, out, c, h_n, c_n, T, B, H, eps,
-                                                                        status);
+                                                                        kf_max, status);
   return check_launch("scan_fwd_col_kernel");
 }
 
 int scan_bwd_chain_launch(const float *z, const float *c, const float *c0, const float *dout, const float *dh_n,
                           const float *dc_n, float *dz, float *dc0, float *db_part, int64_t T, int64_t B, int64_t H,
-                          float eps, unsigned *dz_absmax, int *status, cudaStream_t st) {
+                          float eps, unsigned *dz_absmax, int *status, cudaStream_t st, __half *dzh, __half *dzl,
+                          const unsigned *dz_bound, const int *gate) {
   const int64_t grid = B * ((H + 31) / 32);
   if (grid >= (1ll << 31)) return fail(HS_ERR_UNSUPPORTED, "scan: too many columns");
   if ((T + kBL - 1) / kBL >= (1ll << 32)) return fail(HS_ERR_UNSUPPORTED, "scan: T too large");
   const bool v16 = H % 4 == 0 && aligned(z, 16) && aligned(c, 16) && aligned(dout, 16);
-  const void *fn = v16 ? (const void *)scan_bwd_col_kernel<true> : (const void *)scan_bwd_col_kernel<false>;
-  if (int e = allow_dynamic_smem(fn, kBSmem, &g_bwd_attr[v16])) return e;
-  if (v16)
-    scan_bwd_col_kernel<true><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(z, c, c0, dout, dh_n, dc_n, dz, dc0,
-                                                                       db_part, T, B, H, eps, dz_absmax, status);
+  const bool split = dzh != nullptr;
+  if (split && (!v16 || !dzl || !dz_bound)) return fail(HS_ERR_INVALID_ARG, "scan split: needs H % 4 == 0, aligned inputs");
+  const void *fn = split ? (const void *)scan_bwd_col_kernel<true, true>
+                         : v16 ? (const void *)scan_bwd_col_kernel<true, false>
+                               : (const void *)scan_bwd_col_kernel<false, false>;
+  if (int e = allow_dynamic_smem(fn, kBSmem, &g_bwd_attr[split ? 2 : (int)v16])) return e;
+  if (split)
+    scan_bwd_col_kernel<true, true><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(
+        z, c, c0, dout, dh_n, dc_n, dz, dc0, db_part, T, B, H, eps, dz_absmax, dzh, dzl, dz_bound, gate, status);
+  else if (v16)
+    scan_bwd_col_kernel<true, false><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(
+        z, c, c0, dout, dh_n, dc_n, dz, dc0, db_part, T, B, H, eps, dz_absmax, nullptr, nullptr, nullptr, gate,
+        status);
   else
-    scan_bwd_col_kernel<false><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(z, c, c0, dout, dh_n, dc_n, dz, dc0,
-                                                                        db_part, T, B, H, eps, dz_absmax, status);
+    scan_bwd_col_kernel<false, false><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(
+        z, c, c0, dout, dh_n, dc_n, dz, dc0, db_part, T, B, H, eps, dz_absmax, nullptr, nullptr, nullptr, gate,
+        status);
   return check_launch("scan_bwd_col_kernel");
 }
 

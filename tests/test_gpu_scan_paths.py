@@ -5,6 +5,7 @@ oracle (clamped linear recurrence and its hand-derived gradient), including
 c0, dh_n/dc_n, dc0 and the bias sums, on ragged H (partial 32-unit chains,
 H not a multiple of 4)."""
 
+import math
 import os
 
 import pytest
@@ -141,3 +142,107 @@ def test_scan_backward_absmax(path):
         else:
             assert _rel(v, ref[k]) < TOL, k
     assert am[0].item() == dz.abs().max().reshape(1).view(torch.int32).item()
+
+
+def _split_run(path, z, c0, G, dh_n, dc_n, T, B, H):
+    """hs_scan_forward_kf + hs_scan_backward_split on copies of the
+    inputs; returns (dz rebuilt from the split, scale word, db, dc0)."""
+    from prlstm_b200 import _lib as L
+
+    dev = z.device
+    old = os.environ.get("HS_SCAN_PATH")
+    os.environ["HS_SCAN_PATH"] = path
+    try:
+        lib = L.load()
+        P, st = L.ptr, L.stream_ptr(dev)
+        ws = L.workspace(max(lib.hs_scan_workspace_bytes(T, B, H), lib.hs_scan_split_workspace_bytes(T, B, H)), dev)
+        words = torch.zeros(64, dtype=torch.int32, device=dev)
+        out = torch.empty(T, B, H, device=dev)
+        c = torch.empty(T, B, H, device=dev)
+        L.call("hs_scan_forward_kf", P(z), P(c0), P(out), P(c), None, None, T, B, H, 1e-6, P(ws), ws.numel(),
+               P(words[0:]), P(L.status_word(dev)), st)
+        zc = z.clone()
+        split = torch.empty(lib.hs_split_bytes(T * B, 4 * H), dtype=torch.uint8, device=dev)
+        dc0 = torch.empty(B, H, device=dev)
+        db = torch.empty(4 * H, device=dev)
+        L.call("hs_scan_backward_split", P(zc), P(c), P(c0), P(G), P(dh_n), P(dc_n), P(words[0:]), P(split),
+               P(words[16:]), P(dc0), P(db), T, B, H, 1e-6, P(ws), ws.numel(), P(L.status_word(dev)), st)
+        torch.cuda.synchronize(dev)
+        L.check_device_status(dev)
+    finally:
+        if old is None:
+            del os.environ["HS_SCAN_PATH"]
+        else:
+            os.environ["HS_SCAN_PATH"] = old
+    n = T * B * 4 * H
+    scale_bits = int(words[16].item())
+    m = torch.tensor([scale_bits], dtype=torch.int32).view(torch.float32).item()
+    s = 2.0 ** (14 - math.floor(math.log2(m))) if 0 < m < 3e38 else 1.0
+    hi = split[: 2 * n].view(torch.float16).double()
+    lo = split[2 * n: 4 * n].view(torch.float16).double()
+    dz = ((hi + lo) / s).view(T, B, 4 * H)
+    return dz, m, db, dc0, split, words
+
+
+@pytest.mark.parametrize("path,T,B,H,saturate", [("chain", 700, 3, 96, False), ("chain", 300, 2, 128, True),
+                                                 ("lookback", 500, 3, 100, False)])
+def test_scan_backward_split(path, T, B, H, saturate):
+    """hs_scan_backward_split: dZ rebuilt from its fp16 split (hi + lo, over
+    the scale) equals the float32 dZ of hs_scan_backward to 1e-6 normwise,
+    the scale word bounds max |dZ|, and the bias and c0 gradients are the
+    same.  saturate: output gates near zero make dZ tiny against the bound
+    from sum |dout|, which exercises the exact-maximum re-run."""
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(T + H)
+    z = 2.0 * torch.randn(T, B, 4 * H, device=dev, generator=g)
+    if saturate:
+        z[..., 3 * H:] = -60.0  # o ~ 1e-26
+        z[..., 0:H] = -60.0     # i*g below eps: only the clamp feeds c
+    c0 = torch.rand(B, H, device=dev, generator=g)
+    G = torch.randn(T, B, H, device=dev, generator=g)
+    dh_n = torch.randn(B, H, device=dev, generator=g)
+    dc_n = torch.randn(B, H, device=dev, generator=g)
+    ref = _run(path, z, c0, G, dh_n, dc_n)
+    dz, m, db, dc0, _, _ = _split_run(path, z, c0, G, dh_n, dc_n, T, B, H)
+    ref_dz = ref["dz"].double().cpu()
+    amax = ref_dz.abs().max().item()
+    assert m >= amax, (m, amax)
+    if amax > 0:
+        e = ((dz.cpu() - ref_dz).abs().max() / amax).item()
+        assert e < 1e-6, e
+    assert _rel(db, ref["db"]) < TOL and _rel(dc0, ref["dc0"]) < TOL
+
+
+@pytest.mark.parametrize("path", ["chain", "lookback"])
+def test_linear_backward_from_split(path):
+    """The scan backward's fp16 split of dZ fed to hs_linear_backward_presplit
+    gives dX = dZ.W_ih and dW_ih = dZ^T.x (beta 0 and 1) within 2e-6 of
+    float64 products of the float32 dZ."""
+    from prlstm_b200 import _lib as L
+
+    T, B, H, D = 640, 4, 128, 96
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    z = 2.0 * torch.randn(T, B, 4 * H, device=dev, generator=g)
+    c0 = torch.rand(B, H, device=dev, generator=g)
+    G = torch.randn(T, B, H, device=dev, generator=g)
+    ref = _run(path, z, c0, G, None, None)
+    _, _, _, _, split, words = _split_run(path, z, c0, G, None, None, T, B, H)
+    x = torch.randn(T * B, D, device=dev, generator=g)
+    w = torch.randn(4 * H, D, device=dev, generator=g) / D ** 0.5
+    dw0 = torch.randn(4 * H, D, device=dev, generator=g)
+    lib = L.load()
+    M, N = T * B, 4 * H
+    ws = L.workspace(lib.hs_linear_presplit_workspace_bytes(M, N, D), dev)
+    P, st = L.ptr, L.stream_ptr(dev)
+    dz64 = ref["dz"].double().cpu().reshape(M, N)
+    for beta in (0, 1):
+        dx = torch.empty(M, D, device=dev)
+        dw = dw0.clone()
+        L.call("hs_linear_backward_presplit", P(split), P(words[16:]), P(x), P(w), P(dx), P(dw), M, N, D, beta,
+               P(ws), ws.numel(), P(L.status_word(dev)), st)
+        torch.cuda.synchronize(dev)
+        L.check_device_status(dev)
+        ref_dw = dz64.t() @ x.double().cpu() + (dw0.double().cpu() if beta else 0)
+        assert _rel(dw, ref_dw) < 2e-6
+        assert _rel(dx, dz64 @ w.double().cpu()) < 2e-6
