@@ -419,6 +419,10 @@ def run_ours(args, cfg, rank, world, dev):
         result["scan_roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak_hbm,
                                    "unit": "GB/s", "frac": round(ach / peak_hbm, 4),
                                    "peak_kind": peak_kind}
+        # The scans on their own (plain float32 entry points, one micro-batch,
+        # after the timed region): inside the step the GEMMs hold the SM clock
+        # down under the power cap and the issue-bound scans slow with it.
+        result["scan_alone"] = scan_alone(step, G[0], dev, peak_hbm)
         del step
         torch.cuda.empty_cache()
         # ---------------- e2e through the public module API, host buffers
@@ -429,6 +433,45 @@ def run_ours(args, cfg, rank, world, dev):
         result.update(run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync,
                                     max_over_ranks, allreduce, peak_tf, peak_kind))
     return result
+
+
+def scan_alone(step, G0, dev, peak_hbm, reps=5):
+    """hs_scan_forward and hs_scan_backward (float32 dZ) timed alone with CUDA
+    events on one micro-batch of the step's own inputs (every rank runs it;
+    rank 0 reports)."""
+    L, P = step.L, step.L.ptr
+    T, H, mb = step.cfg["T"], step.cfg["H"], step.mb
+    st = L.stream_ptr(dev)
+    dz = torch.empty_like(step.z)
+
+    def fwd():
+        L.call("hs_scan_forward", P(step.z), P(step.c0), P(step.out), P(step.c), None, None, T, mb, H, 1e-6,
+               P(step.ws), step.ws.numel(), P(step.status), st)
+
+    def bwd():
+        L.call("hs_scan_backward", P(step.z), P(step.c), P(step.c0), P(G0), None, None, P(dz), None,
+               P(step.db_mb), T, mb, H, 1e-6, P(step.ws), step.ws.numel(), P(step.status), st)
+
+    out = {"workload": f"one micro-batch, T={T}, B={mb}, H={H}", "reps": reps}
+    for name, f, bpe in (("scan_fwd", fwd, 24.0), ("scan_bwd", bwd, 40.0)):
+        for _ in range(2):
+            f()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            f()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / reps
+        gbs = bpe * T * mb * H / (ms / 1e3) / 1e9
+        out[name] = {"avg_ms": round(ms, 4), "achieved": round(gbs, 1), "unit": "GB/s",
+                     "frac": round(gbs / peak_hbm, 4)}
+    tot = out["scan_fwd"]["avg_ms"] + out["scan_bwd"]["avg_ms"]
+    gbs = 64.0 * T * mb * H / (tot / 1e3) / 1e9
+    out["combined"] = {"achieved": round(gbs, 1), "frac": round(gbs / peak_hbm, 4)}
+    del dz
+    return out
 
 
 def e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync, max_over_ranks, allreduce):
@@ -793,7 +836,7 @@ def main():
                         if args.config == "cfg4" else "no flush; per-step working set noted"},
                 roofline=res.get("roofline"), e2e=res.get("e2e"), clocks=res.get("clocks"),
                 gpu_launches=res.get("gpu_launches"))
-    for k in ("kernels", "scan_roofline", "recurrent"):
+    for k in ("kernels", "scan_roofline", "scan_alone", "recurrent"):
         if k in res:
             line[k] = res[k]
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
