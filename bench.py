@@ -197,7 +197,9 @@ class ParallelStep:
         # split (hi, lo) with one scale word; the forward's max c feeds the
         # split scale's bound
         self.dz_split = torch.empty(lib.hs_split_bytes(M, 4 * H), dtype=torch.uint8, device=dev)
-        self.words = torch.zeros(64, dtype=torch.int32, device=dev)  # [0] max c, [16] dZ scale
+        # x's split serves both the projection and the weight gradient
+        self.x_split = torch.empty(lib.hs_split_bytes(M, D), dtype=torch.uint8, device=dev)
+        self.words = torch.zeros(64, dtype=torch.int32, device=dev)  # [0] Kf, [16] dZ scale, [32] x scale
         self.names = ("proj_gemm", "scan_fwd", "scan_bwd", "linear_bwd")
         self.ms = {n: 0.0 for n in self.names}
         self.launches = 0
@@ -214,8 +216,10 @@ class ParallelStep:
             e = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if record else None
             if record:
                 e[0].record()
-            L.call("hs_linear_forward", P(xs), P(self.W_ih), P(self.b_ih), P(self.z), M, 4 * H, D,
-                   P(self.ws), self.ws.numel(), P(self.status), st)
+            x_scale = P(self.words[32:])
+            L.call("hs_split", P(xs), M, D, P(self.x_split), x_scale, st)
+            L.call("hs_linear_forward_presplit", P(self.x_split), x_scale, P(self.W_ih), P(self.b_ih), P(self.z), M,
+                   4 * H, D, P(self.ws), self.ws.numel(), P(self.status), st)
             if record:
                 e[1].record()
             cmax, dz_scale = P(self.words[0:]), P(self.words[16:])
@@ -230,16 +234,18 @@ class ParallelStep:
             if record:
                 e[3].record()
             # dX and dW_ih (accumulated over micro-batches) in one call
-            L.call("hs_linear_backward_presplit", P(self.dz_split), dz_scale, P(xs), P(self.W_ih), P(self.dx),
-                   P(self.dW), M, 4 * H, D, 1 if i else 0, P(self.ws), self.ws.numel(), P(self.status), st)
+            L.call("hs_linear_backward_presplit", P(self.dz_split), dz_scale, None, P(self.x_split), x_scale,
+                   P(self.W_ih), P(self.dx), P(self.dW), M, 4 * H, D, 1 if i else 0, P(self.ws), self.ws.numel(),
+                   P(self.status), st)
             if record:
                 e[4].record()
             self.db.add_(self.db_mb) if i else self.db.copy_(self.db_mb)
-            # projection: 2 absmax + 2 split + GEMM; scan forward 1; scan
-            # backward: bound (3), scan, rowsum, check, conditional re-run and
-            # split (2, return at once unless needed); backward GEMMs: 2
-            # absmax + 2 split + 2 GEMMs + split-K reduce
-            self.launches += 5 + 1 + 8 + 7
+            # projection: absmax + split of x and of W_ih, GEMM; scan forward
+            # 1; scan backward: bound (3), scan, rowsum, check, conditional
+            # re-run and split (2, return at once unless needed); backward
+            # GEMMs: absmax + split of W_ih, 2 GEMMs, split-K reduce (x's
+            # split is the projection's)
+            self.launches += 5 + 1 + 8 + 5
             if record:
                 evs.append(e)
         return evs

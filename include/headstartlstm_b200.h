@@ -123,16 +123,30 @@ HS_API int hs_linear_backward_absmax(const float *dy, const float *x, const floa
 /* Bytes of an fp16 split buffer of a [rows][cols] float32 matrix: hi then
  * lo, each [rows][cols rounded up to 8] fp16. */
 HS_API size_t hs_split_bytes(int64_t rows, int64_t cols);
+/* The fp16 split of a contiguous float32 [rows][cols] matrix into dst
+ * (16-byte aligned, hs_split_bytes(rows, cols) bytes), its scale word (the
+ * float32 bits of max |x|) into *scale, for the _presplit entry points. */
+HS_API int hs_split(const float *x, int64_t rows, int64_t cols, void *dst, unsigned *scale,
+                    hs_stream_t stream);
+/* hs_linear_forward from x given as its split (x_split, x_scale from
+ * hs_split of x [M][K]): the same split then serves the weight gradient in
+ * hs_linear_backward_presplit.  Same replacement as hs_linear_forward. */
+HS_API int hs_linear_forward_presplit(const void *x_split, const unsigned *x_scale, const float *w,
+                                      const float *bias, float *y, int64_t M, int64_t N, int64_t K,
+                                      void *workspace, size_t workspace_bytes, int *dev_status,
+                                      hs_stream_t stream);
 /* hs_linear_backward with dy given only as its fp16 split (dy_split, as
  * hs_scan_backward_split writes it; N % 8 == 0) and its scale word dy_scale
- * (float32 bits of an upper bound of max |dy|).  No float32 dy is read, so
- * there is no fallback: shapes the tensor-core path does not take, or a
- * workspace below hs_linear_presplit_workspace_bytes(M, N, K), return an
+ * (float32 bits of an upper bound of max |dy|); x either as float32 (x) or
+ * as its split (x_split, x_scale; x may then be NULL).  No float32 dy is
+ * read, so there is no fallback: shapes the tensor-core path does not take,
+ * or a workspace below hs_linear_presplit_workspace_bytes(M, N, K), return an
  * error.  Same replacement as hs_linear_backward (_torch.py:157-162). */
 HS_API size_t hs_linear_presplit_workspace_bytes(int64_t M, int64_t N, int64_t K);
 HS_API int hs_linear_backward_presplit(const void *dy_split, const unsigned *dy_scale, const float *x,
-                                       const float *w, float *dx, float *dw, int64_t M, int64_t N, int64_t K,
-                                       int beta, void *workspace, size_t workspace_bytes, int *dev_status,
+                                       const void *x_split, const unsigned *x_scale, const float *w,
+                                       float *dx, float *dw, int64_t M, int64_t N, int64_t K, int beta,
+                                       void *workspace, size_t workspace_bytes, int *dev_status,
                                        hs_stream_t stream);
 /* db[N] = beta * db + sum_m dy[m, N]   (beta is 0 or 1) */
 HS_API int hs_colsum(const float *dy, float *db, int64_t M, int64_t N, int beta,

@@ -46,7 +46,9 @@ SIGNATURES = {
     "hs_linear_backward_absmax": (_i32, [_c_p] * 5 + [_i64] * 3 + [_i32, _c_p, _c_p, _sz, _c_p, _c_p]),
     "hs_split_bytes": (_sz, [_i64] * 2),
     "hs_linear_presplit_workspace_bytes": (_sz, [_i64] * 3),
-    "hs_linear_backward_presplit": (_i32, [_c_p] * 6 + [_i64] * 3 + [_i32, _c_p, _sz, _c_p, _c_p]),
+    "hs_split": (_i32, [_c_p, _i64, _i64, _c_p, _c_p, _c_p]),
+    "hs_linear_forward_presplit": (_i32, [_c_p] * 5 + [_i64] * 3 + [_c_p, _sz, _c_p, _c_p]),
+    "hs_linear_backward_presplit": (_i32, [_c_p] * 8 + [_i64] * 3 + [_i32, _c_p, _sz, _c_p, _c_p]),
     "hs_colsum": (_i32, [_c_p, _c_p, _i64, _i64, _i32, _c_p]),
     "hs_scan_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "hs_parallel_workspace_bytes": (_sz, [_i64] * 4),

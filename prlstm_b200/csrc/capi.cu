@@ -177,11 +177,14 @@ int linear_backward_ex(const float *dy, const float *w, float *dx, const float *
 // (hi, lo [M][N], N % 8 == 0, scale word dy_scale); *took = false if the
 // tensor-core path does not take the shape or the workspace (nothing can be
 // done without float32 dy).
-int linear_backward_split_only(const void *dy_split, const unsigned *dy_scale, const float *x, const float *w,
-                               float *dx, float *dw, int64_t M, int64_t N, int64_t K, int beta, void *ws,
-                               size_t ws_bytes, int *status, cudaStream_t st, bool *took) {
+// x may instead be given as its split (x_split, x_scale; x may then be null).
+int linear_backward_split_only(const void *dy_split, const unsigned *dy_scale, const float *x, const void *x_split,
+                               const unsigned *x_scale, const float *w, float *dx, float *dw, int64_t M, int64_t N,
+                               int64_t K, int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st,
+                               bool *took) {
   *took = false;
-  if (M <= 0 || N <= 0 || K <= 0 || !x || !w || !dw || !status) return fail(HS_ERR_INVALID_ARG, "linear backward: bad arguments");
+  if (M <= 0 || N <= 0 || K <= 0 || !(x || (x_split && x_scale)) || !w || !dw || !status)
+    return fail(HS_ERR_INVALID_ARG, "linear backward: bad arguments");
   const size_t sc = 256 + h3_split_bytes(M, K) + h3_split_bytes(N, K);
   if (!ws || !aligned(ws, 256) || ws_bytes < sc || !aligned(dw, 16) || K % 4 || (dx && !aligned(dx, 16))) return HS_OK;
   char *w8 = static_cast<char *>(ws);
@@ -197,12 +200,33 @@ int linear_backward_split_only(const void *dy_split, const unsigned *dy_scale, c
                                  status, st, &ddx))
       return e;
   }
-  if (int e = h3_split(x, M, K, K, am + 1, xs, st)) return e;
-  if (int e = gemm_h3_presplit(dy_split, dy_scale, true, xs, am + 1, true, dw, nullptr, N, K, M, K, beta, tail, tb,
-                               status, st, &ddw))
+  if (!x_split) {
+    if (int e = h3_split(x, M, K, K, am + 1, xs, st)) return e;
+    x_split = xs;
+    x_scale = am + 1;
+  }
+  if (int e = gemm_h3_presplit(dy_split, dy_scale, true, x_split, x_scale, true, dw, nullptr, N, K, M, K, beta, tail,
+                               tb, status, st, &ddw))
     return e;
   *took = ddx && ddw;
   return HS_OK;
+}
+
+// y = x.w^T (+ bias) from x given as its split; *took = false if the
+// tensor-core path does not take it.
+int linear_forward_split_only(const void *x_split, const unsigned *x_scale, const float *w, const float *bias,
+                              float *y, int64_t M, int64_t N, int64_t K, void *ws, size_t ws_bytes, int *status,
+                              cudaStream_t st, bool *took) {
+  *took = false;
+  if (M <= 0 || N <= 0 || K <= 0 || !x_split || !x_scale || !w || !y || !status)
+    return fail(HS_ERR_INVALID_ARG, "linear forward: bad arguments");
+  const size_t sc = 256 + h3_split_bytes(N, K);
+  if (!ws || !aligned(ws, 256) || ws_bytes < sc || !aligned(y, 16) || N % 4) return HS_OK;
+  char *w8 = static_cast<char *>(ws);
+  unsigned *am = reinterpret_cast<unsigned *>(w8);
+  if (int e = h3_split(w, N, K, K, am, w8 + 256, st)) return e;
+  return gemm_h3_presplit(x_split, x_scale, false, w8 + 256, am, false, y, bias, M, N, K, N, 0, w8 + sc,
+                          ws_bytes - sc, status, st, took);
 }
 
 size_t linear_backward_split_ws(int64_t M, int64_t N, int64_t K) {
@@ -369,17 +393,37 @@ int hs_linear_backward_absmax(const float *dy, const float *x, const float *w, f
                                 dev_status, (cudaStream_t)stream, dy_absmax);
 }
 
-int hs_linear_backward_presplit(const void *dy_split, const unsigned *dy_scale, const float *x, const float *w,
-                                float *dx, float *dw, int64_t M, int64_t N, int64_t K, int beta, void *workspace,
-                                size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
+int hs_split(const float *x, int64_t rows, int64_t cols, void *dst, unsigned *scale, hs_stream_t stream) {
+  if (rows <= 0 || cols <= 0 || !x || !dst || !scale || !hs::aligned(dst, 16) || !hs::aligned(scale, 4))
+    return hs::fail(HS_ERR_INVALID_ARG, "hs_split: bad arguments");
+  return hs::h3_split(x, rows, cols, cols, scale, dst, (cudaStream_t)stream);
+}
+
+int hs_linear_forward_presplit(const void *x_split, const unsigned *x_scale, const float *w, const float *bias,
+                               float *y, int64_t M, int64_t N, int64_t K, void *workspace, size_t workspace_bytes,
+                               int *dev_status, hs_stream_t stream) {
+  if (!hs::gemm_h3_enabled() || !hs::gemm_tc_size_ok(M, N, K))
+    return hs::fail(HS_ERR_UNSUPPORTED, "hs_linear_forward_presplit: the fp16-split GEMMs do not take this shape");
+  bool took = false;
+  if (int e = hs::linear_forward_split_only(x_split, x_scale, w, bias, y, M, N, K, workspace, workspace_bytes,
+                                            dev_status, (cudaStream_t)stream, &took))
+    return e;
+  return took ? HS_OK
+              : hs::fail(HS_ERR_WORKSPACE, "hs_linear_forward_presplit: workspace too small or operands unaligned");
+}
+
+int hs_linear_backward_presplit(const void *dy_split, const unsigned *dy_scale, const float *x, const void *x_split,
+                                const unsigned *x_scale, const float *w, float *dx, float *dw, int64_t M, int64_t N,
+                                int64_t K, int beta, void *workspace, size_t workspace_bytes, int *dev_status,
+                                hs_stream_t stream) {
   if (!dy_split || !dy_scale || !hs::aligned(dy_split, 16) || !hs::aligned(dy_scale, 4))
     return hs::fail(HS_ERR_INVALID_ARG, "hs_linear_backward_presplit: null or misaligned dy_split/dy_scale");
   if (N % 8) return hs::fail(HS_ERR_UNSUPPORTED, "hs_linear_backward_presplit: N must be a multiple of 8");
   if (!hs::gemm_h3_enabled() || !hs::gemm_tc_size_ok(M, N, K))
     return hs::fail(HS_ERR_UNSUPPORTED, "hs_linear_backward_presplit: the fp16-split GEMMs do not take this shape");
   bool took = false;
-  if (int e = hs::linear_backward_split_only(dy_split, dy_scale, x, w, dx, dw, M, N, K, beta, workspace,
-                                             workspace_bytes, dev_status, (cudaStream_t)stream, &took))
+  if (int e = hs::linear_backward_split_only(dy_split, dy_scale, x, x_split, x_scale, w, dx, dw, M, N, K, beta,
+                                             workspace, workspace_bytes, dev_status, (cudaStream_t)stream, &took))
     return e;
   return took ? HS_OK
               : hs::fail(HS_ERR_WORKSPACE, "hs_linear_backward_presplit: workspace too small or operands unaligned");

@@ -216,8 +216,9 @@ def test_scan_backward_split(path, T, B, H, saturate):
 @pytest.mark.parametrize("path", ["chain", "lookback"])
 def test_linear_backward_from_split(path):
     """The scan backward's fp16 split of dZ fed to hs_linear_backward_presplit
-    gives dX = dZ.W_ih and dW_ih = dZ^T.x (beta 0 and 1) within 2e-6 of
-    float64 products of the float32 dZ."""
+    gives dX = dZ.W_ih and dW_ih = dZ^T.x (beta 0 and 1, x as float32 or as
+    its hs_split) within 2e-6 of float64 products of the float32 dZ; and
+    hs_linear_forward_presplit from the same split of x gives x.W^T + b."""
     from prlstm_b200 import _lib as L
 
     T, B, H, D = 640, 4, 128, 96
@@ -236,13 +237,24 @@ def test_linear_backward_from_split(path):
     ws = L.workspace(lib.hs_linear_presplit_workspace_bytes(M, N, D), dev)
     P, st = L.ptr, L.stream_ptr(dev)
     dz64 = ref["dz"].double().cpu().reshape(M, N)
-    for beta in (0, 1):
+    xsplit = torch.empty(lib.hs_split_bytes(M, D), dtype=torch.uint8, device=dev)
+    L.call("hs_split", P(x), M, D, P(xsplit), P(words[32:]), st)
+    for beta, given in ((0, "x"), (1, "x"), (0, "split"), (1, "split")):
         dx = torch.empty(M, D, device=dev)
         dw = dw0.clone()
-        L.call("hs_linear_backward_presplit", P(split), P(words[16:]), P(x), P(w), P(dx), P(dw), M, N, D, beta,
-               P(ws), ws.numel(), P(L.status_word(dev)), st)
+        xa, xs, xsc = (P(x), None, None) if given == "x" else (None, P(xsplit), P(words[32:]))
+        L.call("hs_linear_backward_presplit", P(split), P(words[16:]), xa, xs, xsc, P(w), P(dx), P(dw), M, N, D,
+               beta, P(ws), ws.numel(), P(L.status_word(dev)), st)
         torch.cuda.synchronize(dev)
         L.check_device_status(dev)
         ref_dw = dz64.t() @ x.double().cpu() + (dw0.double().cpu() if beta else 0)
         assert _rel(dw, ref_dw) < 2e-6
         assert _rel(dx, dz64 @ w.double().cpu()) < 2e-6
+
+    y = torch.empty(M, N, device=dev)
+    bias = torch.randn(N, device=dev, generator=g)
+    wf = torch.randn(N, D, device=dev, generator=g) / D ** 0.5
+    L.call("hs_linear_forward_presplit", P(xsplit), P(words[32:]), P(wf), P(bias), P(y), M, N, D, P(ws), ws.numel(),
+           P(L.status_word(dev)), st)
+    torch.cuda.synchronize(dev)
+    assert _rel(y, x.double().cpu() @ wf.double().cpu().t() + bias.double().cpu()) < 2e-6
