@@ -72,18 +72,20 @@ HS_DEV float sigf(float x) {
 // whose first omitted term (1382/155925 c^11) is below 1e-8 relative there.
 HS_DEV float tanh_pos(float c) {
 #if HS_TANH_POLY
-  if (c < 0.25f) {
-    const float u = c * c;
-    float p = fmaf(u, 62.0f / 2835.0f, -17.0f / 315.0f);
-    p = fmaf(p, u, 2.0f / 15.0f);
-    p = fmaf(p, u, -1.0f / 3.0f);
-    return fmaf(p * u, c, c);
-  }
+  // both forms, one selected: no divergence where lanes straddle 0.25
+  const float u = c * c;
+  float p = fmaf(u, 62.0f / 2835.0f, -17.0f / 315.0f);
+  p = fmaf(p, u, 2.0f / 15.0f);
+  p = fmaf(p, u, -1.0f / 3.0f);
+  const float tp = fmaf(p * u, c, c);
+  const float e = __expf(-2.0f * c);
+  const float te = __fdividef(1.0f - e, 1.0f + e);
+  return c < 0.25f ? tp : te;
 #else
   if (c < 0.25f) return tanhf(c);
-#endif
   const float e = __expf(-2.0f * c);
   return __fdividef(1.0f - e, 1.0f + e);
+#endif
 }
 
 // The hardware reciprocal alone (about 1 ulp; +inf gives 0).  Enough where
@@ -105,19 +107,16 @@ HS_DEV float sig2(float x, float y) { return rcp_fast((1.0f + __expf(-x)) * (1.0
 // poly(c) / (1 + eo) below 0.25 (odd Taylor series of tanh, as tanh_pos) and
 // (1 - e^-2c) / ((1 + e^-2c)(1 + eo)) above.
 HS_DEV float sig_tanh_pos(float eo, float c) {
-  float num, den;
-  if (c < 0.25f) {
-    const float u = c * c;
-    float p = fmaf(u, 62.0f / 2835.0f, -17.0f / 315.0f);
-    p = fmaf(p, u, 2.0f / 15.0f);
-    p = fmaf(p, u, -1.0f / 3.0f);
-    num = fmaf(p * u, c, c);
-    den = 1.0f + eo;
-  } else {
-    const float e = __expf(-2.0f * c);
-    num = 1.0f - e;
-    den = (1.0f + e) * (1.0f + eo);
-  }
+  // both forms, one selected (no divergence where lanes straddle 0.25)
+  const float u = c * c;
+  float p = fmaf(u, 62.0f / 2835.0f, -17.0f / 315.0f);
+  p = fmaf(p, u, 2.0f / 15.0f);
+  p = fmaf(p, u, -1.0f / 3.0f);
+  const float tp = fmaf(p * u, c, c);
+  const float e = __expf(-2.0f * c);
+  const bool small = c < 0.25f;
+  const float num = small ? tp : 1.0f - e;
+  const float den = small ? 1.0f + eo : (1.0f + e) * (1.0f + eo);
   return num * rcp_fast(den);
 }
 
