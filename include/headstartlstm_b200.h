@@ -198,18 +198,19 @@ HS_API int hs_scan_backward_absmax(const float *z, const float *c, const float *
  * the bound on |dZ| that hs_scan_backward_split uses.  Same replacement as
  * hs_scan_forward. */
 HS_API int hs_scan_forward_kf(const float *z, const float *c0, float *out, float *c, float *h_n,
-                                  float *c_n, int64_t T, int64_t B, int64_t H, float eps,
-                                  void *workspace, size_t workspace_bytes, unsigned *kf_max,
-                                  int *dev_status, hs_stream_t stream);
+                              float *c_n, int64_t T, int64_t B, int64_t H, float eps,
+                              void *workspace, size_t workspace_bytes, unsigned *kf_max,
+                              int *dev_status, hs_stream_t stream);
 /* The scan backward with dZ delivered as its fp16 split for the gradient
  * GEMMs (hs_linear_backward_presplit) instead of float32: dz_split (16-byte
  * aligned, hs_split_bytes(T*B, 4H) bytes) receives hi then lo, *dz_scale the
  * scale word.  The scale is chosen before the scan from an upper bound of
  * max |dZ|: D x max(1/4, Kf), D the largest column sum of |dout| (with
  * |dh_n| + |dc_n|) and Kf the forward's kf_max; the scan writes the split
- * directly, so dZ is never stored in float32.  If the bound turns out more than 2^16 above the exact maximum
- * (or anything is not finite), the scan runs again into float32 dZ in place
- * of z and the split is made from the exact maximum (z is overwritten then).
+ * directly, so dZ is never stored in float32.  If the bound turns out more
+ * than 2^16 above the exact maximum (or anything is not finite), the scan
+ * runs again into float32 dZ in place of z and the split is made from the
+ * exact maximum (z is overwritten then).
  * Replaces, with the GEMMs after it, the autograd backward of
  * headstartlstm_parallel (_parallel.py:38-74). */
 HS_API size_t hs_scan_split_workspace_bytes(int64_t T, int64_t B, int64_t H);
@@ -255,6 +256,24 @@ HS_API int hs_parallel_backward(const float *x, const float *w_ih, float *z, con
                          float *dc0, int64_t T, int64_t B, int64_t D, int64_t H, float eps,
                          void *workspace, size_t workspace_bytes, int *dev_status,
                          hs_stream_t stream);
+
+/* hs_parallel_forward that also writes *kf (device word) for
+ * hs_parallel_backward_kf: with it the backward hands dZ from the scan to
+ * the gradient GEMMs as its fp16 split (hs_scan_backward_split ->
+ * hs_linear_backward_presplit) when the shape, alignment and workspace
+ * (hs_parallel_workspace_bytes covers it) allow, and otherwise takes the
+ * path of hs_parallel_backward.  Same replacements as the two calls above. */
+HS_API int hs_parallel_forward_kf(const float *x, const float *c0, const float *w_ih,
+                                  const float *b_ih, float *z, float *out, float *c, float *h_n,
+                                  float *c_n, int64_t T, int64_t B, int64_t D, int64_t H, float eps,
+                                  void *workspace, size_t workspace_bytes, unsigned *kf,
+                                  int *dev_status, hs_stream_t stream);
+HS_API int hs_parallel_backward_kf(const float *x, const float *w_ih, float *z, const float *c,
+                                   const float *c0, const float *dout, const float *dh_n,
+                                   const float *dc_n, float *dx, float *dw_ih, float *db_ih,
+                                   float *dc0, int64_t T, int64_t B, int64_t D, int64_t H,
+                                   float eps, void *workspace, size_t workspace_bytes,
+                                   const unsigned *kf, int *dev_status, hs_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Recurrent path.  Replaces HeadStartLSTMTorchFn / HeadStartLSTMTritonFn

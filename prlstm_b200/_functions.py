@@ -107,10 +107,13 @@ class ParallelFn(torch.autograd.Function):
         ws = _lib.workspace(lib.hs_parallel_workspace_bytes(T, B, D, H), dev,
                             min_bytes=lib.hs_scan_workspace_bytes(T, B, H))
         P = _lib.ptr
-        _lib.call("hs_parallel_forward", P(x), P(c0), P(W_ih), P(b_ih), P(z), P(out), P(c),
-                  P(h_n), P(c_n), T, B, D, H, float(eps), P(ws), ws.numel(),
+        # kf: the forward's max of c_{t-1} f'(1-f'), which lets the backward
+        # hand dZ to the gradient GEMMs as its fp16 split
+        kf = torch.zeros(1, dtype=torch.int32, device=dev)
+        _lib.call("hs_parallel_forward_kf", P(x), P(c0), P(W_ih), P(b_ih), P(z), P(out), P(c),
+                  P(h_n), P(c_n), T, B, D, H, float(eps), P(ws), ws.numel(), P(kf),
                   P(_lib.status_word(dev)), _lib.stream_ptr(dev))
-        ctx.save_for_backward(x, c0, W_ih, z, c)
+        ctx.save_for_backward(x, c0, W_ih, z, c, kf)
         ctx.shape = (T, B, D, H)
         ctx.eps = float(eps)
         ctx.consumed = False
@@ -122,7 +125,7 @@ class ParallelFn(torch.autograd.Function):
             raise RuntimeError("Trying to backward through a prlstm_b200 parallel graph a "
                                "second time: its saved activations were consumed")
         ctx.consumed = True
-        x, c0, W_ih, z, c = ctx.saved_tensors
+        x, c0, W_ih, z, c, kf = ctx.saved_tensors
         T, B, D, H = ctx.shape
         dev = x.device
         dout = torch.zeros(T, B, H, device=dev) if dout is None else _f32c(dout)
@@ -136,9 +139,9 @@ class ParallelFn(torch.autograd.Function):
         ws = _lib.workspace(lib.hs_parallel_workspace_bytes(T, B, D, H), dev,
                             min_bytes=lib.hs_scan_workspace_bytes(T, B, H))
         P = _lib.ptr
-        _lib.call("hs_parallel_backward", P(x), P(W_ih), P(z), P(c), P(c0), P(dout), P(dh_n),
+        _lib.call("hs_parallel_backward_kf", P(x), P(W_ih), P(z), P(c), P(c0), P(dout), P(dh_n),
                   P(dc_n), P(dx), P(dW_ih), P(db_ih), P(dc0), T, B, D, H, ctx.eps, P(ws),
-                  ws.numel(), P(_lib.status_word(dev)), _lib.stream_ptr(dev))
+                  ws.numel(), P(kf), P(_lib.status_word(dev)), _lib.stream_ptr(dev))
         _lib.note_launch(dev)
         return dx, dc0, dW_ih, db_ih, None
 

@@ -52,6 +52,11 @@ int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStrea
 int scan_forward(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
                  int64_t T, int64_t B, int64_t H, float eps, void *ws, size_t ws_bytes,
                  int *status, cudaStream_t st, unsigned *kf_max = nullptr);
+size_t scan_split_ws_bytes(int64_t T, int64_t B, int64_t H);
+int scan_backward_split(float *z, const float *c, const float *c0, const float *dout, const float *dh_n,
+                        const float *dc_n, const unsigned *kf_max, void *dz_split, unsigned *dz_scale, float *dc0,
+                        float *db, int64_t T, int64_t B, int64_t H, float eps, void *ws_base, size_t ws_bytes,
+                        int *status, cudaStream_t st);
 int scan_backward(const float *z, const float *c, const float *c0, const float *dout,
                   const float *dh_n, const float *dc_n, float *dz, float *dc0, float *db,
                   int64_t T, int64_t B, int64_t H, float eps, void *ws, size_t ws_bytes,
@@ -241,30 +246,64 @@ int linear_backward(const float *dy, const float *x, const float *w, float *dx, 
                             nullptr);
 }
 
-// The scan's and the linear layer's scratch overlap (they run one after the
-// other); the last 256 bytes hold max |dz|, which the scan backward writes
-// and the gradient GEMMs' split reads.
-size_t parallel_ws_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
-  return std::max(scan_workspace(T, B, H), linear_ws_bytes(T * B, 4 * H, D)) + 256;
+// Scratch of the backward that takes dZ to the GEMMs as its fp16 split:
+// [dZ split][256 B: scale word][max(scan split scratch, GEMM scratch)].
+size_t parallel_fused_ws(int64_t T, int64_t B, int64_t D, int64_t H) {
+  const int64_t M = T * B, N = 4 * H;
+  return round_up(h3_split_bytes(M, N), 256) + 256 +
+         std::max(scan_split_ws_bytes(T, B, H), linear_backward_split_ws(M, N, D));
 }
 
+// The scan's and the linear layer's scratch overlap (they run one after the
+// other); the last 256 bytes hold max |dz|, which the scan backward writes
+// and the gradient GEMMs' split reads.  The split-handoff backward's layout
+// (parallel_fused_ws) is covered as well.
+size_t parallel_ws_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
+  return std::max(std::max(scan_workspace(T, B, H), linear_ws_bytes(T * B, 4 * H, D)) + 256,
+                  parallel_fused_ws(T, B, D, H));
+}
+
+// kf (device word, may be null): receives the forward's max of
+// c_{t-1} f'(1 - f') for the backward's dZ split (parallel_backward).
 int parallel_forward(const float *x, const float *c0, const float *w_ih, const float *b_ih,
                      float *z, float *out, float *c, float *h_n, float *c_n, int64_t T, int64_t B,
                      int64_t D, int64_t H, float eps, void *ws, size_t ws_bytes, int *status,
-                     cudaStream_t st) {
+                     cudaStream_t st, unsigned *kf = nullptr) {
   if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return fail(HS_ERR_INVALID_ARG, "T, B, D, H must be positive");
   if (!x || !w_ih || !z) return fail(HS_ERR_INVALID_ARG, "parallel_forward: null x/w_ih/z");
   if (int e = linear_forward(x, w_ih, b_ih, z, T * B, 4 * H, D, ws, ws_bytes, status, st)) return e;
-  return scan_forward(z, c0, out, c, h_n, c_n, T, B, H, eps, ws, ws_bytes, status, st);
+  return scan_forward(z, c0, out, c, h_n, c_n, T, B, H, eps, ws, ws_bytes, status, st, kf);
 }
 
 int parallel_backward(const float *x, const float *w_ih, float *z, const float *c,
                       const float *c0, const float *dout, const float *dh_n, const float *dc_n,
                       float *dx, float *dw_ih, float *db_ih, float *dc0, int64_t T, int64_t B,
                       int64_t D, int64_t H, float eps, void *ws, size_t ws_bytes, int *status,
-                      cudaStream_t st) {
+                      cudaStream_t st, const unsigned *kf = nullptr) {
   if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return fail(HS_ERR_INVALID_ARG, "T, B, D, H must be positive");
   if (!x || !w_ih || !z || !dw_ih || !db_ih) return fail(HS_ERR_INVALID_ARG, "parallel_backward: null x/w_ih/z/dw_ih/db_ih");
+  // With the forward's kf, room for it and a shape the tensor-core GEMMs
+  // take, dZ goes from the scan to the GEMMs as its fp16 split (never stored
+  // in float32); every condition the GEMMs check is checked here first, as
+  // there is no float32 dZ to fall back on afterwards.
+  const int64_t M = T * B, N = 4 * H;
+  if (kf && ws && aligned(ws, 256) && ws_bytes >= parallel_fused_ws(T, B, D, H) && N % 8 == 0 && D % 4 == 0 &&
+      M < (1ll << 31) && gemm_h3_enabled() && gemm_tc_size_ok(M, N, D) && gemm_tc_size_ok(N, D, M) &&
+      aligned(dw_ih, 16) && (!dx || aligned(dx, 16)) && aligned(x, 16) && aligned(w_ih, 16)) {
+    char *w8 = static_cast<char *>(ws);
+    const size_t sb = round_up(h3_split_bytes(M, N), 256);
+    unsigned *scale = reinterpret_cast<unsigned *>(w8 + sb);
+    char *rest = w8 + sb + 256;
+    const size_t rb = ws_bytes - sb - 256;
+    if (int e = scan_backward_split(z, c, c0, dout, dh_n, dc_n, kf, w8, scale, dc0, db_ih, T, B, H, eps, rest, rb,
+                                    status, st))
+      return e;
+    bool took = false;
+    if (int e = linear_backward_split_only(w8, scale, x, nullptr, nullptr, w_ih, dx, dw_ih, M, N, D, 0, rest, rb,
+                                           status, st, &took))
+      return e;
+    return took ? HS_OK : fail(HS_ERR_UNSUPPORTED, "parallel_backward: the split GEMMs declined the shape");
+  }
   // With room for it, max |dz| comes out of the scan (the split then reads dz once, not twice).
   unsigned *dz_absmax = nullptr;
   size_t wsb = ws_bytes & ~(size_t)255;
@@ -454,6 +493,24 @@ int hs_parallel_forward(const float *x, const float *c0, const float *w_ih, cons
                         size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
   return hs::parallel_forward(x, c0, w_ih, b_ih, z, out, c, h_n, c_n, T, B, D, H, eps, workspace,
                               workspace_bytes, dev_status, (cudaStream_t)stream);
+}
+
+int hs_parallel_forward_kf(const float *x, const float *c0, const float *w_ih, const float *b_ih, float *z,
+                           float *out, float *c, float *h_n, float *c_n, int64_t T, int64_t B, int64_t D, int64_t H,
+                           float eps, void *workspace, size_t workspace_bytes, unsigned *kf, int *dev_status,
+                           hs_stream_t stream) {
+  if (!kf || !hs::aligned(kf, 4)) return hs::fail(HS_ERR_INVALID_ARG, "hs_parallel_forward_kf: null or misaligned kf");
+  return hs::parallel_forward(x, c0, w_ih, b_ih, z, out, c, h_n, c_n, T, B, D, H, eps, workspace, workspace_bytes,
+                              dev_status, (cudaStream_t)stream, kf);
+}
+
+int hs_parallel_backward_kf(const float *x, const float *w_ih, float *z, const float *c, const float *c0,
+                            const float *dout, const float *dh_n, const float *dc_n, float *dx, float *dw_ih,
+                            float *db_ih, float *dc0, int64_t T, int64_t B, int64_t D, int64_t H, float eps,
+                            void *workspace, size_t workspace_bytes, const unsigned *kf, int *dev_status,
+                            hs_stream_t stream) {
+  return hs::parallel_backward(x, w_ih, z, c, c0, dout, dh_n, dc_n, dx, dw_ih, db_ih, dc0, T, B, D, H, eps,
+                               workspace, workspace_bytes, dev_status, (cudaStream_t)stream, kf);
 }
 
 int hs_parallel_backward(const float *x, const float *w_ih, float *z, const float *c,

@@ -108,6 +108,9 @@ CONFIGS = {
     "cfg3": dict(T=64, B=32, D=1024, H=2048, a_uniform=(0.0, 0.5), parallel=False),
     # configs[4] at full T on a 2-sequence batch slice
     "cfg4_slice": dict(T=16384, B=2, D=512, H=1024, a=0.0, bias_spread=8.0, parallel=True),
+    # configs[4]'s 32-sequence micro-batch at short T: enough columns for the
+    # per-column scan, so the backward hands dZ to the GEMMs as its fp16 split
+    "cfg4_columns": dict(T=256, B=32, D=512, H=1024, a=0.0, bias_spread=8.0, parallel=True),
 }
 
 
