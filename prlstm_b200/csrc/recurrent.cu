@@ -90,9 +90,16 @@ bool plan_dir(Dir &d, int rows, int BG, int64_t K) {
   return true;
 }
 
+// Largest chunk of the step matvec's k range (smaller chunks start the
+// multiply sooner after the step's exchange rows begin to arrive).
+#ifndef HS_REC_KC_MAX
+#define HS_REC_KC_MAX 256
+#endif
+
 void size_dir(Dir &d, int BP) {
   const size_t red = (size_t)NW * d.rows_pad * BP * 4;
   for (int kc : {256, 128, 64, 32}) {
+    if (kc > HS_REC_KC_MAX) continue;
     d.KC = kc;
     d.K_pad = (d.K + kc - 1) / kc * kc;
     const size_t xbuf = (size_t)kStages * kc * BP * 4;
@@ -101,6 +108,7 @@ void size_dir(Dir &d, int BP) {
   }
   d.resident = false;
   for (int kc : {128, 64, 32}) {
+    if (kc > HS_REC_KC_MAX && kc > 32) continue;
     d.KC = kc;
     d.K_pad = (d.K + kc - 1) / kc * kc;
     d.smem = (size_t)kStages * kc * (BP + d.rows_pad) * 4 + red;
