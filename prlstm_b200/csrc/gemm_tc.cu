@@ -1011,7 +1011,10 @@ gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__
     // ---------------- fold finished groups, epilogue per tile
     const int t = threadIdx.x - 64;  // 0..127
     const int q = warp & 3;
-    const float inv = 1.0f / (pow2_scale(*absmax_a) * pow2_scale(*absmax_b));  // exact: a power of two
+    // Undo the two operand scales one at a time: each inverse is an exact
+    // power of two within float range, their product may not be (tiny
+    // operands get scales up to 2^114 each).
+    const float inv_a = 1.0f / pow2_scale(*absmax_a), inv_b = 1.0f / pow2_scale(*absmax_b);
     int gg = 0;
     bool ok = true;
     for (int tl = blockIdx.x; tl < ntiles_total && ok; tl += gridDim.x) {
@@ -1041,7 +1044,7 @@ gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__
       }
       if (!ok) break;
 #pragma unroll
-      for (int j = 0; j < BN; ++j) tot[j] *= inv;
+      for (int j = 0; j < BN; ++j) tot[j] = (tot[j] * inv_a) * inv_b;
       store_tile_boxes(tot, epi, &tmC, p, q, lane, t, m0, n0, p.partial ? z : 0);
     }
   }
@@ -1301,7 +1304,10 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
     const int half = e >> 2;           // 128-column half of the tile
     const int q = warp & 3;            // TMEM lane quarter of this warp
     const int t = (e & 3) * 32 + lane;  // 0..127 within the half's group
-    const float inv = 1.0f / (pow2_scale(*absmax_a) * pow2_scale(*absmax_b));  // exact: a power of two
+    // Undo the two operand scales one at a time: each inverse is an exact
+    // power of two within float range, their product may not be (tiny
+    // operands get scales up to 2^114 each).
+    const float inv_a = 1.0f / pow2_scale(*absmax_a), inv_b = 1.0f / pow2_scale(*absmax_b);
     const uint32_t pe0 = cluster_addr(&pempty[0], 0), pe1 = cluster_addr(&pempty[1], 0);
     const uint32_t pf0 = cluster_addr(&pfull[0], 1), pf1 = cluster_addr(&pfull[1], 1);
     int gg = 0;
@@ -1334,7 +1340,7 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
       }
       if (!ok) break;
 #pragma unroll
-      for (int j = 0; j < BN; ++j) tot[j] *= inv;
+      for (int j = 0; j < BN; ++j) tot[j] = (tot[j] * inv_a) * inv_b;
       store_tile_boxes(tot, epi + half * (H3_EPI / 4), &tmC, p, q, lane, t, m0 + 128 * (int64_t)rank,
                        n0 + (int64_t)half * BN, p.partial ? z : 0, 1 + half);
     }

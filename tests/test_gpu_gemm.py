@@ -210,3 +210,28 @@ def test_linear_backward_with_known_absmax(M, N, K, beta):
     ref_dw = dy64.t() @ x64 + (dw0.double().cpu() if beta else 0)
     assert _rel(res["loose"][1], ref_dw) < TOL
     assert _rel(res["loose"][0], dy64 @ w64) < TOL
+
+
+@pytest.mark.parametrize("scale", [1e-30, 1e30])
+def test_linear_backward_extreme_magnitudes(scale):
+    """dy of magnitude 1e-30 or 1e30: the operand scales of the fp16 split
+    reach 2^114 / 2^-85, so the descale is applied one operand at a time
+    (their product would leave float range)."""
+    L = _lib()
+    dev = torch.device("cuda", 0)
+    M, N, K = 4096, 1024, 256
+    g = torch.Generator(device=dev).manual_seed(11)
+    dy = torch.randn(M, N, device=dev, generator=g) * scale
+    x = torch.randn(M, K, device=dev, generator=g)
+    w = torch.randn(N, K, device=dev, generator=g) / K ** 0.5
+    dx = torch.empty(M, K, device=dev)
+    dw = torch.empty(N, K, device=dev)
+    ws, n = _ws(L, M, N, K, dev)
+    P = L.ptr
+    L.call("hs_linear_backward", P(dy), P(x), P(w), P(dx), P(dw), M, N, K, 0, P(ws), n, P(L.status_word(dev)),
+           L.stream_ptr(dev))
+    torch.cuda.synchronize(dev)
+    L.check_device_status(dev)
+    dy64, x64, w64 = dy.double().cpu(), x.double().cpu(), w.double().cpu()
+    assert _rel(dx, dy64 @ w64) < TOL
+    assert _rel(dw, dy64.t() @ x64) < TOL

@@ -132,6 +132,64 @@ def test_config_parity_vs_oracle(cfg):
         assert_close(ours, truth, 1e-5, cfg + " vs fp64")
 
 
+def test_split_handoff_rerun_through_module():
+    """Output and input gates saturated shut (biases -60): dZ is some 2^40
+    below the bound from sum |dout|, so the module's backward takes the
+    exact-maximum re-run of the split handoff; gradients still match the
+    float64 oracle."""
+    T, B, D, H = 64, 32, 64, 1024
+    params, x, G = make_inputs(T, B, D, H, a=0.0, seed=4)
+    b_ih = params[2].clone()
+    b_ih[0:H] = -60.0
+    b_ih[3 * H:4 * H] = -60.0
+    params = (params[0], params[1], b_ih, params[3], params[4])
+    ours = run_ours(params, x, G, parallel=True)
+    truth = O.module_forward_backward(tuple(t.double() for t in params), x.double(), G.double(),
+                                      parallel=True, linear_truth=True)
+    assert_close(ours, truth, 1e-5, "saturated gates vs fp64")
+
+
+def test_scan_forward_kf_value():
+    """hs_scan_forward_kf's word equals max over steps of c_{t-1} f'(1 - f')
+    (float64 of the same inputs, relative 1e-5), on both scan paths."""
+    import os
+    from prlstm_b200 import _lib as L
+
+    T, B, H = 300, 24, 256
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(8)
+    z = 2.0 * torch.randn(T, B, 4 * H, device=dev, generator=g)
+    c0 = torch.rand(B, H, device=dev, generator=g)
+    eps = 1e-6
+    zd, c0d = z.double().cpu(), c0.double().cpu()
+    i, f, gg, o = torch.sigmoid(zd).chunk(4, dim=-1)
+    fp, bp = f.clamp(min=eps), (i * gg).clamp(min=eps)
+    cprev = c0d.clamp(min=eps)
+    kf = 0.0
+    for t in range(T):
+        kf = max(kf, (cprev * fp[t] * (1 - fp[t])).max().item())
+        cprev = fp[t] * cprev + bp[t]
+    lib = L.load()
+    for path in ("chain", "lookback"):
+        old = os.environ.get("HS_SCAN_PATH")
+        os.environ["HS_SCAN_PATH"] = path
+        try:
+            ws = L.workspace(lib.hs_scan_workspace_bytes(T, B, H), dev)
+            words = torch.zeros(4, dtype=torch.int32, device=dev)
+            out = torch.empty(T, B, H, device=dev)
+            c = torch.empty(T, B, H, device=dev)
+            L.call("hs_scan_forward_kf", L.ptr(z), L.ptr(c0), L.ptr(out), L.ptr(c), None, None, T, B, H, eps,
+                   L.ptr(ws), ws.numel(), L.ptr(words), L.ptr(L.status_word(dev)), L.stream_ptr(dev))
+            torch.cuda.synchronize(dev)
+        finally:
+            if old is None:
+                del os.environ["HS_SCAN_PATH"]
+            else:
+                os.environ["HS_SCAN_PATH"] = old
+        got = words[:1].cpu().view(torch.float32).item()
+        assert abs(got - kf) <= 1e-5 * kf, (path, got, kf)
+
+
 # ------------------------------------------------------------ reference test suite, ported
 def test_parallel_equals_recurrent_at_zero_a():
     """tests/test_parallel.py:47-60 of the reference."""
