@@ -50,7 +50,7 @@ int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStrea
 namespace {
 
 #ifndef HS_REC_KUNROLL
-#define HS_REC_KUNROLL 1
+#define HS_REC_KUNROLL 4
 #endif
 constexpr int kKUnroll = HS_REC_KUNROLL;  // k-loop unroll of the step matvec
 constexpr int NW = 8;          // warps per CTA
@@ -265,7 +265,9 @@ HS_DEV bool grid_barrier(unsigned *bar, unsigned target, int *status) {
 // K-split FFMA matvec of one step: out[rows_pad][BP] += W[K][rows_pad]^T-contract X[K][BP].
 // W: resident smem (wres != null) or streamed from global wsrc; X streamed from xsrc.
 // Leaves the per-warp partials in red[NW][rows_pad][BP].
-template <int BG, int RG>
+// NR: row tiles per thread the kernel is compiled for (d.NRT <= NR); the
+// accumulators take NR x 16 registers, so small row counts get small kernels.
+template <int BG, int RG, int NR>
 HS_DEV void step_matvec(const float *wres, const float *wsrc, const float *xsrc, float *xbuf,
                         float *wbuf, float *red, const Dir &d, int BP) {
   constexpr int KSL = 32 / (BG * RG);
@@ -276,9 +278,9 @@ HS_DEV void step_matvec(const float *wres, const float *wsrc, const float *xsrc,
   const int q = warp * KSL + ks;  // k-lane index within a chunk
   const int QN = NW * KSL;
   const int rp = d.rows_pad;
-  float acc[4][4][4];
+  float acc[NR][4][4];
 #pragma unroll
-  for (int rt = 0; rt < 4; ++rt)
+  for (int rt = 0; rt < NR; ++rt)
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -314,7 +316,7 @@ HS_DEV void step_matvec(const float *wres, const float *wsrc, const float *xsrc,
     for (int k = q; k < d.KC; k += QN) {
       const float4 xv = *reinterpret_cast<const float4 *>(X + k * BP + bg * 4);
 #pragma unroll
-      for (int rt = 0; rt < 4; ++rt) {
+      for (int rt = 0; rt < NR; ++rt) {
         if (rt < d.NRT) {
           const float4 wv = *reinterpret_cast<const float4 *>(W + k * rp + rt * RG * 4 + rg * 4);
           const float w4[4] = {wv.x, wv.y, wv.z, wv.w};
@@ -332,14 +334,14 @@ HS_DEV void step_matvec(const float *wres, const float *wsrc, const float *xsrc,
 #pragma unroll
   for (int off = 1; off < KSL; off <<= 1)
 #pragma unroll
-    for (int rt = 0; rt < 4; ++rt)
+    for (int rt = 0; rt < NR; ++rt)
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[rt][i][j] += __shfl_xor_sync(0xffffffffu, acc[rt][i][j], off);
   if (ks == 0) {
 #pragma unroll
-    for (int rt = 0; rt < 4; ++rt) {
+    for (int rt = 0; rt < NR; ++rt) {
       if (rt < d.NRT) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -375,7 +377,7 @@ struct RecArgs {
 };
 
 // ------------------------------------------------------------------ forward
-template <int BG, int RG>
+template <int BG, int RG, int NR>
 __global__ void __launch_bounds__(NT, 1) rec_fwd_kernel(RecArgs p) {
   extern __shared__ __align__(16) float smem[];
   const Dir &d = p.d;
@@ -430,7 +432,7 @@ __global__ void __launch_bounds__(NT, 1) rec_fwd_kernel(RecArgs p) {
       }
     }
     const float *xsrc = p.xf + (int64_t)(t & 1) * d.K_pad * BP;
-    step_matvec<BG, RG>(wres, wsrc, xsrc, xbuf, wbuf, red, d, BP);
+    step_matvec<BG, RG, NR>(wres, wsrc, xsrc, xbuf, wbuf, red, d, BP);
     float *xdst = p.xf + (int64_t)((t + 1) & 1) * d.K_pad * BP;
 #pragma unroll
     for (int e = 0; e < kMaxPairs; ++e) {
@@ -463,7 +465,7 @@ __global__ void __launch_bounds__(NT, 1) rec_fwd_kernel(RecArgs p) {
 }
 
 // ------------------------------------------------------------------ backward
-template <int BG, int RG>
+template <int BG, int RG, int NR>
 __global__ void __launch_bounds__(NT, 1) rec_bwd_kernel(RecArgs p) {
   extern __shared__ __align__(16) float smem[];
   const Dir &d = p.d;
@@ -515,7 +517,7 @@ __global__ void __launch_bounds__(NT, 1) rec_bwd_kernel(RecArgs p) {
     }
     if (t < p.T - 1) {
       const float *xsrc = p.xb + (int64_t)((t + 1) & 1) * d.K_pad * BP;
-      step_matvec<BG, RG>(wres, wsrc, xsrc, xbuf, wbuf, red, d, BP);
+      step_matvec<BG, RG, NR>(wres, wsrc, xsrc, xbuf, wbuf, red, d, BP);
     }
     float *xdst = p.xb + (int64_t)(t & 1) * d.K_pad * BP;
 #pragma unroll
@@ -599,24 +601,25 @@ __global__ void rec_da_kernel(const float *__restrict__ part, float *__restrict_
 
 using KernelFn = void (*)(RecArgs);
 
-KernelFn pick_fwd(int BG, int RG) {
-#define HS_CASE(bg, rg) if (BG == bg && RG == rg) return rec_fwd_kernel<bg, rg>;
-  HS_CASE(1, 1) HS_CASE(1, 2) HS_CASE(1, 4) HS_CASE(1, 8)
-  HS_CASE(2, 1) HS_CASE(2, 2) HS_CASE(2, 4) HS_CASE(2, 8)
-  HS_CASE(4, 1) HS_CASE(4, 2) HS_CASE(4, 4) HS_CASE(4, 8)
-  HS_CASE(8, 1) HS_CASE(8, 2) HS_CASE(8, 4)
-#undef HS_CASE
+// NR = 1, 2 or 4 (a plan with 3 row tiles takes the 4-tile kernel).
+#define HS_CASES(K)                                                                        \
+  HS_CASE(K, 1, 1) HS_CASE(K, 1, 2) HS_CASE(K, 1, 4) HS_CASE(K, 1, 8)                       \
+  HS_CASE(K, 2, 1) HS_CASE(K, 2, 2) HS_CASE(K, 2, 4) HS_CASE(K, 2, 8)                       \
+  HS_CASE(K, 4, 1) HS_CASE(K, 4, 2) HS_CASE(K, 4, 4) HS_CASE(K, 4, 8)                       \
+  HS_CASE(K, 8, 1) HS_CASE(K, 8, 2) HS_CASE(K, 8, 4)
+#define HS_CASE(K, bg, rg)                                                                 \
+  if (BG == bg && RG == rg)                                                                \
+    return NRT <= 1 ? K<bg, rg, 1> : NRT <= 2 ? K<bg, rg, 2> : K<bg, rg, 4>;
+KernelFn pick_fwd(int BG, int RG, int NRT) {
+  HS_CASES(rec_fwd_kernel)
   return nullptr;
 }
-KernelFn pick_bwd(int BG, int RG) {
-#define HS_CASE(bg, rg) if (BG == bg && RG == rg) return rec_bwd_kernel<bg, rg>;
-  HS_CASE(1, 1) HS_CASE(1, 2) HS_CASE(1, 4) HS_CASE(1, 8)
-  HS_CASE(2, 1) HS_CASE(2, 2) HS_CASE(2, 4) HS_CASE(2, 8)
-  HS_CASE(4, 1) HS_CASE(4, 2) HS_CASE(4, 4) HS_CASE(4, 8)
-  HS_CASE(8, 1) HS_CASE(8, 2) HS_CASE(8, 4)
-#undef HS_CASE
+KernelFn pick_bwd(int BG, int RG, int NRT) {
+  HS_CASES(rec_bwd_kernel)
   return nullptr;
 }
+#undef HS_CASE
+#undef HS_CASES
 
 int num_sms() {
   int dev = 0, n = 0;
@@ -677,7 +680,7 @@ int rec_forward(const float *x, const float *h0, const float *c0, const float *w
   rec_prep_fwd_kernel<<<dim3((unsigned)((pl.fwd.K_pad + 31) / 32), (unsigned)pl.ncta), 256, 0, st>>>(
       w_hh, b_hh, a, (float *)(w + pl.o_wf), (float *)(w + pl.o_bf), H, pl.U, pl.fwd.rows_pad, pl.fwd.K_pad);
   if (int e = check_launch("rec_prep_fwd_kernel")) return e;
-  KernelFn fn = pick_fwd(pl.BG, pl.fwd.RG);
+  KernelFn fn = pick_fwd(pl.BG, pl.fwd.RG, pl.fwd.NRT);
   if (!fn) return fail(HS_ERR_UNSUPPORTED, "recurrent_forward: no kernel for BG=%d RG=%d", pl.BG, pl.fwd.RG);
   for (int64_t b0 = 0; b0 < B; b0 += kMaxBatch) {
     if (cudaMemsetAsync(w + pl.o_bar, 0, 256, st) != cudaSuccess) return check_launch("memset(bar)");
@@ -729,7 +732,7 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
                                            pl.U, pl.ncta, pl.fwd.rows_pad, pl.fwd.K_pad, pl.bwd.rows_pad,
                                            pl.bwd.K_pad);
   if (int e = check_launch("rec_prep_kernel")) return e;
-  KernelFn fn = pick_bwd(pl.BG, pl.bwd.RG);
+  KernelFn fn = pick_bwd(pl.BG, pl.bwd.RG, pl.bwd.NRT);
   if (!fn) return fail(HS_ERR_UNSUPPORTED, "recurrent_backward: no kernel for BG=%d RG=%d", pl.BG, pl.bwd.RG);
   for (int64_t b0 = 0; b0 < B; b0 += kMaxBatch) {
     if (cudaMemsetAsync(w + pl.o_bar, 0, 256, st) != cudaSuccess) return check_launch("memset(bar)");
