@@ -53,7 +53,10 @@ namespace {
 #define HS_REC_KUNROLL 4
 #endif
 constexpr int kKUnroll = HS_REC_KUNROLL;  // k-loop unroll of the step matvec
-constexpr int NW = 8;          // warps per CTA
+#ifndef HS_REC_NW
+#define HS_REC_NW 8
+#endif
+constexpr int NW = HS_REC_NW;  // warps per CTA
 constexpr int NT = NW * 32;
 constexpr int kMaxPairs = 4;   // (unit, batch) pairs per thread in the epilogue
 constexpr int kMaxBatch = 32;  // batch rows per launch (larger B: several launches)
