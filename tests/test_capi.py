@@ -83,3 +83,32 @@ def test_recurrent_rejects_null_pointers(lib):
 def test_gemm_rejects_negative_extent(lib):
     P = ctypes.c_void_p
     assert lib.hs_linear_forward(P(16), P(16), None, P(16), -1, 4, 4, None, 0, None, None) == 1
+
+
+def test_split_handoff_workspace_queries(lib):
+    """Sizes of the split-handoff path: a split buffer holds hi and lo fp16
+    rows padded to 8 columns; the parallel workspace covers the layout the
+    backward uses for the handoff (dZ split + scale word + scan or GEMM
+    scratch); non-positive extents give 0."""
+    assert lib.hs_split_bytes(4, 8) == 256  # 4 * 4 * 8 bytes rounded up to 256
+    assert lib.hs_split_bytes(1000, 6) >= 4 * 1000 * 8
+    assert lib.hs_split_bytes(0, 8) == 0 and lib.hs_split_bytes(4, 0) == 0
+    T, B, D, H = 16384, 32, 512, 1024
+    M, N = T * B, 4 * H
+    dz_split = lib.hs_split_bytes(M, N)
+    need = dz_split + 256 + max(lib.hs_scan_split_workspace_bytes(T, B, H),
+                                lib.hs_linear_presplit_workspace_bytes(M, N, D))
+    assert lib.hs_parallel_workspace_bytes(T, B, D, H) >= need
+    assert lib.hs_scan_split_workspace_bytes(T, B, H) > lib.hs_scan_workspace_bytes(T, B, H)
+    assert lib.hs_scan_split_workspace_bytes(0, B, H) == 0
+    assert lib.hs_linear_presplit_workspace_bytes(M, N, 0) == 0
+
+
+def test_split_entry_points_reject_bad_arguments(lib):
+    P = ctypes.c_void_p
+    assert lib.hs_split(None, 4, 8, P(256), P(256), None) == 1
+    assert lib.hs_split(P(256), 4, 8, P(8), P(256), None) == 1  # destination not 16-byte aligned
+    assert lib.hs_linear_backward_presplit(None, P(256), P(256), None, None, P(256), P(256), P(256), 64, 64, 64,
+                                           0, P(256), 1 << 20, P(16), None) == 1
+    assert lib.hs_scan_forward_kf(P(16), None, P(16), P(16), None, None, 4, 2, 8, 1e-6, P(256), 1 << 20, None,
+                                  P(16), None) == 1
