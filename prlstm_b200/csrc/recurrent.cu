@@ -50,7 +50,7 @@ int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStrea
 namespace {
 
 #ifndef HS_REC_KUNROLL
-#define HS_REC_KUNROLL 4
+#define HS_REC_KUNROLL 8
 #endif
 constexpr int kKUnroll = HS_REC_KUNROLL;  // k-loop unroll of the step matvec
 #ifndef HS_REC_NW
