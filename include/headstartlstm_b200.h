@@ -65,8 +65,10 @@ HS_API int hs_clear_status(int *dev_status, hs_stream_t stream);
 /* Failure-detection self test: launches one CTA that waits on *flag (a
  * device word nothing sets) with the library's bounded wait, shortened to
  * limit_ns.  The wait gives up, records HS_ERR_DEVICE_TIMEOUT in *dev_status
- * and the kernel returns; the context stays usable.  No reference counterpart
- * (the reference has no device-side waits). */
+ * and the kernel returns; the context stays usable.  dev_status NULL targets
+ * the library's own word of NULL-status hs_scan_forward_noalloc calls on the
+ * current device (read it with hs_scan_noalloc_status).  No reference
+ * counterpart (the reference has no device-side waits). */
 HS_API int hs_selftest_bounded_wait(const unsigned *flag, int *dev_status, uint64_t limit_ns,
                                     hs_stream_t stream);
 /* Accuracy self test of the scan kernels' activation functions: evaluates
@@ -232,11 +234,23 @@ HS_API int hs_scan_backward_split(float *z, const float *c, const float *c0, con
  * The first call on each device looks up the array's device address, so
  * make that first call before any stream capture.  All calls share the
  * array: calls that overlap on the GPU (other streams, other threads) race
- * and must be serialised by the caller.  dev_status may be NULL (a status
- * word inside the library is used).  Allocates nothing. */
+ * and must be serialised by the caller.  Allocates nothing.
+ * dev_status may be NULL: the call then reports into a status word inside the
+ * library (one per device), which it first clears in stream order, so that
+ * word describes the most recent NULL-status call on that device only; read
+ * it with hs_scan_noalloc_status before the next such call.  Shapes that take
+ * the one-CTA-per-column chain kernels (many columns, B * ceil(H/32) filling
+ * the GPU) use no scratch and have no size limit. */
 HS_API int hs_scan_forward_noalloc(const float *z, const float *c0, float *out, float *c,
                                    float *h_n, float *c_n, int64_t T, int64_t B, int64_t H,
                                    float eps, int *dev_status, hs_stream_t stream);
+/* Outcome of the most recent hs_scan_forward_noalloc call made with
+ * dev_status == NULL on the current device: synchronises `stream`, writes
+ * the library's status word (HS_OK, or HS_ERR_DEVICE_TIMEOUT if a bounded
+ * wait gave up and out/c were not fully written) to *host_status and clears
+ * it.  No counterpart in the reference (its calls allocate through PyTorch
+ * and have no device-side waits).  Allocates nothing. */
+HS_API int hs_scan_noalloc_status(int *host_status, hs_stream_t stream);
 
 /* Whole parallel-mode forward: z = x W_ih^T + b_ih (z is caller-owned
  * [T,B,4H] scratch kept for the backward), then hs_scan_forward. */

@@ -228,6 +228,63 @@ def par_backward_linear(saved, dout, dh_n=None, dc_n=None):
     return dx, dW_ih, db_ih, dc0, dZ
 
 
+def par_linear_chunked(zchunk, T, c0, dout, dh_n=None, dc_n=None, eps: float = EPS, chunk: int = 512,
+                       on_dz=None):
+    """``par_forward_linear`` + ``par_backward_linear`` evaluated in chunks of
+    time steps, so that no [T,B,4H] tensor is ever held: the checker for the
+    benchmark's full sizes (T=16384, B=32, H=1024 is 17 GB of float64 Z),
+    run on whatever device its inputs live on.
+
+    ``zchunk(t0, t1)`` returns the gate pre-activations Z[t0:t1] ([n,B,4H]);
+    it is called once per chunk forward and once backward.  ``on_dz(t0, t1,
+    dZ)`` receives dZ[t0:t1] in reverse chunk order (to form dX and dW_ih).
+    Returns dict(out [T,B,H], c [T,B,H], h_n, c_n, dc0, db (sum of dZ over
+    t and b, [4H]))."""
+    c_prev = torch.clamp(c0, min=eps)
+    B, H = c0.shape
+    out = c0.new_empty(T, B, H)
+    c = c0.new_empty(T, B, H)
+    for t0 in range(0, T, chunk):
+        t1 = min(T, t0 + chunk)
+        i_, f_, g_, o_ = torch.sigmoid(zchunk(t0, t1)).chunk(4, dim=-1)
+        fp = torch.clamp(f_, min=eps)
+        bp = torch.clamp(i_ * g_, min=eps)
+        for t in range(t1 - t0):
+            c_prev = fp[t] * c_prev + bp[t]
+            c[t0 + t] = c_prev
+        out[t0:t1] = o_ * torch.tanh(c[t0:t1])
+    e = torch.zeros_like(c0)
+    db = c0.new_zeros(4 * H)
+    c0p = torch.clamp(c0, min=eps)
+    starts = list(range(0, T, chunk))
+    for t0 in reversed(starts):
+        t1 = min(T, t0 + chunk)
+        i_, f_, g_, o_ = torch.sigmoid(zchunk(t0, t1)).chunk(4, dim=-1)
+        fp = torch.clamp(f_, min=eps)
+        b = i_ * g_
+        th = torch.tanh(c[t0:t1])
+        dd = dout[t0:t1].clone()
+        if dh_n is not None and t1 == T:
+            dd[-1] += dh_n
+        dcd = dd * o_ * (1.0 - th * th)
+        if dc_n is not None and t1 == T:
+            dcd[-1] += dc_n
+        dc = torch.empty_like(dcd)
+        for t in range(t1 - t0 - 1, -1, -1):
+            dc[t] = dcd[t] + e
+            e = fp[t] * dc[t]
+        c_prev_c = torch.cat([(c0p if t0 == 0 else c[t0 - 1]).unsqueeze(0), c[t0:t1 - 1]], dim=0)
+        df = dc * c_prev_c * (f_ >= eps).to(c.dtype)
+        dbb = dc * (b >= eps).to(c.dtype)
+        dZ = torch.cat([dbb * g_ * i_ * (1 - i_), df * f_ * (1 - f_),
+                        dbb * i_ * g_ * (1 - g_), dd * th * o_ * (1 - o_)], dim=-1)
+        db += dZ.sum(dim=(0, 1))
+        if on_dz is not None:
+            on_dz(t0, t1, dZ)
+    dc0 = e * (c0 >= eps).to(c.dtype)
+    return dict(out=out, c=c, h_n=out[-1].clone(), c_n=c[-1].clone(), dc0=dc0, db=db)
+
+
 # --------------------------------------------------------------------------
 # Module-level helpers (HeadStartLSTM semantics, __init__.py:131-233)
 # --------------------------------------------------------------------------

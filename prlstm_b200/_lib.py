@@ -54,6 +54,7 @@ SIGNATURES = {
     "hs_parallel_workspace_bytes": (_sz, [_i64] * 4),
     "hs_scan_forward": (_i32, [_c_p] * 6 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_scan_forward_noalloc": (_i32, [_c_p] * 6 + [_i64] * 3 + [_f32, _c_p, _c_p]),
+    "hs_scan_noalloc_status": (_i32, [_c_p, _c_p]),
     "hs_scan_backward": (_i32, [_c_p] * 9 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_scan_backward_absmax": (_i32, [_c_p] * 9 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),
     "hs_scan_forward_kf": (_i32, [_c_p] * 6 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),

@@ -48,6 +48,7 @@ int gemm_h3_presplit(const void *a_split, const unsigned *a_absmax, bool a_mn, c
                      int64_t K, int64_t ldc, int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st,
                      bool *done);
 size_t scan_workspace(int64_t T, int64_t B, int64_t H);
+int noalloc_status_word(int **word);
 int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st);
 int scan_forward(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
                  int64_t T, int64_t B, int64_t H, float eps, void *ws, size_t ws_bytes,
@@ -384,8 +385,13 @@ int hs_clear_status(int *dev_status, hs_stream_t stream) {
 
 int hs_selftest_bounded_wait(const unsigned *flag, int *dev_status, uint64_t limit_ns,
                              hs_stream_t stream) {
-  if (!flag || !dev_status) return hs::fail(HS_ERR_INVALID_ARG, "null flag/status");
+  if (!flag) return hs::fail(HS_ERR_INVALID_ARG, "null flag");
   if (limit_ns > hs::kWaitLimitNs) return hs::fail(HS_ERR_INVALID_ARG, "limit above the library's wait bound");
+  if (!dev_status) {
+    // NULL: the library's own word that NULL-status hs_scan_forward_noalloc
+    // calls report into (so a test can plant a timeout there)
+    if (int e = hs::noalloc_status_word(&dev_status)) return e;
+  }
   hs::selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flag, dev_status, limit_ns);
   return hs::check_launch("selftest_wait_kernel");
 }

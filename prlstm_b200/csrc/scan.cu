@@ -801,20 +801,50 @@ int scan_forward_noalloc(const float *z, const float *c0, float *out, float *c, 
                          int *dev_status, cudaStream_t st) {
   if (int e = check_scan_args(T, B, H)) return e;
   if (!z || !out || !c) return fail(HS_ERR_INVALID_ARG, "scan_forward_noalloc: null z/out/c");
-  const size_t need = ws_layout(make_shape(T, B, H, kFwdL, kFwdWPC), false, nullptr, nullptr);
-  if (need > kNoAllocScratchBytes)
-    return fail(HS_ERR_UNSUPPORTED,
-                "hs_scan_forward_noalloc: T=%lld B=%lld H=%lld needs %zu bytes of scratch, above "
-                "the fixed %zu-byte array; use hs_scan_forward with a caller workspace",
-                (long long)T, (long long)B, (long long)H, need, kNoAllocScratchBytes);
+  // Shapes that scan_forward sends to the one-CTA-per-column chain kernels
+  // use no scratch at all; only the look-back path is limited by the array.
+  if (!scan_chain_wanted(T, B, H)) {
+    const size_t need = ws_layout(make_shape(T, B, H, kFwdL, kFwdWPC), false, nullptr, nullptr);
+    if (need > kNoAllocScratchBytes)
+      return fail(HS_ERR_UNSUPPORTED,
+                  "hs_scan_forward_noalloc: T=%lld B=%lld H=%lld needs %zu bytes of scratch, above "
+                  "the fixed %zu-byte array; use hs_scan_forward with a caller workspace",
+                  (long long)T, (long long)B, (long long)H, need, kNoAllocScratchBytes);
+  }
   void *scratch = nullptr;
   int *own_status = nullptr;
   if (int e = noalloc_scratch(&scratch, &own_status)) return e;
+  if (!dev_status) {
+    // The library's own status word reports this call only: cleared in
+    // stream order first, so a wait that gave up in an earlier call does not
+    // make this one's kernels return at entry.  hs_scan_noalloc_status reads
+    // and clears it.
+    if (cudaMemsetAsync(own_status, 0, sizeof(int), st) != cudaSuccess)
+      return check_launch("hs_scan_forward_noalloc status memset");
+  }
   // scan_forward zeroes the look-back words (all that must start at zero)
   // with a stream-ordered memset before its launch; the chain kernels it may
   // pick instead use no scratch.
   return scan_forward(z, c0, out, c, h_n, c_n, T, B, H, eps, scratch, kNoAllocScratchBytes,
                       dev_status ? dev_status : own_status, st);
+}
+
+int noalloc_status_word(int **word) {
+  void *scratch = nullptr;
+  return noalloc_scratch(&scratch, word);
+}
+
+int scan_noalloc_status(int *host_status, cudaStream_t st) {
+  if (!host_status) return fail(HS_ERR_INVALID_ARG, "hs_scan_noalloc_status: null host_status");
+  void *scratch = nullptr;
+  int *own_status = nullptr;
+  if (int e = noalloc_scratch(&scratch, &own_status)) return e;
+  if (cudaMemcpyAsync(host_status, own_status, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return check_launch("hs_scan_noalloc_status read");
+  if (cudaMemsetAsync(own_status, 0, sizeof(int), st) != cudaSuccess)
+    return check_launch("hs_scan_noalloc_status clear");
+  if (cudaStreamSynchronize(st) != cudaSuccess) return check_launch("hs_scan_noalloc_status sync");
+  return HS_OK;
 }
 
 }  // namespace hs
@@ -880,6 +910,10 @@ int hs_scan_forward_noalloc(const float *z, const float *c0, float *out, float *
                             int *dev_status, hs_stream_t stream) {
   return hs::scan_forward_noalloc(z, c0, out, c, h_n, c_n, T, B, H, eps, dev_status,
                                   (cudaStream_t)stream);
+}
+
+int hs_scan_noalloc_status(int *host_status, hs_stream_t stream) {
+  return hs::scan_noalloc_status(host_status, (cudaStream_t)stream);
 }
 
 }  // extern "C"

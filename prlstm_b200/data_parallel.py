@@ -20,7 +20,8 @@ from typing import Iterable, List, Optional, Sequence, Tuple
 
 import torch
 
-__all__ = ["shard_range", "shard_batch", "GradAllReducer", "allreduce_grads"]
+__all__ = ["shard_range", "shard_batch", "GradAllReducer", "allreduce_grads", "PeerMonitor",
+           "PeerFailure"]
 
 
 def shard_range(batch: int, rank: int, world: int) -> Tuple[int, int]:
@@ -46,8 +47,65 @@ def shard_batch(x: torch.Tensor, rank: int, world: int, batch_first: bool = Fals
     return x.narrow(dim, s, e - s)
 
 
+class PeerFailure(RuntimeError):
+    """A rank did not reach a step within the heartbeat timeout."""
+
+    def __init__(self, step: int, missing: Sequence[int]):
+        self.step = step
+        self.missing = list(missing)
+        super().__init__(f"ranks {self.missing} did not reach step {step}: presumed failed")
+
+
+class PeerMonitor:
+    """Host-side heartbeat through a ``torch.distributed`` store, checked
+    before each step's collective.
+
+    Every rank records the step it has reached (``beat``) and then waits, up
+    to ``timeout_s``, for every other rank's record of the same step
+    (``wait``).  A rank that raised or exited between steps never writes its
+    record, so the others learn of it on the host, with ``PeerFailure``
+    naming it, before they launch a collective that could not complete.  A
+    rank leaves only between steps, with nothing of its own in flight.
+    """
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 10.0, prefix: str = "hs_hb"):
+        self.store = store
+        self.rank = rank
+        self.world = world
+        self.timeout_s = float(timeout_s)
+        self.prefix = prefix
+
+    def _key(self, rank: int, step: int) -> str:
+        return f"{self.prefix}/{step}/{rank}"
+
+    def beat(self, step: int) -> None:
+        self.store.set(self._key(self.rank, step), "1")
+
+    def wait(self, step: int) -> None:
+        import time
+
+        others = [r for r in range(self.world) if r != self.rank]
+        deadline = time.monotonic() + self.timeout_s
+        pending = list(others)
+        while pending:
+            pending = [r for r in pending if not self.store.check([self._key(r, step)])]
+            if not pending:
+                return
+            if time.monotonic() > deadline:
+                raise PeerFailure(step, pending)
+            time.sleep(0.01)
+
+    def step(self, step: int) -> None:
+        self.beat(step)
+        self.wait(step)
+
+
 class GradAllReducer:
     """Sums gradients over the process group with one collective per dtype.
+
+    With a ``PeerMonitor`` every call first checks, on the host, that all
+    ranks reached the same call (a failed rank raises ``PeerFailure`` on the
+    others instead of leaving them in a collective).
 
     The gradients are packed into a persistent flat buffer (allocated on the
     first call, reused afterwards), reduced in place with ``all_reduce(SUM)``
@@ -57,8 +115,10 @@ class GradAllReducer:
     since the collectives pair up by position.
     """
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, monitor: Optional[PeerMonitor] = None):
         self.group = group
+        self.monitor = monitor
+        self.calls = 0
         self._flat = {}
 
     def __call__(self, tensors: Sequence[Optional[torch.Tensor]]) -> None:
@@ -69,6 +129,10 @@ class GradAllReducer:
             return
         if dist.get_world_size(self.group) == 1:
             return
+        if self.monitor is not None:
+            # every peer must have reached this reduction before it launches
+            self.monitor.step(self.calls)
+        self.calls += 1
         by_dtype: dict = {}
         for t in live:
             by_dtype.setdefault((t.dtype, t.device), []).append(t)

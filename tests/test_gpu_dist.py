@@ -46,10 +46,17 @@ def _worker(rank, world, port, case, path):
 
     from prlstm_b200.data_parallel import allreduce_grads, shard_batch
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    # NVLS off; a short process-group timeout with asynchronous error
+    # handling, so that if one rank fails before the all-reduce the other's
+    # collective gives up with an error instead of waiting on the GPU
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      TORCH_NCCL_ASYNC_ERROR_HANDLING="1")
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
     try:
         parallel, T, B, D, H = case
         params, x, G = _inputs(parallel, T, B, D, H)

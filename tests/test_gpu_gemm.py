@@ -1,9 +1,13 @@
 """The three linear-layer GEMMs through the C ABI against a float64 product.
 
-Shapes are chosen so the tcgen05 (3xTF32) path takes them: aligned and
-ragged extents, bias, beta (accumulate), split-K with and without scratch.
-Bound: normwise 2e-6 (3xTF32 with promoted accumulation measures ~1e-6; plain TF32 would be ~7e-4, so
-the bound also proves the lo-part MMAs run)."""
+Shapes are chosen so the tensor-core path takes them: aligned and ragged
+extents, bias, beta (accumulate), split-K with and without scratch.  By
+default that path is the fp16 split (three fp16 tcgen05 products of
+power-of-two-scaled hi/lo parts, the pair kernel on SM pairs); without
+scratch for the split, the 3xTF32 kernels run.  Bound: normwise 2e-6 (the
+fp16 split with promoted accumulation measures 2e-7 to 1.4e-6; a single
+16-bit product would be ~1e-3, so the bound also proves the lo-part
+products run)."""
 
 import pytest
 import torch

@@ -55,3 +55,36 @@ def test_reference_fp32_long_scan_drift_is_recorded():
     e_dw = rel_err(ref32["dW_ih"], truth["dW_ih"])
     print(f"reference fp32 vs fp64 at T=2048: out {e_out:.2e}  dW_ih {e_dw:.2e}")
     assert 1e-7 < e_out < 1e-2 and e_dw < 1e-1
+
+
+def test_chunked_checker_equals_whole_sequence_oracle():
+    """par_linear_chunked (the checker the full-size GPU tests use, which
+    never holds [T,B,4H]) equals par_forward_linear + par_backward_linear to
+    float64 rounding, with dh_n/dc_n, a c0 partly below eps and a chunk length
+    that does not divide T."""
+    g = torch.Generator().manual_seed(3)
+    T, B, D, H = 37, 3, 5, 8
+    x = torch.randn(T, B, D, generator=g, dtype=torch.float64)
+    W = torch.randn(4 * H, D, generator=g, dtype=torch.float64)
+    b = torch.randn(4 * H, generator=g, dtype=torch.float64)
+    c0 = torch.rand(B, H, generator=g, dtype=torch.float64)
+    c0[:, :2] = 0.0
+    G = torch.randn(T, B, H, generator=g, dtype=torch.float64)
+    dh_n = torch.randn(B, H, generator=g, dtype=torch.float64)
+    dc_n = torch.randn(B, H, generator=g, dtype=torch.float64)
+    out, h_n, c_n, saved = O.par_forward_linear(x, c0, W, b)
+    dx, dW, db, dc0, dZ = O.par_backward_linear(saved, G, dh_n, dc_n)
+    got_dx = torch.zeros_like(dx)
+    got_dW = torch.zeros_like(dW)
+    got_dZ = torch.zeros_like(dZ)
+
+    def on_dz(t0, t1, dz):
+        got_dZ[t0:t1] = dz
+        got_dx[t0:t1] = dz @ W
+        got_dW.add_(dz.reshape(-1, 4 * H).t() @ x[t0:t1].reshape(-1, D))
+
+    r = O.par_linear_chunked(lambda t0, t1: torch.nn.functional.linear(x[t0:t1], W, b), T, c0, G,
+                             dh_n, dc_n, chunk=8, on_dz=on_dz)
+    for got, ref in ((r["out"], out), (r["h_n"], h_n), (r["c_n"], c_n), (r["db"], db), (r["dc0"], dc0),
+                     (got_dZ, dZ), (got_dx, dx), (got_dW, dW)):
+        assert ((got - ref).abs().max() / ref.abs().max()).item() < 1e-12
