@@ -88,6 +88,9 @@ HS_DEV float tanh_pos(float c) {
 #endif
 }
 
+// tanh of either sign: tanh_pos of |c| with c's sign.
+HS_DEV float tanh_any(float c) { return copysignf(tanh_pos(fabsf(c)), c); }
+
 // The hardware reciprocal alone (about 1 ulp; +inf gives 0).  Enough where
 // a value's rounding does not compound over time steps: the input and output
 // gates and i*g enter each cell state once, while the forget gate multiplies

@@ -46,6 +46,14 @@ int linear_backward_ex(const float *dy, const float *w, float *dx, const float *
                        float *dw2, int64_t M, int64_t N, int64_t K, int64_t K2, int beta, void *ws, size_t ws_bytes,
                        int *status, cudaStream_t st, const unsigned *dy_absmax);
 int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st);
+bool rec_tc_wanted(int dir, int64_t B, int64_t H);
+size_t rec_tc_ws_bytes(int64_t B, int64_t H);
+int rec_tc_forward(const float *h0, const float *c0, const float *w_hh, const float *b_hh, const float *a,
+                   float *h_save, float *c_save, float *acts, int64_t T, int64_t B, int64_t H, void *ws,
+                   size_t ws_bytes, int *status, cudaStream_t st);
+int rec_tc_backward(const float *w_hh, const float *a, const float *c_save, float *acts, const float *dout,
+                    const float *dh_n, const float *dc_n, int64_t T, int64_t B, int64_t H, void *ws, size_t ws_bytes,
+                    int *status, cudaStream_t st);
 
 namespace {
 
@@ -659,8 +667,8 @@ size_t rec_ws_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
   if (!make_plan(p, B, H, nsm > 0 ? nsm : 148)) return 0;
   // the GEMMs run before the persistent kernels (forward) or after them
   // (backward), so they reuse the same scratch
-  return std::max<size_t>({p.total, linear_ws_bytes(T * B, 4 * H, D), linear_ws_bytes(T * B, 4 * H, H),
-                   linear_backward_ws(T * B, 4 * H, D, H)});
+  return std::max<size_t>({p.total, rec_tc_ws_bytes(B, H), linear_ws_bytes(T * B, 4 * H, D),
+                           linear_ws_bytes(T * B, 4 * H, H), linear_backward_ws(T * B, 4 * H, D, H)});
 }
 
 int rec_forward(const float *x, const float *h0, const float *c0, const float *w_ih,
@@ -679,6 +687,9 @@ int rec_forward(const float *x, const float *h0, const float *c0, const float *w
   char *w = static_cast<char *>(ws);
   // Z = x W_ih^T + b_ih, written into acts (_torch.py:96)
   if (int e = linear_forward(x, w_ih, b_ih, acts, T * B, 4 * H, D, ws, ws_bytes, status, st)) return e;
+  // the step product on the tensor cores where the shape allows
+  if (rec_tc_wanted(0, B, H))
+    return rec_tc_forward(h0, c0, w_hh, b_hh, a, h_save, c_save, acts, T, B, H, ws, ws_bytes, status, st);
   if (pl.fwd.rows_pad > 256) return fail(HS_ERR_UNSUPPORTED, "recurrent: slice of %d rows", pl.fwd.rows_pad);
   rec_prep_fwd_kernel<<<dim3((unsigned)((pl.fwd.K_pad + 31) / 32), (unsigned)pl.ncta), 256, 0, st>>>(
       w_hh, b_hh, a, (float *)(w + pl.o_wf), (float *)(w + pl.o_bf), H, pl.U, pl.fwd.rows_pad, pl.fwd.K_pad);
@@ -729,6 +740,11 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
   if (!make_plan(pl, B, H, nsm)) return fail(HS_ERR_UNSUPPORTED, "recurrent: no tiling for B=%lld H=%lld on %d SMs", (long long)B, (long long)H, nsm);
   if (!ws || ws_bytes < pl.total) return fail(HS_ERR_WORKSPACE, "recurrent_backward: workspace %zu < %zu bytes", ws_bytes, pl.total);
   char *w = static_cast<char *>(ws);
+  if (rec_tc_wanted(1, B, H)) {
+    // the step product on the tensor cores
+    if (int e = rec_tc_backward(w_hh, a, c_save, acts, dout, dh_n, dc_n, T, B, H, ws, ws_bytes, status, st))
+      return e;
+  } else {
   // The scaled backward slices are built here so a backward never depends
   // on workspace contents left by its forward.
   rec_prep_kernel<<<4 * nsm, 256, 0, st>>>(w_hh, b_hh, a, nullptr, nullptr, (float *)(w + pl.o_wb), H,
@@ -760,6 +776,7 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
     args.d = pl.bwd;
     args.BP = pl.BP;
     if (int e = launch_persistent(fn, pl, pl.bwd, args, st)) return e;
+  }
   }
   // Batched parameter gradients (_torch.py:153-162); acts now holds dgates.
   // dX = dG.W_ih, dW_ih = dG^T.x and dW_hh_s = dG^T.h_{t-1} share one

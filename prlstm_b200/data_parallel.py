@@ -20,8 +20,8 @@ from typing import Iterable, List, Optional, Sequence, Tuple
 
 import torch
 
-__all__ = ["shard_range", "shard_batch", "GradAllReducer", "allreduce_grads", "PeerMonitor",
-           "PeerFailure"]
+__all__ = ["shard_range", "shard_batch", "GradAllReducer", "PendingReduction", "allreduce_grads",
+           "PeerMonitor", "PeerFailure"]
 
 
 def shard_range(batch: int, rank: int, world: int) -> Tuple[int, int]:
@@ -122,13 +122,21 @@ class GradAllReducer:
         self._flat = {}
 
     def __call__(self, tensors: Sequence[Optional[torch.Tensor]]) -> None:
+        self.start(tensors).finish()
+
+    def start(self, tensors: Sequence[Optional[torch.Tensor]]) -> "PendingReduction":
+        """Pack the gradients and launch the all-reduce without waiting for
+        it: with NCCL the collective runs on the process group's own stream,
+        so work the caller queues next on its stream (the input-gradient GEMM
+        of a backward, say) overlaps with it.  ``finish()`` on the result
+        makes the caller's stream wait for the reduction and unpacks it."""
         import torch.distributed as dist
 
         live = [t for t in tensors if t is not None]
         if not live or not dist.is_available() or not dist.is_initialized():
-            return
+            return PendingReduction([])
         if dist.get_world_size(self.group) == 1:
-            return
+            return PendingReduction([])
         if self.monitor is not None:
             # every peer must have reached this reduction before it launches
             self.monitor.step(self.calls)
@@ -136,6 +144,7 @@ class GradAllReducer:
         by_dtype: dict = {}
         for t in live:
             by_dtype.setdefault((t.dtype, t.device), []).append(t)
+        parts = []
         for key in sorted(by_dtype, key=str):
             ts = by_dtype[key]
             n = sum(t.numel() for t in ts)
@@ -148,11 +157,25 @@ class GradAllReducer:
             for t in ts:
                 buf[off:off + t.numel()].copy_(t.reshape(-1))
                 off += t.numel()
-            dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.group)
+            work = dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+            parts.append((work, buf, ts))
+        return PendingReduction(parts)
+
+
+class PendingReduction:
+    """An all-reduce launched by ``GradAllReducer.start``."""
+
+    def __init__(self, parts):
+        self.parts = parts
+
+    def finish(self) -> None:
+        for work, buf, ts in self.parts:
+            work.wait()
             off = 0
             for t in ts:
                 t.copy_(buf[off:off + t.numel()].view_as(t))
                 off += t.numel()
+        self.parts = []
 
 
 def allreduce_grads(params: Iterable[torch.nn.Parameter], group=None,
