@@ -263,30 +263,31 @@ __global__ void rtc_absmax_kernel(const float *__restrict__ w_hh, const float *_
   if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
 }
 
-// Weight tiles, one per CTA: the N = 256 operand [128 rows hi | the same 128
+// Weight tiles, one per CTA: the N = 2 UB operand [UB rows hi | the same UB
 // rows lo] over the CTA's k slice, K-major without swizzle (core-matrix
-// columns of 8 k are 256 x 16 = 4096 bytes apart), scaled by the power of two
-// of max |a W_hh|.  One thread writes 8 consecutive k of one row (16 bytes).
-//   forward  CTA (rb, s): row n % 128 = g * 32 + ul is a[g] W_hh[g H + 32 rb + ul][k],
-//            k in [s Ks, (s + 1) Ks) (a unit index);
-//   backward CTA (ub, s): row n % 128 = ul is a[g] W_hh[g H + u'][128 ub + ul] for
-//            the gate row (g, u') at position k of the permuted order in which
-//            each producing CTA's 4 x UCP rows are contiguous: k = (P 4 + g) UCP + l,
-//            u' = (P / KS) 128 + (P % KS) UCP + l.
+// columns of 8 k are 2 UB x 16 bytes apart), scaled by the power of two of
+// max |a W_hh|.  One thread writes 8 consecutive k of one row (16 bytes).
+//   forward  (UB = 128) CTA (rb, s): row n % 128 = g * 32 + ul is
+//            a[g] W_hh[g H + 32 rb + ul][k], k in [s Ks, (s + 1) Ks) (a unit index);
+//   backward (UB = 128 or 64 units) CTA (ub, s): row n % UB = ul is
+//            a[g] W_hh[g H + u'][UB ub + ul] for the gate row (g, u') at position
+//            k of the permuted order in which each producing CTA's 4 x UCP rows
+//            are contiguous: k = (P 4 + g) UCP + l, u' = (P / KS) UB + (P % KS) UCP + l.
 __global__ void rtc_prep_kernel(const float *__restrict__ w_hh, const float *__restrict__ a,
                                 const unsigned *__restrict__ absmax, unsigned char *__restrict__ wg, int dir,
-                                int64_t H, int KS, int UCP, int64_t Ks, int NC) {
+                                int64_t H, int KS, int UCP, int UB, int64_t Ks, int NC) {
   const float s = pow2_scale(*absmax);
+  const int NW = 2 * UB;
   const int64_t nkc = Ks / 8;
-  const int64_t total = (int64_t)NC * nkc * 256;
-  const size_t tile = (size_t)Ks * 256 * 2;
+  const int64_t total = (int64_t)NC * nkc * NW;
+  const size_t tile = (size_t)Ks * NW * 2;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int n = (int)(i % 256);
-    const int64_t kc = (i / 256) % nkc;
-    const int cta = (int)(i / (256 * nkc));
+    const int n = (int)(i % NW);
+    const int64_t kc = (i / NW) % nkc;
+    const int cta = (int)(i / (NW * nkc));
     const int blk = cta / KS, sp = cta % KS;
-    const int r = n % 128;
-    const bool lo = n >= 128;
+    const int r = n % UB;
+    const bool lo = n >= UB;
     __align__(16) __half v[8];
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
@@ -298,14 +299,15 @@ __global__ void rtc_prep_kernel(const float *__restrict__ w_hh, const float *__r
       } else {
         const int64_t P = k / (4 * UCP);
         const int g = (int)((k / UCP) % 4), l = (int)(k % UCP);
-        const int64_t up = (P / KS) * 128 + (P % KS) * UCP + l;
-        w = a[g] * w_hh[(g * H + up) * H + (int64_t)blk * 128 + r];
+        const int64_t up = (P / KS) * UB + (P % KS) * UCP + l;
+        w = a[g] * w_hh[(g * H + up) * H + (int64_t)blk * UB + r];
       }
       __half hi, lh;
       split_h2(w * s, hi, lh);
       v[kk] = lo ? lh : hi;
     }
-    *reinterpret_cast<uint4 *>(wg + (size_t)cta * tile + koff(n, kc * 8, 4096)) = *reinterpret_cast<const uint4 *>(v);
+    *reinterpret_cast<uint4 *>(wg + (size_t)cta * tile + koff(n, kc * 8, (uint32_t)NW * 16)) =
+        *reinterpret_cast<const uint4 *>(v);
   }
 }
 
@@ -326,12 +328,13 @@ struct RtcArgs {
   int64_t Ks;               // k per CTA (slice of the reduction axis)
   size_t xbytes;            // one exchange buffer: K / 8 core columns x 1 KB
   int b0;                   // first sequence of batch group 0 of this launch
-  int NC, KS, UCP, nchunk, gch, stages, resident;
+  int NC, KS, UCP, UB, nchunk, gch, stages, resident;
 };
 
 // Shared-memory carve-up (1024-aligned base):
-//   resident: [W (Ks/8 x 4 KB) | state (Ks/8 x 1 KB) | 1 KB]
-//   streaming: stages of [W chunk 32 KB | state chunk 8 KB], then 1 KB
+//   resident: [W (Ks/8 x NW x 16 B) | state (Ks/8 x 1 KB) | 1 KB]
+//   streaming: stages of [W chunk (8 x NW x 16 B) | state chunk 8 KB], then 1 KB
+//   (NW = 2 UB weight rows: 256, or 128 for 64-unit backward blocks)
 //   then the outgoing partials pout [128][32] f32, the incoming [4096]
 //   f32, 8 floats, the mbarriers and the TMEM address.
 // The 1 KB after the state keeps in bounds the reads of the unused rows
@@ -339,17 +342,18 @@ struct RtcArgs {
 struct Layout {
   size_t w, h, ring, stage, pout, pin, red, bars, holder, total;
 };
-__host__ __device__ inline Layout make_layout(int64_t Ks, int stages, bool resident) {
+__host__ __device__ inline Layout make_layout(int64_t Ks, int stages, bool resident, int NW) {
   Layout L{};
   size_t off = 0;
+  const size_t kstr = (size_t)NW * 16;
   if (resident) {
     L.w = 0;
-    off = (size_t)Ks / 8 * 4096;
+    off = (size_t)Ks / 8 * kstr;
     L.h = off;
     off += (size_t)Ks / 8 * 1024 + 1024;
   } else {
     L.ring = 0;
-    L.stage = 32768 + 8192;
+    L.stage = 8 * kstr + 8192;
     off = (size_t)stages * L.stage + 1024;
   }
   L.pout = off;
@@ -380,9 +384,9 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *sm = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int NC = p.NC, KS = p.KS, UCP = p.UCP;
+  const int NC = p.NC, KS = p.KS, UCP = p.UCP, UB = p.UB, NW = 2 * p.UB;
   const bool resident = p.resident != 0;
-  const Layout L = make_layout(p.Ks, p.stages, resident);
+  const Layout L = make_layout(p.Ks, p.stages, resident, NW);
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + L.bars);
   uint32_t *holder = reinterpret_cast<uint32_t *>(sm + L.holder);
   float *pout = reinterpret_cast<float *>(sm + L.pout);
@@ -400,7 +404,8 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
   const int S = p.stages, nchunk = p.nchunk, gch = p.gch;
   const int ngroups = (nchunk + gch - 1) / gch;
   const int slot_f = DIR == 0 ? 4 * UCP * 32 : UCP * 32;  // floats of one CTA's partial for one owner
-  const uint32_t wchunk = 32768, hchunk = 8192;
+  const uint32_t kstrW = (uint32_t)NW * 16;
+  const uint32_t wchunk = 8 * kstrW, hchunk = 8192;
   const size_t xoff = (size_t)sp * p.Ks / 8 * 1024;       // this CTA's k slice in the exchange buffer
   const int64_t nsteps = DIR == 0 ? T : T - 1;            // steps that run a product
 
@@ -429,11 +434,11 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
   if (warp == 0) {
     // ------------------------------------------------------------ loads
     if (lane == 0) {
-      const unsigned char *wsrc = p.wg + (size_t)cta * p.Ks * 512;
+      const unsigned char *wsrc = p.wg + (size_t)cta * p.Ks * NW * 2;
       bool ok = true;
       int64_t fills = 0;
       if (resident && nsteps > 0) {
-        const size_t wb = (size_t)p.Ks * 512;
+        const size_t wb = (size_t)p.Ks * NW * 2;
         mbar_arrive_expect(&bars[B_W], (uint32_t)wb);
         for (size_t off = 0; off < wb; off += 32768)
           bulk_g2s(sm + L.w + off, wsrc + off, (uint32_t)min((size_t)32768, wb - off), &bars[B_W]);
@@ -500,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(128, 256);
+      const uint32_t idesc = idesc_f16(128, NW);
       bool ok = true;
       if (resident && nsteps > 0) ok = mbar_wait(&bars[B_W], 0, p.status);
       int64_t chunks = 0, groups = 0;
@@ -531,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
             const uint64_t ad = kdesc(su32(hb + 2 * ks * 1024), 1024, 128);  // state rows (M)
-            const uint64_t bd = kdesc(su32(wa + 2 * ks * 4096), 4096, 128);  // weight rows (N)
+            const uint64_t bd = kdesc(su32(wa + 2 * ks * kstrW), kstrW, 128);  // weight rows (N)
             mma_f16(dt, ad, bd, idesc, (j % gch != 0 || ks > 0) ? 1u : 0u);
           }
           if (!resident) mma_commit(&bars[B_EMPTY + (int)(chunks % S)]);
@@ -573,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
         if (drains && !fail && !mbar_wait(&bars[B_SFULL + slot], (uint32_t)((groups / 2) & 1), p.status)) fail = true;
         if (!fail) {
           tc_fence_after();
-          if (drains) {
+          if (drains && 64 * half < UB) {
             float sc = 1.0f;
             if (DIR == 1) sc = __ldcg(&xscale[par * NC + (int)(sp * ngroups + gi)]) * inv_w;
             const uint32_t base = tl + (uint32_t)slot * kSlotCols + (uint32_t)(64 * half);
@@ -583,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
             for (int c = 0; c < 4; ++c) {
               uint32_t v[16], w[16];
               tmem_ld16_nowait(base + 16 * c, v);
-              if (q == 0) tmem_ld16_nowait(base + 128 + 16 * c, w);
+              if (q == 0) tmem_ld16_nowait(base + UB + 16 * c, w);
               tmem_wait_ld();
               if (q == 0) {
 #pragma unroll
@@ -594,6 +599,8 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
                 for (int i = 0; i < 16; ++i) acc[16 * c + i] = fmaf(__uint_as_float(v[i]), sc, acc[16 * c + i]);
               }
             }
+          }
+          if (drains) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars[B_SFREE + slot]);
@@ -604,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
       // The partial sums of the weight rows r (forward: r = gate x 32 + unit;
       // backward: r = unit) for sequence b, pout[r][b]: the lo-state rows'
       // sums first, then the hi-state rows add theirs.
-      if (q == 1 && !fail) {
+      if (q == 1 && !fail && 64 * half < UB) {
 #pragma unroll
         for (int i = 0; i < 64; ++i) pout[(64 * half + i) * 32 + lane] = acc[i];
       }
@@ -612,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
       // every CTA of the cluster before those CTAs published the state this
       // step's MMAs consumed
       if (epi_sync_any(fail)) return false;
-      if (q == 0) {
+      if (q == 0 && 64 * half < UB) {
 #pragma unroll
         for (int i = 0; i < 64; ++i) pout[(64 * half + i) * 32 + lane] += acc[i];
       }
@@ -726,7 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
       _Pragma("unroll") for (int m = 0; m < NCELL; ++m) {
         const int ci = e + kEpi * m;
         const int b = ci & 31, ul = ci >> 5;
-        if (ul < UCP && b < Bc && p.dc_n) dc[m] = p.dc_n[(int64_t)(bg0 + b) * H + (int64_t)blk * 128 + sp * UCP + ul];
+        if (ul < UCP && b < Bc && p.dc_n) dc[m] = p.dc_n[(int64_t)(bg0 + b) * H + (int64_t)blk * UB + sp * UCP + ul];
       }
       for (int64_t t = T - 1; t >= 0; --t) {
         float ld[NCELL][7];  // i, f, g, o, c_t, c_{t-1}, dh
@@ -734,7 +741,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
           const int ci = e + kEpi * m;
           const int b = ci % 32, ul = ci / 32;
           const bool v = ul < UCP && b < Bc;
-          const int64_t u = (int64_t)blk * 128 + sp * UCP + ul, bb = bg0 + b;
+          const int64_t u = (int64_t)blk * UB + sp * UCP + ul, bb = bg0 + b;
           const float *ar = p.zacts + (t * Bt + bb) * 4 * H + u;
 #pragma unroll
           for (int g = 0; g < 4; ++g) ld[m][g] = v ? ld_early(ar + g * H) : 0.f;
@@ -773,7 +780,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
             const int ci = e + kEpi * m;
             const int b = ci & 31, ul = ci >> 5;
             if (ul >= UCP || b >= Bc) continue;
-            const int64_t u = (int64_t)blk * 128 + sp * UCP + ul, bb = bg0 + b;
+            const int64_t u = (int64_t)blk * UB + sp * UCP + ul, bb = bg0 + b;
             float *ar = p.zacts + (t * Bt + bb) * 4 * H + u;
 #pragma unroll
             for (int q2 = 0; q2 < 4; ++q2) ar[q2 * H] = dg[m][q2];
@@ -828,7 +835,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
 
 // ------------------------------------------------------------------ host
 struct RtcPlan {
-  int dir, KS, UCP, NBLK, NC, ngrp, nchunk, gch, stages;
+  int dir, KS, UCP, UB, NBLK, NC, ngrp, nchunk, gch, stages;
   bool resident;
   int64_t K, Ks;
   size_t xbytes, smem;
@@ -839,13 +846,13 @@ std::atomic<unsigned long long> g_attr[6];
 
 // The kernel instance for a direction and k split (cells per epilogue
 // thread = units per CTA x 32 / 256).
-int ncell_of(int dir, int ks) { return (dir == 0 ? 32 : 128) / ks * 32 / kEpi; }
-int attr_index(int dir, int ks) {
-  const int n = ncell_of(dir, ks);
+int ncell_of(int dir, int ks, int ub) { return (dir == 0 ? 32 : ub) / ks * 32 / kEpi; }
+int attr_index(int dir, int ks, int ub) {
+  const int n = ncell_of(dir, ks, ub);
   return dir * 3 + (n <= 1 ? 0 : n == 2 ? 1 : 2);
 }
-const void *rtc_fn(int dir, int ks) {
-  const int n = ncell_of(dir, ks);
+const void *rtc_fn(int dir, int ks, int ub) {
+  const int n = ncell_of(dir, ks, ub);
   if (dir == 0) {
     if (n <= 1) return (const void *)rtc_kernel<0, 1>;
     if (n == 2) return (const void *)rtc_kernel<0, 2>;
@@ -861,8 +868,8 @@ const void *rtc_fn(int dir, int ks) {
 // Clusters of ks CTAs of the direction's kernel with `smem` bytes each that
 // can be resident at once on the current device (0 if the query fails),
 // cached per (device, direction, ks, smem).
-int max_clusters(int dir, int ks, size_t smem) {
-  struct Entry { int dev, dir, ks; size_t smem; int n; };
+int max_clusters(int dir, int ks, int ub, size_t smem) {
+  struct Entry { int dev, dir, ks, ub; size_t smem; int n; };
   static std::mutex mu;
   static Entry cache[64];
   static int ncache = 0;
@@ -870,9 +877,10 @@ int max_clusters(int dir, int ks, size_t smem) {
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < ncache; ++i)
-    if (cache[i].dev == dev && cache[i].dir == dir && cache[i].ks == ks && cache[i].smem == smem) return cache[i].n;
-  const void *fn = rtc_fn(dir, ks);
-  if (!fn || allow_dynamic_smem(fn, kSmemMax, &g_attr[attr_index(dir, ks)]) != HS_OK) return 0;
+    if (cache[i].dev == dev && cache[i].dir == dir && cache[i].ks == ks && cache[i].ub == ub && cache[i].smem == smem)
+      return cache[i].n;
+  const void *fn = rtc_fn(dir, ks, ub);
+  if (!fn || allow_dynamic_smem(fn, kSmemMax, &g_attr[attr_index(dir, ks, ub)]) != HS_OK) return 0;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)ks);
   cfg.blockDim = dim3(kThreads);
@@ -889,7 +897,7 @@ int max_clusters(int dir, int ks, size_t smem) {
     (void)cudaGetLastError();
     n = 0;
   }
-  if (ncache < 64) cache[ncache++] = Entry{dev, dir, ks, smem, n};
+  if (ncache < 64) cache[ncache++] = Entry{dev, dir, ks, ub, smem, n};
   return n;
 }
 
@@ -897,48 +905,65 @@ bool make_rtc_plan(RtcPlan &p, int dir, int64_t B, int64_t H, int nsm) {
   p = RtcPlan{};
   p.dir = dir;
   if (H <= 0 || B <= 0) return false;
-  if (dir == 0 ? (H % 64 != 0) : (H % 128 != 0)) return false;
+  if (dir == 0 ? (H % 64 != 0) : (H % 64 != 0)) return false;
   p.K = dir == 0 ? H : 4 * H;
-  p.NBLK = (int)(dir == 0 ? H / 32 : H / 128);
-  const int unit_block = dir == 0 ? 32 : 128;
-  // The largest k split whose clusters all fit on the GPU at once (one
-  // cluster per weight-row block), with at most 4 cells of 32 sequences per
-  // epilogue thread and whole 64-k chunks per CTA.
+  // Weight blocks: forward 32 units x 4 gates = 128 rows; backward 128 or 64
+  // units.  Among the k splits whose clusters all fit on the GPU at once (at
+  // most 4 cells of 32 sequences per epilogue thread, whole 64-k chunks, a
+  // backward producer block of whole chunks), take the one with the most
+  // CTAs (each CTA streams or holds less of the weights and issues fewer
+  // MMAs per step), then the larger block.
   bool found = false;
-  int fit = 0;
-  for (int ks : {8, 4, 2, 1}) {
-    const int64_t Ks = p.K / ks;
-    if (p.K % ks || Ks % KCH || unit_block % ks || unit_block / ks > 32) continue;
-    if ((int64_t)p.NBLK * ks > nsm) continue;
-    p.KS = ks;
-    p.Ks = Ks;
-    p.UCP = unit_block / ks;
-    p.nchunk = (int)(Ks / KCH);
-    // accumulator groups: forward every 256 k; backward one producer block
-    // (4 x UCP k of one scale)
-    const int64_t gk = dir == 0 ? std::min<int64_t>(256, Ks) : 4 * p.UCP;
-    if (gk % KCH) continue;
-    p.gch = (int)(gk / KCH);
-    const Layout Lr = make_layout(Ks, 0, true);
-    if (Lr.total <= kSmemMax && p.nchunk <= 32) {
-      p.resident = true;
-      p.stages = 0;
-      p.smem = Lr.total;
-    } else {
-      p.resident = false;
-      int S = 0;
-      for (int st = 8; st >= 2; --st)
-        if (make_layout(Ks, st, false).total <= kSmemMax) { S = st; break; }
-      if (!S) continue;
-      p.stages = S;
-      p.smem = make_layout(Ks, S, false).total;
+  RtcPlan best{};
+  int best_fit = 0;
+  for (int ub : {128, 64}) {
+    if (dir == 0 && ub != 128) continue;
+    const int unit_block = dir == 0 ? 32 : ub;
+    if (H % unit_block) continue;
+    for (int ks : {8, 4, 2, 1}) {
+      RtcPlan c = p;
+      c.UB = ub;
+      c.NBLK = (int)(H / unit_block);
+      const int64_t Ks = c.K / ks;
+      if (c.K % ks || Ks % KCH || unit_block % ks || unit_block / ks > 32) continue;
+      if ((int64_t)c.NBLK * ks > nsm) continue;
+      c.KS = ks;
+      c.Ks = Ks;
+      c.UCP = unit_block / ks;
+      c.nchunk = (int)(Ks / KCH);
+      // accumulator groups: forward every 256 k; backward one producer block
+      // (4 x UCP k of one scale)
+      const int64_t gk = dir == 0 ? std::min<int64_t>(256, Ks) : 4 * c.UCP;
+      if (gk % KCH) continue;
+      c.gch = (int)(gk / KCH);
+      const int NW = 2 * ub;
+      const Layout Lr = make_layout(Ks, 0, true, NW);
+      if (Lr.total <= kSmemMax && c.nchunk <= 32) {
+        c.resident = true;
+        c.stages = 0;
+        c.smem = Lr.total;
+      } else {
+        c.resident = false;
+        int S = 0;
+        for (int st = 8; st >= 2; --st)
+          if (make_layout(Ks, st, false, NW).total <= kSmemMax) { S = st; break; }
+        if (!S) continue;
+        c.stages = S;
+        c.smem = make_layout(Ks, S, false, NW).total;
+      }
+      const int fit = max_clusters(dir, ks, ub, c.smem);
+      if (fit < c.NBLK) continue;
+      if (!found || c.NBLK * c.KS > best.NBLK * best.KS) {
+        best = c;
+        best_fit = fit;
+        found = true;
+      }
+      break;  // smaller splits of this block size only have fewer CTAs
     }
-    fit = max_clusters(dir, ks, p.smem);
-    if (fit < p.NBLK) continue;
-    found = true;
-    break;
   }
   if (!found) return false;
+  p = best;
+  const int fit = best_fit;
   p.NC = p.NBLK * p.KS;
   p.ngrp = (int)std::max<int64_t>(1, std::min<int64_t>((B + 31) / 32, fit / p.NBLK));
   p.xbytes = (size_t)p.K / 8 * 1024;
@@ -946,7 +971,7 @@ bool make_rtc_plan(RtcPlan &p, int dir, int64_t B, int64_t H, int nsm) {
   auto take = [&](size_t bytes) { size_t o = off; off = round_up(off + bytes, 256); return o; };
   p.o_bar = take((size_t)p.ngrp * 128);
   p.o_absmax = take(16);
-  p.o_w = take((size_t)p.NC * p.Ks * 512);
+  p.o_w = take((size_t)p.NC * p.Ks * 4 * p.UB);
   p.o_x = take((size_t)p.ngrp * 2 * p.xbytes);
   p.o_xs = take((size_t)p.ngrp * 2 * p.NC * 4);
   p.total = off;
@@ -1003,18 +1028,20 @@ int rtc_launch(const void *fn, const RtcPlan &pl, int ngrp, RtcArgs &args, cudaS
 
 }  // namespace
 
-// Default choice between the two recurrent implementations, from their
-// measured per-step times on B200: at H <= 512 both are bound by the same
-// cross-CTA exchange of the state (~2.5 us per step), and the FFMA kernels'
-// shorter epilogue wins (H = 512, B = 32: 7.0 vs 8.7 us forward, 14.8 vs
-// 15.2 us backward); from H = 1024 the tensor cores' product wins (H = 2048,
-// B = 32: 30.7 vs 64 us forward, 57 vs 77 us backward).
-constexpr int64_t kTcMinH = 1024;
+// Default choice between the two recurrent implementations, per direction,
+// from their per-step times measured on B200 at B = 32 (forward / backward,
+// microseconds): H = 128 FFMA 5.3 / 10.9, tensor cores 8.4 / 13.7; H = 512
+// FFMA 7.0 / 14.8, tensor cores 7.4 / 12.0; H = 2048 FFMA 63.7 / 76.5, tensor
+// cores 26.5 / 48.4.  At small H both are bound by the cross-CTA exchange of
+// the state (about 2.5 us per step) and the FFMA kernels' shorter epilogue
+// wins; the tensor cores take over from H = 512 in the backward (four times
+// the product of the forward per step) and from H = 1024 in the forward.
+constexpr int64_t kTcMinH[2] = {1024, 512};
 
 bool rec_tc_wanted(int dir, int64_t B, int64_t H) {
   const int o = rtc_override();
   if (o == 1) return false;
-  if (o == 0 && H < kTcMinH) return false;
+  if (o == 0 && H < kTcMinH[dir]) return false;
   RtcPlan p;
   const int n = rtc_sms();
   return make_rtc_plan(p, dir, B, H, n > 0 ? n : 148);
@@ -1035,9 +1062,9 @@ int rtc_prepare(const RtcPlan &pl, const float *w_hh, const float *a, int64_t H,
   if (cudaMemsetAsync(absmax, 0, 4, st) != cudaSuccess) return check_launch("memset(absmax)");
   rtc_absmax_kernel<<<2 * nsm, 256, 0, st>>>(w_hh, a, H, absmax);
   if (int e = check_launch("rtc_absmax_kernel")) return e;
-  const int64_t n = (int64_t)pl.NC * (pl.Ks / 8) * 256;
+  const int64_t n = (int64_t)pl.NC * (pl.Ks / 8) * 2 * pl.UB;
   rtc_prep_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 16 * nsm), 256, 0, st>>>(
-      w_hh, a, absmax, reinterpret_cast<unsigned char *>(w + pl.o_w), pl.dir, H, pl.KS, pl.UCP, pl.Ks, pl.NC);
+      w_hh, a, absmax, reinterpret_cast<unsigned char *>(w + pl.o_w), pl.dir, H, pl.KS, pl.UCP, pl.UB, pl.Ks, pl.NC);
   return check_launch("rtc_prep_kernel");
 }
 
@@ -1057,6 +1084,7 @@ void fill_args(RtcArgs &args, const RtcPlan &pl, char *w, int *status, int64_t T
   args.NC = pl.NC;
   args.KS = pl.KS;
   args.UCP = pl.UCP;
+  args.UB = pl.UB;
   args.nchunk = pl.nchunk;
   args.gch = pl.gch;
   args.stages = pl.stages;
@@ -1078,9 +1106,9 @@ int rec_tc_forward(const float *h0, const float *c0, const float *w_hh, const fl
     return fail(HS_ERR_WORKSPACE, "recurrent (tensor cores): workspace %zu < %zu bytes", ws_bytes, pl.total);
   char *w = static_cast<char *>(ws);
   if (int e = rtc_prepare(pl, w_hh, a, H, w, nsm, st)) return e;
-  const void *fn = rtc_fn(0, pl.KS);
+  const void *fn = rtc_fn(0, pl.KS, pl.UB);
   if (!fn) return fail(HS_ERR_UNSUPPORTED, "recurrent (tensor cores): no kernel for KS=%d", pl.KS);
-  if (int e = allow_dynamic_smem(fn, kSmemMax, &g_attr[attr_index(0, pl.KS)])) return e;
+  if (int e = allow_dynamic_smem(fn, kSmemMax, &g_attr[attr_index(0, pl.KS, pl.UB)])) return e;
   for (int64_t b0 = 0; b0 < B; b0 += 32 * pl.ngrp) {
     const int ngrp = (int)std::min<int64_t>(pl.ngrp, (B - b0 + 31) / 32);
     if (cudaMemsetAsync(w + pl.o_bar, 0, (size_t)ngrp * 128, st) != cudaSuccess) return check_launch("memset(bar)");
@@ -1116,9 +1144,9 @@ int rec_tc_backward(const float *w_hh, const float *a, const float *c_save, floa
     return fail(HS_ERR_WORKSPACE, "recurrent backward (tensor cores): workspace %zu < %zu bytes", ws_bytes, pl.total);
   char *w = static_cast<char *>(ws);
   if (int e = rtc_prepare(pl, w_hh, a, H, w, nsm, st)) return e;
-  const void *fn = rtc_fn(1, pl.KS);
+  const void *fn = rtc_fn(1, pl.KS, pl.UB);
   if (!fn) return fail(HS_ERR_UNSUPPORTED, "recurrent backward (tensor cores): no kernel for KS=%d", pl.KS);
-  if (int e = allow_dynamic_smem(fn, kSmemMax, &g_attr[attr_index(1, pl.KS)])) return e;
+  if (int e = allow_dynamic_smem(fn, kSmemMax, &g_attr[attr_index(1, pl.KS, pl.UB)])) return e;
   for (int64_t b0 = 0; b0 < B; b0 += 32 * pl.ngrp) {
     const int ngrp = (int)std::min<int64_t>(pl.ngrp, (B - b0 + 31) / 32);
     if (cudaMemsetAsync(w + pl.o_bar, 0, (size_t)ngrp * 128, st) != cudaSuccess) return check_launch("memset(bar)");
