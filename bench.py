@@ -663,10 +663,13 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
     bound_f = max(step_flop / (peak_tf * 1e12), whh_bytes / smem_bw) * 1e6
     bound_b = max(2 * step_flop / (peak_tf * 1e12), whh_bytes / smem_bw) * 1e6
     us_f, us_b = fwd * 1e3 / T, bwd * 1e3 / T
+    tc = [bool(lib.hs_recurrent_uses_tensor_cores(B_local, H, d)) for d in (0, 1)]
     res = {"value": tokens / (ms / 1e3), "ms_per_step": ms / args.steps, "clocks": ck,
            "gpu_launches": None,
            "recurrent": {"fwd_ms": fwd, "bwd_ms": bwd, "us_per_step_fwd": us_f,
                          "us_per_step_bwd": us_b,
+                         "step_kernel": {"fwd": "tcgen05" if tc[0] else "ffma",
+                                         "bwd": "tcgen05" if tc[1] else "ffma"},
                          "step_bound_us": {"fwd": round(bound_f, 3), "bwd": round(bound_b, 3),
                                            "smem_gbs": round(smem_bw / 1e9, 1), "sm_mhz": mhz},
                          "frac_of_step_bound": {"fwd": round(bound_f / us_f, 4),
@@ -710,10 +713,11 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
     ms_e = max_over_ranks(e0.elapsed_time(e1))
     res["e2e"] = {"value": tokens / (ms_e / 1e3), "unit": "tokens/s",
                   "h2d_bytes_per_step": (x.numel() + G.numel()) * 4, "d2h_bytes_per_step": 4}
-    # launches per step: proj GEMM, prep, fwd kernel x ceil(B/32), prep, bwd kernel x ceil(B/32),
-    # 2 wgrad, colsum, dgrad, unscale
+    # launches per step (approximate): projection GEMM, weight staging (the
+    # tensor-core path: max |a W_hh| then the split tiles), the recurrent
+    # kernel per window of batch groups, the gradient GEMMs, colsum, unscale, da
     nb = (B_local + 31) // 32
-    res["gpu_launches"] = args.steps * (2 + nb + 1 + nb + 5)
+    res["gpu_launches"] = args.steps * ((1 + (2 if tc[0] else 1) + nb) + ((2 if tc[1] else 1) + nb + 6))
     return res
 
 

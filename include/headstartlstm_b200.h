@@ -295,6 +295,13 @@ HS_API int hs_parallel_backward_kf(const float *x, const float *w_ih, float *z, 
  * (_csrc/lstm_cell.cpp:28-78).
  * ---------------------------------------------------------------------- */
 HS_API size_t hs_recurrent_workspace_bytes(int64_t T, int64_t B, int64_t D, int64_t H);
+/* 1 if hs_recurrent_forward (backward = 0) or hs_recurrent_backward
+ * (backward = 1) runs the per-step product on the tensor cores for this B
+ * and H on the current device, 0 if on the FFMA kernels (shapes the tensor-core
+ * kernels do not cover, or where the FFMA kernels measured faster).  A
+ * diagnostic with no reference counterpart; the environment variable
+ * HS_REC_PATH=tc|ffma forces one implementation. */
+HS_API int hs_recurrent_uses_tensor_cores(int64_t B, int64_t H, int backward);
 
 /* Whole recurrent forward.  Inputs x [T,B,D], h0/c0 [B,H] (NULL = zeros),
  * w_ih [4H,D], w_hh [4H,H], b_ih/b_hh [4H], a [4].  Outputs:

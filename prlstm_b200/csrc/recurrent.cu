@@ -798,6 +798,11 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
 
 extern "C" {
 
+int hs_recurrent_uses_tensor_cores(int64_t B, int64_t H, int backward) {
+  if (B <= 0 || H <= 0) return 0;
+  return hs::rec_tc_wanted(backward ? 1 : 0, B, H) ? 1 : 0;
+}
+
 size_t hs_recurrent_workspace_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
   if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return 0;
   return hs::rec_ws_bytes(T, B, D, H);
