@@ -1012,7 +1012,11 @@ int rtc_launch(const void *fn, const RtcPlan &pl, int ngrp, RtcArgs &args, cudaS
   at[1].id = cudaLaunchAttributeCooperative;
   at[1].val.cooperative = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 2;
+  // HS_REC_COOP=0 leaves out the cooperative attribute (for profilers that
+  // cannot launch cooperative cluster kernels); every cluster still fits on
+  // the GPU at once (checked below), and every wait on another CTA is bounded.
+  const char *coop = getenv("HS_REC_COOP");
+  cfg.numAttrs = (coop && coop[0] == '0') ? 1 : 2;
   int nclusters = 0;
   cudaLaunchConfig_t q = cfg;
   q.numAttrs = 1;
