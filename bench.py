@@ -330,6 +330,9 @@ def run_ours(args, cfg, rank, world, dev):
         if world > 1:
             reducer(tensors)
 
+    # launch without waiting (NCCL runs on its own stream): finish() later
+    allreduce.start = lambda tensors: reducer.start(tensors) if world > 1 else None
+
     def sync():
         torch.cuda.synchronize(dev)
         if world > 1:
@@ -488,24 +491,39 @@ def h2d_roofline(e2e, cfg, world, dev, sync, nbytes=1 << 30, reps=4):
 
 
 def scan_alone(step, G0, dev, peak_hbm, reps=5):
-    """hs_scan_forward and hs_scan_backward (float32 dZ) timed alone with CUDA
-    events on one micro-batch of the step's own inputs (every rank runs it;
-    rank 0 reports)."""
+    """The scans timed alone with CUDA events on one micro-batch of the
+    step's own inputs (every rank runs it; rank 0 reports).  "step_kernels"
+    are the calls the training step makes: hs_scan_forward_kf and the
+    split-writing hs_scan_backward_split (its bound pass over dout, the scan
+    writing dZ as the fp16 split, the checks); "float32_dz" the plain entry
+    points, hs_scan_forward and hs_scan_backward writing float32 dZ.  Both
+    against the same algorithmic bytes: 24 B forward, 40 B backward per
+    (t, b, h)."""
     L, P = step.L, step.L.ptr
     T, H, mb = step.cfg["T"], step.cfg["H"], step.mb
     st = L.stream_ptr(dev)
     dz = torch.empty_like(step.z)
 
-    def fwd():
+    def fwd32():
         L.call("hs_scan_forward", P(step.z), P(step.c0), P(step.out), P(step.c), None, None, T, mb, H, 1e-6,
                P(step.ws), step.ws.numel(), P(step.status), st)
 
-    def bwd():
+    def bwd32():
         L.call("hs_scan_backward", P(step.z), P(step.c), P(step.c0), P(G0), None, None, P(dz), None,
                P(step.db_mb), T, mb, H, 1e-6, P(step.ws), step.ws.numel(), P(step.status), st)
 
-    out = {"workload": f"one micro-batch, T={T}, B={mb}, H={H}", "reps": reps}
-    for name, f, bpe in (("scan_fwd", fwd, 24.0), ("scan_bwd", bwd, 40.0)):
+    kf, dz_scale = P(step.words[0:]), P(step.words[16:])
+
+    def fwd_kf():
+        L.call("hs_scan_forward_kf", P(step.z), P(step.c0), P(step.out), P(step.c), P(step.h_n), P(step.c_n),
+               T, mb, H, 1e-6, P(step.ws), step.ws.numel(), kf, P(step.status), st)
+
+    def bwd_split():
+        L.call("hs_scan_backward_split", P(step.z), P(step.c), P(step.c0), P(G0), None, None, kf,
+               P(step.dz_split), dz_scale, None, P(step.db_mb), T, mb, H, 1e-6, P(step.ws), step.ws.numel(),
+               P(step.status), st)
+
+    def timed(f):
         for _ in range(2):
             f()
         torch.cuda.synchronize(dev)
@@ -515,13 +533,20 @@ def scan_alone(step, G0, dev, peak_hbm, reps=5):
             f()
         e1.record()
         torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / reps
-        gbs = bpe * T * mb * H / (ms / 1e3) / 1e9
-        out[name] = {"avg_ms": round(ms, 4), "achieved": round(gbs, 1), "unit": "GB/s",
-                     "frac": round(gbs / peak_hbm, 4)}
-    tot = out["scan_fwd"]["avg_ms"] + out["scan_bwd"]["avg_ms"]
-    gbs = 64.0 * T * mb * H / (tot / 1e3) / 1e9
-    out["combined"] = {"achieved": round(gbs, 1), "frac": round(gbs / peak_hbm, 4)}
+        return e0.elapsed_time(e1) / reps
+
+    out = {"workload": f"one micro-batch, T={T}, B={mb}, H={H}", "reps": reps}
+    for key, pair in (("step_kernels", (fwd_kf, bwd_split)), ("float32_dz", (fwd32, bwd32))):
+        ent = {}
+        for name, f, bpe in (("scan_fwd", pair[0], 24.0), ("scan_bwd", pair[1], 40.0)):
+            ms = timed(f)
+            gbs = bpe * T * mb * H / (ms / 1e3) / 1e9
+            ent[name] = {"avg_ms": round(ms, 4), "achieved": round(gbs, 1), "unit": "GB/s",
+                         "frac": round(gbs / peak_hbm, 4)}
+        tot = ent["scan_fwd"]["avg_ms"] + ent["scan_bwd"]["avg_ms"]
+        gbs = 64.0 * T * mb * H / (tot / 1e3) / 1e9
+        ent["combined"] = {"achieved": round(gbs, 1), "frac": round(gbs / peak_hbm, 4)}
+        out[key] = ent
     del dz
     return out
 
@@ -621,12 +646,22 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
                   P(status), st)
         if record:
             e[1].record()
-        _lib.call("hs_recurrent_backward", P(x), P(W_ih), P(W_hh), P(b_hh), P(a), P(h_save),
-                  P(c_save), P(acts), P(G), None, None, P(dx), P(dW_ih), P(dW_hh), P(db_ih),
-                  P(db_hh), P(da), T, B_local, D, H, P(ws), ws.numel(), P(status), st)
+        if world == 1:
+            _lib.call("hs_recurrent_backward", P(x), P(W_ih), P(W_hh), P(b_hh), P(a), P(h_save),
+                      P(c_save), P(acts), P(G), None, None, P(dx), P(dW_ih), P(dW_hh), P(db_ih),
+                      P(db_hh), P(da), T, B_local, D, H, P(ws), ws.numel(), P(status), st)
+        else:
+            # weight gradients first; their all-reduce (NCCL's stream) overlaps
+            # the input-gradient GEMM dX = dgates . W_ih (acts holds dgates)
+            _lib.call("hs_recurrent_backward", P(x), P(W_ih), P(W_hh), P(b_hh), P(a), P(h_save),
+                      P(c_save), P(acts), P(G), None, None, None, P(dW_ih), P(dW_hh), P(db_ih),
+                      P(db_hh), P(da), T, B_local, D, H, P(ws), ws.numel(), P(status), st)
+            pending = allreduce.start([dW_ih, dW_hh, db_ih, db_hh, da])
+            _lib.call("hs_linear_dgrad", P(acts), P(W_ih), P(dx), T * B_local, 4 * H, D, P(ws), ws.numel(),
+                      P(status), st)
+            pending.finish()
         if record:
             e[2].record()
-        allreduce([dW_ih, dW_hh, db_ih, db_hh, da])
         return e
 
     for _ in range(args.warmup):
@@ -977,6 +1012,9 @@ def main():
                     ent["e2e_vs_cpu_baseline"] = ent["e2e"]["value"] / value
             line["configs"][name] = ent
             torch.cuda.empty_cache()
+        # configs[3]'s bf16-input variant, through the module API
+        line["configs"]["cfg3_bf16"] = run_bf16_module(args, dict(CONFIGS["cfg3"]), world, dev, rank)
+        torch.cuda.empty_cache()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -984,6 +1022,52 @@ def main():
 
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_bf16_module(args, cfg, world, dev, rank, steps=10, warmup=3):
+    """configs[3] with bfloat16 inputs and parameters (the reduced-precision
+    variant): fwd + sum(out*G) backward through prlstm_b200.HeadStartLSTM,
+    inputs resident on the device, CUDA events around the steps.  Every rank
+    runs the full config (replicas); tokens/s is the whole job's."""
+    import torch.distributed as dist
+
+    import prlstm_b200
+
+    T, B, D, H = cfg["T"], cfg["B"], cfg["D"], cfg["H"]
+    params = make_params(cfg)
+    m = prlstm_b200.HeadStartLSTM(D, H).to(dev, torch.bfloat16)
+    with torch.no_grad():
+        for p_, v in zip(m.parameters(), params):
+            p_.copy_(v)
+    x, G = make_data(cfg, B, rank, dev)
+    x, G = x.to(torch.bfloat16), G.to(torch.bfloat16)
+
+    def step():
+        m.zero_grad(set_to_none=True)
+        xd = x.detach().requires_grad_(True)
+        out, _ = m(xd)
+        (out.float() * G.float()).sum().backward()
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"value": T * B * world * steps / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms / steps,
+            "steps": steps, "dtype": "bf16 inputs and parameters, f32 arithmetic",
+            "scaling": "weak (replicas)", "config": _config_obj("cfg3", cfg, world, None),
+            "tolerance": "2e-2 normwise vs float64 fed the bf16-rounded inputs (tests/test_gpu_bf16.py)"}
 
 
 def _config_obj(name, cfg, world, workload):

@@ -22,12 +22,21 @@ TOL_BF16 = 2e-2
     (False, 64, 8, 64, 128, 1e-4),
     (False, 32, 4, 96, 256, 0.3),
     (True, 256, 8, 64, 128, 0.0),
+    # configs[3], "fp32 and bf16-input fwd+bwd": a ~ U(0, 0.5), tensor-core recurrence
+    (False, 64, 32, 1024, 2048, "U(0,0.5)"),
+    # configs[4]'s micro-batch at short T: pair GEMMs, per-column scan, split handoff
+    (True, 256, 32, 512, 1024, "spread"),
 ])
 def test_bf16_module_against_float64_oracle(parallel, T, B, D, H, a):
     import prlstm_b200
 
     dev = torch.device("cuda", 0)
-    params, x, G = make_inputs(T, B, D, H, a=a, seed=T + H)
+    if a == "U(0,0.5)":
+        params, x, G = make_inputs(T, B, D, H, a_uniform=(0.0, 0.5), seed=T + H)
+    elif a == "spread":
+        params, x, G = make_inputs(T, B, D, H, a=0.0, bias_spread=8.0, seed=T + H)
+    else:
+        params, x, G = make_inputs(T, B, D, H, a=a, seed=T + H)
     params = tuple(p.to(torch.bfloat16) for p in params)
     x = x.to(torch.bfloat16)
     G = G.to(torch.bfloat16)
