@@ -371,10 +371,9 @@ __host__ __device__ inline Layout make_layout(int64_t Ks, int stages, bool resid
 }
 
 // Barrier slots: [0, 32) full (ring stages, or the resident state chunks),
-// [32, 40) empty, 40/41 slot_full, 42/43 slot_free, 44 weights loaded, 45
-// MMA drain, 46 partial sums in.
-constexpr int B_FULL = 0, B_EMPTY = 32, B_SFULL = 40, B_SFREE = 42, B_W = 44, B_DONE = 45, B_PIN = 46;
-constexpr uint32_t kSlotCols = 256;
+// [32, 40) empty, [40, 44) slot_full, [44, 48) slot_free, 48 weights loaded,
+// 49 MMA drain, 50 partial sums in.
+constexpr int B_FULL = 0, B_EMPTY = 32, B_SFULL = 40, B_SFREE = 44, B_W = 48, B_DONE = 49, B_PIN = 50;
 
 // NCELL: cells (unit x sequence) per epilogue thread, UCP * 32 / 256 (1, 2
 // or 4), a compile-time constant so that the per-cell state stays in
@@ -402,6 +401,9 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
   unsigned char *xg = p.xg + (size_t)grp * 2 * p.xbytes;
   float *xscale = p.xscale ? p.xscale + (size_t)grp * 2 * NC : nullptr;
   const int S = p.stages, nchunk = p.nchunk, gch = p.gch;
+  // two accumulator slots of NW columns: the MMAs of one group overlap the
+  // drain of the previous one (four slots for 128-row blocks measured slower)
+  const int NS = 2;
   const int ngroups = (nchunk + gch - 1) / gch;
   const int slot_f = DIR == 0 ? 4 * UCP * 32 : UCP * 32;  // floats of one CTA's partial for one owner
   const uint32_t kstrW = (uint32_t)NW * 16;
@@ -418,8 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
   if (threadIdx.x == 32) {
     for (int i = 0; i < 32; ++i) mbar_init(&bars[B_FULL + i], 1);
     for (int i = 0; i < 8; ++i) mbar_init(&bars[B_EMPTY + i], 1);
-    for (int i = 0; i < 2; ++i) mbar_init(&bars[B_SFULL + i], 1);
-    for (int i = 0; i < 2; ++i) mbar_init(&bars[B_SFREE + i], 4);
+    for (int i = 0; i < 4; ++i) mbar_init(&bars[B_SFULL + i], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&bars[B_SFREE + i], 4);
     mbar_init(&bars[B_W], 1);
     mbar_init(&bars[B_DONE], 1);
     mbar_init(&bars[B_PIN], 1);
@@ -513,8 +515,8 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
         int slot = 0;
         for (int j = 0; j < nchunk && ok; ++j) {
           if (j % gch == 0) {
-            slot = (int)(groups & 1);
-            if (groups >= 2 && !mbar_wait(&bars[B_SFREE + slot], (uint32_t)((groups / 2 - 1) & 1), p.status)) {
+            slot = (int)(groups % NS);
+            if (groups >= NS && !mbar_wait(&bars[B_SFREE + slot], (uint32_t)((groups / NS - 1) & 1), p.status)) {
               ok = false;
               break;
             }
@@ -532,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
             hb = wa + wchunk;
           }
           tc_fence_after();
-          const uint32_t dt = tmem + (uint32_t)slot * kSlotCols;
+          const uint32_t dt = tmem + (uint32_t)(slot * NW);
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
             const uint64_t ad = kdesc(su32(hb + 2 * ks * 1024), 1024, 128);  // state rows (M)
@@ -574,14 +576,14 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
       // MMA's next use, so they never fall two phases behind (a warp that
       // waited without gating could miss a phase and wait on the next one).
       for (int gi = 0; gi < ngroups; ++gi) {
-        const int slot = (int)(groups & 1);
-        if (drains && !fail && !mbar_wait(&bars[B_SFULL + slot], (uint32_t)((groups / 2) & 1), p.status)) fail = true;
+        const int slot = (int)(groups % NS);
+        if (drains && !fail && !mbar_wait(&bars[B_SFULL + slot], (uint32_t)((groups / NS) & 1), p.status)) fail = true;
         if (!fail) {
           tc_fence_after();
           if (drains && 64 * half < UB) {
             float sc = 1.0f;
             if (DIR == 1) sc = __ldcg(&xscale[par * NC + (int)(sp * ngroups + gi)]) * inv_w;
-            const uint32_t base = tl + (uint32_t)slot * kSlotCols + (uint32_t)(64 * half);
+            const uint32_t base = tl + (uint32_t)(slot * NW) + (uint32_t)(64 * half);
             // four quarters of 16 weight rows, the loads of a quarter in
             // flight together (registers: the 64 sums + 32 loaded values)
 #pragma unroll
