@@ -252,6 +252,24 @@ HS_API int hs_scan_forward_noalloc(const float *z, const float *c0, float *out, 
  * and have no device-side waits).  Allocates nothing. */
 HS_API int hs_scan_noalloc_status(int *host_status, hs_stream_t stream);
 
+/* Affine maps of one chunk of time steps of the scan, for a sequence split
+ * over time across GPUs (each rank scans its own chunk; the state crossing a
+ * chunk boundary is the only dependency).  z [T,B,4H] is the chunk's gate
+ * pre-activations.  backward = 0: the chunk maps the state entering it to its
+ * last state as c -> A c + C; writes A = prod_t max(f_t, eps) and CD = C (the
+ * chunk's last state from a zero carry), both [B,H].  backward = 1: the chunk
+ * maps the gradient arriving at its last state to the gradient it passes to
+ * the state before it as e -> A e + D; needs c [T,B,H] (the chunk's states),
+ * dout [T,B,H] and dh_last [B,H] (gradient of the chunk's last output, NULL =
+ * zeros); writes A and CD = D.  The carries then follow from all chunks' maps
+ * in order; each rank runs hs_scan_forward with its incoming state as c0 and
+ * hs_scan_backward with its incoming gradient as dc_n.  Sequence-sharded form
+ * of _log_parallel_scan (_parallel.py:21-35), which the reference runs on one
+ * device only. */
+HS_API int hs_scan_chunk_maps(const float *z, const float *c, const float *dout, const float *dh_last,
+                              int64_t T, int64_t B, int64_t H, float eps, float *A, float *CD, int backward,
+                              hs_stream_t stream);
+
 /* Whole parallel-mode forward: z = x W_ih^T + b_ih (z is caller-owned
  * [T,B,4H] scratch kept for the backward), then hs_scan_forward. */
 HS_API int hs_parallel_forward(const float *x, const float *c0, const float *w_ih,

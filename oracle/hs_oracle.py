@@ -285,6 +285,36 @@ def par_linear_chunked(zchunk, T, c0, dout, dh_n=None, dc_n=None, eps: float = E
     return dict(out=out, c=c, h_n=out[-1].clone(), c_n=c[-1].clone(), dc0=dc0, db=db)
 
 
+def par_chunk_maps(Z, c=None, dout=None, dh_last=None, backward=False, eps: float = EPS):
+    """Affine maps of one chunk of time steps of the clamped linear
+    recurrence (the checker of the sequence-sharded scan; _parallel.py:21-35
+    restated as in ``par_forward_linear``).  Z [T,B,4H].  Forward: the chunk
+    maps its entering state to its last state as c -> A c + C; returns (A, C)
+    with A = prod max(f,eps) and C the last state from a zero carry.
+    Backward: it maps the gradient arriving at its last state to the gradient
+    leaving to the state before it as e -> A e + D; needs the chunk's states
+    c and dout (dh_last added at the last step); returns (A, D)."""
+    i_, f_, g_, o_ = torch.sigmoid(Z).chunk(4, dim=-1)
+    fp = torch.clamp(f_, min=eps)
+    T = Z.shape[0]
+    A = torch.prod(fp, dim=0)
+    if not backward:
+        bp = torch.clamp(i_ * g_, min=eps)
+        v = torch.zeros_like(A)
+        for t in range(T):
+            v = fp[t] * v + bp[t]
+        return A, v
+    d = dout.clone()
+    if dh_last is not None:
+        d[-1] += dh_last
+    th = torch.tanh(c)
+    dcd = d * o_ * (1.0 - th * th)
+    v = torch.zeros_like(A)
+    for t in range(T - 1, -1, -1):
+        v = fp[t] * (dcd[t] + v)
+    return A, v
+
+
 # --------------------------------------------------------------------------
 # Module-level helpers (HeadStartLSTM semantics, __init__.py:131-233)
 # --------------------------------------------------------------------------

@@ -60,6 +60,7 @@ SIGNATURES = {
     "hs_scan_forward_kf": (_i32, [_c_p] * 6 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),
     "hs_scan_split_workspace_bytes": (_sz, [_i64] * 3),
     "hs_scan_backward_split": (_i32, [_c_p] * 11 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),
+    "hs_scan_chunk_maps": (_i32, [_c_p] * 4 + [_i64] * 3 + [_f32, _c_p, _c_p, _i32, _c_p]),
     "hs_parallel_forward": (_i32, [_c_p] * 9 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_parallel_backward": (_i32, [_c_p] * 12 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_parallel_forward_kf": (_i32, [_c_p] * 9 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),
