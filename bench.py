@@ -1012,8 +1012,11 @@ def main():
                     ent["e2e_vs_cpu_baseline"] = ent["e2e"]["value"] / value
             line["configs"][name] = ent
             torch.cuda.empty_cache()
-        # configs[3]'s bf16-input variant, through the module API
+        # configs[3]'s bf16-input variant, through the module API, and
+        # configs[4] in bf16 (the bf16 tensor-core GEMMs and dZ writer)
         line["configs"]["cfg3_bf16"] = run_bf16_module(args, dict(CONFIGS["cfg3"]), world, dev, rank)
+        torch.cuda.empty_cache()
+        line["configs"]["cfg4_bf16"] = run_bf16_module(args, dict(CONFIGS["cfg4"]), world, dev, rank, steps=4)
         torch.cuda.empty_cache()
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -1025,28 +1028,45 @@ def main():
 
 
 def run_bf16_module(args, cfg, world, dev, rank, steps=10, warmup=3):
-    """configs[3] with bfloat16 inputs and parameters (the reduced-precision
+    """A config with bfloat16 inputs and parameters (the reduced-precision
     variant): fwd + sum(out*G) backward through prlstm_b200.HeadStartLSTM,
-    inputs resident on the device, CUDA events around the steps.  Every rank
-    runs the full config (replicas); tokens/s is the whole job's."""
+    inputs resident on the device, CUDA events around the steps.  Recurrent
+    configs: every rank runs the full config (replicas).  Parallel configs:
+    the batch is split over ranks and run in micro-batches of MICRO_BATCH
+    sequences (gradients accumulated, then all-reduced), as the float32
+    headline.  tokens/s is the whole job's."""
     import torch.distributed as dist
 
     import prlstm_b200
 
     T, B, D, H = cfg["T"], cfg["B"], cfg["D"], cfg["H"]
+    parallel = cfg["mode"] == "parallel"
     params = make_params(cfg)
-    m = prlstm_b200.HeadStartLSTM(D, H).to(dev, torch.bfloat16)
+    m = prlstm_b200.HeadStartLSTM(D, H, parallel=parallel).to(dev, torch.bfloat16)
     with torch.no_grad():
         for p_, v in zip(m.parameters(), params):
             p_.copy_(v)
-    x, G = make_data(cfg, B, rank, dev)
-    x, G = x.to(torch.bfloat16), G.to(torch.bfloat16)
+    B_local = B // world if parallel else B
+    if parallel:
+        xs, Gs = make_data(cfg, B_local, rank, dev, mb=min(MICRO_BATCH, B_local))
+        xs = [t.to(torch.bfloat16) for t in xs]
+        Gs = [t.to(torch.bfloat16) for t in Gs]
+    else:
+        x, G = make_data(cfg, B, rank, dev)
+        xs, Gs = [x.to(torch.bfloat16)], [G.to(torch.bfloat16)]
+        del x, G
+    torch.cuda.empty_cache()
 
     def step():
         m.zero_grad(set_to_none=True)
-        xd = x.detach().requires_grad_(True)
-        out, _ = m(xd)
-        (out.float() * G.float()).sum().backward()
+        for x, G in zip(xs, Gs):
+            xd = x.detach().requires_grad_(True)
+            out, _ = m(xd)
+            (out * G).sum().backward()  # bf16 product, float32 accumulation in the sum
+        if parallel and world > 1:
+            for p_ in m.parameters():
+                if p_.grad is not None:
+                    dist.all_reduce(p_.grad)
 
     for _ in range(warmup):
         step()
@@ -1064,10 +1084,19 @@ def run_bf16_module(args, cfg, world, dev, rank, steps=10, warmup=3):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    return {"value": T * B * world * steps / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms / steps,
-            "steps": steps, "dtype": "bf16 inputs and parameters, f32 arithmetic",
-            "scaling": "weak (replicas)", "config": _config_obj("cfg3", cfg, world, None),
-            "tolerance": "2e-2 normwise vs float64 fed the bf16-rounded inputs (tests/test_gpu_bf16.py)"}
+    name = "cfg4" if parallel else "cfg3"
+    if parallel:
+        dtype = ("bf16 inputs and parameters: bf16 x bf16 tensor-core products (exact) with f32 accumulation, "
+                 "f32 scan and state, dZ rounded to bf16 for the gradient products")
+        tol = ("2e-2 normwise vs float64 fed the bf16-rounded inputs (tests/test_gpu_bf16.py, "
+               "tests/test_gpu_bf16_path.py at this config's micro-batch)")
+    else:
+        dtype = "bf16 inputs and parameters, f32 arithmetic"
+        tol = "2e-2 normwise vs float64 fed the bf16-rounded inputs (tests/test_gpu_bf16.py)"
+    tokens = T * (B if parallel else B * world)
+    return {"value": tokens * steps / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms / steps,
+            "steps": steps, "dtype": dtype, "scaling": "strong" if parallel else "weak (replicas)",
+            "config": _config_obj(name, cfg, world, None), "tolerance": tol}
 
 
 def _config_obj(name, cfg, world, workload):

@@ -215,6 +215,13 @@ HS_API int hs_scan_forward_kf(const float *z, const float *c0, float *out, float
  * exact maximum (z is overwritten then).
  * Replaces, with the GEMMs after it, the autograd backward of
  * headstartlstm_parallel (_parallel.py:38-74). */
+/* Diagnostic: 1 if the scans of this T, B, H run on the per-column kernels
+ * (one CTA per sequence x 32 units, a fixed order of operations, so results
+ * are the same bit for bit from run to run), 0 if on the look-back kernels
+ * (the carry into a tile is composed from whichever predecessors have
+ * published: float32 results may differ in the last bits between runs).
+ * HS_SCAN_PATH=chain|lookback forces one. */
+HS_API int hs_scan_uses_column_kernels(int64_t T, int64_t B, int64_t H);
 HS_API size_t hs_scan_split_workspace_bytes(int64_t T, int64_t B, int64_t H);
 HS_API int hs_scan_backward_split(float *z, const float *c, const float *c0, const float *dout,
                                   const float *dh_n, const float *dc_n, const unsigned *kf_max,
@@ -306,6 +313,63 @@ HS_API int hs_parallel_backward_kf(const float *x, const float *w_ih, float *z, 
                                    float *dc0, int64_t T, int64_t B, int64_t D, int64_t H,
                                    float eps, void *workspace, size_t workspace_bytes,
                                    const unsigned *kf, int *dev_status, hs_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * bfloat16 module path.  The reference runs the same module with bf16
+ * parameters and data (tests/test_parallel.py:24, tests/test_triton.py:22).
+ * Here a bf16 x bf16 product is exact in one tensor-core MMA with bf16
+ * inputs, accumulated in float32; the scan's arithmetic and carried state
+ * are float32; the saved activations (Z, c) and out, dout, dZ, dx are stored
+ * in bf16 (half the bytes).  bf16 arguments are `void *` (uint16 storage),
+ * 16-byte aligned, with row lengths (D, 4H, H) multiples of 8.
+ * HS_ERR_UNSUPPORTED when the shape or alignment does not suit (the caller
+ * then widens to float32 and takes the calls above).
+ * ---------------------------------------------------------------------- */
+HS_API size_t hs_linear_bf16_workspace_bytes(int64_t M, int64_t N, int64_t K);
+/* y[M,N] = x[M,K].w[N,K]^T (+ bias[N]), x and w bf16, bias and y float32.
+ * Replaces F.linear on bf16 tensors (_torch.py:96, _parallel.py:56). */
+HS_API int hs_linear_forward_bf16(const void *x, const void *w, const float *bias, float *y, int64_t M,
+                                  int64_t N, int64_t K, void *workspace, size_t workspace_bytes,
+                                  int *dev_status, hs_stream_t stream);
+/* dx[M,K] = dy[M,N].w[N,K] (dx may be NULL) and dw[N,K] = beta*dw + dy^T.x;
+ * dy, x, w bf16, dx and dw float32.  Replaces the gradient products of
+ * F.linear on bf16 tensors (_torch.py:157-162). */
+HS_API int hs_linear_backward_bf16(const void *dy, const void *x, const void *w, float *dx, float *dw,
+                                   int64_t M, int64_t N, int64_t K, int beta, void *workspace,
+                                   size_t workspace_bytes, int *dev_status, hs_stream_t stream);
+/* The scan forward with z [T*B][4H], out and c [T][B][H] in bf16 (c0, h_n,
+ * c_n float32).  No workspace.  Shapes the per-column kernels take
+ * (hs_scan_uses_column_kernels) with H % 8 == 0.  Replaces
+ * _log_parallel_scan with the activations (_parallel.py:21-35, :56-74) on
+ * bf16 tensors. */
+HS_API int hs_scan_forward_bf16(const void *z, const float *c0, void *out, void *c, float *h_n,
+                                float *c_n, int64_t T, int64_t B, int64_t H, float eps, int *dev_status,
+                                hs_stream_t stream);
+/* Its backward: z, c, dout bf16 in, dz [T*B][4H] bf16 out (the operand of
+ * hs_linear_backward_bf16); dh_n, dc_n, dc0, db float32.  Workspace (for db):
+ * hs_scan_bf16_workspace_bytes. */
+HS_API size_t hs_scan_bf16_workspace_bytes(int64_t T, int64_t B, int64_t H);
+HS_API int hs_scan_backward_bf16(const void *z, const void *c, const float *c0, const void *dout,
+                                 const float *dh_n, const float *dc_n, void *dz, float *dc0, float *db,
+                                 int64_t T, int64_t B, int64_t H, float eps, void *workspace,
+                                 size_t workspace_bytes, int *dev_status, hs_stream_t stream);
+/* hs_parallel_forward / hs_parallel_backward for a bf16 module: x, w_ih,
+ * z, out, c, dout and dx bf16; c0, b_ih, h_n, c_n, dh_n, dc_n, dw_ih, db_ih,
+ * dc0 float32.  hs_parallel_bf16_supported says whether the shape is taken;
+ * one workspace size covers both calls.  Replaces headstartlstm_parallel +
+ * its autograd (_parallel.py:38-74) on bf16 tensors. */
+HS_API int hs_parallel_bf16_supported(int64_t T, int64_t B, int64_t D, int64_t H);
+HS_API size_t hs_parallel_bf16_workspace_bytes(int64_t T, int64_t B, int64_t D, int64_t H);
+HS_API int hs_parallel_forward_bf16(const void *x, const float *c0, const void *w_ih, const float *b_ih,
+                                    void *z, void *out, void *c, float *h_n, float *c_n, int64_t T,
+                                    int64_t B, int64_t D, int64_t H, float eps, void *workspace,
+                                    size_t workspace_bytes, int *dev_status, hs_stream_t stream);
+HS_API int hs_parallel_backward_bf16(const void *x, const void *w_ih, const void *z, const void *c,
+                                     const float *c0, const void *dout, const float *dh_n,
+                                     const float *dc_n, void *dx, float *dw_ih, float *db_ih, float *dc0,
+                                     int64_t T, int64_t B, int64_t D, int64_t H, float eps,
+                                     void *workspace, size_t workspace_bytes, int *dev_status,
+                                     hs_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Recurrent path.  Replaces HeadStartLSTMTorchFn / HeadStartLSTMTritonFn

@@ -58,6 +58,7 @@ SIGNATURES = {
     "hs_scan_backward": (_i32, [_c_p] * 9 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_scan_backward_absmax": (_i32, [_c_p] * 9 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),
     "hs_scan_forward_kf": (_i32, [_c_p] * 6 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),
+    "hs_scan_uses_column_kernels": (_i32, [_i64] * 3),
     "hs_scan_split_workspace_bytes": (_sz, [_i64] * 3),
     "hs_scan_backward_split": (_i32, [_c_p] * 11 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_scan_chunk_maps": (_i32, [_c_p] * 4 + [_i64] * 3 + [_f32, _c_p, _c_p, _i32, _c_p]),
@@ -65,6 +66,16 @@ SIGNATURES = {
     "hs_parallel_backward": (_i32, [_c_p] * 12 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_parallel_forward_kf": (_i32, [_c_p] * 9 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),
     "hs_parallel_backward_kf": (_i32, [_c_p] * 12 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),
+    "hs_linear_bf16_workspace_bytes": (_sz, [_i64] * 3),
+    "hs_linear_forward_bf16": (_i32, [_c_p] * 4 + [_i64] * 3 + [_c_p, _sz, _c_p, _c_p]),
+    "hs_linear_backward_bf16": (_i32, [_c_p] * 5 + [_i64] * 3 + [_i32, _c_p, _sz, _c_p, _c_p]),
+    "hs_scan_forward_bf16": (_i32, [_c_p] * 6 + [_i64] * 3 + [_f32, _c_p, _c_p]),
+    "hs_scan_bf16_workspace_bytes": (_sz, [_i64] * 3),
+    "hs_scan_backward_bf16": (_i32, [_c_p] * 9 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),
+    "hs_parallel_bf16_supported": (_i32, [_i64] * 4),
+    "hs_parallel_bf16_workspace_bytes": (_sz, [_i64] * 4),
+    "hs_parallel_forward_bf16": (_i32, [_c_p] * 9 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p]),
+    "hs_parallel_backward_bf16": (_i32, [_c_p] * 12 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_recurrent_workspace_bytes": (_sz, [_i64] * 4),
     "hs_recurrent_uses_tensor_cores": (_i32, [_i64, _i64, _i32]),
     "hs_recurrent_forward": (_i32, [_c_p] * 11 + [_i64] * 4 + [_c_p, _sz, _c_p, _c_p]),

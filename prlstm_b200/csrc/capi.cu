@@ -321,6 +321,116 @@ int parallel_backward(const float *x, const float *w_ih, float *z, const float *
                             dz_absmax);
 }
 
+// ---------------------------------------------------------------- bf16 operands
+// A bfloat16 module's linear-layer products: bf16 x bf16 products are exact
+// in one kind::f16 tensor-core MMA with bf16 inputs (no fp16 split, no
+// operand scale), accumulated in float32.
+int gemm_bf16(const void *a, int64_t a_ld, bool a_mn, const void *b, int64_t b_ld, bool b_mn, void *C,
+              const float *bias, int64_t M, int64_t N, int64_t K, int64_t ldc, int beta, void *ws, size_t ws_bytes,
+              int *status, cudaStream_t st, bool *done, bool c_bf16);
+size_t gemm_bf16_partial_bound(int64_t M, int64_t N, int64_t K);
+bool scan_bf16_ok(int64_t T, int64_t B, int64_t H);
+size_t scan_bf16_ws_bytes(int64_t B, int64_t H);
+int scan_forward_bf16(const void *z, const float *c0, void *out, void *c, float *h_n, float *c_n, int64_t T, int64_t B,
+                      int64_t H, float eps, int *status, cudaStream_t st);
+int scan_backward_bf16(const void *z, const void *c, const float *c0, const void *dout, const float *dh_n,
+                       const float *dc_n, void *dz, float *dc0, float *db, int64_t T, int64_t B, int64_t H, float eps,
+                       void *ws, size_t ws_bytes, int *status, cudaStream_t st);
+
+size_t linear_bf16_ws(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  return std::max({gemm_bf16_partial_bound(M, N, K), gemm_bf16_partial_bound(M, K, N),
+                   gemm_bf16_partial_bound(N, K, M), (size_t)256});
+}
+
+static int bf16_declined(const char *what) {
+  return fail(HS_ERR_UNSUPPORTED, "%s: the bf16 tensor-core GEMM declined (operands must be 16-byte aligned, "
+              "the tensor cores enabled)", what);
+}
+
+// y[M,N] = x[M,K].w[N,K]^T (+ bias): x, w bf16; bias float32; y float32, or
+// bf16 if y_bf16.
+int linear_forward_bf16(const void *x, const void *w, const float *bias, void *y, int64_t M, int64_t N, int64_t K,
+                        void *ws, size_t ws_bytes, int *status, cudaStream_t st, bool y_bf16 = false) {
+  if (int e = check_gemm(x, w, y, M, N, K)) return e;
+  if (!status) return fail(HS_ERR_INVALID_ARG, "bf16 linear: null status");
+  if (K % 8 || N % (y_bf16 ? 8 : 4)) return fail(HS_ERR_UNSUPPORTED, "bf16 linear: K must be a multiple of 8, N of 4 (8 for bf16 y)");
+  if (!M || !N) return HS_OK;
+  bool done = false;
+  if (int e = gemm_bf16(x, K, false, w, K, false, y, bias, M, N, K, N, 0, ws, ws_bytes, status, st, &done, y_bf16))
+    return e;
+  return done ? HS_OK : bf16_declined("bf16 linear forward");
+}
+
+// dx[M,K] = dy[M,N].w[N,K] (dx may be null; float32, or bf16 if dx_bf16) and
+// dw[N,K] = beta*dw + dy^T.x (float32): dy, x, w bf16.
+int linear_backward_bf16(const void *dy, const void *x, const void *w, void *dx, float *dw, int64_t M, int64_t N,
+                         int64_t K, int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st,
+                         bool dx_bf16 = false) {
+  if (int e = check_gemm(dy, x, dw, N, K, M)) return e;
+  if (dx && !w) return fail(HS_ERR_INVALID_ARG, "bf16 linear backward: dx wanted without w");
+  if (!status) return fail(HS_ERR_INVALID_ARG, "bf16 linear backward: null status");
+  if (K % 8 || N % 8) return fail(HS_ERR_UNSUPPORTED, "bf16 linear backward: N and K must be multiples of 8");
+  if (!M || !N || !K) return HS_OK;
+  bool done = false;
+  if (dx) {
+    if (int e = gemm_bf16(dy, N, false, w, K, true, dx, nullptr, M, K, N, K, 0, ws, ws_bytes, status, st, &done,
+                          dx_bf16))
+      return e;
+    if (!done) return bf16_declined("bf16 linear dgrad");
+  }
+  if (int e = gemm_bf16(dy, N, true, x, K, true, dw, nullptr, N, K, M, K, beta, ws, ws_bytes, status, st, &done,
+                        false))
+    return e;
+  return done ? HS_OK : bf16_declined("bf16 linear wgrad");
+}
+
+// The whole parallel path of a bf16 module with bf16 saved activations:
+// x, w_ih, z, out, c, dout, dx bf16; c0, b_ih, h_n, c_n, dh_n, dc_n, dw_ih,
+// db_ih, dc0 float32.
+bool parallel_bf16_ok(int64_t T, int64_t B, int64_t D, int64_t H) {
+  return D > 0 && D % 8 == 0 && scan_bf16_ok(T, B, H) && T * B < (1ll << 31);
+}
+
+// [dZ bf16 [T*B][4H]][max(scan scratch, GEMM scratch)]
+size_t parallel_bf16_ws(int64_t T, int64_t B, int64_t D, int64_t H) {
+  const int64_t M = T * B, N = 4 * H;
+  return round_up((size_t)M * N * 2, 256) + std::max(scan_bf16_ws_bytes(B, H), linear_bf16_ws(M, N, D));
+}
+
+int parallel_forward_bf16(const void *x, const float *c0, const void *w_ih, const float *b_ih, void *z, void *out,
+                          void *c, float *h_n, float *c_n, int64_t T, int64_t B, int64_t D, int64_t H, float eps,
+                          void *ws, size_t ws_bytes, int *status, cudaStream_t st) {
+  if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return fail(HS_ERR_INVALID_ARG, "T, B, D, H must be positive");
+  if (!x || !w_ih || !z) return fail(HS_ERR_INVALID_ARG, "parallel_forward_bf16: null x/w_ih/z");
+  if (!parallel_bf16_ok(T, B, D, H))
+    return fail(HS_ERR_UNSUPPORTED, "bf16 parallel path: needs D, H multiples of 8 and a shape the per-column scan takes");
+  if (int e = linear_forward_bf16(x, w_ih, b_ih, z, T * B, 4 * H, D, ws, ws_bytes, status, st, true)) return e;
+  return scan_forward_bf16(z, c0, out, c, h_n, c_n, T, B, H, eps, status, st);
+}
+
+int parallel_backward_bf16(const void *x, const void *w_ih, const void *z, const void *c, const float *c0,
+                           const void *dout, const float *dh_n, const float *dc_n, void *dx, float *dw_ih, float *db_ih,
+                           float *dc0, int64_t T, int64_t B, int64_t D, int64_t H, float eps, void *ws, size_t ws_bytes,
+                           int *status, cudaStream_t st) {
+  if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return fail(HS_ERR_INVALID_ARG, "T, B, D, H must be positive");
+  if (!x || !w_ih || !z || !dw_ih || !db_ih)
+    return fail(HS_ERR_INVALID_ARG, "parallel_backward_bf16: null x/w_ih/z/dw_ih/db_ih");
+  if (!parallel_bf16_ok(T, B, D, H))
+    return fail(HS_ERR_UNSUPPORTED, "bf16 parallel path: needs D, H multiples of 8 and a shape the per-column scan takes");
+  if (!ws || !aligned(ws, 256)) return fail(HS_ERR_INVALID_ARG, "workspace must be non-null and 256-byte aligned");
+  if (ws_bytes < parallel_bf16_ws(T, B, D, H))
+    return fail(HS_ERR_WORKSPACE, "parallel_backward_bf16: workspace %zu < %zu bytes", ws_bytes,
+                parallel_bf16_ws(T, B, D, H));
+  const int64_t M = T * B, N = 4 * H;
+  const size_t sb = round_up((size_t)M * N * 2, 256);
+  char *rest = static_cast<char *>(ws) + sb;
+  const size_t rb = ws_bytes - sb;
+  if (int e = scan_backward_bf16(z, c, c0, dout, dh_n, dc_n, ws, dc0, db_ih, T, B, H, eps, rest, rb, status, st))
+    return e;
+  return linear_backward_bf16(ws, x, w_ih, dx, dw_ih, M, N, D, 0, rest, rb, status, st, true);
+}
+
 namespace {
 __global__ void selftest_wait_kernel(const unsigned *flag, int *status, uint64_t limit_ns) {
   if (threadIdx.x == 0) (void)wait_flag(flag, status, limit_ns);
@@ -527,6 +637,45 @@ int hs_parallel_backward(const float *x, const float *w_ih, float *z, const floa
   return hs::parallel_backward(x, w_ih, z, c, c0, dout, dh_n, dc_n, dx, dw_ih, db_ih, dc0, T, B,
                                D, H, eps, workspace, workspace_bytes, dev_status,
                                (cudaStream_t)stream);
+}
+
+size_t hs_linear_bf16_workspace_bytes(int64_t M, int64_t N, int64_t K) { return hs::linear_bf16_ws(M, N, K); }
+
+int hs_linear_forward_bf16(const void *x, const void *w, const float *bias, float *y, int64_t M, int64_t N, int64_t K,
+                           void *workspace, size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
+  return hs::linear_forward_bf16(x, w, bias, y, M, N, K, workspace, workspace_bytes, dev_status,
+                                 (cudaStream_t)stream);
+}
+
+int hs_linear_backward_bf16(const void *dy, const void *x, const void *w, float *dx, float *dw, int64_t M, int64_t N,
+                            int64_t K, int beta, void *workspace, size_t workspace_bytes, int *dev_status,
+                            hs_stream_t stream) {
+  return hs::linear_backward_bf16(dy, x, w, dx, dw, M, N, K, beta, workspace, workspace_bytes, dev_status,
+                                  (cudaStream_t)stream);
+}
+
+int hs_parallel_bf16_supported(int64_t T, int64_t B, int64_t D, int64_t H) {
+  return (T > 0 && B > 0 && H > 0 && hs::parallel_bf16_ok(T, B, D, H)) ? 1 : 0;
+}
+
+size_t hs_parallel_bf16_workspace_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
+  if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return 0;
+  return hs::parallel_bf16_ws(T, B, D, H);
+}
+
+int hs_parallel_forward_bf16(const void *x, const float *c0, const void *w_ih, const float *b_ih, void *z, void *out,
+                             void *c, float *h_n, float *c_n, int64_t T, int64_t B, int64_t D, int64_t H, float eps,
+                             void *workspace, size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
+  return hs::parallel_forward_bf16(x, c0, w_ih, b_ih, z, out, c, h_n, c_n, T, B, D, H, eps, workspace,
+                                   workspace_bytes, dev_status, (cudaStream_t)stream);
+}
+
+int hs_parallel_backward_bf16(const void *x, const void *w_ih, const void *z, const void *c, const float *c0,
+                              const void *dout, const float *dh_n, const float *dc_n, void *dx, float *dw_ih,
+                              float *db_ih, float *dc0, int64_t T, int64_t B, int64_t D, int64_t H, float eps,
+                              void *workspace, size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
+  return hs::parallel_backward_bf16(x, w_ih, z, c, c0, dout, dh_n, dc_n, dx, dw_ih, db_ih, dc0, T, B, D, H, eps,
+                                    workspace, workspace_bytes, dev_status, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -36,6 +36,7 @@
 //               the transform running ahead of the tensor core.
 // No cluster multicast anywhere.  Every mbarrier wait is bounded.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
@@ -217,6 +218,7 @@ struct TcArgs {
   int kb_per_split;
   int nkb;
   int *status;
+  int out_bf16 = 0;  // pair kernel, bf16 operands: the output is bf16 (no split-K, no beta)
 };
 
 // Epilogue of the fold warps (128 threads, thread = tile row q*32+lane):
@@ -860,6 +862,42 @@ HS_DEV void store_tile_boxes(const float (&tot)[BN], float *box, const CUtensorM
   }
 }
 
+// The same epilogue writing bf16 (a bf16 module's Z or dX): 128-row x
+// 64-column bf16 boxes (128-byte rows, the same swizzle), bias added in
+// float32 before the rounding.  No split-K partials, no beta.
+HS_DEV uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t *>(&v);
+}
+HS_DEV void store_tile_boxes_bf16(const float (&tot)[BN], float *boxf, const CUtensorMap *tmC_, const TcArgs &p,
+                                  int q, int lane, int t, int64_t m0, int64_t n0, int bar_id) {
+  const CUtensorMap &tmC = *tmC_;
+  const int r = q * 32 + lane;
+  uint4 *box = reinterpret_cast<uint4 *>(boxf);
+#pragma unroll
+  for (int c = 0; c < BN / 64; ++c) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int64_t n = n0 + c * 64 + 8 * j + e;
+        v[e] = tot[c * 64 + 8 * j + e] + ((p.bias && n < p.N) ? p.bias[n] : 0.f);
+      }
+      box[r * 8 + (j ^ (r & 7))] =
+          make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    named_sync(bar_id);
+    if (t == 0) {
+      tma_store_3d(&tmC, box, (int)n0 + 64 * c, (int)m0, 0);
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // box free again
+    }
+    named_sync(bar_id);
+  }
+}
+
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(H3_THREADS, 1)
 gemm_h3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
@@ -1101,6 +1139,13 @@ constexpr int P_SMEM = P_STAGES * P_STAGE + 2 * H3_EPI + 1024 + 256;
 static_assert(P_SMEM <= 232448, "shared memory per block");
 constexpr int P_BM = 256, P_BN = 256;                // pair tile
 constexpr uint32_t P_ACC_COLS = 256;                 // one accumulator buffer
+// bf16 variant (BF): the operands are bf16 themselves, whose products are
+// exact in one kind::f16 MMA with bf16 inputs, so a stage holds A and B only
+// (twice the stages in the same ring), one MMA per k-step, no operand
+// scales; accumulator groups of 8 k-blocks (512 k) bound the tensor core's
+// truncating accumulation to ~2e-5 relative per group before the fp32 fold.
+constexpr int P_PROMOTE_BF = 8 * 64 / P_BK;
+static_assert(2 * P_STAGES * 2 * P_TILE == P_STAGES * P_STAGE, "bf16 ring reuses the split ring's bytes");
 
 HS_DEV uint32_t cluster_rank() {
   uint32_t r;
@@ -1142,18 +1187,22 @@ HS_DEV void mma_commit_pair(uint64_t *b) {
                : "memory");
 }
 
-template <bool A_MN, bool B_MN>
+// BF: bf16 operands in tmAh / tmBh (tmAl, tmBl unused), one product.
+template <bool A_MN, bool B_MN, bool BF = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
 gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                     const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
                     const __grid_constant__ CUtensorMap tmC, TcArgs p, const unsigned *absmax_a,
                     const unsigned *absmax_b, int mtiles, int ntiles, int ntiles_total) {
+  constexpr int NSTG = BF ? 2 * P_STAGES : P_STAGES;     // ring stages
+  constexpr int SBYTES = BF ? 2 * P_TILE : P_STAGE;      // bytes per stage per CTA
+  constexpr int PROM = BF ? P_PROMOTE_BF : P_PROMOTE;    // k-blocks per accumulator group
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float *epi = reinterpret_cast<float *>(smem + P_STAGES * P_STAGE);  // two 16 KB boxes
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE + 2 * H3_EPI);
-  uint64_t *empty = full + P_STAGES;
-  uint64_t *pfull = empty + P_STAGES;
+  float *epi = reinterpret_cast<float *>(smem + NSTG * SBYTES);  // two 16 KB boxes
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + NSTG * SBYTES + 2 * H3_EPI);
+  uint64_t *empty = full + NSTG;
+  uint64_t *pfull = empty + NSTG;
   uint64_t *pempty = pfull + 2;
   uint64_t *mdone = pempty + 2;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(mdone + 1);
@@ -1173,7 +1222,7 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
   };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < P_STAGES; ++s) {
+    for (int s = 0; s < NSTG; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -1209,16 +1258,34 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
         tile_of(tl, m0, n0, z, nk);
         const int mr = (int)m0 + 128 * (int)rank, nr = (int)n0 + 128 * (int)rank;
         for (int i = 0; i < nk; ++i, ++it) {
-          const int s = it % P_STAGES;
-          const uint32_t ph = (it / P_STAGES) & 1;
+          const int s = it % NSTG;
+          const uint32_t ph = (it / NSTG) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, p.status)) { ok = false; break; }
           // pass a real release (not the first use of a stage) on to the
           // second CTA first, so that its loads start with this CTA's
-          if (rank == 0 && it >= P_STAGES) mbar_arrive_cluster(cluster_addr(&empty[s], 1));
+          if (rank == 0 && it >= NSTG) mbar_arrive_cluster(cluster_addr(&empty[s], 1));
           const uint32_t fb = cluster_addr(&full[s], 0);
-          unsigned char *st = smem + s * P_STAGE;
-          if (rank == 0) mbar_expect_tx(&full[s], 2 * P_STAGE);  // both CTAs' bytes
+          unsigned char *st = smem + s * SBYTES;
+          if (rank == 0) mbar_expect_tx(&full[s], 2 * SBYTES);  // both CTAs' bytes
           const int k0 = (z * p.kb_per_split + i) * P_BK;
+          if (BF) {
+            // A then B, one part each
+            if (A_MN) {
+#pragma unroll
+              for (int j = 0; j < P_MN_NBOX; ++j) tma_2d_pair(st + j * P_MN_BOX, &tmAh, fb, mr + P_BK * j, k0);
+            } else {
+              tma_2d_pair(st, &tmAh, fb, k0, mr);
+            }
+            if (B_MN) {
+#pragma unroll
+              for (int j = 0; j < P_MN_NBOX; ++j)
+                tma_2d_pair(st + P_TILE + j * P_MN_BOX, &tmBh, fb, nr + P_BK * j, k0);
+            } else {
+              tma_2d_pair(st + P_TILE, &tmBh, fb, k0, nr);
+            }
+            ++issued;
+            continue;
+          }
           if (A_MN) {
 #pragma unroll
             for (int j = 0; j < P_MN_NBOX; ++j) {
@@ -1245,17 +1312,18 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
       // The first CTA's barrier counts both CTAs' bytes: never leave while a
       // copy into either CTA's shared memory is in flight.
       if (rank == 0) {
-        for (int j = std::max(0, issued - P_STAGES); j < issued; ++j) {
-          if (ld_status(p.status)) mbar_drain(&full[j % P_STAGES], (j / P_STAGES) & 1);
-          else (void)mbar_wait(&full[j % P_STAGES], (j / P_STAGES) & 1, p.status);
+        for (int j = std::max(0, issued - NSTG); j < issued; ++j) {
+          if (ld_status(p.status)) mbar_drain(&full[j % NSTG], (j / NSTG) & 1);
+          else (void)mbar_wait(&full[j % NSTG], (j / NSTG) & 1, p.status);
         }
       }
     }
   } else if (!skip && warp == 1) {
     // ---------------- MMA issuer (first CTA only)
     if (rank == 0 && lane == 0) {
-      constexpr uint32_t idesc =
-          idesc_f16(P_BM, P_BN) | ((A_MN ? 1u : 0u) << 15) | ((B_MN ? 1u : 0u) << 16);
+      // bf16: A and B format fields (bits 7-9, 10-12) = 1; fp16 is 0
+      constexpr uint32_t idesc = idesc_f16(P_BM, P_BN) | ((A_MN ? 1u : 0u) << 15) | ((B_MN ? 1u : 0u) << 16) |
+                                 (BF ? ((1u << 7) | (1u << 10)) : 0u);
       int it = 0, gg = 0;
       bool ok = true;
       for (int tl = pair; tl < ntiles_total && ok; tl += npairs) {
@@ -1263,15 +1331,15 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
         int z, nk;
         tile_of(tl, m0, n0, z, nk);
         for (int i = 0; i < nk; ++i, ++it) {
-          const int s = it % P_STAGES;
-          const uint32_t ph = (it / P_STAGES) & 1;
-          const bool gstart = (i % P_PROMOTE) == 0;
+          const int s = it % NSTG;
+          const uint32_t ph = (it / NSTG) & 1;
+          const bool gstart = (i % PROM) == 0;
           const int b = gg & 1;
           if (gstart && !mbar_wait(&pempty[b], ((gg >> 1) & 1) ^ 1, p.status)) { ok = false; break; }
           if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t ah = su32(smem + s * P_STAGE);
-          const uint32_t al = ah + P_TILE, bh = ah + 2 * P_TILE, bl = ah + 3 * P_TILE;
+          const uint32_t ah = su32(smem + s * SBYTES);
+          const uint32_t al = ah + P_TILE, bh = ah + (BF ? 1 : 2) * P_TILE, bl = ah + 3 * P_TILE;
           const uint32_t t_acc = tmem + (uint32_t)(b * P_ACC_COLS);
 #pragma unroll
           for (int kk = 0; kk < P_BK / 16; ++kk) {
@@ -1283,11 +1351,13 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
             const uint64_t dBh = sdesc(bh + ob, lb, P_SBO, P_LAYOUT), dBl = sdesc(bl + ob, lb, P_SBO, P_LAYOUT);
             const uint32_t acc = (gstart && kk == 0) ? 0u : 1u;
             mma_f16_pair(t_acc, dAh, dBh, idesc, acc);
-            mma_f16_pair(t_acc, dAh, dBl, idesc, 1u);
-            mma_f16_pair(t_acc, dAl, dBh, idesc, 1u);
+            if (!BF) {
+              mma_f16_pair(t_acc, dAh, dBl, idesc, 1u);
+              mma_f16_pair(t_acc, dAl, dBh, idesc, 1u);
+            }
           }
           mma_commit_pair(&empty[s]);
-          if ((i % P_PROMOTE) == P_PROMOTE - 1 || i == nk - 1) {
+          if ((i % PROM) == PROM - 1 || i == nk - 1) {
             mma_commit_pair(&pfull[b]);
             ++gg;
           }
@@ -1307,7 +1377,7 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
     // Undo the two operand scales one at a time: each inverse is an exact
     // power of two within float range, their product may not be (tiny
     // operands get scales up to 2^114 each).
-    const float inv_a = 1.0f / pow2_scale(*absmax_a), inv_b = 1.0f / pow2_scale(*absmax_b);
+    const float inv_a = BF ? 1.f : 1.0f / pow2_scale(*absmax_a), inv_b = BF ? 1.f : 1.0f / pow2_scale(*absmax_b);
     const uint32_t pe0 = cluster_addr(&pempty[0], 0), pe1 = cluster_addr(&pempty[1], 0);
     const uint32_t pf0 = cluster_addr(&pfull[0], 1), pf1 = cluster_addr(&pfull[1], 1);
     int gg = 0;
@@ -1316,7 +1386,7 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
       int64_t m0, n0;
       int z, nk;
       tile_of(tl, m0, n0, z, nk);
-      const int ngroups = (nk + P_PROMOTE - 1) / P_PROMOTE;
+      const int ngroups = (nk + PROM - 1) / PROM;
       float tot[BN];
 #pragma unroll
       for (int j = 0; j < BN; ++j) tot[j] = 0.f;
@@ -1341,8 +1411,12 @@ gemm_h3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_const
       if (!ok) break;
 #pragma unroll
       for (int j = 0; j < BN; ++j) tot[j] = (tot[j] * inv_a) * inv_b;
-      store_tile_boxes(tot, epi + half * (H3_EPI / 4), &tmC, p, q, lane, t, m0 + 128 * (int64_t)rank,
-                       n0 + (int64_t)half * BN, p.partial ? z : 0, 1 + half);
+      if (BF && p.out_bf16)
+        store_tile_boxes_bf16(tot, epi + half * (H3_EPI / 4), &tmC, p, q, lane, t, m0 + 128 * (int64_t)rank,
+                              n0 + (int64_t)half * BN, 1 + half);
+      else
+        store_tile_boxes(tot, epi + half * (H3_EPI / 4), &tmC, p, q, lane, t, m0 + 128 * (int64_t)rank,
+                         n0 + (int64_t)half * BN, p.partial ? z : 0, 1 + half);
     }
   }
 
@@ -1386,6 +1460,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // Output map: C [splits][M][N] fp32 with row stride ld; 32-column x 128-row
 // boxes, 128-byte swizzle (matches the epilogue's shared-memory staging).
+// bf16 output [M][ld]: 3D {N, M, 1}, box {64, 128, 1} (128-byte rows).
+bool make_out_map_bf16(CUtensorMap *tm, void *ptr, int64_t M, int64_t N, int64_t ld) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, 1};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)(ld * M * 2)};
+  cuuint32_t box[3] = {64, (cuuint32_t)BM, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ptr, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool make_out_map(CUtensorMap *tm, float *ptr, int64_t splits, int64_t M, int64_t N, int64_t ld) {
   auto enc = encode_fn();
   if (!enc) return false;
@@ -1570,15 +1657,17 @@ bool make_map_f16(CUtensorMap *tm, const __half *ptr, int64_t rows, int64_t ld, 
 }
 
 // The pair kernel's maps: K-major box {P_BK k, 128 rows}, MN-major box
-// {P_BK columns, P_BK k rows}, swizzled to the row width (128 or 64 bytes).
-bool make_map_f16_pair(CUtensorMap *tm, const __half *ptr, int64_t rows, int64_t ld, bool mn) {
+// {P_BK columns, P_BK k rows}, swizzled to the row width (128 or 64 bytes);
+// fp16 elements, or bf16 (bf).
+bool make_map_f16_pair(CUtensorMap *tm, const void *ptr, int64_t rows, int64_t ld, bool mn, bool bf = false) {
   auto enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
   cuuint32_t box[2] = {(cuuint32_t)P_BK, mn ? (cuuint32_t)P_BK : 128u};
   cuuint32_t es[2] = {1, 1};
-  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)ptr, dims, strides, box, es,
+  return enc(tm, bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)ptr, dims,
+             strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, P_BK == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -1630,10 +1719,10 @@ int absmax_rows(const float *x, int64_t rows, int64_t cols, int64_t ld, unsigned
 // Largest number of pairs (clusters of two CTAs) of this kernel variant
 // resident at once on the current device; 0 if none.
 int pair_capacity(const void *fn, int variant) {
-  static std::atomic<int> cached[64][4];
+  static std::atomic<int> cached[64][8];
   int dev = 0;
   cudaGetDevice(&dev);
-  std::atomic<int> &c = cached[dev & 63][variant & 3];
+  std::atomic<int> &c = cached[dev & 63][variant & 7];
   int v = c.load(std::memory_order_relaxed);
   if (v > 0) return v - 1;
   cudaLaunchConfig_t cfg = {};
@@ -1649,39 +1738,48 @@ int pair_capacity(const void *fn, int variant) {
   return n;
 }
 
-// The pair kernel on already encoded operand maps; *done = false if it does
-// not apply (no pair fits, or a split-K partial would not fit ws).
-int gemm_h3_pair(const __half *ah, const __half *al, int64_t a_rows, int64_t a_ld, bool a_mn, const __half *bh,
-                 const __half *bl, int64_t b_rows, int64_t b_ld, bool b_mn, const unsigned *a_absmax,
-                 const unsigned *b_absmax, float *C, const float *bias, int64_t M, int64_t N, int64_t K, int64_t ldc,
-                 int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st, bool *done) {
+using PairFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                       const CUtensorMap, TcArgs, const unsigned *, const unsigned *, int, int, int);
+
+template <bool BF>
+PairFn pair_fn(bool a_mn, bool b_mn) {
+  if (a_mn) return b_mn ? gemm_h3_pair_kernel<true, true, BF> : gemm_h3_pair_kernel<true, false, BF>;
+  return b_mn ? gemm_h3_pair_kernel<false, true, BF> : gemm_h3_pair_kernel<false, false, BF>;
+}
+
+// The pair kernel on encoded operand maps (tal, tbl unused when bf); *done =
+// false if it does not apply (no pair fits, or a split-K partial would not
+// fit ws).
+// c_bf16 (bf operands only): C is bf16, written without split-K or beta.
+static int pair_run(bool bf, const CUtensorMap &tah, const CUtensorMap &tal, const CUtensorMap &tbh, const CUtensorMap &tbl,
+             bool a_mn, bool b_mn, const unsigned *a_absmax, const unsigned *b_absmax, void *Cv, const float *bias,
+             int64_t M, int64_t N, int64_t K, int64_t ldc, int beta, void *ws, size_t ws_bytes, int *status,
+             cudaStream_t st, bool *done, bool c_bf16 = false) {
   *done = false;
-  CUtensorMap tah, tal, tbh, tbl;
-  if (!make_map_f16_pair(&tah, ah, a_rows, a_ld, a_mn) || !make_map_f16_pair(&tal, al, a_rows, a_ld, a_mn) ||
-      !make_map_f16_pair(&tbh, bh, b_rows, b_ld, b_mn) || !make_map_f16_pair(&tbl, bl, b_rows, b_ld, b_mn))
-    return HS_OK;
-  void (*fn)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs,
-             const unsigned *, const unsigned *, int, int, int);
-  if (a_mn) fn = b_mn ? gemm_h3_pair_kernel<true, true> : gemm_h3_pair_kernel<true, false>;
-  else fn = b_mn ? gemm_h3_pair_kernel<false, true> : gemm_h3_pair_kernel<false, false>;
-  const int variant = (a_mn ? 2 : 0) + (b_mn ? 1 : 0);
-  static std::atomic<unsigned long long> attr_set[4];
+  if (c_bf16 && (!bf || beta)) return HS_OK;
+  float *C = static_cast<float *>(Cv);
+  const PairFn fn = bf ? pair_fn<true>(a_mn, b_mn) : pair_fn<false>(a_mn, b_mn);
+  const int variant = (bf ? 4 : 0) + (a_mn ? 2 : 0) + (b_mn ? 1 : 0);
+  static std::atomic<unsigned long long> attr_set[8];
   if (int e = allow_dynamic_smem((const void *)fn, P_SMEM, &attr_set[variant])) return e;
   const int npairs = pair_capacity((const void *)fn, variant);
   if (npairs < 1) return HS_OK;
   const int nkb = (int)((round8(K) + P_BK - 1) / P_BK);
   const int64_t mt = (M + P_BM - 1) / P_BM, nt = (N + P_BN - 1) / P_BN;
-  int splits = pair_split_count(mt * nt, nkb, npairs);
+  int splits = c_bf16 ? 1 : pair_split_count(mt * nt, nkb, npairs);
   if (splits > 1 && (!ws || !aligned(ws, 256) || ws_bytes < (size_t)splits * M * N * 4)) splits = 1;
   const int kbps = (nkb + splits - 1) / splits;
   splits = (nkb + kbps - 1) / kbps;
   float *partial = splits > 1 ? static_cast<float *>(ws) : nullptr;
   CUtensorMap tc;
-  if (!make_out_map(&tc, splits > 1 ? partial : C, splits, M, N, splits > 1 ? N : ldc)) return HS_OK;
+  if (c_bf16 ? !make_out_map_bf16(&tc, Cv, M, N, ldc)
+             : !make_out_map(&tc, splits > 1 ? partial : C, splits, M, N, splits > 1 ? N : ldc))
+    return HS_OK;
   const int64_t ntot = mt * nt * splits;
   if (ntot >= (1ll << 30)) return HS_OK;
   const unsigned grid = 2u * (unsigned)std::min<int64_t>(ntot, npairs);
   TcArgs args;
+  args.out_bf16 = c_bf16 ? 1 : 0;
   args.C = C;
   args.bias = bias;
   args.partial = partial;
@@ -1702,6 +1800,20 @@ int gemm_h3_pair(const __half *ah, const __half *al, int64_t a_rows, int64_t a_l
   }
   *done = true;
   return HS_OK;
+}
+
+// The pair kernel on the fp16 split operands.
+int gemm_h3_pair(const __half *ah, const __half *al, int64_t a_rows, int64_t a_ld, bool a_mn, const __half *bh,
+                 const __half *bl, int64_t b_rows, int64_t b_ld, bool b_mn, const unsigned *a_absmax,
+                 const unsigned *b_absmax, float *C, const float *bias, int64_t M, int64_t N, int64_t K, int64_t ldc,
+                 int beta, void *ws, size_t ws_bytes, int *status, cudaStream_t st, bool *done) {
+  *done = false;
+  CUtensorMap tah, tal, tbh, tbl;
+  if (!make_map_f16_pair(&tah, ah, a_rows, a_ld, a_mn) || !make_map_f16_pair(&tal, al, a_rows, a_ld, a_mn) ||
+      !make_map_f16_pair(&tbh, bh, b_rows, b_ld, b_mn) || !make_map_f16_pair(&tbl, bl, b_rows, b_ld, b_mn))
+    return HS_OK;
+  return pair_run(false, tah, tal, tbh, tbl, a_mn, b_mn, a_absmax, b_absmax, C, bias, M, N, K, ldc, beta, ws,
+                  ws_bytes, status, st, done);
 }
 
 // C[M,N] = A.B^T over K (+bias, beta) from split operands.  A is stored
@@ -1777,6 +1889,39 @@ int gemm_h3_presplit(const void *a_split, const unsigned *a_absmax, bool a_mn, c
   }
   *done = true;
   return HS_OK;
+}
+
+// C[M,N] = A.B^T over K (+bias, beta) from bf16 operands, one bf16 MMA per
+// k-step on SM pairs.  A is stored [M][a_ld] (a_mn false, K-major) or
+// [K][a_ld] (a_mn true, M-major); B likewise with N.  Leading dimensions
+// must be multiples of 8 elements (16-byte TMA strides) and the operands
+// 16-byte aligned; *done = false if the shape, the alignment or the scratch
+// (split-K partials) does not suit.
+// c_bf16: C is bf16 [M][ldc] (ldc, N multiples of 8; beta 0), else float32.
+int gemm_bf16(const void *a, int64_t a_ld, bool a_mn, const void *b, int64_t b_ld, bool b_mn, void *C,
+              const float *bias, int64_t M, int64_t N, int64_t K, int64_t ldc, int beta, void *ws, size_t ws_bytes,
+              int *status, cudaStream_t st, bool *done, bool c_bf16) {
+  *done = false;
+  if (!tc_enabled() || !status || M <= 0 || N <= 0 || K <= 0) return HS_OK;
+  if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) return HS_OK;
+  if (!aligned(C, 16) || ldc % 4 || N % 4 || !aligned(a, 16) || !aligned(b, 16) || a_ld % 8 || b_ld % 8) return HS_OK;
+  if (c_bf16 && (ldc % 8 || N % 8 || beta)) return HS_OK;
+  if (a_ld < (a_mn ? M : K) || b_ld < (b_mn ? N : K)) return HS_OK;
+  CUtensorMap ta, tb;
+  if (!make_map_f16_pair(&ta, a, a_mn ? K : M, a_ld, a_mn, true) ||
+      !make_map_f16_pair(&tb, b, b_mn ? K : N, b_ld, b_mn, true))
+    return HS_OK;
+  return pair_run(true, ta, ta, tb, tb, a_mn, b_mn, nullptr, nullptr, C, bias, M, N, K, ldc, beta, ws, ws_bytes,
+                  status, st, done, c_bf16);
+}
+
+// Split-K partial scratch the bf16 pair GEMM may use for an M x N product over K.
+size_t gemm_bf16_partial_bound(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const int nkb = (int)((round8(K) + P_BK - 1) / P_BK);
+  const int64_t ptiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
+  if (ptiles >= 128 || nkb < 16) return 0;
+  return (size_t)std::min(kPairMaxSplits, std::max(1, nkb / 8)) * M * N * 4;
 }
 
 namespace {

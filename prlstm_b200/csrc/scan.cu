@@ -38,6 +38,7 @@
 // column kernels of scan_chain.cu run instead (see scan_chain_wanted): they
 // pass the carry between the warps of a CTA through shared memory and need
 // no look-back scratch.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <mutex>
@@ -752,6 +753,55 @@ int scan_backward_split(float *z, const float *c, const float *c0, const float *
   return HS_OK;
 }
 
+// ------------------------------------------------------------------ bf16 storage
+// A bf16 module's scans: Z, c, out and dout stored in bf16 (half the bytes of
+// the saved activations), dZ written in bf16 for the bf16 gradient GEMMs;
+// the arithmetic and the carried state stay float32.  Per-column kernels
+// only (every 8-unit bf16 copy inside one column): shapes they do not take
+// are refused, and the caller widens to float32 instead.
+int scan_fwd_chain_launch_bf16(const void *z, const float *c0, void *out, void *c, float *h_n, float *c_n, int64_t T,
+                               int64_t B, int64_t H, float eps, int *status, cudaStream_t st);
+int scan_bwd_chain_launch_bf16(const void *z, const void *c, const float *c0, const void *dout, const float *dh_n,
+                               const float *dc_n, void *dz, float *dc0, float *db_part, int64_t T, int64_t B,
+                               int64_t H, float eps, int *status, cudaStream_t st);
+
+bool scan_bf16_ok(int64_t T, int64_t B, int64_t H) {
+  return T > 0 && B > 0 && H > 0 && H % 8 == 0 && scan_chain_wanted(T, B, H);
+}
+size_t scan_bf16_ws_bytes(int64_t B, int64_t H) { return round_up((size_t)B * 4 * H * 4, 256); }
+
+int scan_forward_bf16(const void *z, const float *c0, void *out, void *c, float *h_n, float *c_n, int64_t T, int64_t B,
+                      int64_t H, float eps, int *status, cudaStream_t st) {
+  if (int e = check_scan_args(T, B, H)) return e;
+  if (!z || !out || !c || !status) return fail(HS_ERR_INVALID_ARG, "scan_forward_bf16: null z/out/c/status");
+  if (!scan_bf16_ok(T, B, H))
+    return fail(HS_ERR_UNSUPPORTED, "bf16 scan: needs H %% 8 == 0 and a shape the per-column kernels take");
+  return scan_fwd_chain_launch_bf16(z, c0, out, c, h_n, c_n, T, B, H, eps, status, st);
+}
+
+int scan_backward_bf16(const void *z, const void *c, const float *c0, const void *dout, const float *dh_n,
+                       const float *dc_n, void *dz, float *dc0, float *db, int64_t T, int64_t B, int64_t H, float eps,
+                       void *ws, size_t ws_bytes, int *status, cudaStream_t st) {
+  if (int e = check_scan_args(T, B, H)) return e;
+  if (!z || !c || !dout || !dz || !status) return fail(HS_ERR_INVALID_ARG, "scan_backward_bf16: null z/c/dout/dz/status");
+  if (!scan_bf16_ok(T, B, H))
+    return fail(HS_ERR_UNSUPPORTED, "bf16 scan: needs H %% 8 == 0 and a shape the per-column kernels take");
+  const int64_t N = 4 * H;
+  float *part = nullptr;
+  if (db) {
+    if (!ws || !aligned(ws, 256) || ws_bytes < scan_bf16_ws_bytes(B, H))
+      return fail(HS_ERR_WORKSPACE, "scan_backward_bf16: workspace %zu < %zu bytes", ws_bytes, scan_bf16_ws_bytes(B, H));
+    part = static_cast<float *>(ws);
+  }
+  if (int e = scan_bwd_chain_launch_bf16(z, c, c0, dout, dh_n, dc_n, dz, dc0, part, T, B, H, eps, status, st))
+    return e;
+  if (db) {
+    rowsum_kernel<<<(unsigned)((N + 31) / 32), 256, 0, st>>>(part, db, B, N, 0);
+    return check_launch("rowsum_kernel");
+  }
+  return HS_OK;
+}
+
 // ------------------------------------------------------------------ no-allocation variant
 // Some callers cannot allocate device memory at all: a host framework that
 // hands this library only its input and output buffers (no device allocator
@@ -882,6 +932,26 @@ int hs_scan_backward_absmax(const float *z, const float *c, const float *c0, con
     return hs::check_launch("hs_scan_backward_absmax memset");
   return hs::scan_backward(z, c, c0, dout, dh_n, dc_n, dz, dc0, db, T, B, H, eps, workspace, workspace_bytes,
                            dev_status, (cudaStream_t)stream, dz_absmax);
+}
+
+int hs_scan_forward_bf16(const void *z, const float *c0, void *out, void *c, float *h_n, float *c_n, int64_t T,
+                         int64_t B, int64_t H, float eps, int *dev_status, hs_stream_t stream) {
+  return hs::scan_forward_bf16(z, c0, out, c, h_n, c_n, T, B, H, eps, dev_status, (cudaStream_t)stream);
+}
+
+size_t hs_scan_bf16_workspace_bytes(int64_t T, int64_t B, int64_t H) {
+  return (T > 0 && B > 0 && H > 0) ? hs::scan_bf16_ws_bytes(B, H) : 0;
+}
+
+int hs_scan_backward_bf16(const void *z, const void *c, const float *c0, const void *dout, const float *dh_n,
+                          const float *dc_n, void *dz, float *dc0, float *db, int64_t T, int64_t B, int64_t H,
+                          float eps, void *workspace, size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
+  return hs::scan_backward_bf16(z, c, c0, dout, dh_n, dc_n, dz, dc0, db, T, B, H, eps, workspace, workspace_bytes,
+                                dev_status, (cudaStream_t)stream);
+}
+
+int hs_scan_uses_column_kernels(int64_t T, int64_t B, int64_t H) {
+  return (T > 0 && B > 0 && H > 0 && hs::scan_chain_wanted(T, B, H)) ? 1 : 0;
 }
 
 size_t hs_scan_split_workspace_bytes(int64_t T, int64_t B, int64_t H) {

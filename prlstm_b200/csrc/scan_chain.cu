@@ -21,6 +21,7 @@
 // floats are 128-byte aligned segments: every warp access is one full line.
 // Per (t,b,h) element the forward moves its 24 algorithmic bytes and the
 // backward its 40, plus one c row per backward chunk (c_{t0-1}).
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <type_traits>
@@ -66,7 +67,7 @@ static_assert(kBNW * 2 * kBBuf >= kBNW * 4 * 32, "db reduction area");
 // 16- and 4-byte copies global -> shared; .cg bypasses L1, so in-flight lines
 // do not compete with the shared-memory carve-out.
 // Destinations are shared-window addresses (see sa()).
-HS_DEV void cp16(unsigned dst, const float *src) {
+HS_DEV void cp16(unsigned dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 HS_DEV void cp4(unsigned dst, const float *src) {
@@ -75,6 +76,18 @@ HS_DEV void cp4(unsigned dst, const float *src) {
 HS_DEV unsigned sa(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
 HS_DEV void commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N> HS_DEV void wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Storage of Z, c, out and dout: float32, or bf16 (a bf16 module's path,
+// whose saved activations are half the bytes).  Staged rows keep the float32
+// layout's element positions (32 units per gate row), at 2 bytes each.
+template <typename TS> HS_DEV float lds(const float *buf, int i) {
+  if constexpr (std::is_same<TS, float>::value) return buf[i];
+  else return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(buf)[i]);
+}
+template <typename TS> HS_DEV void st_cs(TS *p, float v) {
+  if constexpr (std::is_same<TS, float>::value) __stcs(p, v);
+  else __stcs(reinterpret_cast<unsigned short *>(p), __bfloat16_as_ushort(__float2bfloat16_rn(v)));
+}
 
 // Carry slots: one 64-bit shared word per (consumer warp, lane), holding
 // (chunk index << 32) | float bits.  The consumer of chunk c (c >= 1) waits for
@@ -114,11 +127,15 @@ HS_DEV bool slot_wait(const unsigned long long *s, unsigned tag, float *v, int *
 }
 
 // ------------------------------------------------------------------ forward
-template <bool V16>
+// TS = __nv_bfloat16: z, out and c in bf16 (needs V16: H % 8 == 0, 16-byte
+// aligned), c0, h_n, c_n float32.
+template <bool V16, typename TS = float>
 __global__ void __launch_bounds__(kFNW * 32, V16 ? kMinCtas : kMinCtas - 2)
-scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, float *__restrict__ out,
-                    float *__restrict__ cbuf, float *__restrict__ h_n, float *__restrict__ c_n, int64_t T,
+scan_fwd_col_kernel(const TS *__restrict__ z, const float *__restrict__ c0, TS *__restrict__ out,
+                    TS *__restrict__ cbuf, float *__restrict__ h_n, float *__restrict__ c_n, int64_t T,
                     int64_t B, int64_t H, float eps, unsigned *kf_max, int *status) {
+  constexpr bool BF = !std::is_same<TS, float>::value;
+  static_assert(!BF || V16, "bf16 storage takes the 16-byte copies");
   extern __shared__ float4 smem_f4[];
   float *sm = reinterpret_cast<float *>(smem_f4);
   unsigned long long *slots = reinterpret_cast<unsigned long long *>(sm + kFNW * 2 * kFBuf);  // [NW][32]
@@ -130,7 +147,7 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
   const bool hv = h < H;
   const int64_t nchunk = (T + kFL - 1) / kFL;
   const int64_t zstep = B * 4 * H, ostep = B * H;
-  const float *zb = z + b * 4 * H;
+  const TS *zb = z + b * 4 * H;
   float *buf0 = sm + warp * 2 * kFBuf;
   slots[warp * 32 + lane] = 0ull;
   __syncthreads();
@@ -140,7 +157,16 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
   auto stage = [&](int64_t c, float *dst) {
     const int64_t t0 = c * kFL;
     const int n = (int)min((int64_t)kFL, T - t0);
-    if (V16) {
+    if constexpr (BF) {
+      // a step row is 4 gates x 32 units x 2 bytes = 16 copies of 8 units:
+      // lanes 0-15 take the chunk's even steps, 16-31 the odd ones
+      const int g = (lane & 15) >> 2, k = (lane & 3) * 8, s0 = lane >> 4;
+      if (h0 + k < H) {
+        const TS *src = zb + (t0 + s0) * zstep + g * H + h0 + k;
+        unsigned d = sa(dst) + (unsigned)((s0 * kFRow + g * 32 + k) * 2);
+        for (int s = s0; s < n; s += 2, src += 2 * zstep, d += 2 * kFRow * 2) cp16(d, src);
+      }
+    } else if (V16) {
       const int g = lane >> 3, k = (lane & 7) * 4;
       if (h0 + k < H) {
         const float *src = zb + t0 * zstep + g * H + h0 + k;
@@ -180,10 +206,10 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
 #pragma unroll
       for (int s = 0; s < kFL; ++s) {
         if (decltype(full_tag)::value || (s < n && hv)) {
-          const float *r = buf + s * kFRow + lane;
-          fp[s] = fmaxf(sigf(r[32]), eps);
-          bp[s] = fmaxf(sig2(r[0], r[64]), eps);
-          eo[s] = __expf(-r[96]);
+          const int r = s * kFRow + lane;
+          fp[s] = fmaxf(sigf(lds<TS>(buf, r + 32)), eps);
+          bp[s] = fmaxf(sig2(lds<TS>(buf, r), lds<TS>(buf, r + 64)), eps);
+          eo[s] = __expf(-lds<TS>(buf, r + 96));
           C = fmaf(fp[s], C, bp[s]);
           A *= fp[s];
         } else {
@@ -204,8 +230,8 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
     if (c + 1 < nchunk) slot_put(&slots[((warp + 1) % kFNW) * 32 + lane], (unsigned)(c + 1), fmaf(A, cin, C));
     if (hv) {
       float cc = cin, o = 0.f;
-      float *ob = out + (t0 * B + b) * H + h;
-      float *cb = cbuf + (t0 * B + b) * H + h;
+      TS *ob = out + (t0 * B + b) * H + h;
+      TS *cb = cbuf + (t0 * B + b) * H + h;
       auto emit = [&](auto full_tag) {
 #pragma unroll
         for (int s = 0; s < kFL; ++s) {
@@ -213,8 +239,8 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
             kmax = fmaxf(kmax, cc * fp[s] * (1.f - fp[s]));
             cc = fmaf(fp[s], cc, bp[s]);
             o = sig_tanh_pos(eo[s], cc);
-            __stcs(cb + s * ostep, cc);
-            __stcs(ob + s * ostep, o);
+            st_cs(cb + s * ostep, cc);
+            st_cs(ob + s * ostep, o);
           }
         }
       };
@@ -240,17 +266,24 @@ scan_fwd_col_kernel(const float *__restrict__ z, const float *__restrict__ c0, f
 // after in time.  Bias sums are kept per lane over all of a warp's chunks and
 // added over the CTA's warps in a fixed order at the end: one partial row per
 // sequence.
-// SPLIT: dZ is written as its 3 x fp16 split (hi, lo [T*B][4H] fp16, scaled
-// by pow2_scale(*dz_bound), *dz_bound being an upper bound of max |dZ|)
-// instead of float32 into dz.  gate (may be null): the kernel does nothing
-// unless *gate != 0 (a conditional re-run).
-template <bool V16, bool SPLIT>
+// OUT selects how dZ is written: kDzF32 float32 into dz; kDzSplit its
+// 3 x fp16 split (hi, lo [T*B][4H] fp16, scaled by pow2_scale(*dz_bound),
+// *dz_bound being an upper bound of max |dZ|); kDzBf16 bf16 into dzb (the
+// bf16 gradient GEMMs' operand: bf16 keeps float32's exponent range, so no
+// scale).  gate (may be null): the kernel does nothing unless *gate != 0 (a
+// conditional re-run).
+// TS = __nv_bfloat16: z, c and dout in bf16 (needs V16 and OUT = kDzBf16).
+constexpr int kDzF32 = 0, kDzSplit = 1, kDzBf16 = 2;
+template <bool V16, int OUT, typename TS = float>
 __global__ void __launch_bounds__(kBNW * 32, V16 ? kMinCtas : kMinCtas - 2)
-scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float *__restrict__ c0,
-                    const float *__restrict__ dout, const float *__restrict__ dh_n, const float *__restrict__ dc_n,
+scan_bwd_col_kernel(const TS *z, const TS *__restrict__ cbuf, const float *__restrict__ c0,
+                    const TS *__restrict__ dout, const float *__restrict__ dh_n, const float *__restrict__ dc_n,
                     float *dz, float *__restrict__ dc0, float *__restrict__ db_part, int64_t T, int64_t B,
                     int64_t H, float eps, unsigned *dz_absmax, __half *__restrict__ dzh, __half *__restrict__ dzl,
-                    const unsigned *__restrict__ dz_bound, const int *gate, int *status) {
+                    const unsigned *__restrict__ dz_bound, __nv_bfloat16 *__restrict__ dzb, const int *gate,
+                    int *status) {
+  constexpr bool BF = !std::is_same<TS, float>::value;
+  static_assert(!BF || (V16 && OUT == kDzBf16), "bf16 storage: 16-byte copies, bf16 dZ");
   if (gate && *gate == 0) return;
   extern __shared__ float4 smem_f4[];
   float *sm = reinterpret_cast<float *>(smem_f4);
@@ -271,7 +304,23 @@ scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float 
   auto stage = [&](int64_t q, float *dst) {
     const int64_t t0 = (nchunk - 1 - q) * kBL;
     const int n = (int)min((int64_t)kBL, T - t0);
-    if (V16) {
+    if constexpr (BF) {
+      // a step row is 6 rows (z_i, z_f, z_g, z_o, c, dout) x 32 units x 2
+      // bytes = 24 copies of 8 units, one per lane 0-23; lanes 24-27 copy
+      // the c_{t0-1} row
+      const int rr = lane >> 2, k = (lane & 3) * 8;
+      if (h0 + k < H) {
+        if (rr < 6) {
+          const TS *src = rr < 4 ? z + (t0 * B + b) * 4 * H + rr * H + h0 + k
+                                 : (rr == 4 ? cbuf : dout) + (t0 * B + b) * H + h0 + k;
+          const int64_t step = rr < 4 ? zstep : sstep;
+          unsigned d = sa(dst) + (unsigned)((rr * 32 + k) * 2);
+          for (int s = 0; s < n; ++s, src += step, d += kBRow * 2) cp16(d, src);
+        } else if (rr == 6 && t0 > 0) {
+          cp16(sa(dst) + (unsigned)((kBL * kBRow + k) * 2), cbuf + ((t0 - 1) * B + b) * H + h0 + k);
+        }
+      }
+    } else if (V16) {
       const int g = lane >> 3, k = (lane & 7) * 4;
       if (h0 + k < H) {
         const float *zsrc = z + (t0 * B + b) * 4 * H + g * H + h0 + k;
@@ -301,14 +350,16 @@ scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float 
 
   float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
   float amax = 0.f;  // max |dz| of this lane (NaN ignored), if dz_absmax is wanted
-  const float sc = SPLIT ? pow2_scale(*dz_bound) : 1.f;
+  const float sc = OUT == kDzSplit ? pow2_scale(*dz_bound) : 1.f;
   // One dZ element at offset i of the [T*B][4H] layout.
   auto put = [&](int64_t i, float v) {
-    if (SPLIT) {
+    if (OUT == kDzSplit) {
       const float y = v * sc;
       const __half hv = __float2half_rn(y);
       __stcs(dzh + i, hv);
       __stcs(dzl + i, __float2half_rn(y - __half2float(hv)));
+    } else if (OUT == kDzBf16) {
+      __stcs(reinterpret_cast<unsigned short *>(dzb) + i, __bfloat16_as_ushort(__float2bfloat16_rn(v)));
     } else {
       __stcs(dz + i, v);
     }
@@ -324,9 +375,9 @@ scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float 
     __syncwarp();
     const int64_t t0 = (nchunk - 1 - q) * kBL;
     const int n = (int)min((int64_t)kBL, T - t0);
-    // dh_n joins dout of the last step (in the staged copy); dc_n is the
-    // initial carry of the reverse scan (below).
-    if (q == 0 && dh_n && hv) buf[(n - 1) * kBRow + 160 + lane] += dh_n[b * H + h];
+    // dh_n joins dout of the sequence's last step; dc_n is the initial
+    // carry of the reverse scan (below).
+    const float dhn = (q == 0 && dh_n && hv) ? dh_n[b * H + h] : 0.f;
     // Pass 1 (reverse time): per-step coefficients, the o-gate gradient
     // (final already) and the chunk's map of e.
     float FP[kBL], DCD[kBL], KI[kBL], KF[kBL], KG[kBL];
@@ -339,11 +390,12 @@ scan_bwd_col_kernel(const float *z, const float *__restrict__ cbuf, const float 
       FP[s] = 1.f;
       DCD[s] = KI[s] = KF[s] = KG[s] = 0.f;
       if (s < n && hv) {
-        const float *r = buf + s * kBRow + lane;
-        const float d = r[160];
-        const float cp = s > 0 ? r[128 - kBRow] : (t0 > 0 ? buf[kBL * kBRow + lane] : c0p);
-        const float ig = sig_fast(r[0]), f = sigf(r[32]), g = sig_fast(r[64]), o = sig_fast(r[96]);
-        const float th = tanh_pos(r[128]);
+        const int r = s * kBRow + lane;
+        const float d = lds<TS>(buf, r + 160) + (s == n - 1 ? dhn : 0.f);
+        const float cp = s > 0 ? lds<TS>(buf, r + 128 - kBRow) : (t0 > 0 ? lds<TS>(buf, kBL * kBRow + lane) : c0p);
+        const float ig = sig_fast(lds<TS>(buf, r)), f = sigf(lds<TS>(buf, r + 32)), g = sig_fast(lds<TS>(buf, r + 64)),
+                    o = sig_fast(lds<TS>(buf, r + 96));
+        const float th = tanh_pos(lds<TS>(buf, r + 128));
         const float mb = (ig * g >= eps) ? 1.f : 0.f;
         const float mf = (f >= eps) ? 1.f : 0.f;
         const float dcd = d * o * (1.f - th * th);
@@ -433,7 +485,7 @@ int sm_count() {
   return n;
 }
 
-std::atomic<unsigned long long> g_fwd_attr[2], g_bwd_attr[3];
+std::atomic<unsigned long long> g_fwd_attr[3], g_bwd_attr[5];
 
 }  // namespace
 
@@ -466,6 +518,7 @@ int scan_fwd_chain_launch(const float *z, const float *c0, float *out, float *c,
   return check_launch("scan_fwd_col_kernel");
 }
 
+// dZ goes to dz (float32), or to its fp16 split (dzh, dzl, dz_bound).
 int scan_bwd_chain_launch(const float *z, const float *c, const float *c0, const float *dout, const float *dh_n,
                           const float *dc_n, float *dz, float *dc0, float *db_part, int64_t T, int64_t B, int64_t H,
                           float eps, unsigned *dz_absmax, int *status, cudaStream_t st, __half *dzh, __half *dzl,
@@ -476,22 +529,65 @@ int scan_bwd_chain_launch(const float *z, const float *c, const float *c0, const
   const bool v16 = H % 4 == 0 && aligned(z, 16) && aligned(c, 16) && aligned(dout, 16);
   const bool split = dzh != nullptr;
   if (split && (!v16 || !dzl || !dz_bound)) return fail(HS_ERR_INVALID_ARG, "scan split: needs H % 4 == 0, aligned inputs");
-  const void *fn = split ? (const void *)scan_bwd_col_kernel<true, true>
-                         : v16 ? (const void *)scan_bwd_col_kernel<true, false>
-                               : (const void *)scan_bwd_col_kernel<false, false>;
+  const void *fn = split ? (const void *)scan_bwd_col_kernel<true, kDzSplit>
+                         : v16 ? (const void *)scan_bwd_col_kernel<true, kDzF32>
+                               : (const void *)scan_bwd_col_kernel<false, kDzF32>;
   if (int e = allow_dynamic_smem(fn, kBSmem, &g_bwd_attr[split ? 2 : (int)v16])) return e;
   if (split)
-    scan_bwd_col_kernel<true, true><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(
-        z, c, c0, dout, dh_n, dc_n, dz, dc0, db_part, T, B, H, eps, dz_absmax, dzh, dzl, dz_bound, gate, status);
+    scan_bwd_col_kernel<true, kDzSplit><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(
+        z, c, c0, dout, dh_n, dc_n, dz, dc0, db_part, T, B, H, eps, dz_absmax, dzh, dzl, dz_bound, nullptr, gate,
+        status);
   else if (v16)
-    scan_bwd_col_kernel<true, false><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(
-        z, c, c0, dout, dh_n, dc_n, dz, dc0, db_part, T, B, H, eps, dz_absmax, nullptr, nullptr, nullptr, gate,
-        status);
+    scan_bwd_col_kernel<true, kDzF32><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(
+        z, c, c0, dout, dh_n, dc_n, dz, dc0, db_part, T, B, H, eps, dz_absmax, nullptr, nullptr, nullptr, nullptr,
+        gate, status);
   else
-    scan_bwd_col_kernel<false, false><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(
-        z, c, c0, dout, dh_n, dc_n, dz, dc0, db_part, T, B, H, eps, dz_absmax, nullptr, nullptr, nullptr, gate,
-        status);
+    scan_bwd_col_kernel<false, kDzF32><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(
+        z, c, c0, dout, dh_n, dc_n, dz, dc0, db_part, T, B, H, eps, dz_absmax, nullptr, nullptr, nullptr, nullptr,
+        gate, status);
   return check_launch("scan_bwd_col_kernel");
+}
+
+// bf16 storage (a bf16 module's path): z, out, c (forward) and z, c, dout
+// (backward) in bf16, dZ written as bf16.  Needs H % 8 == 0 and 16-byte
+// aligned tensors (every 8-unit copy then lies inside one column).
+bool scan_chain_bf16_ok(int64_t H, std::initializer_list<const void *> ptrs) {
+  if (H % 8) return false;
+  for (const void *p : ptrs)
+    if (!aligned(p, 16)) return false;
+  return true;
+}
+
+int scan_fwd_chain_launch_bf16(const void *z, const float *c0, void *out, void *c, float *h_n, float *c_n, int64_t T,
+                               int64_t B, int64_t H, float eps, int *status, cudaStream_t st) {
+  const int64_t grid = B * ((H + 31) / 32);
+  if (grid >= (1ll << 31)) return fail(HS_ERR_UNSUPPORTED, "scan: too many columns");
+  if ((T + kFL - 1) / kFL >= (1ll << 32)) return fail(HS_ERR_UNSUPPORTED, "scan: T too large");
+  if (!scan_chain_bf16_ok(H, {z, out, c})) return fail(HS_ERR_UNSUPPORTED, "bf16 scan: needs H % 8 == 0, 16-byte aligned z/out/c");
+  using K = __nv_bfloat16;
+  const void *fn = (const void *)scan_fwd_col_kernel<true, K>;
+  if (int e = allow_dynamic_smem(fn, kFSmem, &g_fwd_attr[2])) return e;
+  scan_fwd_col_kernel<true, K><<<(unsigned)grid, kFNW * 32, kFSmem, st>>>(
+      static_cast<const K *>(z), c0, static_cast<K *>(out), static_cast<K *>(c), h_n, c_n, T, B, H, eps, nullptr,
+      status);
+  return check_launch("scan_fwd_col_kernel<bf16>");
+}
+
+int scan_bwd_chain_launch_bf16(const void *z, const void *c, const float *c0, const void *dout, const float *dh_n,
+                               const float *dc_n, void *dz, float *dc0, float *db_part, int64_t T, int64_t B,
+                               int64_t H, float eps, int *status, cudaStream_t st) {
+  const int64_t grid = B * ((H + 31) / 32);
+  if (grid >= (1ll << 31)) return fail(HS_ERR_UNSUPPORTED, "scan: too many columns");
+  if ((T + kBL - 1) / kBL >= (1ll << 32)) return fail(HS_ERR_UNSUPPORTED, "scan: T too large");
+  if (!scan_chain_bf16_ok(H, {z, c, dout, dz}))
+    return fail(HS_ERR_UNSUPPORTED, "bf16 scan: needs H % 8 == 0, 16-byte aligned z/c/dout/dz");
+  using K = __nv_bfloat16;
+  const void *fn = (const void *)scan_bwd_col_kernel<true, kDzBf16, K>;
+  if (int e = allow_dynamic_smem(fn, kBSmem, &g_bwd_attr[4])) return e;
+  scan_bwd_col_kernel<true, kDzBf16, K><<<(unsigned)grid, kBNW * 32, kBSmem, st>>>(
+      static_cast<const K *>(z), static_cast<const K *>(c), c0, static_cast<const K *>(dout), dh_n, dc_n, nullptr,
+      dc0, db_part, T, B, H, eps, nullptr, nullptr, nullptr, nullptr, static_cast<K *>(dz), nullptr, status);
+  return check_launch("scan_bwd_col_kernel<bf16>");
 }
 
 }  // namespace hs
