@@ -249,10 +249,15 @@ class ParallelStep:
             # re-run and split (2, return at once unless needed); backward
             # GEMMs: absmax + split of W_ih, 2 GEMMs, split-K reduce (x's
             # split is the projection's)
-            self.launches += 5 + 1 + 8 + 5
+            self.launches += self.LAUNCHES_PER_MB
             if record:
                 evs.append(e)
         return evs
+
+    LAUNCHES_PER_MB = 5 + 1 + 8 + 5
+
+    def per_step_launches(self):
+        return self.LAUNCHES_PER_MB * self.nmb
 
     def collect(self, evs):
         for e in evs:
@@ -265,6 +270,19 @@ class ParallelStep:
             return T * mb * H
         nprod = 2 if kernel == "linear_bwd" else 1  # dX and dW_ih
         return nprod * 2.0 * T * mb * 4 * H * D  # flops of the call
+
+
+def use_graph(args, cfg, B_local, world):
+    """Whether the parallel step is captured in a CUDA graph: on one GPU (no
+    collective inside the step), for steps of at most 2^16 tokens per rank,
+    whose kernels take a few tens of microseconds; --graph
+    on/off overrides.  Returns True or None."""
+    mode = getattr(args, "graph", "auto")
+    if world > 1 or mode == "off":
+        return None
+    if mode == "on" or cfg["T"] * B_local <= (1 << 16):
+        return True
+    return None
 
 
 def cublas_refs(cfg, mb, dev):
@@ -355,6 +373,26 @@ def run_ours(args, cfg, rank, world, dev):
         _lib.check_device_status(dev)
         step.ms = {n: 0.0 for n in step.names}
         step.launches = 0
+        graph = use_graph(args, cfg, B_local, world)
+        if graph is not None:
+            # Launch-bound step (kernels of a few tens of us): the whole step
+            # is captured once in a CUDA graph and replayed, so the timed
+            # region holds every kernel of every step without the per-call
+            # host work.  The per-kernel breakdown comes from an ungraphed
+            # pass after it (device times do not depend on how the kernels
+            # were launched).
+            graph = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                step.run(x, G)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            with torch.cuda.graph(graph):
+                step.run(x, G)
+            graph.replay()
+            sync()
+            _lib.check_device_status(dev)
+            step.launches = 0
         clocks = ClockSampler(_gpu_id(dev))
         clocks.start()
         sync()
@@ -363,12 +401,24 @@ def run_ours(args, cfg, rank, world, dev):
         t0.record()
         allev = []
         for _ in range(args.steps):
-            allev.extend(step.run(x, G, record=True))
+            if graph is not None:
+                graph.replay()
+                step.launches += step.per_step_launches()
+            else:
+                allev.extend(step.run(x, G, record=True))
             allreduce([step.dW, step.db])
         t1.record()
         sync()
         ck = clocks.stop()
         ms = t0.elapsed_time(t1)
+        if graph is not None:
+            launches = step.launches
+            for _ in range(args.steps):
+                allev.extend(step.run(x, G, record=True))
+            sync()
+            step.launches = launches
+            result["launch"] = "cuda_graph (one capture of the step, replayed every step)"
+            del graph
         step.collect(allev)
         _lib.check_device_status(dev)
         ms = max_over_ranks(ms)
@@ -600,6 +650,43 @@ def e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync, max_over_ra
         torch.cuda.current_stream(dev).synchronize()
         return float(loss_host.item())
 
+    graphed = None
+    if use_graph(args, cfg, B_local, world) is not None and nmb == 1:
+        # A launch-bound step through the module as a user graphs it: the
+        # forward and backward captured once (torch.cuda.graph), replayed
+        # every step on static input buffers that the step's host->device
+        # copies fill; the loss is read back after each replay.
+        sx = torch.empty(T, mb, D, device=dev)
+        sG = torch.empty(T, mb, H, device=dev)
+        sx.copy_(hx[0])
+        sG.copy_(hG[0])
+        xleaf = sx.detach().requires_grad_(True)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                m.zero_grad(set_to_none=True)
+                out, _ = m(xleaf)
+                (out * sG).sum().backward()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        m.zero_grad(set_to_none=True)
+        xleaf.grad = None
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out, _ = m(xleaf)
+            sloss = (out * sG).sum()
+            sloss.backward()
+
+        def graphed():
+            sx.copy_(hx[0], non_blocking=True)
+            sG.copy_(hG[0], non_blocking=True)
+            g.replay()
+            loss_host.copy_(sloss.detach().reshape(1), non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+            return float(loss_host.item())
+
+        one_step = graphed
+
     for _ in range(max(1, min(args.warmup, 2))):
         one_step()
     sync()
@@ -614,8 +701,11 @@ def e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync, max_over_ra
     sync()
     ms = max_over_ranks(e0.elapsed_time(e1))
     h2d = sum(t.numel() * 4 for t in hx) + sum(t.numel() * 4 for t in hG)
-    return {"value": T * cfg["B"] * steps / (ms / 1e3), "unit": "tokens/s",
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "steps": steps}
+    res = {"value": T * cfg["B"] * steps / (ms / 1e3), "unit": "tokens/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "steps": steps}
+    if graphed is not None:
+        res["launch"] = "module forward + backward captured in a CUDA graph (torch.cuda.graph), replayed per step"
+    return res
 
 
 def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_ranks, allreduce,
@@ -909,6 +999,8 @@ def main():
                     help="skip timing cuBLAS TF32/FP32 on the GEMM shapes (GEMM ceilings)")
     ap.add_argument("--seq-len", type=int, default=None,
                     help="override T (small cases for profiling)")
+    ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
+                    help="capture the parallel step in a CUDA graph (auto: launch-bound steps on one GPU)")
     ap.add_argument("--no-configs", action="store_true",
                     help="time only the headline config (not configs[0-3] after it)")
     args = ap.parse_args()
@@ -973,7 +1065,7 @@ def main():
                 config=_config_obj(args.config, cfg, world, workload),
                 roofline=res.get("roofline"), e2e=res.get("e2e"), clocks=res.get("clocks"),
                 gpu_launches=res.get("gpu_launches"))
-    for k in ("kernels", "scan_roofline", "scan_alone", "recurrent"):
+    for k in ("kernels", "scan_roofline", "scan_alone", "recurrent", "launch"):
         if k in res:
             line[k] = res[k]
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1000,6 +1092,8 @@ def main():
                    "roofline": r.get("roofline"), "gpu_launches": r.get("gpu_launches")}
             if "recurrent" in r:
                 ent["recurrent"] = r["recurrent"]
+            if "launch" in r:
+                ent["launch"] = r["launch"]
             if "scan_roofline" in r:
                 ent["scan_roofline"] = r["scan_roofline"]
             if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -144,7 +144,11 @@ def status_word(device: torch.device) -> torch.Tensor:
 
 def note_launch(device: torch.device):
     """Queue an asynchronous read-back of the status word; the value is
-    checked (without a sync) the next time the library is called."""
+    checked (without a sync) the next time the library is called.  Skipped
+    while the stream is being captured into a CUDA graph (an event query is
+    not allowed there): a graphed step reports through check_device_status."""
+    if torch.cuda.is_current_stream_capturing():
+        return
     idx = device.index if device.index is not None else torch.cuda.current_device()
     poll(device)
     host = torch.empty(1, dtype=torch.int32, pin_memory=True)
@@ -161,6 +165,8 @@ def _raise_status(code: int):
 
 
 def poll(device: torch.device):
+    if torch.cuda.is_current_stream_capturing():
+        return
     idx = device.index if device.index is not None else torch.cuda.current_device()
     item = _pending.get(idx)
     if item is None:
