@@ -409,6 +409,26 @@ HS_API int hs_recurrent_backward(const float *x, const float *w_ih, const float 
                           int64_t T, int64_t B, int64_t D, int64_t H,
                           void *workspace, size_t workspace_bytes, int *dev_status,
                           hs_stream_t stream);
+/* The same two calls for a bfloat16 module (inputs and parameters
+ * bf16-valued, passed widened to float32): where the per-step product runs
+ * on the tensor cores (hs_recurrent_uses_tensor_cores), a*W_hh and the state
+ * carried between steps (h forward, dgates backward) are rounded to bf16 and
+ * multiplied in one bf16 product per instruction with float32 accumulation,
+ * as the reference's bf16 module computes its per-step GEMM in bf16
+ * (_torch.py:111-120, :150; _triton.py:230, :299); elsewhere float32 on the
+ * bf16 values.  Same workspace size. */
+HS_API int hs_recurrent_forward_bf16(const float *x, const float *h0, const float *c0, const float *w_ih,
+                                     const float *w_hh, const float *b_ih, const float *b_hh, const float *a,
+                                     float *h_save, float *c_save, float *acts, int64_t T, int64_t B,
+                                     int64_t D, int64_t H, void *workspace, size_t workspace_bytes,
+                                     int *dev_status, hs_stream_t stream);
+HS_API int hs_recurrent_backward_bf16(const float *x, const float *w_ih, const float *w_hh,
+                                      const float *b_hh, const float *a, const float *h_save,
+                                      const float *c_save, float *acts, const float *dout,
+                                      const float *dh_n, const float *dc_n, float *dx, float *dw_ih,
+                                      float *dw_hh, float *db_ih, float *db_hh, float *da, int64_t T,
+                                      int64_t B, int64_t D, int64_t H, void *workspace,
+                                      size_t workspace_bytes, int *dev_status, hs_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -38,6 +38,8 @@ class RecurrentFn(torch.autograd.Function):
         T, B, D = x.shape
         H = W_hh.shape[1]
         dev = x.device
+        # a bf16 module: the step product in bf16 where it runs on the tensor cores
+        bf = x.dtype == torch.bfloat16 and W_hh.dtype == torch.bfloat16
         x, h0, c0 = _f32c(x), _f32c(h0), _f32c(c0)
         W_ih, W_hh, b_ih, b_hh, a = (_f32c(t) for t in (W_ih, W_hh, b_ih, b_hh, a))
         _lib.poll(dev)
@@ -50,11 +52,12 @@ class RecurrentFn(torch.autograd.Function):
             raise RuntimeError(f"recurrent path: unsupported shape T={T} B={B} D={D} H={H}")
         ws = _lib.workspace(nws, dev)
         P = _lib.ptr
-        _lib.call("hs_recurrent_forward", P(x), P(h0), P(c0), P(W_ih), P(W_hh), P(b_ih), P(b_hh),
-                  P(a), P(h_save), P(c_save), P(acts), T, B, D, H, P(ws), ws.numel(),
+        _lib.call("hs_recurrent_forward_bf16" if bf else "hs_recurrent_forward", P(x), P(h0), P(c0), P(W_ih),
+                  P(W_hh), P(b_ih), P(b_hh), P(a), P(h_save), P(c_save), P(acts), T, B, D, H, P(ws), ws.numel(),
                   P(_lib.status_word(dev)), _lib.stream_ptr(dev))
         ctx.save_for_backward(x, W_ih, W_hh, b_hh, a, h_save, c_save, acts)
         ctx.shape = (T, B, D, H)
+        ctx.bf = bf
         ctx.consumed = False
         return h_save[1:], h_save[T], c_save[T]
 
@@ -80,7 +83,8 @@ class RecurrentFn(torch.autograd.Function):
         lib = _lib.load()
         ws = _lib.workspace(lib.hs_recurrent_workspace_bytes(T, B, D, H), dev)
         P = _lib.ptr
-        _lib.call("hs_recurrent_backward", P(x), P(W_ih), P(W_hh), P(b_hh), P(a), P(h_save),
+        _lib.call("hs_recurrent_backward_bf16" if ctx.bf else "hs_recurrent_backward", P(x), P(W_ih), P(W_hh),
+                  P(b_hh), P(a), P(h_save),
                   P(c_save), P(acts), P(dout), P(dh_n), P(dc_n), P(dx), P(dW_ih), P(dW_hh),
                   P(db_ih), P(db_hh), P(da), T, B, D, H, P(ws), ws.numel(),
                   P(_lib.status_word(dev)), _lib.stream_ptr(dev))

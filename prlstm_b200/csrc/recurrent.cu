@@ -46,14 +46,14 @@ int linear_backward_ex(const float *dy, const float *w, float *dx, const float *
                        float *dw2, int64_t M, int64_t N, int64_t K, int64_t K2, int beta, void *ws, size_t ws_bytes,
                        int *status, cudaStream_t st, const unsigned *dy_absmax);
 int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st);
-bool rec_tc_wanted(int dir, int64_t B, int64_t H);
+bool rec_tc_wanted(int dir, int64_t B, int64_t H, bool bf = false);
 size_t rec_tc_ws_bytes(int64_t B, int64_t H);
 int rec_tc_forward(const float *h0, const float *c0, const float *w_hh, const float *b_hh, const float *a,
                    float *h_save, float *c_save, float *acts, int64_t T, int64_t B, int64_t H, void *ws,
-                   size_t ws_bytes, int *status, cudaStream_t st);
+                   size_t ws_bytes, int *status, cudaStream_t st, bool bf);
 int rec_tc_backward(const float *w_hh, const float *a, const float *c_save, float *acts, const float *dout,
                     const float *dh_n, const float *dc_n, int64_t T, int64_t B, int64_t H, void *ws, size_t ws_bytes,
-                    int *status, cudaStream_t st);
+                    int *status, cudaStream_t st, bool bf);
 
 namespace {
 
@@ -671,10 +671,13 @@ size_t rec_ws_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
                            linear_ws_bytes(T * B, 4 * H, H), linear_backward_ws(T * B, 4 * H, D, H)});
 }
 
+// bf: a bfloat16 module's step product (bf16 weights and state, one product
+// per instruction) where the step runs on the tensor cores; the FFMA kernels
+// compute in float32 on the same (bf16-valued) inputs either way.
 int rec_forward(const float *x, const float *h0, const float *c0, const float *w_ih,
                 const float *w_hh, const float *b_ih, const float *b_hh, const float *a,
                 float *h_save, float *c_save, float *acts, int64_t T, int64_t B, int64_t D,
-                int64_t H, void *ws, size_t ws_bytes, int *status, cudaStream_t st) {
+                int64_t H, void *ws, size_t ws_bytes, int *status, cudaStream_t st, bool bf = false) {
   if (int e = check_rec_args(T, B, D, H)) return e;
   if (!x || !w_ih || !w_hh || !b_ih || !b_hh || !a || !h_save || !c_save || !acts || !status)
     return fail(HS_ERR_INVALID_ARG, "recurrent_forward: null required pointer");
@@ -688,8 +691,8 @@ int rec_forward(const float *x, const float *h0, const float *c0, const float *w
   // Z = x W_ih^T + b_ih, written into acts (_torch.py:96)
   if (int e = linear_forward(x, w_ih, b_ih, acts, T * B, 4 * H, D, ws, ws_bytes, status, st)) return e;
   // the step product on the tensor cores where the shape allows
-  if (rec_tc_wanted(0, B, H))
-    return rec_tc_forward(h0, c0, w_hh, b_hh, a, h_save, c_save, acts, T, B, H, ws, ws_bytes, status, st);
+  if (rec_tc_wanted(0, B, H, bf))
+    return rec_tc_forward(h0, c0, w_hh, b_hh, a, h_save, c_save, acts, T, B, H, ws, ws_bytes, status, st, bf);
   if (pl.fwd.rows_pad > 256) return fail(HS_ERR_UNSUPPORTED, "recurrent: slice of %d rows", pl.fwd.rows_pad);
   rec_prep_fwd_kernel<<<dim3((unsigned)((pl.fwd.K_pad + 31) / 32), (unsigned)pl.ncta), 256, 0, st>>>(
       w_hh, b_hh, a, (float *)(w + pl.o_wf), (float *)(w + pl.o_bf), H, pl.U, pl.fwd.rows_pad, pl.fwd.K_pad);
@@ -729,7 +732,7 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
                  const float *dout, const float *dh_n, const float *dc_n, float *dx,
                  float *dw_ih, float *dw_hh, float *db_ih, float *db_hh, float *da, int64_t T,
                  int64_t B, int64_t D, int64_t H, void *ws, size_t ws_bytes, int *status,
-                 cudaStream_t st) {
+                 cudaStream_t st, bool bf = false) {
   if (int e = check_rec_args(T, B, D, H)) return e;
   if (!x || !w_ih || !w_hh || !b_hh || !a || !h_save || !c_save || !acts || !dout || !dw_ih ||
       !dw_hh || !db_ih || !db_hh || !da || !status)
@@ -740,9 +743,9 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
   if (!make_plan(pl, B, H, nsm)) return fail(HS_ERR_UNSUPPORTED, "recurrent: no tiling for B=%lld H=%lld on %d SMs", (long long)B, (long long)H, nsm);
   if (!ws || ws_bytes < pl.total) return fail(HS_ERR_WORKSPACE, "recurrent_backward: workspace %zu < %zu bytes", ws_bytes, pl.total);
   char *w = static_cast<char *>(ws);
-  if (rec_tc_wanted(1, B, H)) {
+  if (rec_tc_wanted(1, B, H, bf)) {
     // the step product on the tensor cores
-    if (int e = rec_tc_backward(w_hh, a, c_save, acts, dout, dh_n, dc_n, T, B, H, ws, ws_bytes, status, st))
+    if (int e = rec_tc_backward(w_hh, a, c_save, acts, dout, dh_n, dc_n, T, B, H, ws, ws_bytes, status, st, bf))
       return e;
   } else {
   // The scaled backward slices are built here so a backward never depends
@@ -827,6 +830,24 @@ int hs_recurrent_backward(const float *x, const float *w_ih, const float *w_hh,
   return hs::rec_backward(x, w_ih, w_hh, b_hh, a, h_save, c_save, acts, dout, dh_n, dc_n, dx,
                           dw_ih, dw_hh, db_ih, db_hh, da, T, B, D, H, workspace, workspace_bytes,
                           dev_status, (cudaStream_t)stream);
+}
+
+int hs_recurrent_forward_bf16(const float *x, const float *h0, const float *c0, const float *w_ih,
+                              const float *w_hh, const float *b_ih, const float *b_hh, const float *a,
+                              float *h_save, float *c_save, float *acts, int64_t T, int64_t B, int64_t D, int64_t H,
+                              void *workspace, size_t workspace_bytes, int *dev_status, hs_stream_t stream) {
+  return hs::rec_forward(x, h0, c0, w_ih, w_hh, b_ih, b_hh, a, h_save, c_save, acts, T, B, D, H, workspace,
+                         workspace_bytes, dev_status, (cudaStream_t)stream, true);
+}
+
+int hs_recurrent_backward_bf16(const float *x, const float *w_ih, const float *w_hh, const float *b_hh,
+                               const float *a, const float *h_save, const float *c_save, float *acts,
+                               const float *dout, const float *dh_n, const float *dc_n, float *dx, float *dw_ih,
+                               float *dw_hh, float *db_ih, float *db_hh, float *da, int64_t T, int64_t B, int64_t D,
+                               int64_t H, void *workspace, size_t workspace_bytes, int *dev_status,
+                               hs_stream_t stream) {
+  return hs::rec_backward(x, w_ih, w_hh, b_hh, a, h_save, c_save, acts, dout, dh_n, dc_n, dx, dw_ih, dw_hh, db_ih,
+                          db_hh, da, T, B, D, H, workspace, workspace_bytes, dev_status, (cudaStream_t)stream, true);
 }
 
 }  // extern "C"

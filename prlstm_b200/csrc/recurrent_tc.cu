@@ -51,7 +51,15 @@
 // Every wait on another CTA is bounded (kWaitLimitNs); a CTA that gives up
 // records HS_ERR_DEVICE_TIMEOUT in the caller's status word, waits (bounded)
 // for its own copies and MMAs in flight, frees its tensor memory and returns.
+// bf16 mode (a bfloat16 module): the weights a*W_hh rounded to bf16 and the
+// state (h forward, dgates backward) rounded to bf16 each step, one product
+// per instruction with bf16 operands and float32 accumulation: the weight
+// operand is the N = UB rows themselves (half the bytes, no lo part), the
+// state occupies rows 0-31 only (rows 32-63 of the exchange buffer stay zero),
+// no operand scales.  Blocks, clusters, the exchange and the cell are the
+// same as in the float32 mode.
 // No cluster multicast.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -273,11 +281,12 @@ __global__ void rtc_absmax_kernel(const float *__restrict__ w_hh, const float *_
 //            a[g] W_hh[g H + u'][UB ub + ul] for the gate row (g, u') at position
 //            k of the permuted order in which each producing CTA's 4 x UCP rows
 //            are contiguous: k = (P 4 + g) UCP + l, u' = (P / KS) UB + (P % KS) UCP + l.
+// bf != 0: the N = UB operand of the rows themselves in bf16, unscaled.
 __global__ void rtc_prep_kernel(const float *__restrict__ w_hh, const float *__restrict__ a,
                                 const unsigned *__restrict__ absmax, unsigned char *__restrict__ wg, int dir,
-                                int64_t H, int KS, int UCP, int UB, int64_t Ks, int NC) {
-  const float s = pow2_scale(*absmax);
-  const int NW = 2 * UB;
+                                int64_t H, int KS, int UCP, int UB, int64_t Ks, int NC, int bf) {
+  const float s = bf ? 1.0f : pow2_scale(*absmax);
+  const int NW = bf ? UB : 2 * UB;
   const int64_t nkc = Ks / 8;
   const int64_t total = (int64_t)NC * nkc * NW;
   const size_t tile = (size_t)Ks * NW * 2;
@@ -302,9 +311,13 @@ __global__ void rtc_prep_kernel(const float *__restrict__ w_hh, const float *__r
         const int64_t up = (P / KS) * UB + (P % KS) * UCP + l;
         w = a[g] * w_hh[(g * H + up) * H + (int64_t)blk * UB + r];
       }
-      __half hi, lh;
-      split_h2(w * s, hi, lh);
-      v[kk] = lo ? lh : hi;
+      if (bf) {
+        v[kk] = __ushort_as_half(__bfloat16_as_ushort(__float2bfloat16_rn(w)));
+      } else {
+        __half hi, lh;
+        split_h2(w * s, hi, lh);
+        v[kk] = lo ? lh : hi;
+      }
     }
     *reinterpret_cast<uint4 *>(wg + (size_t)cta * tile + koff(n, kc * 8, (uint32_t)NW * 16)) =
         *reinterpret_cast<const uint4 *>(v);
@@ -325,6 +338,7 @@ struct RtcArgs {
   const float *dout, *dh_n, *dc_n;
   const float *b_hh, *a;
   int64_t T, Bt, H;
+  int bf;                   // bf16 mode (see the top of the file)
   int64_t Ks;               // k per CTA (slice of the reduction axis)
   size_t xbytes;            // one exchange buffer: K / 8 core columns x 1 KB
   int b0;                   // first sequence of batch group 0 of this launch
@@ -383,7 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *sm = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int NC = p.NC, KS = p.KS, UCP = p.UCP, UB = p.UB, NW = 2 * p.UB;
+  const bool bf = p.bf != 0;
+  const int NC = p.NC, KS = p.KS, UCP = p.UCP, UB = p.UB, NW = bf ? p.UB : 2 * p.UB;
   const bool resident = p.resident != 0;
   const Layout L = make_layout(p.Ks, p.stages, resident, NW);
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + L.bars);
@@ -421,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
     for (int i = 0; i < 32; ++i) mbar_init(&bars[B_FULL + i], 1);
     for (int i = 0; i < 8; ++i) mbar_init(&bars[B_EMPTY + i], 1);
     for (int i = 0; i < 4; ++i) mbar_init(&bars[B_SFULL + i], 1);
-    for (int i = 0; i < 4; ++i) mbar_init(&bars[B_SFREE + i], 4);
+    for (int i = 0; i < 4; ++i) mbar_init(&bars[B_SFREE + i], bf ? 2 : 4);  // the draining warps
     mbar_init(&bars[B_W], 1);
     mbar_init(&bars[B_DONE], 1);
     mbar_init(&bars[B_PIN], 1);
@@ -507,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(128, NW);
+      const uint32_t idesc = idesc_f16(128, NW) | (bf ? ((1u << 7) | (1u << 10)) : 0u);  // bf16 A and B
       bool ok = true;
       if (resident && nsteps > 0) ok = mbar_wait(&bars[B_W], 0, p.status);
       int64_t chunks = 0, groups = 0;
@@ -556,9 +571,10 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 2, q = warp & 3, half = ew >> 2;
     const int e = ew * 32 + lane;  // 0..255
-    const bool drains = q < 2;     // TMEM lanes 0-31 (hi state rows) and 32-63 (lo state rows)
+    // TMEM lanes 0-31 (hi state rows) and 32-63 (lo state rows; none in bf16 mode)
+    const bool drains = bf ? q == 0 : q < 2;
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
-    const float inv_w = 1.0f / pow2_scale(*p.w_absmax);
+    const float inv_w = bf ? 1.0f : 1.0f / pow2_scale(*p.w_absmax);
     int64_t groups = 0;
     bool fail = false;
     int64_t pin_armed = 0, pin_seen = 0;  // phases of the partial-sums barrier
@@ -582,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
           tc_fence_after();
           if (drains && 64 * half < UB) {
             float sc = 1.0f;
-            if (DIR == 1) sc = __ldcg(&xscale[par * NC + (int)(sp * ngroups + gi)]) * inv_w;
+            if (DIR == 1 && !bf) sc = __ldcg(&xscale[par * NC + (int)(sp * ngroups + gi)]) * inv_w;
             const uint32_t base = tl + (uint32_t)(slot * NW) + (uint32_t)(64 * half);
             // four quarters of 16 weight rows, the loads of a quarter in
             // flight together (registers: the 64 sums + 32 loaded values)
@@ -590,9 +606,9 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
             for (int c = 0; c < 4; ++c) {
               uint32_t v[16], w[16];
               tmem_ld16_nowait(base + 16 * c, v);
-              if (q == 0) tmem_ld16_nowait(base + UB + 16 * c, w);
+              if (q == 0 && !bf) tmem_ld16_nowait(base + UB + 16 * c, w);
               tmem_wait_ld();
-              if (q == 0) {
+              if (q == 0 && !bf) {
 #pragma unroll
                 for (int i = 0; i < 16; ++i)
                   acc[16 * c + i] = fmaf(__uint_as_float(v[i]) + __uint_as_float(w[i]), sc, acc[16 * c + i]);
@@ -613,7 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
       // The partial sums of the weight rows r (forward: r = gate x 32 + unit;
       // backward: r = unit) for sequence b, pout[r][b]: the lo-state rows'
       // sums first, then the hi-state rows add theirs.
-      if (q == 1 && !fail && 64 * half < UB) {
+      if (q == (bf ? 0 : 1) && !fail && 64 * half < UB) {
 #pragma unroll
         for (int i = 0; i < 64; ++i) pout[(64 * half + i) * 32 + lane] = acc[i];
       }
@@ -621,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
       // every CTA of the cluster before those CTAs published the state this
       // step's MMAs consumed
       if (epi_sync_any(fail)) return false;
-      if (q == 0 && 64 * half < UB) {
+      if (q == 0 && !bf && 64 * half < UB) {
 #pragma unroll
         for (int i = 0; i < 64; ++i) pout[(64 * half + i) * 32 + lane] += acc[i];
       }
@@ -662,15 +678,19 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
         cst[m] = c;
         p.h_save[bb * H + u] = h;
         p.c_save[bb * H + u] = c;
-        __half hi, lo;
-        split_h2(h * 16384.0f, hi, lo);
-        *reinterpret_cast<__half *>(xg + koff(b, u, 1024)) = hi;
-        *reinterpret_cast<__half *>(xg + koff(32 + b, u, 1024)) = lo;
+        if (bf) {
+          *reinterpret_cast<__nv_bfloat16 *>(xg + koff(b, u, 1024)) = __float2bfloat16_rn(h);
+        } else {
+          __half hi, lo;
+          split_h2(h * 16384.0f, hi, lo);
+          *reinterpret_cast<__half *>(xg + koff(b, u, 1024)) = hi;
+          *reinterpret_cast<__half *>(xg + koff(32 + b, u, 1024)) = lo;
+        }
       }
       asm volatile("fence.proxy.async.global;" ::: "memory");
       epi_sync();
       if (e == 0) arrive_counter(bar);
-      const float inv = inv_w * (1.0f / 16384.0f);
+      const float inv = bf ? 1.0f : inv_w * (1.0f / 16384.0f);
       float bias[NCELL][4];  // a-scaled b_hh of the thread's cells (_torch.py:93)
       _Pragma("unroll") for (int m = 0; m < NCELL; ++m) {
         const int ul = (e + kEpi * m) >> 5;
@@ -707,10 +727,14 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
           hv[m] = act[m][3] * tanh_any(c);
           cst[m] = c;
           if (t + 1 < T) {
-            __half hi, lo;
-            split_h2(hv[m] * 16384.0f, hi, lo);
-            *reinterpret_cast<__half *>(xdst + koff(b, u, 1024)) = hi;
-            *reinterpret_cast<__half *>(xdst + koff(32 + b, u, 1024)) = lo;
+            if (bf) {
+              *reinterpret_cast<__nv_bfloat16 *>(xdst + koff(b, u, 1024)) = __float2bfloat16_rn(hv[m]);
+            } else {
+              __half hi, lo;
+              split_h2(hv[m] * 16384.0f, hi, lo);
+              *reinterpret_cast<__half *>(xdst + koff(b, u, 1024)) = hi;
+              *reinterpret_cast<__half *>(xdst + koff(32 + b, u, 1024)) = lo;
+            }
           }
         }
         // publish the exchange slice first; the step's outputs, which no
@@ -808,14 +832,18 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
           if (ul >= UCP || b >= Bc) continue;
 #pragma unroll
           for (int q2 = 0; q2 < 4; ++q2) {
-            __half hi, lo;
-            split_h2(dg[m][q2] * scl, hi, lo);
             const int64_t k = ((int64_t)cta * 4 + q2) * UCP + ul;  // producer-major gate-row order
-            *reinterpret_cast<__half *>(xdst + koff(b, k, 1024)) = hi;
-            *reinterpret_cast<__half *>(xdst + koff(32 + b, k, 1024)) = lo;
+            if (bf) {
+              *reinterpret_cast<__nv_bfloat16 *>(xdst + koff(b, k, 1024)) = __float2bfloat16_rn(dg[m][q2]);
+            } else {
+              __half hi, lo;
+              split_h2(dg[m][q2] * scl, hi, lo);
+              *reinterpret_cast<__half *>(xdst + koff(b, k, 1024)) = hi;
+              *reinterpret_cast<__half *>(xdst + koff(32 + b, k, 1024)) = lo;
+            }
           }
         }
-        if (e == 0) __stcg(&xscale[(t & 1) * NC + cta], 1.0f / scl);
+        if (e == 0 && !bf) __stcg(&xscale[(t & 1) * NC + cta], 1.0f / scl);
         asm volatile("fence.proxy.async.global;" ::: "memory");
         if (epi_sync_any(fail)) { fail = true; break; }
         if (e == 0) arrive_counter(bar);
@@ -838,7 +866,7 @@ __global__ void __launch_bounds__(kThreads, 1) rtc_kernel(RtcArgs p) {
 // ------------------------------------------------------------------ host
 struct RtcPlan {
   int dir, KS, UCP, UB, NBLK, NC, ngrp, nchunk, gch, stages;
-  bool resident;
+  bool resident, bf;
   int64_t K, Ks;
   size_t xbytes, smem;
   size_t o_bar, o_absmax, o_w, o_x, o_xs, total;
@@ -903,9 +931,10 @@ int max_clusters(int dir, int ks, int ub, size_t smem) {
   return n;
 }
 
-bool make_rtc_plan(RtcPlan &p, int dir, int64_t B, int64_t H, int nsm) {
+bool make_rtc_plan(RtcPlan &p, int dir, int64_t B, int64_t H, int nsm, bool bf = false) {
   p = RtcPlan{};
   p.dir = dir;
+  p.bf = bf;
   if (H <= 0 || B <= 0) return false;
   if (dir == 0 ? (H % 64 != 0) : (H % 64 != 0)) return false;
   p.K = dir == 0 ? H : 4 * H;
@@ -938,7 +967,7 @@ bool make_rtc_plan(RtcPlan &p, int dir, int64_t B, int64_t H, int nsm) {
       const int64_t gk = dir == 0 ? std::min<int64_t>(256, Ks) : 4 * c.UCP;
       if (gk % KCH) continue;
       c.gch = (int)(gk / KCH);
-      const int NW = 2 * ub;
+      const int NW = bf ? ub : 2 * ub;
       const Layout Lr = make_layout(Ks, 0, true, NW);
       if (Lr.total <= kSmemMax && c.nchunk <= 32) {
         c.resident = true;
@@ -1044,33 +1073,38 @@ int rtc_launch(const void *fn, const RtcPlan &pl, int ngrp, RtcArgs &args, cudaS
 // the product of the forward per step) and from H = 1024 in the forward.
 constexpr int64_t kTcMinH[2] = {1024, 512};
 
-bool rec_tc_wanted(int dir, int64_t B, int64_t H) {
+bool rec_tc_wanted(int dir, int64_t B, int64_t H, bool bf) {
   const int o = rtc_override();
   if (o == 1) return false;
   if (o == 0 && H < kTcMinH[dir]) return false;
   RtcPlan p;
   const int n = rtc_sms();
-  return make_rtc_plan(p, dir, B, H, n > 0 ? n : 148);
+  return make_rtc_plan(p, dir, B, H, n > 0 ? n : 148, bf);
 }
 
 size_t rec_tc_ws_bytes(int64_t B, int64_t H) {
-  RtcPlan f, b;
   const int n = rtc_sms() > 0 ? rtc_sms() : 148;
   size_t m = 0;
-  if (make_rtc_plan(f, 0, B, H, n)) m = std::max(m, f.total);
-  if (make_rtc_plan(b, 1, B, H, n)) m = std::max(m, b.total);
+  for (int dir = 0; dir < 2; ++dir)
+    for (bool bf : {false, true}) {
+      RtcPlan pl;
+      if (make_rtc_plan(pl, dir, B, H, n, bf)) m = std::max(m, pl.total);
+    }
   return m;
 }
 
 namespace {
 int rtc_prepare(const RtcPlan &pl, const float *w_hh, const float *a, int64_t H, char *w, int nsm, cudaStream_t st) {
   unsigned *absmax = reinterpret_cast<unsigned *>(w + pl.o_absmax);
-  if (cudaMemsetAsync(absmax, 0, 4, st) != cudaSuccess) return check_launch("memset(absmax)");
-  rtc_absmax_kernel<<<2 * nsm, 256, 0, st>>>(w_hh, a, H, absmax);
-  if (int e = check_launch("rtc_absmax_kernel")) return e;
-  const int64_t n = (int64_t)pl.NC * (pl.Ks / 8) * 2 * pl.UB;
+  if (!pl.bf) {  // the fp16 split's weight scale (bf16 needs none)
+    if (cudaMemsetAsync(absmax, 0, 4, st) != cudaSuccess) return check_launch("memset(absmax)");
+    rtc_absmax_kernel<<<2 * nsm, 256, 0, st>>>(w_hh, a, H, absmax);
+    if (int e = check_launch("rtc_absmax_kernel")) return e;
+  }
+  const int64_t n = (int64_t)pl.NC * (pl.Ks / 8) * (pl.bf ? 1 : 2) * pl.UB;
   rtc_prep_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 16 * nsm), 256, 0, st>>>(
-      w_hh, a, absmax, reinterpret_cast<unsigned char *>(w + pl.o_w), pl.dir, H, pl.KS, pl.UCP, pl.UB, pl.Ks, pl.NC);
+      w_hh, a, absmax, reinterpret_cast<unsigned char *>(w + pl.o_w), pl.dir, H, pl.KS, pl.UCP, pl.UB, pl.Ks, pl.NC,
+      pl.bf ? 1 : 0);
   return check_launch("rtc_prep_kernel");
 }
 
@@ -1084,6 +1118,7 @@ void fill_args(RtcArgs &args, const RtcPlan &pl, char *w, int *status, int64_t T
   args.T = T;
   args.Bt = B;
   args.H = H;
+  args.bf = pl.bf ? 1 : 0;
   args.Ks = pl.Ks;
   args.xbytes = pl.xbytes;
   args.b0 = (int)b0;
@@ -1100,13 +1135,14 @@ void fill_args(RtcArgs &args, const RtcPlan &pl, char *w, int *status, int64_t T
 
 // Forward recurrence on the tensor cores; acts holds Z on entry (the input
 // projection) and the gate activations on return.
+// bf: bf16 mode (see the top of the file).
 int rec_tc_forward(const float *h0, const float *c0, const float *w_hh, const float *b_hh, const float *a,
                    float *h_save, float *c_save, float *acts, int64_t T, int64_t B, int64_t H, void *ws,
-                   size_t ws_bytes, int *status, cudaStream_t st) {
+                   size_t ws_bytes, int *status, cudaStream_t st, bool bf) {
   RtcPlan pl;
   const int nsm = rtc_sms();
   if (nsm <= 0) return fail(HS_ERR_CUDA, "no CUDA device");
-  if (!make_rtc_plan(pl, 0, B, H, nsm))
+  if (!make_rtc_plan(pl, 0, B, H, nsm, bf))
     return fail(HS_ERR_UNSUPPORTED, "recurrent (tensor cores): no plan for B=%lld H=%lld", (long long)B, (long long)H);
   if (!ws || ws_bytes < pl.total || !aligned(ws, 256))
     return fail(HS_ERR_WORKSPACE, "recurrent (tensor cores): workspace %zu < %zu bytes", ws_bytes, pl.total);
@@ -1139,11 +1175,11 @@ int rec_tc_forward(const float *h0, const float *c0, const float *w_hh, const fl
 // activations on entry and dgates on return.
 int rec_tc_backward(const float *w_hh, const float *a, const float *c_save, float *acts, const float *dout,
                     const float *dh_n, const float *dc_n, int64_t T, int64_t B, int64_t H, void *ws, size_t ws_bytes,
-                    int *status, cudaStream_t st) {
+                    int *status, cudaStream_t st, bool bf) {
   RtcPlan pl;
   const int nsm = rtc_sms();
   if (nsm <= 0) return fail(HS_ERR_CUDA, "no CUDA device");
-  if (!make_rtc_plan(pl, 1, B, H, nsm))
+  if (!make_rtc_plan(pl, 1, B, H, nsm, bf))
     return fail(HS_ERR_UNSUPPORTED, "recurrent backward (tensor cores): no plan for B=%lld H=%lld", (long long)B,
                 (long long)H);
   if (!ws || ws_bytes < pl.total || !aligned(ws, 256))

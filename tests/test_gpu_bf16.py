@@ -2,11 +2,17 @@
 
 The reference runs the same module in bfloat16 end to end and checks its
 backends against each other at 1e-2 absolute (tests/test_parallel.py:24,
-tests/test_triton.py:22).  Here the variant is checked against the float64
+tests/test_triton.py:22).  A recurrent bf16 module whose step runs on the
+tensor cores multiplies bf16 a*W_hh by the bf16-rounded state each step
+(configs[3], and H=512 forced onto the tensor cores); parallel bf16 modules
+of the per-column scan's shapes run bf16 products with bf16 saved
+activations.  Here the variant is checked against the float64
 oracle fed the same bf16-rounded inputs and weights, with the stated
 tolerance of 2e-2 normwise (outputs and gradients are returned in bfloat16,
 whose rounding alone is 2^-9 relative).  Output and gradient dtypes must be
 the module's."""
+
+import os
 
 import pytest
 import torch
@@ -26,11 +32,16 @@ TOL_BF16 = 2e-2
     (False, 64, 32, 1024, 2048, "U(0,0.5)"),
     # configs[4]'s micro-batch at short T: pair GEMMs, per-column scan, split handoff
     (True, 256, 32, 512, 1024, "spread"),
+    # the bf16 step product on the tensor cores with resident weights, both directions
+    (False, 48, 20, 128, 512, "tc"),
 ])
-def test_bf16_module_against_float64_oracle(parallel, T, B, D, H, a):
+def test_bf16_module_against_float64_oracle(parallel, T, B, D, H, a, monkeypatch):
     import prlstm_b200
 
     dev = torch.device("cuda", 0)
+    if a == "tc":
+        monkeypatch.setenv("HS_REC_PATH", "tc")
+        a = 0.3
     if a == "U(0,0.5)":
         params, x, G = make_inputs(T, B, D, H, a_uniform=(0.0, 0.5), seed=T + H)
     elif a == "spread":
