@@ -384,6 +384,13 @@ HS_API size_t hs_recurrent_workspace_bytes(int64_t T, int64_t B, int64_t D, int6
  * diagnostic with no reference counterpart; the environment variable
  * HS_REC_PATH=tc|ffma forces one implementation. */
 HS_API int hs_recurrent_uses_tensor_cores(int64_t B, int64_t H, int backward);
+/* Diagnostic: which kernels run the recurrence of this B, H on the current
+ * device: 0 FFMA kernels over the whole GPU (one grid barrier per step),
+ * 1 tensor-core kernels, 2 one thread-block cluster per batch group of 32
+ * sequences with the weights resident and the state exchanged in
+ * distributed shared memory (H <= 128); -1 for bad arguments.
+ * HS_REC_PATH=ffma|tc|cluster forces one where it applies. */
+HS_API int hs_recurrent_path(int64_t B, int64_t H, int backward);
 
 /* Whole recurrent forward.  Inputs x [T,B,D], h0/c0 [B,H] (NULL = zeros),
  * w_ih [4H,D], w_hh [4H,H], b_ih/b_hh [4H], a [4].  Outputs:

@@ -78,6 +78,7 @@ SIGNATURES = {
     "hs_parallel_backward_bf16": (_i32, [_c_p] * 12 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_recurrent_workspace_bytes": (_sz, [_i64] * 4),
     "hs_recurrent_uses_tensor_cores": (_i32, [_i64, _i64, _i32]),
+    "hs_recurrent_path": (_i32, [_i64, _i64, _i32]),
     "hs_recurrent_forward": (_i32, [_c_p] * 11 + [_i64] * 4 + [_c_p, _sz, _c_p, _c_p]),
     "hs_recurrent_backward": (_i32, [_c_p] * 17 + [_i64] * 4 + [_c_p, _sz, _c_p, _c_p]),
     "hs_recurrent_forward_bf16": (_i32, [_c_p] * 11 + [_i64] * 4 + [_c_p, _sz, _c_p, _c_p]),
