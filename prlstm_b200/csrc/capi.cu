@@ -30,7 +30,8 @@ int check_launch(const char *what) {
 
 int gemm_simt(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
               int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kcontig, bool b_kcontig,
-              int beta, cudaStream_t st);
+              int beta, cudaStream_t st, void *ws, size_t ws_bytes);
+size_t gemm_simt_ws_bound(int64_t M, int64_t N);
 int gemm_tc_try(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
                 int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kc, bool b_kc, int beta,
                 void *ws, size_t ws_bytes, int *status, cudaStream_t st, bool *done);
@@ -72,7 +73,7 @@ static int gemm(const float *A, const float *B, float *C, const float *bias, int
                           st, &done))
     return e;
   if (done) return HS_OK;
-  return gemm_simt(A, B, C, bias, M, N, K, lda, ldb, ldc, a_kc, b_kc, beta, st);
+  return gemm_simt(A, B, C, bias, M, N, K, lda, ldb, ldc, a_kc, b_kc, beta, st, ws, ws_bytes);
 }
 
 // Scratch any of the three linear-layer products of these extents may use.
@@ -82,7 +83,8 @@ size_t linear_ws_bytes(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   return std::max({gemm_tc_workspace_bound(M, N, K, true), gemm_tc_workspace_bound(M, K, N, false),
                    gemm_tc_workspace_bound(N, K, M, false),
-                   linear_backward_ws(M, N, K, 0)});
+                   linear_backward_ws(M, N, K, 0), gemm_simt_ws_bound(M, N), gemm_simt_ws_bound(M, K),
+                   gemm_simt_ws_bound(N, K)});
 }
 
 static int check_gemm(const void *a, const void *b, const void *c, int64_t M, int64_t N, int64_t K) {

@@ -10,7 +10,12 @@
 //   dgrad    dx = dy w      A = dy [M,N] K-contig, B = w [N,K] N-contig
 //   wgrad    dw = dy^T x    A = dy [M,N] M-contig, B = x [M,K] N-contig
 // 128x128 output tile per 256-thread CTA, 8x8 outputs per thread, k-step 8,
-// register-prefetched double buffering of the shared-memory tiles.
+// register-prefetched double buffering of the shared-memory tiles.  Shapes
+// with few output tiles and a long K (the gradient products of a short
+// recurrent sequence: N = D or H, K = T*B) split K over blockIdx.z into
+// partial tiles in caller scratch, added in a fixed order by a second pass.
+#include <algorithm>
+
 #include "hs_common.cuh"
 
 namespace hs {
@@ -26,6 +31,8 @@ struct GemmArgs {
   int64_t lda, ldb, ldc;
   int a_kcontig, b_kcontig;
   int beta;            // 0 or 1: C = beta*C + A.B (+bias)
+  float *partial;      // split-K: [splits][M][N], or null
+  int64_t kps;         // k per split (multiple of BK)
 };
 
 __device__ __forceinline__ float ldA(const GemmArgs &g, int64_t m, int64_t k) {
@@ -43,6 +50,7 @@ __global__ void __launch_bounds__(NT) gemm_simt_kernel(GemmArgs g) {
   const int tid = threadIdx.x;
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
   const int tx = tid % 16, ty = tid / 16;
+  const int64_t kbeg = (int64_t)blockIdx.z * g.kps, kend = min(g.K, kbeg + g.kps);
 
   // Load mapping: 1024 elements per operand tile, 4 per thread.  For a
   // K-contiguous operand consecutive threads walk k first; otherwise m/n.
@@ -53,10 +61,10 @@ __global__ void __launch_bounds__(NT) gemm_simt_kernel(GemmArgs g) {
       const int e = tid + i * NT;
       int mm, kk;
       if (g.a_kcontig) { mm = e / BK; kk = e % BK; } else { mm = e % BM; kk = e / BM; }
-      ra[i] = ldA(g, m0 + mm, k0 + kk);
+      ra[i] = (k0 + kk < kend) ? ldA(g, m0 + mm, k0 + kk) : 0.f;
       int nn, kb;
       if (g.b_kcontig) { nn = e / BK; kb = e % BK; } else { nn = e % BN; kb = e / BN; }
-      rb[i] = ldB(g, k0 + kb, n0 + nn);
+      rb[i] = (k0 + kb < kend) ? ldB(g, k0 + kb, n0 + nn) : 0.f;
     }
   };
   auto sstore = [&](int buf) {
@@ -78,13 +86,13 @@ __global__ void __launch_bounds__(NT) gemm_simt_kernel(GemmArgs g) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
 
-  const int64_t nk = (g.K + BK - 1) / BK;
-  gload(0);
+  const int64_t nk = (kend - kbeg + BK - 1) / BK;
+  gload(kbeg);
   sstore(0);
   __syncthreads();
   for (int64_t kt = 0; kt < nk; ++kt) {
     const int buf = kt & 1;
-    if (kt + 1 < nk) gload((kt + 1) * BK);
+    if (kt + 1 < nk) gload(kbeg + (kt + 1) * BK);
 #pragma unroll
     for (int k = 0; k < BK; ++k) {
       float a[8], b[8];
@@ -114,11 +122,31 @@ __global__ void __launch_bounds__(NT) gemm_simt_kernel(GemmArgs g) {
       const int64_t n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
       if (n >= g.N) continue;
       float v = acc[i][j];
+      if (g.partial) {
+        g.partial[((int64_t)blockIdx.z * g.M + m) * g.N + n] = v;
+        continue;
+      }
       if (g.bias) v += g.bias[n];
       float *cp = g.C + m * g.ldc + n;
       if (g.beta) v += *cp;
       *cp = v;
     }
+  }
+}
+
+// C = beta*C + sum over splits (in order) + bias.
+__global__ void simt_splitk_reduce_kernel(const float *__restrict__ part, float *__restrict__ C,
+                                          const float *__restrict__ bias, int64_t M, int64_t N, int64_t ldc,
+                                          int splits, int beta) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M * N; i += stride) {
+    float v = 0.f;
+    for (int z = 0; z < splits; ++z) v += part[(int64_t)z * M * N + i];
+    const int64_t m = i / N, n = i - m * N;
+    if (bias) v += bias[n];
+    float *cp = C + m * ldc + n;
+    if (beta) v += *cp;
+    *cp = v;
   }
 }
 
@@ -156,15 +184,44 @@ __global__ void __launch_bounds__(1024) colsum_kernel(const float *__restrict__ 
 
 }  // namespace
 
+// ws (may be null): scratch for split-K partials; without enough of it the
+// product runs unsplit.
 int gemm_simt(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
               int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kcontig, bool b_kcontig,
-              int beta, cudaStream_t st) {
+              int beta, cudaStream_t st, void *ws, size_t ws_bytes) {
   if (M == 0 || N == 0) return HS_OK;
-  GemmArgs g{A, B, C, bias, M, N, K, lda, ldb, ldc, a_kcontig ? 1 : 0, b_kcontig ? 1 : 0, beta};
+  GemmArgs g{A, B, C, bias, M, N, K, lda, ldb, ldc, a_kcontig ? 1 : 0, b_kcontig ? 1 : 0, beta, nullptr, 0};
   const int64_t gy = (M + BM - 1) / BM, gx = (N + BN - 1) / BN;
   if (gy > 65535) return fail(HS_ERR_UNSUPPORTED, "gemm: M=%lld too large for the FFMA path", (long long)M);
-  gemm_simt_kernel<<<dim3((unsigned)gx, (unsigned)gy), NT, 0, st>>>(g);
-  return check_launch("gemm_simt_kernel");
+  // split K while the tiles fill fewer than ~148 CTAs and every split keeps
+  // at least 32 k (4 k-steps)
+  const int64_t nkb = (K + BK - 1) / BK;
+  int64_t splits = 1;
+  while (gx * gy * splits * 2 <= 160 && nkb / (splits * 2) >= 4) splits *= 2;
+  while (splits > 1 && (!ws || !aligned(ws, 16) || ws_bytes < (size_t)splits * M * N * 4)) splits /= 2;
+  const int64_t kps = (nkb + splits - 1) / splits * BK;
+  splits = (K + kps - 1) / kps;
+  g.kps = splits > 1 ? kps : K;
+  if (splits > 1) g.partial = static_cast<float *>(ws);
+  gemm_simt_kernel<<<dim3((unsigned)gx, (unsigned)gy, (unsigned)std::max<int64_t>(1, splits)), NT, 0, st>>>(g);
+  if (int e = check_launch("gemm_simt_kernel")) return e;
+  if (splits > 1) {
+    const int64_t n = M * N;
+    simt_splitk_reduce_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 1024), 256, 0, st>>>(
+        g.partial, C, bias, M, N, ldc, (int)splits, beta);
+    return check_launch("simt_splitk_reduce_kernel");
+  }
+  return HS_OK;
+}
+
+// Scratch the split-K partials of an M x N product may use (zero for
+// products with enough tiles not to split).
+size_t gemm_simt_ws_bound(int64_t M, int64_t N) {
+  if (M <= 0 || N <= 0) return 0;
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  int64_t splits = 1;
+  while (tiles * splits * 2 <= 160) splits *= 2;
+  return splits > 1 ? (size_t)splits * M * N * 4 : 0;
 }
 
 int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st) {

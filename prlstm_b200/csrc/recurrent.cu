@@ -31,9 +31,6 @@
 
 namespace hs {
 
-int gemm_simt(const float *A, const float *B, float *C, const float *bias, int64_t M, int64_t N,
-              int64_t K, int64_t lda, int64_t ldb, int64_t ldc, bool a_kcontig, bool b_kcontig,
-              int beta, cudaStream_t st);
 int linear_forward(const float *x, const float *w, const float *bias, float *y, int64_t M,
                    int64_t N, int64_t K, void *ws, size_t ws_bytes, int *status, cudaStream_t st);
 int linear_dgrad(const float *dy, const float *w, float *dx, int64_t M, int64_t N, int64_t K,

@@ -239,3 +239,35 @@ def test_linear_backward_extreme_magnitudes(scale):
     dy64, x64, w64 = dy.double().cpu(), x.double().cpu(), w.double().cpu()
     assert _rel(dx, dy64 @ w64) < TOL
     assert _rel(dw, dy64.t() @ x64) < TOL
+
+
+@pytest.mark.parametrize("M,N,K,beta,use_ws", [(4096, 64, 32, 0, True), (4096, 64, 32, 1, True),
+                                               (512, 512, 64, 1, True), (3000, 100, 20, 0, True),
+                                               (4096, 64, 32, 1, False)])
+def test_small_products_split_k(M, N, K, beta, use_ws):
+    """Products below the tensor-core threshold run on the FFMA kernel; with
+    few output tiles and a long reduction (the gradient products of a short
+    recurrent sequence) it splits the reduction into partial tiles added in a
+    fixed order, and runs unsplit without scratch.  wgrad reduces over M,
+    dgrad over N, the forward over K (with bias)."""
+    L = _lib()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(M + N + K + beta)
+    dy = torch.randn(M, N, device=dev, generator=g)
+    x = torch.randn(M, K, device=dev, generator=g)
+    w = torch.randn(N, K, device=dev, generator=g)
+    b = torch.randn(N, device=dev, generator=g)
+    ws, n = _ws(L, M, N, K, dev, use_ws)
+    P, st, sw = L.ptr, L.stream_ptr(dev), L.status_word(dev)
+    dw = torch.randn(N, K, device=dev, generator=g) if beta else torch.empty(N, K, device=dev)
+    ref_dw = dy.double().t() @ x.double() + (dw.double() if beta else 0)
+    L.call("hs_linear_wgrad", P(dy), P(x), P(dw), M, N, K, beta, P(ws), n, P(sw), st)
+    dx = torch.empty(M, K, device=dev)
+    L.call("hs_linear_dgrad", P(dy), P(w), P(dx), M, N, K, P(ws), n, P(sw), st)
+    y = torch.empty(M, N, device=dev)
+    L.call("hs_linear_forward", P(x), P(w), P(b), P(y), M, N, K, P(ws), n, P(sw), st)
+    torch.cuda.synchronize(dev)
+    L.check_device_status(dev)
+    assert _rel(dw, ref_dw) < TOL
+    assert _rel(dx, dy.double() @ w.double()) < TOL
+    assert _rel(y, x.double() @ w.double().t() + b.double()) < TOL
