@@ -106,6 +106,17 @@ HS_DEV void cbulk_s2c(uint32_t dst, const void *src, uint32_t bytes, uint32_t ba
       : "memory");
 }
 
+// Sequence blocks of 4 per row block: the fewest that cover Bc sequences for
+// which the thread count splits k evenly (kCT / (rows * nbq) groups dividing
+// K), at most 8.
+HS_DEV int seq_blocks(int Bc, int rows, int K, int lo) {
+  int nbq = lo;
+  while (nbq < 8 && (4 * nbq < Bc || kCT % (rows * nbq) != 0 || kCT / (rows * nbq) > K ||
+                     K % (kCT / (rows * nbq)) != 0))
+    nbq *= 2;
+  return nbq;
+}
+
 struct RclArgs {
   const float *w;      // forward: [C][H][4UC] (k-major, row ul*4+g); backward: [C][4H][UC] (row u*4+g)
   const float *bias;   // forward: [C][4UC], a*b_hh
@@ -145,9 +156,8 @@ __global__ void __launch_bounds__(kCT, 1) rcl_fwd_kernel(RclArgs p) {
   const int C = p.C, UC = p.UC, R = 4 * UC;
   const int64_t H = p.H, Bt = p.Bt, T = p.T;
   const int K = (int)H;
-  const int nblk = UC * 8, KG = kCT / nblk, KL = K / KG;  // 4x4 blocks, k-groups
   const int SB = UC * kBC;
-  const CLayout L = clayout(R, K, KG, SB, C);
+  const CLayout L = clayout(R, K, kCT / (UC * 8), SB, C);
   float *W = smc + L.w, *bias = smc + L.bias, *rx = smc + L.rx, *stage = smc + L.stage, *red = smc + L.red;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smc + L.bars);
   const uint32_t j = crank();
@@ -156,6 +166,11 @@ __global__ void __launch_bounds__(kCT, 1) rcl_fwd_kernel(RclArgs p) {
   const int Bc = (int)min((int64_t)kBC, Bt - b0);
   const int tid = threadIdx.x;
   const uint32_t sbytes = (uint32_t)SB * 4;
+  // 4 x 4 blocks of (rows, sequences) over this group's BP = 4 nbq padded
+  // sequences; the threads left over split k into KG groups (partial sums
+  // [KG][R][BP]: 4096 floats whatever nbq)
+  const int nbq = seq_blocks(Bc, UC, K, 1);
+  const int BP = 4 * nbq, nblk = UC * nbq, KG = kCT / nblk, KL = K / KG;
 
   // weights and bias of this CTA, resident for the launch
   const float4 *wsrc = reinterpret_cast<const float4 *>(p.w + (size_t)j * K * R);
@@ -198,14 +213,13 @@ __global__ void __launch_bounds__(kCT, 1) rcl_fwd_kernel(RclArgs p) {
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   __syncthreads();
-  if (tid == 0)
-    for (int r = 0; r < C; ++r)
-      cbulk_s2c(cpeer(rx + j * SB, (uint32_t)r), stg0, sbytes, cpeer(&bars[0], (uint32_t)r));
+  if (tid < C)  // one copy per peer, issued by thread r for rank r
+    cbulk_s2c(cpeer(rx + j * SB, (uint32_t)tid), stg0, sbytes, cpeer(&bars[0], (uint32_t)tid));
 
   __shared__ int s_fail;
   int64_t waited = 0;  // uses of the receive barriers completed by this CTA
   bool fail = false;
-  const int kg = tid / nblk, blk = tid % nblk, rb = blk / 8, bq = blk % 8;
+  const int kg = tid / nblk, blk = tid % nblk, rb = blk / nbq, bq = blk % nbq;
   for (int64_t t = 0; t < T && !fail; ++t) {
     const int par = (int)(t & 1);
     // this step's input projection for the thread's cells (before the wait)
@@ -231,6 +245,7 @@ __global__ void __launch_bounds__(kCT, 1) rcl_fwd_kernel(RclArgs p) {
     // gates = h_{t-1} W^T over this thread's k group: 4 rows x 4 sequences
     const float *X = rx + par * C * SB;  // [K][32]
     float acc[4][4] = {};
+#pragma unroll 4
     for (int k = kg * KL; k < (kg + 1) * KL; ++k) {
       const float4 wv = *reinterpret_cast<const float4 *>(W + k * R + 4 * rb);
       const float4 xv = *reinterpret_cast<const float4 *>(X + k * kBC + 4 * bq);
@@ -242,43 +257,51 @@ __global__ void __launch_bounds__(kCT, 1) rcl_fwd_kernel(RclArgs p) {
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i)
-      *reinterpret_cast<float4 *>(red + (kg * R + 4 * rb + i) * kBC + 4 * bq) =
+      *reinterpret_cast<float4 *>(red + (kg * R + 4 * rb + i) * BP + 4 * bq) =
           make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
     __syncthreads();
-    // cells; h_t into staging block par
+    // cells; h_t into staging block par (the outputs no other CTA reads are
+    // stored after the send)
     float *stg = stage + par * SB;
+    float act[kMaxCells][4], hv[kMaxCells];
 #pragma unroll
     for (int m = 0; m < kMaxCells; ++m) {
       const int ci = tid + kCT * m;
       if (ci >= ncell) continue;
       const int ul = ci / kBC, b = ci % kBC;
-      float act[4];
+      if (b >= BP) {  // beyond the computed sequences: zero state
+        stg[ul * kBC + b] = 0.f;
+        continue;
+      }
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         const int row = ul * 4 + g;
         float s = 0.f;
-        for (int q = 0; q < KG; ++q) s += red[(q * R + row) * kBC + b];
-        act[g] = sigm(zg[m][g] + s + bias[row]);
+        for (int q = 0; q < KG; ++q) s += red[(q * R + row) * BP + b];
+        act[m][g] = sigf(zg[m][g] + s + bias[row]);
       }
-      const float c = fmaf(act[1], cst[m], act[0] * act[2]);
-      const float h = act[3] * tanhf(c);
+      const float c = fmaf(act[m][1], cst[m], act[m][0] * act[m][2]);
+      hv[m] = act[m][3] * tanh_any(c);
       cst[m] = c;
-      stg[ul * kBC + b] = b < Bc ? h : 0.f;
-      if (b < Bc) {
-        const int64_t bb = b0 + b, u = (int64_t)j * UC + ul;
-        float *ar = p.zacts + (t * Bt + bb) * 4 * H + u;
-#pragma unroll
-        for (int g = 0; g < 4; ++g) ar[g * H] = act[g];
-        p.h_save[((t + 1) * Bt + bb) * H + u] = h;
-        p.c_save[((t + 1) * Bt + bb) * H + u] = c;
-      }
+      stg[ul * kBC + b] = b < Bc ? hv[m] : 0.f;
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
-    if (tid == 0 && t + 1 < T)
-      for (int r = 0; r < C; ++r)
-        cbulk_s2c(cpeer(rx + (par ^ 1) * C * SB + j * SB, (uint32_t)r), stg, sbytes,
-                  cpeer(&bars[par ^ 1], (uint32_t)r));
+    if (tid < C && t + 1 < T)
+      cbulk_s2c(cpeer(rx + (par ^ 1) * C * SB + j * SB, (uint32_t)tid), stg, sbytes,
+                cpeer(&bars[par ^ 1], (uint32_t)tid));
+#pragma unroll
+    for (int m = 0; m < kMaxCells; ++m) {
+      const int ci = tid + kCT * m;
+      const int ul = ci / kBC, b = ci % kBC;
+      if (ci >= ncell || b >= Bc) continue;
+      const int64_t bb = b0 + b, u = (int64_t)j * UC + ul;
+      float *ar = p.zacts + (t * Bt + bb) * 4 * H + u;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) ar[g * H] = act[m][g];
+      p.h_save[((t + 1) * Bt + bb) * H + u] = hv[m];
+      p.c_save[((t + 1) * Bt + bb) * H + u] = cst[m];
+    }
   }
   // On the way out after a failure: the blocks of the armed uses may still be
   // landing; let them (bounded) before meeting the cluster.
@@ -296,9 +319,8 @@ __global__ void __launch_bounds__(kCT, 1) rcl_bwd_kernel(RclArgs p) {
   const int C = p.C, UC = p.UC;
   const int64_t H = p.H, Bt = p.Bt, T = p.T;
   const int K = (int)(4 * H), R = UC;
-  const int nblk = (UC / 2) * 8, KG = kCT / nblk, KL = K / KG;  // 2x4 blocks, k-groups
   const int SB = 4 * UC * kBC;
-  const CLayout L = clayout(R, K, KG, SB, C);
+  const CLayout L = clayout(R, K, kCT / ((UC / 2) * 8), SB, C);
   float *W = smc + L.w, *rx = smc + L.rx, *stage = smc + L.stage, *red = smc + L.red;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smc + L.bars);
   const uint32_t j = crank();
@@ -307,6 +329,9 @@ __global__ void __launch_bounds__(kCT, 1) rcl_bwd_kernel(RclArgs p) {
   const int Bc = (int)min((int64_t)kBC, Bt - b0);
   const int tid = threadIdx.x;
   const uint32_t sbytes = (uint32_t)SB * 4;
+  // 2 x 4 blocks of (units, sequences), the rest of the threads split k
+  const int nbq = seq_blocks(Bc, UC / 2, K, 1);
+  const int BP = 4 * nbq, nblk = (UC / 2) * nbq, KG = kCT / nblk, KL = K / KG;
 
   const float4 *wsrc = reinterpret_cast<const float4 *>(p.w + (size_t)j * K * R);
   for (int i = tid; i < K * R / 4; i += kCT) reinterpret_cast<float4 *>(W)[i] = wsrc[i];
@@ -333,7 +358,7 @@ __global__ void __launch_bounds__(kCT, 1) rcl_bwd_kernel(RclArgs p) {
   __shared__ int s_fail;
   int64_t waited = 0;
   bool fail = false;
-  const int kg = tid / nblk, blk = tid % nblk, ub = blk / 8, bq = blk % 8;
+  const int kg = tid / nblk, blk = tid % nblk, ub = blk / nbq, bq = blk % nbq;
   for (int64_t t = T - 1; t >= 0 && !fail; --t) {
     const int par = (int)(t & 1);  // dgates of step t+1 arrived in rx[par]
     float ld[kMaxCells][7];        // i, f, g, o, c_t, c_{t-1}, dh
@@ -365,6 +390,7 @@ __global__ void __launch_bounds__(kCT, 1) rcl_bwd_kernel(RclArgs p) {
       // dh = dgates_{t+1} (a W_hh) over this thread's k group: 2 units x 4 sequences
       const float *X = rx + par * C * SB;  // [4H][32], row u*4+g
       float acc[2][4] = {};
+#pragma unroll 4
       for (int k = kg * KL; k < (kg + 1) * KL; ++k) {
         const float2 wv = *reinterpret_cast<const float2 *>(W + k * R + 2 * ub);
         const float4 xv = *reinterpret_cast<const float4 *>(X + k * kBC + 4 * bq);
@@ -376,21 +402,22 @@ __global__ void __launch_bounds__(kCT, 1) rcl_bwd_kernel(RclArgs p) {
       }
 #pragma unroll
       for (int i = 0; i < 2; ++i)
-        *reinterpret_cast<float4 *>(red + (kg * R + 2 * ub + i) * kBC + 4 * bq) =
+        *reinterpret_cast<float4 *>(red + (kg * R + 2 * ub + i) * BP + 4 * bq) =
             make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
       __syncthreads();
     }
     float *stg = stage + par * SB;  // dgates of step t, rows ul*4+g
+    float dgs[kMaxCells][4];        // stored to acts after the send
 #pragma unroll
     for (int m = 0; m < kMaxCells; ++m) {
       const int ci = tid + kCT * m;
       if (ci >= ncell) continue;
       const int ul = ci / kBC, b = ci % kBC;
       float dh = ld[m][6];
-      if (t < T - 1)
-        for (int q = 0; q < KG; ++q) dh += red[(q * R + ul) * kBC + b];
+      if (t < T - 1 && b < BP)
+        for (int q = 0; q < KG; ++q) dh += red[(q * R + ul) * BP + b];
       const float i = ld[m][0], f = ld[m][1], g = ld[m][2], o = ld[m][3];
-      const float th = tanhf(ld[m][4]);
+      const float th = tanh_any(ld[m][4]);
       const float dct = dcst[m] + dh * o * (1.f - th * th);
       float dg[4];
       dg[0] = dct * g * i * (1.f - i);
@@ -400,20 +427,26 @@ __global__ void __launch_bounds__(kCT, 1) rcl_bwd_kernel(RclArgs p) {
       dcst[m] = dct * f;
       const bool v = b < Bc;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) stg[(ul * 4 + q) * kBC + b] = v ? dg[q] : 0.f;
-      if (v) {
-        float *ar = p.zacts + (t * Bt + b0 + b) * 4 * H + (int64_t)j * UC + ul;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) ar[q * H] = dg[q];
+      for (int q = 0; q < 4; ++q) {
+        stg[(ul * 4 + q) * kBC + b] = v ? dg[q] : 0.f;
+        dgs[m][q] = dg[q];
       }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
     // dgates of step t, read by step t-1 from rx[(t-1)&1]
-    if (tid == 0 && t > 0)
-      for (int r = 0; r < C; ++r)
-        cbulk_s2c(cpeer(rx + (par ^ 1) * C * SB + j * SB, (uint32_t)r), stg, sbytes,
-                  cpeer(&bars[par ^ 1], (uint32_t)r));
+    if (tid < C && t > 0)
+      cbulk_s2c(cpeer(rx + (par ^ 1) * C * SB + j * SB, (uint32_t)tid), stg, sbytes,
+                cpeer(&bars[par ^ 1], (uint32_t)tid));
+#pragma unroll
+    for (int m = 0; m < kMaxCells; ++m) {
+      const int ci = tid + kCT * m;
+      const int ul = ci / kBC, b = ci % kBC;
+      if (ci >= ncell || b >= Bc) continue;
+      float *ar = p.zacts + (t * Bt + b0 + b) * 4 * H + (int64_t)j * UC + ul;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) ar[q * H] = dgs[m][q];
+    }
   }
   if (tid == 0 && fail) {
     for (int64_t u2 = waited; u2 < std::min<int64_t>(T - 1, waited + 2); ++u2) {
