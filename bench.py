@@ -419,6 +419,10 @@ def run_ours(args, cfg, rank, world, dev):
             step.launches = launches
             result["launch"] = "cuda_graph (one capture of the step, replayed every step)"
             del graph
+            dev_ms = sum(e[0].elapsed_time(e[-1]) for e in allev) / args.steps
+            if ms / args.steps < 0.5 * dev_ms:
+                raise RuntimeError(f"graphed step {ms / args.steps:.4f} ms is shorter than half the ungraphed "
+                                   f"device time {dev_ms:.4f} ms: the capture missed the step's kernels")
         step.collect(allev)
         _lib.check_device_status(dev)
         ms = max_over_ranks(ms)
@@ -725,9 +729,9 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
     db_ih, db_hh, da = torch.empty(4 * H, device=dev), torch.empty(4 * H, device=dev), torch.empty(4, device=dev)
     ws = _lib.workspace(lib.hs_recurrent_workspace_bytes(T, B_local, D, H), dev)
     status = _lib.status_word(dev)
-    st = _lib.stream_ptr(dev)
 
     def step(record=False):
+        st = _lib.stream_ptr(dev)  # the current stream: the capture stream inside a graph capture
         e = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if record else None
         if record:
             e[0].record()
@@ -758,20 +762,49 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
         step()
     sync()
     _lib.check_device_status(dev)
+    # Both directions on the cluster kernels (plain cluster launches, no
+    # cooperative launch): the step is captured once in a CUDA graph and
+    # replayed, as for the launch-bound parallel configs; the fwd/bwd
+    # breakdown comes from an ungraphed pass after the timed region.
+    paths = [lib.hs_recurrent_path(B_local, H, d) for d in (0, 1)]
+    graph = None
+    if world == 1 and getattr(args, "graph", "auto") != "off" and paths == [2, 2]:
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        sync()
+        _lib.check_device_status(dev)
     clocks = ClockSampler(_gpu_id(dev))
     clocks.start()
     sync()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
-    evs = [step(record=True) for _ in range(args.steps)]
+    if graph is not None:
+        for _ in range(args.steps):
+            graph.replay()
+    else:
+        evs = [step(record=True) for _ in range(args.steps)]
     t1.record()
     sync()
     ck = clocks.stop()
+    if graph is not None:
+        evs = [step(record=True) for _ in range(args.steps)]
+        sync()
+        del graph
     _lib.check_device_status(dev)
     ms = max_over_ranks(t0.elapsed_time(t1))
     fwd = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
     bwd = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
+    if paths == [2, 2] and world == 1 and ms / args.steps < 0.5 * (fwd + bwd):
+        raise RuntimeError(f"graphed recurrent step {ms / args.steps:.4f} ms is shorter than half the ungraphed "
+                           f"device time {fwd + bwd:.4f} ms: the capture missed the step's kernels")
     flops = 24.0 * T * B_local * H * (D + H)
     tokens = T * B_local * world * args.steps
     ach = flops / ((fwd + bwd) / 1e3) / 1e12
@@ -788,13 +821,12 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
     bound_f = max(step_flop / (peak_tf * 1e12), whh_bytes / smem_bw) * 1e6
     bound_b = max(2 * step_flop / (peak_tf * 1e12), whh_bytes / smem_bw) * 1e6
     us_f, us_b = fwd * 1e3 / T, bwd * 1e3 / T
-    tc = [bool(lib.hs_recurrent_uses_tensor_cores(B_local, H, d)) for d in (0, 1)]
+    kname = {0: "ffma", 1: "tcgen05", 2: "cluster (DSMEM exchange)"}
     res = {"value": tokens / (ms / 1e3), "ms_per_step": ms / args.steps, "clocks": ck,
            "gpu_launches": None,
            "recurrent": {"fwd_ms": fwd, "bwd_ms": bwd, "us_per_step_fwd": us_f,
                          "us_per_step_bwd": us_b,
-                         "step_kernel": {"fwd": "tcgen05" if tc[0] else "ffma",
-                                         "bwd": "tcgen05" if tc[1] else "ffma"},
+                         "step_kernel": {"fwd": kname.get(paths[0], "?"), "bwd": kname.get(paths[1], "?")},
                          "step_bound_us": {"fwd": round(bound_f, 3), "bwd": round(bound_b, 3),
                                            "smem_gbs": round(smem_bw / 1e9, 1), "sm_mhz": mhz},
                          "frac_of_step_bound": {"fwd": round(bound_f / us_f, 4),
@@ -803,6 +835,8 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
                         "peak": peak_tf, "unit": "TFLOP/s", "frac": round(ach / peak_tf, 5),
                         "peak_kind": peak_kind, "traffic": None,
                         "note": "latency-bound recurrence: see recurrent.frac_of_step_bound"}}
+    if paths == [2, 2] and world == 1 and getattr(args, "graph", "auto") != "off":
+        res["launch"] = "cuda_graph (one capture of the step, replayed every step)"
     if args.no_e2e:
         return res
     # e2e through the module API with host buffers
@@ -825,6 +859,37 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
         loss_host.copy_(lo.detach().reshape(1), non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
 
+    graphed = "launch" in res
+    if graphed:
+        # the module's forward and backward captured once (torch.cuda.graph)
+        # on static inputs that each step's host-to-device copies fill
+        sx, sG = torch.empty_like(x), torch.empty_like(G)
+        sx.copy_(hx_)
+        sG.copy_(hG_)
+        xleaf = sx.detach().requires_grad_(True)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                m.zero_grad(set_to_none=True)
+                out, _ = m(xleaf)
+                (out * sG).sum().backward()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        m.zero_grad(set_to_none=True)
+        xleaf.grad = None
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out, _ = m(xleaf)
+            sloss = (out * sG).sum()
+            sloss.backward()
+
+        def e2e_step():
+            sx.copy_(hx_, non_blocking=True)
+            sG.copy_(hG_, non_blocking=True)
+            g.replay()
+            loss_host.copy_(sloss.detach().reshape(1), non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+
     for _ in range(args.warmup):
         e2e_step()
     sync()
@@ -838,11 +903,16 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
     ms_e = max_over_ranks(e0.elapsed_time(e1))
     res["e2e"] = {"value": tokens / (ms_e / 1e3), "unit": "tokens/s",
                   "h2d_bytes_per_step": (x.numel() + G.numel()) * 4, "d2h_bytes_per_step": 4}
+    if graphed:
+        res["e2e"]["launch"] = "module forward + backward captured in a CUDA graph (torch.cuda.graph), replayed per step"
     # launches per step (approximate): projection GEMM, weight staging (the
     # tensor-core path: max |a W_hh| then the split tiles), the recurrent
-    # kernel per window of batch groups, the gradient GEMMs, colsum, unscale, da
+    # kernel per window of batch groups (one launch on the cluster path), the
+    # gradient GEMMs, colsum, unscale, da
     nb = (B_local + 31) // 32
-    res["gpu_launches"] = args.steps * ((1 + (2 if tc[0] else 1) + nb) + ((2 if tc[1] else 1) + nb + 6))
+    nk = [1 if pth == 2 else nb for pth in paths]
+    res["gpu_launches"] = args.steps * ((1 + (2 if paths[0] == 1 else 1) + nk[0]) +
+                                        ((2 if paths[1] == 1 else 1) + nk[1] + 6))
     return res
 
 

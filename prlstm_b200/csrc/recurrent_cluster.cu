@@ -540,10 +540,20 @@ bool make_rcl_plan(RclPlan &pl, int64_t H, bool check_fit = true) {
 
 // Kernel attributes for a cluster size: dynamic shared memory up to what the
 // kernel may need, non-portable cluster sizes allowed.
+// Set once per device (bit dev of *attr for the shared memory, of
+// g_rcl_np for the cluster size), so that launches inside a stream capture
+// make no attribute calls.
+std::atomic<unsigned long long> g_rcl_np[2];
 int rcl_prepare_fn(const void *fn, std::atomic<unsigned long long> *attr) {
   if (int e = allow_dynamic_smem(fn, 200 * 1024, attr)) return e;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("cudaGetDevice");
+  std::atomic<unsigned long long> &np = g_rcl_np[attr == &g_rcl_attr[0] ? 0 : 1];
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (np.load(std::memory_order_acquire) & bit) return HS_OK;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
     return check_launch("cudaFuncSetAttribute(non-portable cluster)");
+  np.fetch_or(bit, std::memory_order_acq_rel);
   return HS_OK;
 }
 

@@ -82,3 +82,59 @@ def test_graphed_step_equals_eager(dtype, chain_path):
             assert torch.equal(a, b), (k, i)
     prlstm_b200.check_device_status(dev)
     del graph
+
+
+def test_graphed_recurrent_step_equals_eager():
+    """configs[0]'s recurrent shape, whose recurrence runs on the cluster
+    kernels (plain cluster launches, capturable; the FFMA and tensor-core
+    recurrent kernels are cooperative launches and are not captured)."""
+    import prlstm_b200
+    from prlstm_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    T, B, D, H = 32, 16, 64, 128
+    assert _lib.load().hs_recurrent_path(B, H, 0) == 2 and _lib.load().hs_recurrent_path(B, H, 1) == 2
+    params, _, _ = make_inputs(8, 1, D, H, a=1e-4, seed=4)
+    m = prlstm_b200.HeadStartLSTM(D, H).to(dev)
+    with torch.no_grad():
+        for p, v in zip(m.parameters(), params):
+            p.copy_(v)
+    g = torch.Generator(device=dev).manual_seed(6)
+    xs = [torch.randn(T, B, D, device=dev, generator=g) for _ in range(3)]
+    Gs = [torch.randn(T, B, H, device=dev, generator=g) for _ in range(3)]
+
+    def eager(x, G):
+        m.zero_grad(set_to_none=True)
+        xl = x.clone().requires_grad_(True)
+        out, (h_n, c_n) = m(xl)
+        (out * G).sum().backward()
+        return [out.detach().clone(), h_n.detach().clone(), c_n.detach().clone(), xl.grad.clone()] + \
+               [p.grad.clone() for p in m.parameters()]
+
+    want = [eager(x, G) for x, G in zip(xs, Gs)]
+    sx, sG = xs[0].clone(), Gs[0].clone()
+    xleaf = sx.detach().requires_grad_(True)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            m.zero_grad(set_to_none=True)
+            out, _ = m(xleaf)
+            (out * sG).sum().backward()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    m.zero_grad(set_to_none=True)
+    xleaf.grad = None
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out, (h_n, c_n) = m(xleaf)
+        (out * sG).sum().backward()
+    for k, (x, G) in enumerate(zip(xs, Gs)):
+        sx.copy_(x)
+        sG.copy_(G)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        got = [out, h_n, c_n, xleaf.grad] + [p.grad for p in m.parameters()]
+        for i, (a, b) in enumerate(zip(got, want[k])):
+            assert torch.equal(a, b), (k, i)
+    prlstm_b200.check_device_status(dev)
+    del graph
