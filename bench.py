@@ -272,6 +272,38 @@ class ParallelStep:
         return nprod * 2.0 * T * mb * 4 * H * D  # flops of the call
 
 
+class PrefetchedInputs:
+    """The step's inputs for a graphed end-to-end leg: each step's
+    host-to-device copies run on a copy stream into a device staging buffer,
+    issued right after the previous step's replay was launched (so that they
+    overlap it), and are moved into the graph's static input buffers (a
+    device-to-device copy) before the step's own replay.  Every step copies
+    its inputs from pinned host memory inside the timed region."""
+
+    def __init__(self, host, static, dev):
+        self.host, self.static = host, static
+        self.stage = [torch.empty_like(t) for t in static]
+        self.cs = torch.cuda.Stream(dev)
+        self.free = torch.cuda.Event()
+        self.free.record()
+        self.ready = None
+
+    def issue(self):
+        with torch.cuda.stream(self.cs):
+            self.cs.wait_event(self.free)  # the staging buffer was read by the last move
+            for st, h in zip(self.stage, self.host):
+                st.copy_(h, non_blocking=True)
+            self.ready = torch.cuda.Event()
+            self.ready.record()
+
+    def consume(self):
+        torch.cuda.current_stream().wait_event(self.ready)
+        for t, st in zip(self.static, self.stage):
+            t.copy_(st, non_blocking=True)
+        self.free = torch.cuda.Event()
+        self.free.record()
+
+
 def use_graph(args, cfg, B_local, world):
     """Whether the parallel step is captured in a CUDA graph: on one GPU (no
     collective inside the step), for steps of at most 2^16 tokens per rank,
@@ -681,10 +713,13 @@ def e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync, max_over_ra
             sloss = (out * sG).sum()
             sloss.backward()
 
+        pf = PrefetchedInputs([hx[0], hG[0]], [sx, sG], dev)
+        pf.issue()
+
         def graphed():
-            sx.copy_(hx[0], non_blocking=True)
-            sG.copy_(hG[0], non_blocking=True)
+            pf.consume()  # this step's inputs, copied while the previous step ran
             g.replay()
+            pf.issue()    # the next step's inputs, overlapping this replay
             loss_host.copy_(sloss.detach().reshape(1), non_blocking=True)
             torch.cuda.current_stream(dev).synchronize()
             return float(loss_host.item())
@@ -708,7 +743,8 @@ def e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync, max_over_ra
     res = {"value": T * cfg["B"] * steps / (ms / 1e3), "unit": "tokens/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "steps": steps}
     if graphed is not None:
-        res["launch"] = "module forward + backward captured in a CUDA graph (torch.cuda.graph), replayed per step"
+        res["launch"] = ("module forward + backward captured in a CUDA graph (torch.cuda.graph), replayed per "
+                         "step; each step's host-to-device copies overlap the previous step's replay")
     return res
 
 
@@ -883,10 +919,13 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
             sloss = (out * sG).sum()
             sloss.backward()
 
+        pf = PrefetchedInputs([hx_, hG_], [sx, sG], dev)
+        pf.issue()
+
         def e2e_step():
-            sx.copy_(hx_, non_blocking=True)
-            sG.copy_(hG_, non_blocking=True)
+            pf.consume()
             g.replay()
+            pf.issue()
             loss_host.copy_(sloss.detach().reshape(1), non_blocking=True)
             torch.cuda.current_stream(dev).synchronize()
 
@@ -904,7 +943,8 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
     res["e2e"] = {"value": tokens / (ms_e / 1e3), "unit": "tokens/s",
                   "h2d_bytes_per_step": (x.numel() + G.numel()) * 4, "d2h_bytes_per_step": 4}
     if graphed:
-        res["e2e"]["launch"] = "module forward + backward captured in a CUDA graph (torch.cuda.graph), replayed per step"
+        res["e2e"]["launch"] = ("module forward + backward captured in a CUDA graph (torch.cuda.graph), replayed "
+                                "per step; each step's host-to-device copies overlap the previous step's replay")
     # launches per step (approximate): projection GEMM, weight staging (the
     # tensor-core path: max |a W_hh| then the split tiles), the recurrent
     # kernel per window of batch groups (one launch on the cluster path), the
