@@ -259,16 +259,29 @@ HS_DEV void bulk_s2c(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar
 }
 
 // ------------------------------------------------------------------ staging
-// max |a[g] W_hh[r][k]| as float bits into *out (zeroed by the caller).
+// max |a[g] W_hh[r][k]| as float bits into *out (zeroed by the caller): the
+// max |W_hh| of gate block blockIdx.y (float4 loads, H % 4 == 0) times
+// |a[g]|; rounding is monotone, so this is the max of the rounded products.
+// vec: w_hh is 16-byte aligned (else scalar loads).
 __global__ void rtc_absmax_kernel(const float *__restrict__ w_hh, const float *__restrict__ a, int64_t H,
-                                  unsigned *out) {
-  const int64_t n = 4 * H * H;
+                                  unsigned *out, int vec) {
+  const int g = blockIdx.y;
+  const float *blk = w_hh + (int64_t)g * H * H;
   float m = 0.f;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    m = fmaxf(m, fabsf(a[i / (H * H)] * w_hh[i]));
+  if (vec) {
+    const int64_t n4 = H * H / 4;
+    const float4 *src = reinterpret_cast<const float4 *>(blk);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+      const float4 v = __ldg(src + i);
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+  } else {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < H * H; i += (int64_t)gridDim.x * blockDim.x)
+      m = fmaxf(m, fabsf(blk[i]));
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(fabsf(a[g]) * m));
 }
 
 // Weight tiles, one per CTA: the N = 2 UB operand [UB rows hi | the same UB
@@ -284,33 +297,50 @@ __global__ void rtc_absmax_kernel(const float *__restrict__ w_hh, const float *_
 // bf != 0: the N = UB operand of the rows themselves in bf16, unscaled.
 __global__ void rtc_prep_kernel(const float *__restrict__ w_hh, const float *__restrict__ a,
                                 const unsigned *__restrict__ absmax, unsigned char *__restrict__ wg, int dir,
-                                int64_t H, int KS, int UCP, int UB, int64_t Ks, int NC, int bf) {
+                                int64_t H, int KS, int UCP, int UB, int64_t Ks, int NC, int bf, int vec) {
   const float s = bf ? 1.0f : pow2_scale(*absmax);
   const int NW = bf ? UB : 2 * UB;
-  const int64_t nkc = Ks / 8;
-  const int64_t total = (int64_t)NC * nkc * NW;
+  // 32-bit index arithmetic: NC * Ks/8 * NW < 2^31 for every plan (H <= 2^14)
+  const int nkc = (int)(Ks / 8);
+  const int total = NC * nkc * NW;
   const size_t tile = (size_t)Ks * NW * 2;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int n = (int)(i % NW);
-    const int64_t kc = (i / NW) % nkc;
-    const int cta = (int)(i / (NW * nkc));
+  const int Hi = (int)H;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int n = i % NW;
+    const int kc = (i / NW) % nkc;
+    const int cta = i / (NW * nkc);
     const int blk = cta / KS, sp = cta % KS;
     const int r = n % UB;
     const bool lo = n >= UB;
+    float wv[8];
+    const int k0 = sp * (int)Ks + kc * 8;
+    if (dir == 0) {
+      // 8 consecutive k of one row: two 16-byte loads (k0 is a multiple of 8)
+      const int g = r / 32, ul = r % 32;
+      const float ag = a[g];
+      const float *row = w_hh + ((int64_t)g * Hi + blk * 32 + ul) * Hi + k0;
+      if (vec) {
+        const float4 v0 = __ldg(reinterpret_cast<const float4 *>(row)), v1 = __ldg(reinterpret_cast<const float4 *>(row) + 1);
+        wv[0] = ag * v0.x; wv[1] = ag * v0.y; wv[2] = ag * v0.z; wv[3] = ag * v0.w;
+        wv[4] = ag * v1.x; wv[5] = ag * v1.y; wv[6] = ag * v1.z; wv[7] = ag * v1.w;
+      } else {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) wv[kk] = ag * row[kk];
+      }
+    } else {
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int k = k0 + kk;
+        const int P = k / (4 * UCP);
+        const int g = (k / UCP) % 4, l = k % UCP;
+        const int up = (P / KS) * UB + (P % KS) * UCP + l;
+        wv[kk] = a[g] * w_hh[((int64_t)g * Hi + up) * Hi + blk * UB + r];
+      }
+    }
     __align__(16) __half v[8];
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
-      const int64_t k = sp * Ks + kc * 8 + kk;
-      float w;
-      if (dir == 0) {
-        const int g = r / 32, ul = r % 32;
-        w = a[g] * w_hh[(g * H + (int64_t)blk * 32 + ul) * H + k];
-      } else {
-        const int64_t P = k / (4 * UCP);
-        const int g = (int)((k / UCP) % 4), l = (int)(k % UCP);
-        const int64_t up = (P / KS) * UB + (P % KS) * UCP + l;
-        w = a[g] * w_hh[(g * H + up) * H + (int64_t)blk * UB + r];
-      }
+      const float w = wv[kk];
       if (bf) {
         v[kk] = __ushort_as_half(__bfloat16_as_ushort(__float2bfloat16_rn(w)));
       } else {
@@ -1098,13 +1128,14 @@ int rtc_prepare(const RtcPlan &pl, const float *w_hh, const float *a, int64_t H,
   unsigned *absmax = reinterpret_cast<unsigned *>(w + pl.o_absmax);
   if (!pl.bf) {  // the fp16 split's weight scale (bf16 needs none)
     if (cudaMemsetAsync(absmax, 0, 4, st) != cudaSuccess) return check_launch("memset(absmax)");
-    rtc_absmax_kernel<<<2 * nsm, 256, 0, st>>>(w_hh, a, H, absmax);
+    const int vec = aligned(w_hh, 16) ? 1 : 0;  // H is a multiple of 64
+    rtc_absmax_kernel<<<dim3((unsigned)std::max(1, nsm / 2), 4), 256, 0, st>>>(w_hh, a, H, absmax, vec);
     if (int e = check_launch("rtc_absmax_kernel")) return e;
   }
   const int64_t n = (int64_t)pl.NC * (pl.Ks / 8) * (pl.bf ? 1 : 2) * pl.UB;
   rtc_prep_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 16 * nsm), 256, 0, st>>>(
       w_hh, a, absmax, reinterpret_cast<unsigned char *>(w + pl.o_w), pl.dir, H, pl.KS, pl.UCP, pl.UB, pl.Ks, pl.NC,
-      pl.bf ? 1 : 0);
+      pl.bf ? 1 : 0, aligned(w_hh, 16) ? 1 : 0);
   return check_launch("rtc_prep_kernel");
 }
 
