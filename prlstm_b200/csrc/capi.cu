@@ -50,7 +50,8 @@ int gemm_h3_presplit(const void *a_split, const unsigned *a_absmax, bool a_mn, c
                      bool *done);
 size_t scan_workspace(int64_t T, int64_t B, int64_t H);
 int noalloc_status_word(int **word);
-int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st);
+int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st, void *ws = nullptr,
+           size_t ws_bytes = 0);
 int scan_forward(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
                  int64_t T, int64_t B, int64_t H, float eps, void *ws, size_t ws_bytes,
                  int *status, cudaStream_t st, unsigned *kf_max = nullptr);

@@ -156,21 +156,26 @@ __global__ void simt_splitk_reduce_kernel(const float *__restrict__ part, float 
 // out[n] = beta*out[n] + sum_m x[m][n]: 32 columns per CTA, 32 warps over
 // rows with four independent accumulators each (enough loads in flight to
 // stream from HBM), warp partials added in a fixed order.
+// With gridDim.y = S > 1 the rows are cut into S slices (slice y: rows
+// [y*rps, (y+1)*rps)) whose sums go to part_out[y][n], added in order by
+// colsum_parts_kernel.
 __global__ void __launch_bounds__(1024) colsum_kernel(const float *__restrict__ x, float *__restrict__ out,
-                                                      int64_t M, int64_t N, int beta) {
+                                                      int64_t M, int64_t N, int beta, float *__restrict__ part_out,
+                                                      int64_t rps) {
   __shared__ float part[32][33];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int64_t n = (int64_t)blockIdx.x * 32 + lane;
+  const int64_t r0 = (int64_t)blockIdx.y * rps, r1 = min(M, r0 + rps);
   float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
   if (n < N) {
-    int64_t r = w;
-    for (; r + 96 < M; r += 128) {
+    int64_t r = r0 + w;
+    for (; r + 96 < r1; r += 128) {
       s0 += x[r * N + n];
       s1 += x[(r + 32) * N + n];
       s2 += x[(r + 64) * N + n];
       s3 += x[(r + 96) * N + n];
     }
-    for (; r < M; r += 32) s0 += x[r * N + n];
+    for (; r < r1; r += 32) s0 += x[r * N + n];
   }
   part[w][lane] = (s0 + s1) + (s2 + s3);
   __syncthreads();
@@ -178,8 +183,18 @@ __global__ void __launch_bounds__(1024) colsum_kernel(const float *__restrict__ 
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) s += part[i][lane];
-    out[n] = beta ? out[n] + s : s;
+    if (part_out) part_out[(int64_t)blockIdx.y * N + n] = s;
+    else out[n] = beta ? out[n] + s : s;
   }
+}
+
+__global__ void colsum_parts_kernel(const float *__restrict__ part, float *__restrict__ out, int64_t N, int S,
+                                    int beta) {
+  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  float s = 0.f;
+  for (int y = 0; y < S; ++y) s += part[(int64_t)y * N + n];
+  out[n] = beta ? out[n] + s : s;
 }
 
 }  // namespace
@@ -224,10 +239,24 @@ size_t gemm_simt_ws_bound(int64_t M, int64_t N) {
   return splits > 1 ? (size_t)splits * M * N * 4 : 0;
 }
 
-int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st) {
+// ws (may be null): with room for S x N floats, the rows are split into S
+// slices so that the column blocks and slices fill the GPU.
+int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st, void *ws,
+           size_t ws_bytes) {
   if (N == 0) return HS_OK;
-  colsum_kernel<<<(unsigned)((N + 31) / 32), 1024, 0, st>>>(x, out, M, N, beta);
-  return check_launch("colsum_kernel");
+  const int64_t nb = (N + 31) / 32;
+  int64_t S = 1;
+  while (nb * S * 2 <= 296 && M / (S * 2) >= 512) S *= 2;
+  while (S > 1 && (!ws || !aligned(ws, 16) || ws_bytes < (size_t)S * N * 4)) S /= 2;
+  const int64_t rps = (M + S - 1) / S;
+  float *part = S > 1 ? static_cast<float *>(ws) : nullptr;
+  colsum_kernel<<<dim3((unsigned)nb, (unsigned)S), 1024, 0, st>>>(x, out, M, N, beta, part, S > 1 ? rps : M);
+  if (int e = check_launch("colsum_kernel")) return e;
+  if (S > 1) {
+    colsum_parts_kernel<<<(unsigned)((N + 255) / 256), 256, 0, st>>>(part, out, N, (int)S, beta);
+    return check_launch("colsum_parts_kernel");
+  }
+  return HS_OK;
 }
 
 }  // namespace hs

@@ -42,7 +42,8 @@ size_t linear_backward_ws(int64_t M, int64_t N, int64_t K, int64_t K2);
 int linear_backward_ex(const float *dy, const float *w, float *dx, const float *x, float *dw, const float *x2,
                        float *dw2, int64_t M, int64_t N, int64_t K, int64_t K2, int beta, void *ws, size_t ws_bytes,
                        int *status, cudaStream_t st, const unsigned *dy_absmax);
-int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st);
+int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStream_t st, void *ws = nullptr,
+           size_t ws_bytes = 0);
 bool rec_tc_wanted(int dir, int64_t B, int64_t H, bool bf = false);
 bool rec_cluster_wanted(int64_t B, int64_t H);
 size_t rec_cluster_ws_bytes(int64_t H);
@@ -799,7 +800,7 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
   if (int e = linear_backward_ex(acts, w_ih, dx, x, dw_ih, h_save, dw_hh, M, N, D, H, 0, ws, ws_bytes, status, st,
                                   nullptr))
     return e;
-  if (int e = colsum(acts, db_ih, M, N, 0, st)) return e;
+  if (int e = colsum(acts, db_ih, M, N, 0, st, ws, ws_bytes)) return e;
   // partial sums of da in the (now free) workspace
   float *part = reinterpret_cast<float *>(w);
   rec_unscale_kernel<<<dim3(kUnscaleParts, 4), 256, 0, st>>>(w_hh, b_hh, a, dw_hh, db_ih, db_hh, part, H);
