@@ -328,14 +328,15 @@ __global__ void rtc_prep_kernel(const float *__restrict__ w_hh, const float *__r
         for (int kk = 0; kk < 8; ++kk) wv[kk] = ag * row[kk];
       }
     } else {
+      // UCP is a multiple of 8 (UB / KS with UB in {64, 128}, KS <= 8), so
+      // the 8 consecutive k share one producer block P and gate g
+      const int P = k0 / (4 * UCP);
+      const int g = (k0 / UCP) % 4, l0 = k0 % UCP;
+      const int up0 = (P / KS) * UB + (P % KS) * UCP + l0;
+      const float ag = a[g];
+      const float *col = w_hh + ((int64_t)g * Hi + up0) * Hi + blk * UB + r;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const int k = k0 + kk;
-        const int P = k / (4 * UCP);
-        const int g = (k / UCP) % 4, l = k % UCP;
-        const int up = (P / KS) * UB + (P % KS) * UCP + l;
-        wv[kk] = a[g] * w_hh[((int64_t)g * Hi + up) * Hi + blk * UB + r];
-      }
+      for (int kk = 0; kk < 8; ++kk) wv[kk] = ag * col[(int64_t)kk * Hi];
     }
     __align__(16) __half v[8];
 #pragma unroll
@@ -991,6 +992,7 @@ bool make_rtc_plan(RtcPlan &p, int dir, int64_t B, int64_t H, int nsm, bool bf =
       c.KS = ks;
       c.Ks = Ks;
       c.UCP = unit_block / ks;
+      if (dir == 1 && c.UCP % 8) continue;  // the backward tile prep reads 8 k of one block
       c.nchunk = (int)(Ks / KCH);
       // accumulator groups: forward every 256 k; backward one producer block
       // (4 x UCP k of one scale)
