@@ -2,8 +2,12 @@
 
 Two ranks each run the module forward/backward on their contiguous shard of
 the batch and sum the gradients with prlstm_b200.data_parallel; the result
-must equal one full-batch run on a single GPU (the sum of per-sequence
-gradients is the same sum, only the order of the final addition differs)."""
+must equal one full-batch run on a single GPU to float32 rounding: the sum
+of per-sequence gradients is the same sum, but the order of its additions
+depends on each run's batch extent (the recurrent cluster kernels size their
+sequence blocks to the batch group, the FFMA GEMMs split their reduction by
+its length), so the bound is the recurrent parity bound, 1e-5 of the
+largest gradient entry (measured differences reach 1.3e-6)."""
 
 import os
 import socket
@@ -89,4 +93,4 @@ def test_two_gpu_sharded_gradients_equal_full_batch(case, tmp_path):
             continue
         g = got[n]
         err = ((g - p.grad.cpu()).abs().max() / p.grad.abs().max().cpu()).item()
-        assert err < 1e-6, f"{n}: {err:.3e}"
+        assert err < 1e-5, f"{n}: {err:.3e}"
