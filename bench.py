@@ -193,9 +193,13 @@ class ParallelStep:
         self.db_mb = torch.empty(4 * H, device=dev)
         lib = _lib.load()
         M = T * mb
+        # the projection and the scan forward as one kernel where the library
+        # takes it for this micro-batch (HS_PROJ_SCAN=0 times the two calls)
+        self.fused = bool(lib.hs_projection_scan_supported(T, mb, D, H))
         self.ws = _lib.workspace(max(lib.hs_parallel_workspace_bytes(T, mb, D, H),
                                      lib.hs_scan_split_workspace_bytes(T, mb, H),
-                                     lib.hs_linear_presplit_workspace_bytes(M, 4 * H, D)), dev)
+                                     lib.hs_linear_presplit_workspace_bytes(M, 4 * H, D),
+                                     lib.hs_projection_scan_workspace_bytes(T, mb, D, H)), dev)
         self.status = _lib.status_word(dev)
         # dZ travels from the scan backward to the gradient GEMMs as its fp16
         # split (hi, lo) with one scale word; the forward's max c feeds the
@@ -204,7 +208,8 @@ class ParallelStep:
         # x's split serves both the projection and the weight gradient
         self.x_split = torch.empty(lib.hs_split_bytes(M, D), dtype=torch.uint8, device=dev)
         self.words = torch.zeros(64, dtype=torch.int32, device=dev)  # [0] Kf, [16] dZ scale, [32] x scale
-        self.names = ("proj_gemm", "scan_fwd", "scan_bwd", "linear_bwd")
+        self.names = (("proj_scan", "scan_bwd", "linear_bwd") if self.fused else
+                      ("proj_gemm", "scan_fwd", "scan_bwd", "linear_bwd"))
         self.ms = {n: 0.0 for n in self.names}
         self.launches = 0
 
@@ -217,47 +222,55 @@ class ParallelStep:
         evs = []
         for i in range(self.nmb):
             xs, Gs = x[i], G[i]
-            e = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if record else None
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(len(self.names) + 1)] if record else None
             if record:
                 e[0].record()
             x_scale = P(self.words[32:])
-            L.call("hs_split", P(xs), M, D, P(self.x_split), x_scale, st)
-            L.call("hs_linear_forward_presplit", P(self.x_split), x_scale, P(self.W_ih), P(self.b_ih), P(self.z), M,
-                   4 * H, D, P(self.ws), self.ws.numel(), P(self.status), st)
-            if record:
-                e[1].record()
             cmax, dz_scale = P(self.words[0:]), P(self.words[16:])
-            L.call("hs_scan_forward_kf", P(self.z), P(self.c0), P(self.out), P(self.c), P(self.h_n),
-                   P(self.c_n), T, mb, H, 1e-6, P(self.ws), self.ws.numel(), cmax, P(self.status), st)
+            L.call("hs_split", P(xs), M, D, P(self.x_split), x_scale, st)
+            if self.fused:
+                # Z, out, c, h_n, c_n and the backward's bound in one kernel
+                L.call("hs_projection_scan_forward", P(self.x_split), x_scale, P(self.W_ih), P(self.b_ih),
+                       P(self.c0), P(self.z), P(self.out), P(self.c), P(self.h_n), P(self.c_n), T, mb, D, H,
+                       1e-6, P(self.ws), self.ws.numel(), cmax, P(self.status), st)
+            else:
+                L.call("hs_linear_forward_presplit", P(self.x_split), x_scale, P(self.W_ih), P(self.b_ih),
+                       P(self.z), M, 4 * H, D, P(self.ws), self.ws.numel(), P(self.status), st)
+                if record:
+                    e[1].record()
+                L.call("hs_scan_forward_kf", P(self.z), P(self.c0), P(self.out), P(self.c), P(self.h_n),
+                       P(self.c_n), T, mb, H, 1e-6, P(self.ws), self.ws.numel(), cmax, P(self.status), st)
             if record:
-                e[2].record()
+                e[len(self.names) - 2].record()
             # the scan backward writes dZ as the fp16 split the GEMMs read
             L.call("hs_scan_backward_split", P(self.z), P(self.c), P(self.c0), P(Gs), None, None, cmax,
                    P(self.dz_split), dz_scale, None, P(self.db_mb), T, mb, H, 1e-6, P(self.ws),
                    self.ws.numel(), P(self.status), st)
             if record:
-                e[3].record()
+                e[len(self.names) - 1].record()
             # dX and dW_ih (accumulated over micro-batches) in one call
             L.call("hs_linear_backward_presplit", P(self.dz_split), dz_scale, None, P(self.x_split), x_scale,
                    P(self.W_ih), P(self.dx), P(self.dW), M, 4 * H, D, 1 if i else 0, P(self.ws), self.ws.numel(),
                    P(self.status), st)
             if record:
-                e[4].record()
+                e[len(self.names)].record()
             self.db.add_(self.db_mb) if i else self.db.copy_(self.db_mb)
             # projection: absmax + split of x and of W_ih, GEMM; scan forward
-            # 1; scan backward: bound (3), scan, rowsum, check, conditional
-            # re-run and split (2, return at once unless needed); backward
-            # GEMMs: absmax + split of W_ih, 2 GEMMs, split-K reduce (x's
-            # split is the projection's)
-            self.launches += self.LAUNCHES_PER_MB
+            # 1 (fused: the same splits and one kernel for both); scan
+            # backward: bound (3), scan, rowsum, check, conditional re-run and
+            # split (2, return at once unless needed); backward GEMMs: absmax +
+            # split of W_ih, 2 GEMMs, split-K reduce (x's split is the
+            # projection's)
+            self.launches += self.launches_per_mb()
             if record:
                 evs.append(e)
         return evs
 
-    LAUNCHES_PER_MB = 5 + 1 + 8 + 5
+    def launches_per_mb(self):
+        return (5 if self.fused else 5 + 1) + 8 + 5
 
     def per_step_launches(self):
-        return self.LAUNCHES_PER_MB * self.nmb
+        return self.launches_per_mb() * self.nmb
 
     def collect(self, evs):
         for e in evs:
@@ -268,7 +281,7 @@ class ParallelStep:
         T, D, H, mb = self.cfg["T"], self.cfg["D"], self.cfg["H"], self.mb
         if kernel in ("scan_fwd", "scan_bwd"):
             return T * mb * H
-        nprod = 2 if kernel == "linear_bwd" else 1  # dX and dW_ih
+        nprod = 2 if kernel == "linear_bwd" else 1  # dX and dW_ih; proj_scan: the projection's flops
         return nprod * 2.0 * T * mb * 4 * H * D  # flops of the call
 
 
@@ -499,7 +512,7 @@ def run_ours(args, cfg, rank, world, dev):
             # the backward call holds both products: its references are their
             # time-weighted combination (equal FLOPs each)
             rb = {k: 2.0 / (1.0 / refs["dgrad"][k] + 1.0 / refs["wgrad"][k]) for k in refs["dgrad"]}
-            refs = {"proj_gemm": refs["proj_gemm"], "linear_bwd": rb}
+            refs = {("proj_scan" if step.fused else "proj_gemm"): refs["proj_gemm"], "linear_bwd": rb}
             for n, r in refs.items():
                 kern[n].update(r)
                 kern[n]["speedup_vs_cublas_fp32"] = kern[n]["achieved"] / r["cublas_fp32_tflops"]
@@ -515,13 +528,23 @@ def run_ours(args, cfg, rank, world, dev):
             result["roofline"]["frac_of_burst_peak"] = round(kern[dom]["frac_of_burst_peak"], 4)
             result["roofline"]["f16x3_ceiling"] = round(peak_tf / 3.0, 1)
             result["roofline"]["frac_of_f16x3_ceiling"] = round(kern[dom]["frac_of_f16x3_ceiling"], 4)
+        if step.fused:
+            # the fused kernel's DRAM bytes per unit (t, b, h): x's split
+            # (4 D / H B), Z written (16 B), out and c written (8 B)
+            f = kern["proj_scan"]
+            byt = (24.0 + 4.0 * D / H) * step.units("scan_bwd")
+            f["hbm_bytes_per_launch"] = byt
+            f["hbm_gbs"] = round(byt / (f["avg_ms"] / 1e3) / 1e9, 1)
         result["kernels"] = {n: {k: (round(v, 4) if isinstance(v, float) else v) for k, v in kern[n].items()}
                              for n in kern}
-        scan = {n: kern[n] for n in ("scan_fwd", "scan_bwd")}
-        tot_ms = scan["scan_fwd"]["avg_ms"] + scan["scan_bwd"]["avg_ms"]
-        ach = 64.0 * step.units("scan_fwd") / (tot_ms / 1e3) / 1e9
-        result["scan_roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak_hbm,
-                                   "unit": "GB/s", "frac": round(ach / peak_hbm, 4),
+        # the scans of the step (with the projection fused, the forward's
+        # scan has no kernel of its own: the backward's alone)
+        scan = {n: kern[n] for n in ("scan_fwd", "scan_bwd") if n in kern}
+        tot_ms = sum(v["avg_ms"] for v in scan.values())
+        per_unit = (24.0 if "scan_fwd" in scan else 0.0) + 40.0
+        ach = per_unit * step.units("scan_bwd") / (tot_ms / 1e3) / 1e9
+        result["scan_roofline"] = {"kernels": sorted(scan), "bound": "hbm", "achieved": round(ach, 1),
+                                   "peak": peak_hbm, "unit": "GB/s", "frac": round(ach / peak_hbm, 4),
                                    "peak_kind": peak_kind}
         # The scans on their own (plain float32 entry points, one micro-batch,
         # after the timed region): inside the step the GEMMs hold the SM clock

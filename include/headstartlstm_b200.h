@@ -203,6 +203,26 @@ HS_API int hs_scan_forward_kf(const float *z, const float *c0, float *out, float
                               float *c_n, int64_t T, int64_t B, int64_t H, float eps,
                               void *workspace, size_t workspace_bytes, unsigned *kf_max,
                               int *dev_status, hs_stream_t stream);
+/* The projection and the scan forward as ONE kernel: z = x W_ih^T + b_ih
+ * (x given as its fp16 split, x_split and x_scale from hs_split of x
+ * [T*B][D]) on the tensor cores, with the gates, the scan, out, c, h_n, c_n
+ * and *kf (as hs_scan_forward_kf; may be NULL) computed in the GEMM's
+ * epilogue.  z [T,B,4H] is written for the backward but never read back.
+ * Needs H % 64 == 0, 16-byte aligned z, out, c, x_split (and b_ih if given)
+ * and dev_status; workspace >= hs_projection_scan_workspace_bytes (256-byte
+ * aligned).  hs_projection_scan_supported says whether the library's own
+ * forward (hs_parallel_forward*) takes this kernel for a shape by default
+ * (it does when the (sequence pair, 64-unit block) chains fill the GPU, or
+ * T <= 128); HS_PROJ_SCAN=0 / 1 turns that off / on for every shape it can
+ * run.  Replaces, with hs_split, the projection `linear` and the scan of
+ * headstartlstm_parallel (_parallel.py:38-74, _parallel.py:21-35). */
+HS_API size_t hs_projection_scan_workspace_bytes(int64_t T, int64_t B, int64_t D, int64_t H);
+HS_API int hs_projection_scan_supported(int64_t T, int64_t B, int64_t D, int64_t H);
+HS_API int hs_projection_scan_forward(const void *x_split, const unsigned *x_scale, const float *w_ih,
+                                      const float *b_ih, const float *c0, float *z, float *out, float *c,
+                                      float *h_n, float *c_n, int64_t T, int64_t B, int64_t D, int64_t H,
+                                      float eps, void *workspace, size_t workspace_bytes, unsigned *kf,
+                                      int *dev_status, hs_stream_t stream);
 /* The scan backward with dZ delivered as its fp16 split for the gradient
  * GEMMs (hs_linear_backward_presplit) instead of float32: dz_split (16-byte
  * aligned, hs_split_bytes(T*B, 4H) bytes) receives hi then lo, *dz_scale the

@@ -58,6 +58,9 @@ SIGNATURES = {
     "hs_scan_backward": (_i32, [_c_p] * 9 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_scan_backward_absmax": (_i32, [_c_p] * 9 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),
     "hs_scan_forward_kf": (_i32, [_c_p] * 6 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),
+    "hs_projection_scan_workspace_bytes": (_sz, [_i64] * 4),
+    "hs_projection_scan_supported": (_i32, [_i64] * 4),
+    "hs_projection_scan_forward": (_i32, [_c_p] * 10 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),
     "hs_scan_uses_column_kernels": (_i32, [_i64] * 3),
     "hs_scan_split_workspace_bytes": (_sz, [_i64] * 3),
     "hs_scan_backward_split": (_i32, [_c_p] * 11 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),

@@ -56,6 +56,13 @@ int scan_forward(const float *z, const float *c0, float *out, float *c, float *h
                  int64_t T, int64_t B, int64_t H, float eps, void *ws, size_t ws_bytes,
                  int *status, cudaStream_t st, unsigned *kf_max = nullptr);
 size_t scan_split_ws_bytes(int64_t T, int64_t B, int64_t H);
+size_t proj_scan_ws(int64_t T, int64_t B, int64_t D, int64_t H);
+bool proj_scan_shape_ok(int64_t T, int64_t B, int64_t D, int64_t H);
+bool proj_scan_wanted(int64_t T, int64_t B, int64_t D, int64_t H);
+int proj_scan_forward(const void *x_split, const unsigned *x_scale, const float *w, const float *bias,
+                      const float *c0, float *z, float *out, float *c, float *h_n, float *c_n, int64_t T, int64_t B,
+                      int64_t D, int64_t H, float eps, void *ws, size_t ws_bytes, unsigned *kf, int *status,
+                      cudaStream_t st, bool *took, const char **why = nullptr);
 int scan_backward_split(float *z, const float *c, const float *c0, const float *dout, const float *dh_n,
                         const float *dc_n, const unsigned *kf_max, void *dz_split, unsigned *dz_scale, float *dc0,
                         float *db, int64_t T, int64_t B, int64_t H, float eps, void *ws_base, size_t ws_bytes,
@@ -262,9 +269,17 @@ size_t parallel_fused_ws(int64_t T, int64_t B, int64_t D, int64_t H) {
 // other); the last 256 bytes hold max |dz|, which the scan backward writes
 // and the gradient GEMMs' split reads.  The split-handoff backward's layout
 // (parallel_fused_ws) is covered as well.
+// The forward that runs the projection and the scan as one kernel needs
+// x's fp16 split and its scale word ahead of the kernel's own scratch.
+size_t proj_scan_fwd_ws(int64_t T, int64_t B, int64_t D, int64_t H) {
+  return round_up(h3_split_bytes(T * B, D), 256) + 256 + proj_scan_ws(T, B, D, H);
+}
+
 size_t parallel_ws_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
-  return std::max(std::max(scan_workspace(T, B, H), linear_ws_bytes(T * B, 4 * H, D)) + 256,
-                  parallel_fused_ws(T, B, D, H));
+  size_t b = std::max(std::max(scan_workspace(T, B, H), linear_ws_bytes(T * B, 4 * H, D)) + 256,
+                      parallel_fused_ws(T, B, D, H));
+  if (proj_scan_shape_ok(T, B, D, H)) b = std::max(b, proj_scan_fwd_ws(T, B, D, H));
+  return b;
 }
 
 // kf (device word, may be null): receives the forward's max of
@@ -275,6 +290,20 @@ int parallel_forward(const float *x, const float *c0, const float *w_ih, const f
                      cudaStream_t st, unsigned *kf = nullptr) {
   if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return fail(HS_ERR_INVALID_ARG, "T, B, D, H must be positive");
   if (!x || !w_ih || !z) return fail(HS_ERR_INVALID_ARG, "parallel_forward: null x/w_ih/z");
+  // The projection with the scan in its epilogue (one kernel, Z written for
+  // the backward but not read back), where the shape fills the GPU with it.
+  if (out && c && aligned(x, 16) && ws && aligned(ws, 256) && ws_bytes >= proj_scan_fwd_ws(T, B, D, H) &&
+      proj_scan_wanted(T, B, D, H)) {
+    char *w8 = static_cast<char *>(ws);
+    const size_t xb = round_up(h3_split_bytes(T * B, D), 256);
+    unsigned *x_scale = reinterpret_cast<unsigned *>(w8 + xb);
+    if (int e = h3_split(x, T * B, D, D, x_scale, w8, st)) return e;
+    bool took = false;
+    if (int e = proj_scan_forward(w8, x_scale, w_ih, b_ih, c0, z, out, c, h_n, c_n, T, B, D, H, eps, w8 + xb + 256,
+                                  ws_bytes - xb - 256, kf, status, st, &took))
+      return e;
+    if (took) return HS_OK;
+  }
   if (int e = linear_forward(x, w_ih, b_ih, z, T * B, 4 * H, D, ws, ws_bytes, status, st)) return e;
   return scan_forward(z, c0, out, c, h_n, c_n, T, B, H, eps, ws, ws_bytes, status, st, kf);
 }
@@ -568,6 +597,32 @@ int hs_linear_forward_presplit(const void *x_split, const unsigned *x_scale, con
     return e;
   return took ? HS_OK
               : hs::fail(HS_ERR_WORKSPACE, "hs_linear_forward_presplit: workspace too small or operands unaligned");
+}
+
+size_t hs_projection_scan_workspace_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
+  return (T > 0 && B > 0 && D > 0 && H > 0) ? hs::proj_scan_ws(T, B, D, H) : 0;
+}
+
+int hs_projection_scan_supported(int64_t T, int64_t B, int64_t D, int64_t H) {
+  return hs::proj_scan_wanted(T, B, D, H) ? 1 : 0;
+}
+
+int hs_projection_scan_forward(const void *x_split, const unsigned *x_scale, const float *w_ih, const float *b_ih,
+                               const float *c0, float *z, float *out, float *c, float *h_n, float *c_n, int64_t T,
+                               int64_t B, int64_t D, int64_t H, float eps, void *workspace, size_t workspace_bytes,
+                               unsigned *kf, int *dev_status, hs_stream_t stream) {
+  if (T <= 0 || B <= 0 || D <= 0 || H <= 0) return hs::fail(HS_ERR_INVALID_ARG, "T, B, D, H must be positive");
+  if (!x_split || !x_scale || !w_ih || !z || !out || !c || !dev_status)
+    return hs::fail(HS_ERR_INVALID_ARG, "hs_projection_scan_forward: null argument");
+  if (!hs::proj_scan_shape_ok(T, B, D, H))
+    return hs::fail(HS_ERR_UNSUPPORTED,
+                    "hs_projection_scan_forward: needs H %% 64 == 0 and a shape the fp16-split GEMMs take");
+  bool took = false;
+  const char *why = "";
+  if (int e = hs::proj_scan_forward(x_split, x_scale, w_ih, b_ih, c0, z, out, c, h_n, c_n, T, B, D, H, eps, workspace,
+                                    workspace_bytes, kf, dev_status, (cudaStream_t)stream, &took, &why))
+    return e;
+  return took ? HS_OK : hs::fail(HS_ERR_WORKSPACE, "hs_projection_scan_forward: %s", why);
 }
 
 int hs_linear_backward_presplit(const void *dy_split, const unsigned *dy_scale, const float *x, const void *x_split,

@@ -1,0 +1,665 @@
+// The input projection with the parallel-mode scan forward in its epilogue:
+// one persistent kernel computes Z = x.W_ih^T + b_ih on the tensor cores
+// (3 x fp16 split, 2-SM pairs, as the projection GEMM), and, per output
+// tile, the gates, the cell-state recurrence c_t = f'_t c_{t-1} + (i g)'_t,
+// out_t = o_t tanh(c_t), h_n, c_n and the backward's bound max c_{t-1}
+// f'(1-f').  Z is still written once (the backward reads it), but it is
+// never read back for the forward.
+//
+// Reference: the projection `linear(x, W_ih, b_ih)` followed by the gate
+// activations and the Heinsen scan, src/headstartlstm/_parallel.py:38-74
+// (log-domain scan restated as the clamped affine recurrence it computes,
+// _parallel.py:21-35).
+//
+// Tiles.  A tile is one pair of CTAs: each CTA takes 128 consecutive time
+// steps of ONE sequence (its TMA box runs along t with the sequence fixed:
+// x is [T, B, D], the box {64 k, 1 b, 128 t}), the two CTAs of a pair take
+// two sequences over the same steps, and both take the same block of 64
+// hidden units: the 256 output columns are gates i, f (the first CTA's half
+// of W_ih's rows) and g, o (the second's) of those units.  So every thread
+// of the epilogue holds all four gates of 32 units for one time step.
+//
+// Chains.  (sequence pair, unit block) is a chain; its time tiles follow
+// one another.  Tiles are numbered time-major, tile = tt * chains + chain,
+// and dealt round-robin to the resident pairs, which keeps every pair busy
+// (no chain is pinned to a pair).  A tile's carry-in (c just before its
+// first step) comes from the chain's previous tile through global memory:
+// per (sequence, 32-unit half) a flag counts the published tiles, the value
+// sits in a carry buffer.  The tile it waits for has a smaller number, and
+// every pair takes its tiles in increasing order, so the smallest unfinished
+// tile can always proceed (the grid never exceeds the resident pairs).
+// With chains >= pairs the tile waited for finished rounds earlier.
+//
+// The scan inside a tile: each warp holds 32 steps (lane = step) and runs
+// an inclusive Kogge-Stone scan of the affine maps (f', (i g)') over its
+// lanes per unit; the four warps' aggregates meet in shared memory, where
+// one warp composes the tile's total map, waits for the carry, publishes the
+// tile's end carry (end = A_total c_in + C_total) and hands c_in to the
+// others.  Every product of maps is of nonnegative terms (no cancellation).
+//
+// Every wait is bounded; a failed wait is made uniform across the 128
+// threads of an epilogue half by a reducing named barrier.  No cluster
+// multicast.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+
+#include "hs_common.cuh"
+#include "tc_dev.cuh"
+
+namespace hs {
+
+// from gemm_tc.cu / capi.cu
+size_t h3_split_bytes(int64_t rows, int64_t cols);
+int h3_split(const float *x, int64_t rows, int64_t cols, int64_t ld, unsigned *absmax, void *dst, cudaStream_t st);
+bool gemm_h3_enabled();
+bool gemm_tc_size_ok(int64_t M, int64_t N, int64_t K);
+
+namespace {
+
+constexpr int PS_BK = 64;                        // fp16 k per block: one 128-byte row
+constexpr int PS_TILE = 128 * PS_BK * 2;         // 16 KB per operand part per CTA
+constexpr int PS_STAGE = 4 * PS_TILE;            // Ah, Al, Bh, Bl
+constexpr int PS_STAGES = 3;
+constexpr int PS_PROM = 4;                       // k-blocks per accumulator group
+constexpr int PS_THREADS = 320;                  // producer, MMA, 2 x 4 epilogue warps
+constexpr int PS_TT = 128;                       // time steps per CTA tile
+constexpr int PS_UB = 64;                        // hidden units per chain
+constexpr int PS_BOX = 128 * 32 * 4;             // 16 KB staging box per epilogue half
+constexpr int PS_SMEM = PS_STAGES * PS_STAGE + 2 * PS_BOX + 1024 + 256;
+static_assert(PS_SMEM <= 232448, "shared memory per block");
+constexpr uint32_t PS_TMEM_COLS = 512;           // two 256-column accumulators
+constexpr uint32_t PS_ACC = 256;
+constexpr uint32_t PS_SBO = 8 * PS_BK * 2;       // 8-row core-matrix groups (1 KB)
+
+struct PsArgs {
+  const float *bias;            // b_ih [4H] or null
+  const float *c0;              // [B][H] or null
+  float *h_n, *c_n;             // [B][H] or null
+  float *carry;                 // [B][H] chain carries (scratch)
+  unsigned *flags;              // [B][H/64][2] published tiles per chain half (zeroed per call)
+  unsigned *kf;                 // max c_{t-1} f'(1-f') as float bits, or null
+  const unsigned *absmax_a;     // x's split scale word
+  const unsigned *absmax_b;     // W_ih's split scale word
+  int *status;
+  int T, B, H;
+  int nkb;                      // k-blocks over D
+  int nub;                      // unit blocks, H / 64
+  int nch;                      // chains, ceil(B / 2) * nub
+  int ntt;                      // time tiles, ceil(T / 128)
+  int ntiles;                   // ntt * nch
+  float eps;
+};
+
+HS_DEV void tma_3d_pair(void *dst, const CUtensorMap *tm, uint32_t bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(su32(dst)),
+      "l"(tm), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+
+// Named barrier of the 128 threads of one epilogue half that also ANDs a
+// predicate over them: every thread leaves with the same answer.
+HS_DEV bool named_and(int id, bool v) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.s32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, 128, p;\n\t"
+      "selp.s32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((int)v), "r"(id)
+      : "memory");
+  return r != 0;
+}
+
+// Wait until *flag >= want (acquire), bounded like every device wait.
+HS_DEV bool wait_count(const unsigned *flag, unsigned want, int *status) {
+  if (ld_acquire(flag) >= want) return true;
+  const uint64_t t0 = globaltimer();
+  unsigned n = 0;
+  while (ld_acquire(flag) < want) {
+    if ((++n & 63u) == 0) {
+      if (ld_status(status) != 0) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        set_status(status, HS_ERR_DEVICE_TIMEOUT);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// Stage NB 128-row x 32-column float boxes of this thread's row (v[OFF +
+// 32 k + j], k < NB) through the half's 16 KB box (128-byte swizzle,
+// conflict-free row-per-thread writes) and store box k with TMA at
+// (n0 + n_step k, b, t0).
+template <int NB, int OFF>
+HS_DEV void store_boxes(const float (&v)[128], float *box, const CUtensorMap *tm, int r, bool issuer, int bar,
+                        int n0, int n_step, int b, int t0) {
+#pragma unroll
+  for (int k = 0; k < NB; ++k) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int o = OFF + k * 32 + 4 * j;
+      *reinterpret_cast<float4 *>(box + r * 32 + ((j ^ (r & 7)) * 4)) = make_float4(v[o], v[o + 1], v[o + 2], v[o + 3]);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    named_sync(bar);
+    if (issuer) {
+      tma_store_3d(tm, box, n0 + n_step * k, b, t0);
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // box free again
+    }
+    named_sync(bar);
+  }
+}
+
+// Roles as in the projection's pair GEMM: warp 0 loads (both CTAs, each its
+// own rows; the bytes of both land on the first CTA's barrier), warp 1 of
+// the first CTA issues the MMAs, warps 2-9 of both CTAs fold the
+// accumulator groups and run the epilogue (two halves of four warps, one
+// per 32 units, thread = time step).
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PS_THREADS, 1)
+proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+                      const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
+                      const __grid_constant__ CUtensorMap tmZ, const __grid_constant__ CUtensorMap tmO,
+                      const __grid_constant__ CUtensorMap tmC, const PsArgs p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float *epi = reinterpret_cast<float *>(smem + PS_STAGES * PS_STAGE);  // two 16 KB boxes
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + PS_STAGES * PS_STAGE + 2 * PS_BOX);
+  uint64_t *empty = full + PS_STAGES;
+  uint64_t *pfull = empty + PS_STAGES;
+  uint64_t *pempty = pfull + 2;
+  uint64_t *mdone = pempty + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(mdone + 1);
+  int *abort_flag = reinterpret_cast<int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PS_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pfull[b], 1);
+      mbar_init(&pempty[b], 16);  // 8 epilogue warps x 2 CTAs (used in the first CTA)
+    }
+    mbar_init(mdone, 1);
+    *abort_flag = ld_status(p.status) != 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_holder)),
+                 "r"(PS_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync_all();  // barriers and TMEM of both CTAs ready before any cross-CTA use
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_holder;
+  const bool skip = *abort_flag != 0;
+
+  if (!skip && warp == 0) {
+    // ---------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      int it = 0, issued = 0;
+      bool ok = true;
+      const int g0 = 2 * (int)rank;  // gates i, f (first CTA) or g, o (second)
+      for (int tl = pair; tl < p.ntiles && ok; tl += npairs) {
+        const int tt = tl / p.nch, ch = tl - tt * p.nch;
+        const int bq = 2 * (ch / p.nub) + (int)rank;  // this CTA's sequence
+        const int u0 = (ch % p.nub) * PS_UB;
+        const int t0 = tt * PS_TT;
+        for (int i = 0; i < p.nkb; ++i, ++it) {
+          const int s = it % PS_STAGES;
+          const uint32_t ph = (it / PS_STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.status)) { ok = false; break; }
+          // pass a real release (not the first use of a stage) on to the
+          // second CTA first, so that its loads start with this CTA's
+          if (rank == 0 && it >= PS_STAGES) mbar_arrive_cluster(cluster_addr(&empty[s], 1));
+          const uint32_t fb = cluster_addr(&full[s], 0);
+          unsigned char *st = smem + s * PS_STAGE;
+          if (rank == 0) mbar_expect_tx(&full[s], 2 * PS_STAGE);  // both CTAs' bytes
+          const int k0 = i * PS_BK;
+          tma_3d_pair(st, &tmAh, fb, k0, bq, t0);
+          tma_3d_pair(st + PS_TILE, &tmAl, fb, k0, bq, t0);
+          // B: two 64-row boxes per part, gate g0's rows then gate g0+1's
+          tma_2d_pair(st + 2 * PS_TILE, &tmBh, fb, k0, g0 * p.H + u0);
+          tma_2d_pair(st + 2 * PS_TILE + PS_TILE / 2, &tmBh, fb, k0, (g0 + 1) * p.H + u0);
+          tma_2d_pair(st + 3 * PS_TILE, &tmBl, fb, k0, g0 * p.H + u0);
+          tma_2d_pair(st + 3 * PS_TILE + PS_TILE / 2, &tmBl, fb, k0, (g0 + 1) * p.H + u0);
+          ++issued;
+        }
+      }
+      // The first CTA's barrier counts both CTAs' bytes: never leave while a
+      // copy into either CTA's shared memory is in flight.
+      if (rank == 0) {
+        for (int j = std::max(0, issued - PS_STAGES); j < issued; ++j) {
+          if (ld_status(p.status)) mbar_drain(&full[j % PS_STAGES], (j / PS_STAGES) & 1);
+          else (void)mbar_wait(&full[j % PS_STAGES], (j / PS_STAGES) & 1, p.status);
+        }
+      }
+    }
+  } else if (!skip && warp == 1) {
+    // ---------------- MMA issuer (first CTA only): three fp16 products per
+    // k-step into one accumulator, groups of PS_PROM k-blocks
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(256, 256);
+      int it = 0, gg = 0;
+      bool ok = true;
+      for (int tl = pair; tl < p.ntiles && ok; tl += npairs) {
+        for (int i = 0; i < p.nkb; ++i, ++it) {
+          const int s = it % PS_STAGES;
+          const uint32_t ph = (it / PS_STAGES) & 1;
+          const bool gstart = (i % PS_PROM) == 0;
+          const int b = gg & 1;
+          if (gstart && !mbar_wait(&pempty[b], ((gg >> 1) & 1) ^ 1, p.status)) { ok = false; break; }
+          if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t ah = su32(smem + s * PS_STAGE);
+          const uint32_t al = ah + PS_TILE, bh = ah + 2 * PS_TILE, bl = ah + 3 * PS_TILE;
+          const uint32_t t_acc = tmem + (uint32_t)(b * PS_ACC);
+#pragma unroll
+          for (int kk = 0; kk < PS_BK / 16; ++kk) {
+            const uint32_t o = kk * 32;  // 16 fp16 = 32 bytes into each row
+            const uint64_t dAh = sdesc(ah + o, 16, PS_SBO, 2), dAl = sdesc(al + o, 16, PS_SBO, 2);
+            const uint64_t dBh = sdesc(bh + o, 16, PS_SBO, 2), dBl = sdesc(bl + o, 16, PS_SBO, 2);
+            mma_f16_pair(t_acc, dAh, dBh, idesc, (gstart && kk == 0) ? 0u : 1u);
+            mma_f16_pair(t_acc, dAh, dBl, idesc, 1u);
+            mma_f16_pair(t_acc, dAl, dBh, idesc, 1u);
+          }
+          mma_commit_pair(&empty[s]);
+          if ((i % PS_PROM) == PS_PROM - 1 || i == p.nkb - 1) {
+            mma_commit_pair(&pfull[b]);
+            ++gg;
+          }
+        }
+      }
+      // all issued MMAs complete before the CTAs may leave
+      mma_commit_pair(mdone);
+      if (ld_status(p.status)) mbar_drain(mdone, 0);
+      else (void)mbar_wait(mdone, 0, p.status);
+    }
+  } else if (!skip) {
+    // ---------------- epilogue (both CTAs)
+    const int e = warp - 2;           // 0..7
+    const int half = e >> 2;          // units 32 half .. 32 half + 31 of the chain's block
+    const int q = warp & 3;           // TMEM lane quarter: tile rows 32q .. 32q + 31
+    const int r = q * 32 + lane;      // tile row = time step t0 + r
+    const int bar = 1 + half;
+    const bool lead = (e & 3) == 0;   // the half's carry warp; its lane 0 issues the stores
+    const bool issuer = lead && lane == 0;
+    float *box = epi + half * (PS_BOX / 4);
+    float *aggA = box, *aggC = box + 128, *cin_s = box + 256;  // while the box is not staging
+    // Undo the two operand scales one at a time (each inverse is an exact
+    // power of two within float range, their product may not be).
+    const float inv_a = 1.0f / pow2_scale(*p.absmax_a), inv_b = 1.0f / pow2_scale(*p.absmax_b);
+    const uint32_t pe0 = cluster_addr(&pempty[0], 0), pe1 = cluster_addr(&pempty[1], 0);
+    const uint32_t pf0 = cluster_addr(&pfull[0], 1), pf1 = cluster_addr(&pfull[1], 1);
+    const int ngroups = (p.nkb + PS_PROM - 1) / PS_PROM;
+    const int H = p.H;
+    const float eps = p.eps;
+    float kmax = 0.f;
+    int gg = 0;
+    for (int tl = pair; tl < p.ntiles; tl += npairs) {
+      const int tt = tl / p.nch, ch = tl - tt * p.nch;
+      const int bq = 2 * (ch / p.nub) + (int)rank;
+      const int ub = ch % p.nub;
+      const int u0 = ub * PS_UB + 32 * half;
+      const int t0 = tt * PS_TT;
+      const bool bvalid = bq < p.B;
+      // v[32 gate + j]: gate (i, f, g, o) of unit u0 + j at step t0 + r
+      float v[128];
+#pragma unroll
+      for (int j = 0; j < 128; ++j) v[j] = 0.f;
+      bool ok = true;
+      for (int g = 0; g < ngroups; ++g, ++gg) {
+        const int b = gg & 1;
+        if (!mbar_wait(&pfull[b], (gg >> 1) & 1, p.status)) { ok = false; break; }
+        if (rank == 0 && e == 0 && lane == 0) mbar_arrive_cluster(b ? pf1 : pf0);  // tell the second CTA
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * PS_ACC) + (uint32_t)(32 * half);
+#pragma unroll
+        for (int gate = 0; gate < 4; ++gate) {
+#pragma unroll
+          for (int c = 0; c < 32; c += 16) {
+            float w[16];
+            tmem_ld16(base + (uint32_t)(gate * 64 + c), w);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) v[gate * 32 + c + k] += w[k];
+          }
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(b ? pe1 : pe0);
+      }
+      if (!named_and(bar, ok && ld_status(p.status) == 0)) break;
+
+      // Z = acc / (s_A s_B) + b_ih, stored for the backward (one box per gate)
+#pragma unroll
+      for (int gate = 0; gate < 4; ++gate) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 bb = p.bias ? *reinterpret_cast<const float4 *>(p.bias + gate * H + u0 + j)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+          const int o = gate * 32 + j;
+          v[o] = (v[o] * inv_a) * inv_b + bb.x;
+          v[o + 1] = (v[o + 1] * inv_a) * inv_b + bb.y;
+          v[o + 2] = (v[o + 2] * inv_a) * inv_b + bb.z;
+          v[o + 3] = (v[o + 3] * inv_a) * inv_b + bb.w;
+        }
+      }
+      store_boxes<4, 0>(v, box, &tmZ, r, issuer, bar, u0, H, bq, t0);
+
+      // gates, then each warp's inclusive scan of the step maps over its 32
+      // steps: c_r = A_r c_in + C_r (v[j] <- A, v[64 + j] <- C, v[32 + j] <-
+      // f', v[96 + j] <- e^-o)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float fp = fmaxf(sigf(v[32 + j]), eps);
+        float C = fmaxf(sig2(v[j], v[64 + j]), eps);
+        float A = fp;
+        v[32 + j] = fp;
+        v[96 + j] = __expf(-v[96 + j]);
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const float Ap = __shfl_up_sync(0xffffffffu, A, off), Cp = __shfl_up_sync(0xffffffffu, C, off);
+          if (lane >= off) {
+            C = fmaf(A, Cp, C);
+            A *= Ap;
+          }
+        }
+        v[j] = A;
+        v[64 + j] = C;
+      }
+      if (lane == 31) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          aggA[q * 32 + j] = v[j];
+          aggC[q * 32 + j] = v[64 + j];
+        }
+      }
+      named_sync(bar);
+
+      // The carry warp (lane = unit): the tile's total map, the chain's carry
+      // in, the tile's end carry out (published before the outputs are made).
+      bool good = true;
+      if (lead) {
+        float At = aggA[lane], Ct = aggC[lane];
+#pragma unroll
+        for (int k = 1; k < 4; ++k) {
+          const float a = aggA[k * 32 + lane];
+          Ct = fmaf(a, Ct, aggC[k * 32 + lane]);
+          At *= a;
+        }
+        float cin = eps;
+        if (bvalid) {
+          const int64_t ci = (int64_t)bq * H + u0 + lane;
+          unsigned *flag = p.flags + ((int64_t)bq * p.nub + ub) * 2 + half;
+          if (tt == 0) cin = fmaxf(p.c0 ? p.c0[ci] : 0.f, eps);
+          else if (wait_count(flag, (unsigned)tt, p.status)) cin = __ldcg(p.carry + ci);
+          else good = false;
+          good = __all_sync(0xffffffffu, good);
+          if (good && tt + 1 < p.ntt) {
+            __stcg(p.carry + ci, fmaf(At, cin, Ct));
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) st_release(flag, (unsigned)(tt + 1));
+          }
+        }
+        cin_s[lane] = cin;
+      }
+      if (!named_and(bar, good && ld_status(p.status) == 0)) break;
+
+      // c, out and the backward's bound at every step of this warp
+      const bool rvalid = bvalid && t0 + r < p.T;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float cw = cin_s[j];  // c just before this warp's first step
+        for (int k = 0; k < q; ++k) cw = fmaf(aggA[k * 32 + j], cw, aggC[k * 32 + j]);
+        const float c = fmaf(v[j], cw, v[64 + j]);
+        float cprev = __shfl_up_sync(0xffffffffu, c, 1);
+        if (lane == 0) cprev = cw;
+        const float fp = v[32 + j];
+        if (rvalid) kmax = fmaxf(kmax, cprev * fp * (1.f - fp));
+        v[64 + j] = c;
+        v[j] = sig_tanh_pos(v[96 + j], c);
+      }
+      named_sync(bar);  // the aggregates are read before the box stages again
+      store_boxes<1, 64>(v, box, &tmC, r, issuer, bar, u0, 0, bq, t0);
+      store_boxes<1, 0>(v, box, &tmO, r, issuer, bar, u0, 0, bq, t0);
+      if (rvalid && t0 + r == p.T - 1) {
+        const int64_t ci = (int64_t)bq * H + u0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (p.h_n) p.h_n[ci + j] = v[j];
+          if (p.c_n) p.c_n[ci + j] = v[64 + j];
+        }
+      }
+    }
+    if (p.kf) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) kmax = fmaxf(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+      if (lane == 0) atomicMax(p.kf, __float_as_uint(kmax));
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncwarp();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA frees TMEM or leaves while the pair's work may touch it
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PS_TMEM_COLS) : "memory");
+  }
+}
+
+
+// ---------------------------------------------------------------- host side
+// x split [T*B][ld] fp16 as the 3D tensor {ld, B, T}: box {64 k, 1 b, 128 t}.
+bool make_map_x(CUtensorMap *tm, const __half *ptr, int64_t T, int64_t B, int64_t ld) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)ld, (cuuint64_t)B, (cuuint64_t)T};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)(B * ld * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)PS_BK, 1, (cuuint32_t)PS_TT};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, (void *)ptr, dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// W_ih split [4H][ld] fp16: box {64 k, 64 rows} (one gate's rows of a chain).
+bool make_map_w(CUtensorMap *tm, const __half *ptr, int64_t rows, int64_t ld) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)PS_BK, (cuuint32_t)PS_UB};
+  cuuint32_t es[2] = {1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)ptr, dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// [T][B][N] float32 output as {N, B, T}: box {32 columns, 1 b, 128 t},
+// 128-byte swizzle (the epilogue's staging layout).
+bool make_map_tbn(CUtensorMap *tm, float *ptr, int64_t T, int64_t B, int64_t N) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)B, (cuuint64_t)T};
+  cuuint64_t strides[2] = {(cuuint64_t)N * 4, (cuuint64_t)(B * N * 4)};
+  cuuint32_t box[3] = {32, 1, (cuuint32_t)PS_TT};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)ptr, dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+std::atomic<unsigned long long> g_ps_attr{0};
+char g_ps_cap_msg[256] = "";
+
+// Pairs of this kernel resident at once on the current device (0: none,
+// g_ps_cap_msg says why).
+int ps_capacity() {
+  static std::atomic<int> cached[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::atomic<int> &c = cached[dev & 63];
+  int v = c.load(std::memory_order_relaxed);
+  if (v > 0) return v - 1;
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (allow_dynamic_smem((const void *)proj_scan_pair_kernel, PS_SMEM, &g_ps_attr) != HS_OK) {
+    snprintf(g_ps_cap_msg, sizeof(g_ps_cap_msg), "setting %d bytes of dynamic shared memory failed", PS_SMEM);
+    (void)cudaGetLastError();
+    return 0;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (unsigned)std::max(sms, 2), 1, 1);
+  cfg.blockDim = dim3(PS_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = PS_SMEM;
+  int n = 0;
+  const cudaError_t err = cudaOccupancyMaxActiveClusters(&n, (const void *)proj_scan_pair_kernel, &cfg);
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = 0;
+  }
+  if (n < 1) {
+    cudaFuncAttributes fa = {};
+    (void)cudaFuncGetAttributes(&fa, (const void *)proj_scan_pair_kernel);
+    (void)cudaGetLastError();
+    snprintf(g_ps_cap_msg, sizeof(g_ps_cap_msg),
+             "cluster occupancy %d (%s); kernel: %d registers, %zu static + %d dynamic smem bytes, max %d threads",
+             n, cudaGetErrorString(err), fa.numRegs, fa.sharedSizeBytes, PS_SMEM, fa.maxThreadsPerBlock);
+  }
+  c.store(n + 1, std::memory_order_relaxed);
+  return n;
+}
+
+// HS_PROJ_SCAN: 0 never takes the fused kernel, 1 takes it for every shape
+// it can run (tests of small shapes); unset, it is taken when the chains
+// fill the resident pairs or the sequence fits one time tile.
+int ps_mode() {
+  static int v = -2;
+  if (v == -2) {
+    const char *e = getenv("HS_PROJ_SCAN");
+    v = (e && e[0] == '0') ? 0 : (e && e[0] == '1') ? 1 : -1;
+  }
+  return v;
+}
+
+int64_t ps_round8(int64_t x) { return (x + 7) / 8 * 8; }
+
+}  // namespace
+
+size_t proj_scan_ws(int64_t T, int64_t B, int64_t D, int64_t H) {
+  (void)T;
+  if (B <= 0 || D <= 0 || H <= 0) return 0;
+  return 256 + h3_split_bytes(4 * H, D) + round_up((size_t)B * H * 4, 256) +
+         round_up((size_t)B * ((H + PS_UB - 1) / PS_UB) * 2 * 4, 256);
+}
+
+// Shapes the fused kernel can run: 64-unit chain blocks, int32 tile and
+// coordinate arithmetic, the fp16-split tensor-core GEMMs enabled.
+bool proj_scan_shape_ok(int64_t T, int64_t B, int64_t D, int64_t H) {
+  if (T <= 0 || B <= 0 || D <= 0 || H <= 0 || H % PS_UB) return false;
+  if (T >= (1ll << 30) || B >= (1ll << 30) || 4 * H >= (1ll << 30) || T * B >= (1ll << 31)) return false;
+  const int64_t ntt = (T + PS_TT - 1) / PS_TT, nch = (B + 1) / 2 * (H / PS_UB);
+  if (ntt * nch >= (1ll << 31) || D >= (1ll << 30)) return false;
+  return gemm_h3_enabled() && gemm_tc_size_ok(T * B, 4 * H, D);
+}
+
+bool proj_scan_wanted(int64_t T, int64_t B, int64_t D, int64_t H) {
+  const int mode = ps_mode();
+  if (mode == 0 || !proj_scan_shape_ok(T, B, D, H)) return false;
+  const int npairs = ps_capacity();
+  if (npairs < 1) return false;
+  if (mode == 1) return true;
+  const int64_t ntt = (T + PS_TT - 1) / PS_TT, nch = (B + 1) / 2 * (H / PS_UB);
+  return ntt == 1 || nch >= npairs;
+}
+
+// Z, out, c [T][B][4H | H | H], h_n, c_n and *kf (max c_{t-1} f'(1-f')) from
+// x's fp16 split (hs_split layout, with its scale word) and float32 W_ih,
+// b_ih, c0.  *took = false (nothing launched, *why says which condition) if
+// the shape, the alignment or the scratch does not suit; the caller then
+// runs the GEMM and the scan.
+int proj_scan_forward(const void *x_split, const unsigned *x_scale, const float *w, const float *bias,
+                      const float *c0, float *z, float *out, float *c, float *h_n, float *c_n, int64_t T, int64_t B,
+                      int64_t D, int64_t H, float eps, void *ws, size_t ws_bytes, unsigned *kf, int *status,
+                      cudaStream_t st, bool *took, const char **why) {
+  *took = false;
+  const char *dummy = nullptr;
+  if (!why) why = &dummy;
+  *why = "shape or null argument";
+  if (!proj_scan_shape_ok(T, B, D, H) || !status || !x_split || !x_scale || !w || !z || !out || !c) return HS_OK;
+  *why = "x_split, z, out, c or b_ih not 16-byte aligned";
+  if (!aligned(x_split, 16) || !aligned(z, 16) || !aligned(out, 16) || !aligned(c, 16) ||
+      (bias && !aligned(bias, 16)) || (kf && !aligned(kf, 4)))
+    return HS_OK;
+  *why = "workspace missing, not 256-byte aligned or too small";
+  if (!ws || !aligned(ws, 256) || ws_bytes < proj_scan_ws(T, B, D, H)) return HS_OK;
+  const int npairs = ps_capacity();
+  *why = g_ps_cap_msg;
+  if (npairs < 1) return HS_OK;
+  const int64_t D8 = ps_round8(D), N = 4 * H;
+  char *w8 = static_cast<char *>(ws);
+  unsigned *w_scale = reinterpret_cast<unsigned *>(w8);
+  __half *wh = reinterpret_cast<__half *>(w8 + 256);
+  const __half *wl = wh + N * D8;
+  float *carry = reinterpret_cast<float *>(w8 + 256 + h3_split_bytes(N, D));
+  unsigned *flags = reinterpret_cast<unsigned *>(reinterpret_cast<char *>(carry) + round_up((size_t)B * H * 4, 256));
+  const size_t flag_bytes = (size_t)B * (H / PS_UB) * 2 * 4;
+  const __half *xh = static_cast<const __half *>(x_split);
+  const __half *xl = xh + T * B * D8;
+  CUtensorMap tah, tal, tbh, tbl, tz, to, tc;
+  if (!make_map_x(&tah, xh, T, B, D8) || !make_map_x(&tal, xl, T, B, D8) || !make_map_w(&tbh, wh, N, D8) ||
+      !make_map_w(&tbl, wl, N, D8) || !make_map_tbn(&tz, z, T, B, N) || !make_map_tbn(&to, out, T, B, H) ||
+      !make_map_tbn(&tc, c, T, B, H)) {
+    *why = "tensor-map encoding failed";
+    return HS_OK;
+  }
+  if (int e = h3_split(w, N, D, D, w_scale, wh, st)) return e;
+  if (cudaMemsetAsync(flags, 0, flag_bytes, st) != cudaSuccess) return check_launch("proj_scan flags memset");
+  if (kf && cudaMemsetAsync(kf, 0, 4, st) != cudaSuccess) return check_launch("proj_scan kf memset");
+  PsArgs a;
+  a.bias = bias;
+  a.c0 = c0;
+  a.h_n = h_n;
+  a.c_n = c_n;
+  a.carry = carry;
+  a.flags = flags;
+  a.kf = kf;
+  a.absmax_a = x_scale;
+  a.absmax_b = w_scale;
+  a.status = status;
+  a.T = (int)T;
+  a.B = (int)B;
+  a.H = (int)H;
+  a.nkb = (int)((D8 + PS_BK - 1) / PS_BK);
+  a.nub = (int)(H / PS_UB);
+  a.nch = (int)((B + 1) / 2 * a.nub);
+  a.ntt = (int)((T + PS_TT - 1) / PS_TT);
+  a.ntiles = a.ntt * a.nch;
+  a.eps = eps;
+  if (int e = allow_dynamic_smem((const void *)proj_scan_pair_kernel, PS_SMEM, &g_ps_attr)) return e;
+  const unsigned grid = 2u * (unsigned)std::min<int64_t>(a.ntiles, npairs);
+  proj_scan_pair_kernel<<<grid, PS_THREADS, PS_SMEM, st>>>(tah, tal, tbh, tbl, tz, to, tc, a);
+  if (int e = check_launch("proj_scan_pair_kernel")) return e;
+  *took = true;
+  return HS_OK;
+}
+
+}  // namespace hs
