@@ -208,11 +208,11 @@ HS_API int hs_scan_forward_kf(const float *z, const float *c0, float *out, float
  * [T*B][D]) on the tensor cores, with the gates, the scan, out, c, h_n, c_n
  * and *kf (as hs_scan_forward_kf; may be NULL) computed in the GEMM's
  * epilogue.  z [T,B,4H] is written for the backward but never read back.
- * Needs H % 64 == 0, 16-byte aligned z, out, c, x_split (and b_ih if given)
+ * Needs H % 32 == 0, 16-byte aligned z, out, c, x_split (and b_ih if given)
  * and dev_status; workspace >= hs_projection_scan_workspace_bytes (256-byte
  * aligned).  hs_projection_scan_supported says whether the library's own
  * forward (hs_parallel_forward*) takes this kernel for a shape by default
- * (it does when the (sequence pair, 64-unit block) chains fill the GPU, or
+ * (it does when the (sequence pair, 32-unit block) chains fill the GPU, or
  * T <= 128); HS_PROJ_SCAN=0 / 1 turns that off / on for every shape it can
  * run.  Replaces, with hs_split, the projection `linear` and the scan of
  * headstartlstm_parallel (_parallel.py:38-74, _parallel.py:21-35). */

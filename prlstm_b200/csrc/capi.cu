@@ -616,7 +616,7 @@ int hs_projection_scan_forward(const void *x_split, const unsigned *x_scale, con
     return hs::fail(HS_ERR_INVALID_ARG, "hs_projection_scan_forward: null argument");
   if (!hs::proj_scan_shape_ok(T, B, D, H))
     return hs::fail(HS_ERR_UNSUPPORTED,
-                    "hs_projection_scan_forward: needs H %% 64 == 0 and a shape the fp16-split GEMMs take");
+                    "hs_projection_scan_forward: needs H %% 32 == 0 and a shape the fp16-split GEMMs take");
   bool took = false;
   const char *why = "";
   if (int e = hs::proj_scan_forward(x_split, x_scale, w_ih, b_ih, c0, z, out, c, h_n, c_n, T, B, D, H, eps, workspace,

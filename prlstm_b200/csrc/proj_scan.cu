@@ -14,18 +14,22 @@
 // Tiles.  A tile is one pair of CTAs: each CTA takes 128 consecutive time
 // steps of ONE sequence (its TMA box runs along t with the sequence fixed:
 // x is [T, B, D], the box {64 k, 1 b, 128 t}), the two CTAs of a pair take
-// two sequences over the same steps, and both take the same block of 64
-// hidden units: the 256 output columns are gates i, f (the first CTA's half
+// two sequences over the same steps, and both take the same block of 32
+// hidden units: the 128 output columns are gates i, f (the first CTA's half
 // of W_ih's rows) and g, o (the second's) of those units.  So every thread
-// of the epilogue holds all four gates of 32 units for one time step.
+// of the epilogue holds all four gates of its units for one time step: four
+// quads of four warps split the block's 32 units, 8 per thread (32 values
+// in registers, four warps per scheduler to hide each other's latency).
+// Four TMEM accumulators of 128 columns let the MMAs run up to two tiles
+// ahead of the epilogue.
 //
 // Chains.  (sequence pair, unit block) is a chain; its time tiles follow
 // one another.  Tiles are numbered time-major, tile = tt * chains + chain,
 // and dealt round-robin to the resident pairs, which keeps every pair busy
 // (no chain is pinned to a pair).  A tile's carry-in (c just before its
 // first step) comes from the chain's previous tile through global memory:
-// per (sequence, 32-unit half) a flag counts the published tiles, the value
-// sits in a carry buffer.  The tile it waits for has a smaller number, and
+// per (sequence, unit) one 64-bit word holds the carry and the number of the
+// tile it is for.  The tile it waits for has a smaller number, and
 // every pair takes its tiles in increasing order, so the smallest unfinished
 // tile can always proceed (the grid never exceeds the resident pairs).
 // With chains >= pairs the tile waited for finished rounds earlier.
@@ -38,7 +42,7 @@
 // others.  Every product of maps is of nonnegative terms (no cancellation).
 //
 // Every wait is bounded; a failed wait is made uniform across the 128
-// threads of an epilogue half by a reducing named barrier.  No cluster
+// threads of an epilogue quad by a reducing named barrier.  No cluster
 // multicast.
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -62,33 +66,40 @@ bool gemm_tc_size_ok(int64_t M, int64_t N, int64_t K);
 namespace {
 
 constexpr int PS_BK = 64;                        // fp16 k per block: one 128-byte row
-constexpr int PS_TILE = 128 * PS_BK * 2;         // 16 KB per operand part per CTA
-constexpr int PS_STAGE = 4 * PS_TILE;            // Ah, Al, Bh, Bl
+constexpr int PS_TT = 128;                       // time steps per CTA tile (TMEM lanes)
+constexpr int PS_UB = 32;                        // hidden units per chain
+constexpr int PS_N = 4 * PS_UB;                  // output columns per pair tile (4 gates)
+constexpr int PS_ATILE = PS_TT * PS_BK * 2;      // 16 KB: one A part (x hi or lo) per CTA
+constexpr int PS_BGATE = PS_UB * PS_BK * 2;      // 4 KB: one gate's rows of one B part
+constexpr int PS_BTILE = 2 * PS_BGATE;           // 8 KB: a CTA's half of one B part
+constexpr int PS_STAGE = 2 * PS_ATILE + 2 * PS_BTILE;  // 48 KB: Ah, Al, Bh, Bl
 constexpr int PS_STAGES = 3;
 constexpr int PS_PROM = 4;                       // k-blocks per accumulator group
-constexpr int PS_THREADS = 320;                  // producer, MMA, 2 x 4 epilogue warps
-constexpr int PS_TT = 128;                       // time steps per CTA tile
-constexpr int PS_UB = 64;                        // hidden units per chain
-constexpr int PS_BOX = 128 * 32 * 4;             // 16 KB staging box per epilogue half
-constexpr int PS_SMEM = PS_STAGES * PS_STAGE + 2 * PS_BOX + 1024 + 256;
+constexpr int PS_NACC = 4;                       // accumulator buffers (PS_N TMEM columns each)
+constexpr int PS_NQ = 4;                         // epilogue quads (4 warps each)
+constexpr int PS_QU = PS_UB / PS_NQ;             // units per quad
+constexpr int PS_THREADS = 64 + PS_NQ * 128;     // producer, MMA, 16 epilogue warps
+constexpr int PS_BOX = PS_TT * PS_QU * 4;        // 4 KB staging box (32-byte rows)
+constexpr int PS_NBUF = 4;                       // staging boxes per quad
+constexpr int PS_AGG = 12 * PS_QU;               // per quad: 4 row blocks x (A, C, carry in)
+constexpr int PS_SMEM = PS_STAGES * PS_STAGE + PS_NQ * (PS_NBUF * PS_BOX + PS_AGG * 4) + 1024 + 256;
 static_assert(PS_SMEM <= 232448, "shared memory per block");
-constexpr uint32_t PS_TMEM_COLS = 512;           // two 256-column accumulators
-constexpr uint32_t PS_ACC = 256;
+static_assert(PS_QU == 8, "the epilogue's boxes and TMEM loads are 8 columns wide");
+constexpr uint32_t PS_TMEM_COLS = PS_NACC * PS_N;  // 512
 constexpr uint32_t PS_SBO = 8 * PS_BK * 2;       // 8-row core-matrix groups (1 KB)
 
 struct PsArgs {
   const float *bias;            // b_ih [4H] or null
   const float *c0;              // [B][H] or null
   float *h_n, *c_n;             // [B][H] or null
-  float *carry;                 // [B][H] chain carries (scratch)
-  unsigned *flags;              // [B][H/64][2] published tiles per chain half (zeroed per call)
+  unsigned long long *slots;    // [B][H] chain carries: (tile tag << 32) | float bits (zeroed per call)
   unsigned *kf;                 // max c_{t-1} f'(1-f') as float bits, or null
   const unsigned *absmax_a;     // x's split scale word
   const unsigned *absmax_b;     // W_ih's split scale word
   int *status;
   int T, B, H;
   int nkb;                      // k-blocks over D
-  int nub;                      // unit blocks, H / 64
+  int nub;                      // unit blocks, H / 32
   int nch;                      // chains, ceil(B / 2) * nub
   int ntt;                      // time tiles, ceil(T / 128)
   int ntiles;                   // ntt * nch
@@ -103,7 +114,7 @@ HS_DEV void tma_3d_pair(void *dst, const CUtensorMap *tm, uint32_t bar, int c0, 
       : "memory");
 }
 
-// Named barrier of the 128 threads of one epilogue half that also ANDs a
+// Named barrier of the 128 threads of one epilogue quad that also ANDs a
 // predicate over them: every thread leaves with the same answer.
 HS_DEV bool named_and(int id, bool v) {
   int r;
@@ -118,13 +129,44 @@ HS_DEV bool named_and(int id, bool v) {
   return r != 0;
 }
 
-// Wait until *flag >= want (acquire), bounded like every device wait.
-HS_DEV bool wait_count(const unsigned *flag, unsigned want, int *status) {
-  if (ld_acquire(flag) >= want) return true;
-  const uint64_t t0 = globaltimer();
-  unsigned n = 0;
-  while (ld_acquire(flag) < want) {
-    if ((++n & 63u) == 0) {
+// Eight TMEM columns of this warp's 32 lanes, no wait: the registers are
+// valid only after tmem_wait_ld below, which takes them as operands so that
+// no use is scheduled ahead of it.
+HS_DEV void tmem_ld8_nowait(uint32_t taddr, uint32_t *r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+HS_DEV void tmem_wait_ld(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+        "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+        "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+        "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
+
+// A chain's carry: one 64-bit word per (sequence, unit) holding the value
+// and the number of the time tile that follows it, written and read whole
+// (single-copy atomic), so the value needs no fence or flag of its own.
+HS_DEV void gslot_put(unsigned long long *s, unsigned tag, float v) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(s), "l"(w) : "memory");
+}
+// Waits (bounded) for tag in *s and returns its value in *v.
+HS_DEV bool gslot_wait(const unsigned long long *s, unsigned tag, float *v, int *status) {
+  uint64_t t0 = 0;
+  for (unsigned n = 0;; ++n) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(s) : "memory");
+    if ((unsigned)(w >> 32) == tag) {
+      *v = __uint_as_float((unsigned)w);
+      return true;
+    }
+    if ((n & 63u) == 63u) {
+      if (t0 == 0) t0 = globaltimer();
       if (ld_status(status) != 0) return false;
       if (globaltimer() - t0 > kWaitLimitNs) {
         set_status(status, HS_ERR_DEVICE_TIMEOUT);
@@ -132,39 +174,46 @@ HS_DEV bool wait_count(const unsigned *flag, unsigned want, int *status) {
       }
     }
   }
-  return true;
 }
 
-// Stage NB 128-row x 32-column float boxes of this thread's row (v[OFF +
-// 32 k + j], k < NB) through the half's 16 KB box (128-byte swizzle,
-// conflict-free row-per-thread writes) and store box k with TMA at
-// (n0 + n_step k, b, t0).
-template <int NB, int OFF>
-HS_DEV void store_boxes(const float (&v)[128], float *box, const CUtensorMap *tm, int r, bool issuer, int bar,
-                        int n0, int n_step, int b, int t0) {
+// Stage two 128-row x 8-column float boxes of this thread's row (v[OFF0 ..
+// OFF0 + 7] and v[OFF1 .. OFF1 + 7]) in one of the quad's two pairs of
+// staging buffers and store them with TMA at (n0, b, t0) and (n1, b, t0),
+// one bulk group.  The pairs alternate (sp counts the quad's staged pairs):
+// this pair is free on entry, and before the barrier that releases this
+// pair's stores the issuer waits for the OTHER pair's stores (issued one
+// stage of work earlier) to have read it, so the next call finds its pair
+// free without waiting on the stores just issued.  32-byte rows with the
+// 32-byte swizzle: the 16-byte chunk c of row r sits at chunk c ^ ((r >> 2)
+// & 1).
+template <int OFF0, int OFF1>
+HS_DEV void store_two(const float (&v)[4 * PS_QU], float *stg, int &sp, const CUtensorMap *tm0,
+                      const CUtensorMap *tm1, int r, bool issuer, int bar, int n0, int n1, int b, int t0) {
+  float *b0 = stg + (sp & 1) * 2 * (PS_BOX / 4), *b1 = b0 + PS_BOX / 4;
 #pragma unroll
-  for (int k = 0; k < NB; ++k) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int o = OFF + k * 32 + 4 * j;
-      *reinterpret_cast<float4 *>(box + r * 32 + ((j ^ (r & 7)) * 4)) = make_float4(v[o], v[o + 1], v[o + 2], v[o + 3]);
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    named_sync(bar);
-    if (issuer) {
-      tma_store_3d(tm, box, n0 + n_step * k, b, t0);
-      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // box free again
-    }
-    named_sync(bar);
+  for (int c = 0; c < 2; ++c) {
+    const int o = r * PS_QU + ((c ^ ((r >> 2) & 1)) * 4);
+    *reinterpret_cast<float4 *>(b0 + o) =
+        make_float4(v[OFF0 + 4 * c], v[OFF0 + 4 * c + 1], v[OFF0 + 4 * c + 2], v[OFF0 + 4 * c + 3]);
+    *reinterpret_cast<float4 *>(b1 + o) =
+        make_float4(v[OFF1 + 4 * c], v[OFF1 + 4 * c + 1], v[OFF1 + 4 * c + 2], v[OFF1 + 4 * c + 3]);
   }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the other pair is read
+  named_sync(bar);
+  if (issuer) {
+    tma_store_3d(tm0, b0, n0, b, t0);
+    tma_store_3d(tm1, b1, n1, b, t0);
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  }
+  ++sp;
 }
 
 // Roles as in the projection's pair GEMM: warp 0 loads (both CTAs, each its
 // own rows; the bytes of both land on the first CTA's barrier), warp 1 of
-// the first CTA issues the MMAs, warps 2-9 of both CTAs fold the
-// accumulator groups and run the epilogue (two halves of four warps, one
-// per 32 units, thread = time step).
+// the first CTA issues the MMAs, warps 2-17 of both CTAs fold the
+// accumulator groups and run the epilogue (four quads of four warps, one
+// per 8 units, thread = time step).
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PS_THREADS, 1)
 proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                       const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
@@ -173,12 +222,13 @@ proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_con
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float *epi = reinterpret_cast<float *>(smem + PS_STAGES * PS_STAGE);  // two 16 KB boxes
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + PS_STAGES * PS_STAGE + 2 * PS_BOX);
+  float *epi = reinterpret_cast<float *>(smem + PS_STAGES * PS_STAGE);  // 4 quads x PS_NBUF staging boxes
+  float *aggs = epi + PS_NQ * PS_NBUF * (PS_BOX / 4);                   // 4 quads x PS_AGG floats
+  uint64_t *full = reinterpret_cast<uint64_t *>(aggs + PS_NQ * PS_AGG);
   uint64_t *empty = full + PS_STAGES;
   uint64_t *pfull = empty + PS_STAGES;
-  uint64_t *pempty = pfull + 2;
-  uint64_t *mdone = pempty + 2;
+  uint64_t *pempty = pfull + PS_NACC;
+  uint64_t *mdone = pempty + PS_NACC;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(mdone + 1);
   int *abort_flag = reinterpret_cast<int *>(tmem_holder + 1);
 
@@ -191,9 +241,9 @@ proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_con
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < PS_NACC; ++b) {
       mbar_init(&pfull[b], 1);
-      mbar_init(&pempty[b], 16);  // 8 epilogue warps x 2 CTAs (used in the first CTA)
+      mbar_init(&pempty[b], 2 * PS_NQ * 4);  // 16 epilogue warps x 2 CTAs (used in the first CTA)
     }
     mbar_init(mdone, 1);
     *abort_flag = ld_status(p.status) != 0;
@@ -235,12 +285,13 @@ proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_con
           if (rank == 0) mbar_expect_tx(&full[s], 2 * PS_STAGE);  // both CTAs' bytes
           const int k0 = i * PS_BK;
           tma_3d_pair(st, &tmAh, fb, k0, bq, t0);
-          tma_3d_pair(st + PS_TILE, &tmAl, fb, k0, bq, t0);
-          // B: two 64-row boxes per part, gate g0's rows then gate g0+1's
-          tma_2d_pair(st + 2 * PS_TILE, &tmBh, fb, k0, g0 * p.H + u0);
-          tma_2d_pair(st + 2 * PS_TILE + PS_TILE / 2, &tmBh, fb, k0, (g0 + 1) * p.H + u0);
-          tma_2d_pair(st + 3 * PS_TILE, &tmBl, fb, k0, g0 * p.H + u0);
-          tma_2d_pair(st + 3 * PS_TILE + PS_TILE / 2, &tmBl, fb, k0, (g0 + 1) * p.H + u0);
+          tma_3d_pair(st + PS_ATILE, &tmAl, fb, k0, bq, t0);
+          // B: two PS_UB-row boxes per part, gate g0's rows then gate g0+1's
+          unsigned char *sb = st + 2 * PS_ATILE;
+          tma_2d_pair(sb, &tmBh, fb, k0, g0 * p.H + u0);
+          tma_2d_pair(sb + PS_BGATE, &tmBh, fb, k0, (g0 + 1) * p.H + u0);
+          tma_2d_pair(sb + PS_BTILE, &tmBl, fb, k0, g0 * p.H + u0);
+          tma_2d_pair(sb + PS_BTILE + PS_BGATE, &tmBl, fb, k0, (g0 + 1) * p.H + u0);
           ++issued;
         }
       }
@@ -255,9 +306,10 @@ proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_con
     }
   } else if (!skip && warp == 1) {
     // ---------------- MMA issuer (first CTA only): three fp16 products per
-    // k-step into one accumulator, groups of PS_PROM k-blocks
+    // k-step into one accumulator, groups of PS_PROM k-blocks, PS_NACC
+    // accumulator buffers in turn
     if (rank == 0 && lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(256, 256);
+      constexpr uint32_t idesc = idesc_f16(256, PS_N);
       int it = 0, gg = 0;
       bool ok = true;
       for (int tl = pair; tl < p.ntiles && ok; tl += npairs) {
@@ -265,13 +317,13 @@ proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_con
           const int s = it % PS_STAGES;
           const uint32_t ph = (it / PS_STAGES) & 1;
           const bool gstart = (i % PS_PROM) == 0;
-          const int b = gg & 1;
-          if (gstart && !mbar_wait(&pempty[b], ((gg >> 1) & 1) ^ 1, p.status)) { ok = false; break; }
+          const int b = gg % PS_NACC;
+          if (gstart && !mbar_wait(&pempty[b], ((gg / PS_NACC) & 1) ^ 1, p.status)) { ok = false; break; }
           if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t ah = su32(smem + s * PS_STAGE);
-          const uint32_t al = ah + PS_TILE, bh = ah + 2 * PS_TILE, bl = ah + 3 * PS_TILE;
-          const uint32_t t_acc = tmem + (uint32_t)(b * PS_ACC);
+          const uint32_t al = ah + PS_ATILE, bh = ah + 2 * PS_ATILE, bl = bh + PS_BTILE;
+          const uint32_t t_acc = tmem + (uint32_t)(b * PS_N);
 #pragma unroll
           for (int kk = 0; kk < PS_BK / 16; ++kk) {
             const uint32_t o = kk * 32;  // 16 fp16 = 32 bytes into each row
@@ -294,21 +346,27 @@ proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_con
       else (void)mbar_wait(mdone, 0, p.status);
     }
   } else if (!skip) {
-    // ---------------- epilogue (both CTAs)
-    const int e = warp - 2;           // 0..7
-    const int half = e >> 2;          // units 32 half .. 32 half + 31 of the chain's block
+    // ---------------- epilogue (both CTAs): four quads of four warps, quad
+    // w takes units 8 w .. 8 w + 7 of the chain's block, thread = step.
+    // Per tile, five barriers of the quad: after the fold, after the staged
+    // Z of gates i and f, after the step maps and the Z of g and o, after
+    // the carry, after the staged c and out.  The staged pairs alternate
+    // between two pairs of buffers (store_two), so no wait for a store's
+    // read follows right behind that store.
+    const int e = warp - 2;           // 0..15
+    const int quad = e >> 2;
     const int q = warp & 3;           // TMEM lane quarter: tile rows 32q .. 32q + 31
     const int r = q * 32 + lane;      // tile row = time step t0 + r
-    const int bar = 1 + half;
-    const bool lead = (e & 3) == 0;   // the half's carry warp; its lane 0 issues the stores
+    const int bar = 1 + quad;
+    const bool lead = (e & 3) == 0;   // the quad's carry warp; its lane 0 issues the stores
     const bool issuer = lead && lane == 0;
-    float *box = epi + half * (PS_BOX / 4);
-    float *aggA = box, *aggC = box + 128, *cin_s = box + 256;  // while the box is not staging
+    float *stg = epi + quad * PS_NBUF * (PS_BOX / 4);
+    int sp = 0;  // staged pairs so far (alternating buffer pairs)
+    // the row blocks' step maps and the carries into them
+    float *aggA = aggs + quad * PS_AGG, *aggC = aggA + 4 * PS_QU, *cwin = aggA + 8 * PS_QU;
     // Undo the two operand scales one at a time (each inverse is an exact
     // power of two within float range, their product may not be).
     const float inv_a = 1.0f / pow2_scale(*p.absmax_a), inv_b = 1.0f / pow2_scale(*p.absmax_b);
-    const uint32_t pe0 = cluster_addr(&pempty[0], 0), pe1 = cluster_addr(&pempty[1], 0);
-    const uint32_t pf0 = cluster_addr(&pfull[0], 1), pf1 = cluster_addr(&pfull[1], 1);
     const int ngroups = (p.nkb + PS_PROM - 1) / PS_PROM;
     const int H = p.H;
     const float eps = p.eps;
@@ -318,62 +376,61 @@ proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_con
       const int tt = tl / p.nch, ch = tl - tt * p.nch;
       const int bq = 2 * (ch / p.nub) + (int)rank;
       const int ub = ch % p.nub;
-      const int u0 = ub * PS_UB + 32 * half;
+      const int u0 = ub * PS_UB + PS_QU * quad;
       const int t0 = tt * PS_TT;
       const bool bvalid = bq < p.B;
-      // v[32 gate + j]: gate (i, f, g, o) of unit u0 + j at step t0 + r
-      float v[128];
+      // the bias of this tile's units, loaded before the accumulator wait
+      float4 bias4[8];
 #pragma unroll
-      for (int j = 0; j < 128; ++j) v[j] = 0.f;
+      for (int k = 0; k < 8; ++k)
+        bias4[k] = p.bias ? *reinterpret_cast<const float4 *>(p.bias + (k >> 1) * H + u0 + 4 * (k & 1))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+      // v[8 gate + j]: gate (i, f, g, o) of unit u0 + j at step t0 + r
+      float v[4 * PS_QU];
+#pragma unroll
+      for (int j = 0; j < 4 * PS_QU; ++j) v[j] = 0.f;
       bool ok = true;
       for (int g = 0; g < ngroups; ++g, ++gg) {
-        const int b = gg & 1;
-        if (!mbar_wait(&pfull[b], (gg >> 1) & 1, p.status)) { ok = false; break; }
-        if (rank == 0 && e == 0 && lane == 0) mbar_arrive_cluster(b ? pf1 : pf0);  // tell the second CTA
+        const int b = gg % PS_NACC;
+        if (!mbar_wait(&pfull[b], (gg / PS_NACC) & 1, p.status)) { ok = false; break; }
+        if (rank == 0 && e == 0 && lane == 0) mbar_arrive_cluster(cluster_addr(&pfull[b], 1));  // tell the second CTA
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * PS_ACC) + (uint32_t)(32 * half);
+        const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * PS_N) + (uint32_t)(PS_QU * quad);
+        uint32_t w[32];
 #pragma unroll
-        for (int gate = 0; gate < 4; ++gate) {
+        for (int gate = 0; gate < 4; ++gate) tmem_ld8_nowait(base + (uint32_t)(gate * PS_UB), w + 8 * gate);
+        tmem_wait_ld(w);
 #pragma unroll
-          for (int c = 0; c < 32; c += 16) {
-            float w[16];
-            tmem_ld16(base + (uint32_t)(gate * 64 + c), w);
-#pragma unroll
-            for (int k = 0; k < 16; ++k) v[gate * 32 + c + k] += w[k];
-          }
-        }
+        for (int k = 0; k < 32; ++k) v[k] += __uint_as_float(w[k]);
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(b ? pe1 : pe0);
+        if (lane == 0) mbar_arrive_cluster(cluster_addr(&pempty[b], 0));
       }
       if (!named_and(bar, ok && ld_status(p.status) == 0)) break;
 
-      // Z = acc / (s_A s_B) + b_ih, stored for the backward (one box per gate)
+      // Z = acc / (s_A s_B) + b_ih, stored for the backward
 #pragma unroll
-      for (int gate = 0; gate < 4; ++gate) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const float4 bb = p.bias ? *reinterpret_cast<const float4 *>(p.bias + gate * H + u0 + j)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-          const int o = gate * 32 + j;
-          v[o] = (v[o] * inv_a) * inv_b + bb.x;
-          v[o + 1] = (v[o + 1] * inv_a) * inv_b + bb.y;
-          v[o + 2] = (v[o + 2] * inv_a) * inv_b + bb.z;
-          v[o + 3] = (v[o + 3] * inv_a) * inv_b + bb.w;
-        }
+      for (int k = 0; k < 8; ++k) {
+        const int o = 4 * k;
+        v[o] = (v[o] * inv_a) * inv_b + bias4[k].x;
+        v[o + 1] = (v[o + 1] * inv_a) * inv_b + bias4[k].y;
+        v[o + 2] = (v[o + 2] * inv_a) * inv_b + bias4[k].z;
+        v[o + 3] = (v[o + 3] * inv_a) * inv_b + bias4[k].w;
       }
-      store_boxes<4, 0>(v, box, &tmZ, r, issuer, bar, u0, H, bq, t0);
+      store_two<0, PS_QU>(v, stg, sp, &tmZ, &tmZ, r, issuer, bar, u0, H + u0, bq, t0);
 
-      // gates, then each warp's inclusive scan of the step maps over its 32
-      // steps: c_r = A_r c_in + C_r (v[j] <- A, v[64 + j] <- C, v[32 + j] <-
-      // f', v[96 + j] <- e^-o)
+      // gates (z_i, z_f are staged; z_g, z_o stay until their boxes), then
+      // each warp's inclusive scan of the step maps over its 32 steps:
+      // c_r = A_r c_in + C_r.  f' -> v[8 + j], C -> v[j], A -> a[j],
+      // e^-o -> eo[j].
+      float a[PS_QU], eo[PS_QU];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float fp = fmaxf(sigf(v[32 + j]), eps);
-        float C = fmaxf(sig2(v[j], v[64 + j]), eps);
+      for (int j = 0; j < PS_QU; ++j) {
+        const float fp = fmaxf(sigf(v[PS_QU + j]), eps);
+        float C = fmaxf(sig2(v[j], v[2 * PS_QU + j]), eps);
         float A = fp;
-        v[32 + j] = fp;
-        v[96 + j] = __expf(-v[96 + j]);
+        v[PS_QU + j] = fp;
+        eo[j] = __expf(-v[3 * PS_QU + j]);
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
           const float Ap = __shfl_up_sync(0xffffffffu, A, off), Cp = __shfl_up_sync(0xffffffffu, C, off);
@@ -382,74 +439,77 @@ proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_con
             A *= Ap;
           }
         }
-        v[j] = A;
-        v[64 + j] = C;
+        a[j] = A;
+        v[j] = C;
       }
       if (lane == 31) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          aggA[q * 32 + j] = v[j];
-          aggC[q * 32 + j] = v[64 + j];
+        for (int j = 0; j < PS_QU; ++j) {
+          aggA[q * PS_QU + j] = a[j];
+          aggC[q * PS_QU + j] = v[j];
         }
       }
-      named_sync(bar);
+      // the Z of g and o; its barrier also makes the step maps visible
+      store_two<2 * PS_QU, 3 * PS_QU>(v, stg, sp, &tmZ, &tmZ, r, issuer, bar, 2 * H + u0, 3 * H + u0, bq, t0);
 
-      // The carry warp (lane = unit): the tile's total map, the chain's carry
-      // in, the tile's end carry out (published before the outputs are made).
+      // The carry warp (lanes 0..7 = units): the tile's total map, the
+      // chain's carry in, the tile's end carry out (published first), then
+      // the carry into each row block.
       bool good = true;
       if (lead) {
-        float At = aggA[lane], Ct = aggC[lane];
+        const int j = lane & (PS_QU - 1);
+        float At = aggA[j], Ct = aggC[j];
 #pragma unroll
         for (int k = 1; k < 4; ++k) {
-          const float a = aggA[k * 32 + lane];
-          Ct = fmaf(a, Ct, aggC[k * 32 + lane]);
-          At *= a;
+          const float a2 = aggA[k * PS_QU + j];
+          Ct = fmaf(a2, Ct, aggC[k * PS_QU + j]);
+          At *= a2;
         }
         float cin = eps;
         if (bvalid) {
-          const int64_t ci = (int64_t)bq * H + u0 + lane;
-          unsigned *flag = p.flags + ((int64_t)bq * p.nub + ub) * 2 + half;
-          if (tt == 0) cin = fmaxf(p.c0 ? p.c0[ci] : 0.f, eps);
-          else if (wait_count(flag, (unsigned)tt, p.status)) cin = __ldcg(p.carry + ci);
-          else good = false;
+          unsigned long long *slot = p.slots + (int64_t)bq * H + u0 + j;
+          if (tt == 0) cin = fmaxf(p.c0 ? p.c0[(int64_t)bq * H + u0 + j] : 0.f, eps);
+          else good = gslot_wait(slot, (unsigned)tt, &cin, p.status);
           good = __all_sync(0xffffffffu, good);
-          if (good && tt + 1 < p.ntt) {
-            __stcg(p.carry + ci, fmaf(At, cin, Ct));
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) st_release(flag, (unsigned)(tt + 1));
+          if (good && tt + 1 < p.ntt && lane < PS_QU) gslot_put(slot, (unsigned)(tt + 1), fmaf(At, cin, Ct));
+        }
+        if (lane < PS_QU) {
+          float cw = cin;
+          cwin[j] = cw;
+#pragma unroll
+          for (int k = 0; k < 3; ++k) {
+            cw = fmaf(aggA[k * PS_QU + j], cw, aggC[k * PS_QU + j]);
+            cwin[(k + 1) * PS_QU + j] = cw;
           }
         }
-        cin_s[lane] = cin;
       }
       if (!named_and(bar, good && ld_status(p.status) == 0)) break;
 
-      // c, out and the backward's bound at every step of this warp
+      // c -> v[16 + j], out -> v[24 + j], and the backward's bound
       const bool rvalid = bvalid && t0 + r < p.T;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        float cw = cin_s[j];  // c just before this warp's first step
-        for (int k = 0; k < q; ++k) cw = fmaf(aggA[k * 32 + j], cw, aggC[k * 32 + j]);
-        const float c = fmaf(v[j], cw, v[64 + j]);
+      for (int j = 0; j < PS_QU; ++j) {
+        const float cw = cwin[q * PS_QU + j];  // c just before this warp's first step
+        const float c = fmaf(a[j], cw, v[j]);
         float cprev = __shfl_up_sync(0xffffffffu, c, 1);
         if (lane == 0) cprev = cw;
-        const float fp = v[32 + j];
+        const float fp = v[PS_QU + j];
         if (rvalid) kmax = fmaxf(kmax, cprev * fp * (1.f - fp));
-        v[64 + j] = c;
-        v[j] = sig_tanh_pos(v[96 + j], c);
+        v[2 * PS_QU + j] = c;
+        v[3 * PS_QU + j] = sig_tanh_pos(eo[j], c);
       }
-      named_sync(bar);  // the aggregates are read before the box stages again
-      store_boxes<1, 64>(v, box, &tmC, r, issuer, bar, u0, 0, bq, t0);
-      store_boxes<1, 0>(v, box, &tmO, r, issuer, bar, u0, 0, bq, t0);
+      store_two<2 * PS_QU, 3 * PS_QU>(v, stg, sp, &tmC, &tmO, r, issuer, bar, u0, u0, bq, t0);
       if (rvalid && t0 + r == p.T - 1) {
         const int64_t ci = (int64_t)bq * H + u0;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (p.h_n) p.h_n[ci + j] = v[j];
-          if (p.c_n) p.c_n[ci + j] = v[64 + j];
+        for (int j = 0; j < PS_QU; ++j) {
+          if (p.h_n) p.h_n[ci + j] = v[3 * PS_QU + j];
+          if (p.c_n) p.c_n[ci + j] = v[2 * PS_QU + j];
         }
       }
     }
+    // every store has read its staging buffer before the CTA may leave
+    if (issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
     if (p.kf) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) kmax = fmaxf(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
@@ -467,7 +527,6 @@ proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_con
   }
 }
 
-
 // ---------------------------------------------------------------- host side
 // x split [T*B][ld] fp16 as the 3D tensor {ld, B, T}: box {64 k, 1 b, 128 t}.
 bool make_map_x(CUtensorMap *tm, const __half *ptr, int64_t T, int64_t B, int64_t ld) {
@@ -481,7 +540,7 @@ bool make_map_x(CUtensorMap *tm, const __half *ptr, int64_t T, int64_t B, int64_
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
-// W_ih split [4H][ld] fp16: box {64 k, 64 rows} (one gate's rows of a chain).
+// W_ih split [4H][ld] fp16: box {64 k, 32 rows} (one gate's rows of a chain).
 bool make_map_w(CUtensorMap *tm, const __half *ptr, int64_t rows, int64_t ld) {
   auto enc = encode_fn();
   if (!enc) return false;
@@ -493,17 +552,17 @@ bool make_map_w(CUtensorMap *tm, const __half *ptr, int64_t rows, int64_t ld) {
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
-// [T][B][N] float32 output as {N, B, T}: box {32 columns, 1 b, 128 t},
-// 128-byte swizzle (the epilogue's staging layout).
+// [T][B][N] float32 output as {N, B, T}: box {8 columns, 1 b, 128 t},
+// 32-byte swizzle (the epilogue's staging layout).
 bool make_map_tbn(CUtensorMap *tm, float *ptr, int64_t T, int64_t B, int64_t N) {
   auto enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)B, (cuuint64_t)T};
   cuuint64_t strides[2] = {(cuuint64_t)N * 4, (cuuint64_t)(B * N * 4)};
-  cuuint32_t box[3] = {32, 1, (cuuint32_t)PS_TT};
+  cuuint32_t box[3] = {(cuuint32_t)PS_QU, 1, (cuuint32_t)PS_TT};
   cuuint32_t es[3] = {1, 1, 1};
   return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)ptr, dims, strides, box, es,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -567,11 +626,10 @@ int64_t ps_round8(int64_t x) { return (x + 7) / 8 * 8; }
 size_t proj_scan_ws(int64_t T, int64_t B, int64_t D, int64_t H) {
   (void)T;
   if (B <= 0 || D <= 0 || H <= 0) return 0;
-  return 256 + h3_split_bytes(4 * H, D) + round_up((size_t)B * H * 4, 256) +
-         round_up((size_t)B * ((H + PS_UB - 1) / PS_UB) * 2 * 4, 256);
+  return 256 + h3_split_bytes(4 * H, D) + round_up((size_t)B * H * 8, 256);
 }
 
-// Shapes the fused kernel can run: 64-unit chain blocks, int32 tile and
+// Shapes the fused kernel can run: 32-unit chain blocks, int32 tile and
 // coordinate arithmetic, the fp16-split tensor-core GEMMs enabled.
 bool proj_scan_shape_ok(int64_t T, int64_t B, int64_t D, int64_t H) {
   if (T <= 0 || B <= 0 || D <= 0 || H <= 0 || H % PS_UB) return false;
@@ -619,9 +677,7 @@ int proj_scan_forward(const void *x_split, const unsigned *x_scale, const float 
   unsigned *w_scale = reinterpret_cast<unsigned *>(w8);
   __half *wh = reinterpret_cast<__half *>(w8 + 256);
   const __half *wl = wh + N * D8;
-  float *carry = reinterpret_cast<float *>(w8 + 256 + h3_split_bytes(N, D));
-  unsigned *flags = reinterpret_cast<unsigned *>(reinterpret_cast<char *>(carry) + round_up((size_t)B * H * 4, 256));
-  const size_t flag_bytes = (size_t)B * (H / PS_UB) * 2 * 4;
+  unsigned long long *slots = reinterpret_cast<unsigned long long *>(w8 + 256 + h3_split_bytes(N, D));
   const __half *xh = static_cast<const __half *>(x_split);
   const __half *xl = xh + T * B * D8;
   CUtensorMap tah, tal, tbh, tbl, tz, to, tc;
@@ -632,15 +688,14 @@ int proj_scan_forward(const void *x_split, const unsigned *x_scale, const float 
     return HS_OK;
   }
   if (int e = h3_split(w, N, D, D, w_scale, wh, st)) return e;
-  if (cudaMemsetAsync(flags, 0, flag_bytes, st) != cudaSuccess) return check_launch("proj_scan flags memset");
+  if (cudaMemsetAsync(slots, 0, (size_t)B * H * 8, st) != cudaSuccess) return check_launch("proj_scan slots memset");
   if (kf && cudaMemsetAsync(kf, 0, 4, st) != cudaSuccess) return check_launch("proj_scan kf memset");
   PsArgs a;
   a.bias = bias;
   a.c0 = c0;
   a.h_n = h_n;
   a.c_n = c_n;
-  a.carry = carry;
-  a.flags = flags;
+  a.slots = slots;
   a.kf = kf;
   a.absmax_a = x_scale;
   a.absmax_b = w_scale;

@@ -8,8 +8,8 @@ Shapes: a partial last time tile (T not a multiple of 128), odd B (the
 second CTA of the last pair has no sequence), D not a multiple of 64 (a
 zero-filled k tail), no bias, c0 given or not, several time tiles per chain
 (carries handed between tiles), one time tile (no carries), a configs[4]
-micro-batch width (256 chains), and configs[4]'s full T = 16384 on a few
-chains (128 tiles per chain)."""
+micro-batch width (512 chains of 2 sequences x 32 units), and configs[4]'s
+full T = 16384 on a few chains (128 tiles per chain)."""
 
 import pytest
 import torch
@@ -133,7 +133,7 @@ def test_projection_scan_policy_and_errors():
     assert lib.hs_projection_scan_supported(16384, 32, 512, 1024) == 1
     assert lib.hs_projection_scan_supported(128, 32, 256, 256) == 1
     assert lib.hs_projection_scan_supported(16384, 2, 512, 1024) == 0
-    assert lib.hs_projection_scan_supported(256, 32, 512, 1000) == 0  # H % 64
+    assert lib.hs_projection_scan_supported(256, 32, 512, 1000) == 0  # H % 32
     dev = torch.device("cuda", 0)
     z = torch.empty(16, device=dev)
     with pytest.raises(RuntimeError):
