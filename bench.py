@@ -167,7 +167,7 @@ class ParallelStep:
     """One parallel-mode training step on this rank through the C ABI, with
     CUDA events around every library call (the kernel breakdown)."""
 
-    def __init__(self, cfg, params, B_local, dev):
+    def __init__(self, cfg, params, B_local, dev, fused=None):
         from prlstm_b200 import _lib
 
         self.L = _lib
@@ -194,8 +194,9 @@ class ParallelStep:
         lib = _lib.load()
         M = T * mb
         # the projection and the scan forward as one kernel where the library
-        # takes it for this micro-batch (HS_PROJ_SCAN=0 times the two calls)
-        self.fused = bool(lib.hs_projection_scan_supported(T, mb, D, H))
+        # takes it for this micro-batch (HS_PROJ_SCAN=0 times the two calls),
+        # or where the caller asks for it (fused=True)
+        self.fused = bool(lib.hs_projection_scan_supported(T, mb, D, H)) if fused is None else fused
         self.ws = _lib.workspace(max(lib.hs_parallel_workspace_bytes(T, mb, D, H),
                                      lib.hs_scan_split_workspace_bytes(T, mb, H),
                                      lib.hs_linear_presplit_workspace_bytes(M, 4 * H, D),
@@ -550,8 +551,12 @@ def run_ours(args, cfg, rank, world, dev):
         # after the timed region): inside the step the GEMMs hold the SM clock
         # down under the power cap and the issue-bound scans slow with it.
         result["scan_alone"] = scan_alone(step, G[0], dev, peak_hbm)
+        fused_here = step.fused
         del step
         torch.cuda.empty_cache()
+        if not fused_here and H % 32 == 0:
+            result["fused_projection_scan_step"] = fused_variant(args, cfg, params, x, G, B_local, dev, sync,
+                                                                max_over_ranks, peak_hbm)
         # ---------------- e2e through the public module API, host buffers
         if not args.no_e2e:
             result["e2e"] = e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync,
@@ -562,6 +567,47 @@ def run_ours(args, cfg, rank, world, dev):
     if result.get("e2e") and not args.no_e2e:
         result["e2e"]["h2d_roofline"] = h2d_roofline(result["e2e"], cfg, world, dev, sync)
     return result
+
+
+def fused_variant(args, cfg, params, x, G, B_local, dev, sync, max_over_ranks, peak_hbm, steps=3):
+    """The same step with the projection and the scan forward as one kernel
+    (hs_projection_scan_forward), where the library's default takes the two
+    calls for this shape: timed the same way (CUDA events, max over ranks,
+    no gradient all-reduce), with the forward's algorithmic DRAM bytes per
+    micro-batch of both variants.  Reported beside the headline, which
+    stays on the library's default path."""
+    T, D, H = cfg["T"], cfg["D"], cfg["H"]
+    step = ParallelStep(cfg, params, B_local, dev, fused=True)
+    for _ in range(2):
+        step.run(x, G)
+    sync()
+    step.ms = {n: 0.0 for n in step.names}
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    allev = []
+    for _ in range(steps):
+        allev.extend(step.run(x, G, record=True))
+    t1.record()
+    sync()
+    ms = max_over_ranks(t0.elapsed_time(t1))
+    step.collect(allev)
+    from prlstm_b200 import _lib
+    _lib.check_device_status(dev)
+    units = T * step.mb * H  # (t, b, h) per micro-batch
+    nl = steps * step.nmb
+    res = {
+        "what": "the same training step with hs_projection_scan_forward in place of the projection GEMM and "
+                "the scan forward (not the library default for this shape)",
+        "value": T * cfg["B"] * steps / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms / steps,
+        "kernels_ms": {n: round(step.ms[n] / nl, 4) for n in step.names},
+        # forward DRAM bytes per micro-batch (x's split read by both)
+        "forward_hbm_bytes_per_microbatch": {"fused": (24.0 + 4.0 * D / H) * units,
+                                             "two_calls": (40.0 + 4.0 * D / H) * units},
+    }
+    del step
+    torch.cuda.empty_cache()
+    return res
 
 
 def h2d_roofline(e2e, cfg, world, dev, sync, nbytes=1 << 30, reps=4):

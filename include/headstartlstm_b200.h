@@ -212,9 +212,9 @@ HS_API int hs_scan_forward_kf(const float *z, const float *c0, float *out, float
  * and dev_status; workspace >= hs_projection_scan_workspace_bytes (256-byte
  * aligned).  hs_projection_scan_supported says whether the library's own
  * forward (hs_parallel_forward*) takes this kernel for a shape by default
- * (it does when the (sequence pair, 32-unit block) chains fill the GPU, or
- * T <= 128); HS_PROJ_SCAN=0 / 1 turns that off / on for every shape it can
- * run.  Replaces, with hs_split, the projection `linear` and the scan of
+ * (it does for T <= 128, where it is faster than the GEMM and the scan as
+ * two calls; at longer T it is about as fast and is not the default);
+ * HS_PROJ_SCAN=0 / 1 turns that off / on for every shape it can run.  Replaces, with hs_split, the projection `linear` and the scan of
  * headstartlstm_parallel (_parallel.py:38-74, _parallel.py:21-35). */
 HS_API size_t hs_projection_scan_workspace_bytes(int64_t T, int64_t B, int64_t D, int64_t H);
 HS_API int hs_projection_scan_supported(int64_t T, int64_t B, int64_t D, int64_t H);

@@ -124,14 +124,14 @@ def test_projection_scan_matches_oracle_and_two_call_path(case):
 
 
 def test_projection_scan_policy_and_errors():
-    """The default policy takes the fused kernel when the chains fill the
-    GPU (configs[4]'s micro-batch) or T fits one time tile, not for few
-    chains over long T; shapes it cannot run are refused with an error."""
+    """The default policy takes the fused kernel when T fits one time tile
+    (configs[1]), not over longer T (configs[4], where the two calls are as
+    fast); shapes it cannot run are refused with an error."""
     from prlstm_b200 import _lib as L
 
     lib = L.load()
-    assert lib.hs_projection_scan_supported(16384, 32, 512, 1024) == 1
     assert lib.hs_projection_scan_supported(128, 32, 256, 256) == 1
+    assert lib.hs_projection_scan_supported(16384, 32, 512, 1024) == 0
     assert lib.hs_projection_scan_supported(16384, 2, 512, 1024) == 0
     assert lib.hs_projection_scan_supported(256, 32, 512, 1000) == 0  # H % 32
     dev = torch.device("cuda", 0)
