@@ -1244,7 +1244,7 @@ def main():
                 config=_config_obj(args.config, cfg, world, workload),
                 roofline=res.get("roofline"), e2e=res.get("e2e"), clocks=res.get("clocks"),
                 gpu_launches=res.get("gpu_launches"))
-    for k in ("kernels", "scan_roofline", "scan_alone", "recurrent", "launch"):
+    for k in ("kernels", "scan_roofline", "scan_alone", "fused_projection_scan_step", "recurrent", "launch"):
         if k in res:
             line[k] = res[k]
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
