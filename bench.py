@@ -1162,6 +1162,36 @@ def run_reference_gpu(args, cfg, dev):
             "micro_batch": mb if parallel else None}, None
 
 
+def reference_gpu_beside(args, cfg, line, dev):
+    """The reference's stock GPU paths (run_reference_gpu: its Triton
+    backend for the recurrent configs, its parallel=True torch path for the
+    parallel ones) on the headline config and on each float32 config this
+    run timed, with this build's device-timed value over the reference's.
+    Not the driver's reference arm (the CPU path): a comparison on the same
+    GPU, recorded in the same JSON line.  Each failure is recorded, never
+    raised."""
+    out = {}
+    todo = [(args.config, cfg, line["value"])]
+    todo += [(n, dict(CONFIGS[n]), e["value"]) for n, e in line.get("configs", {}).items()
+             if n in CONFIGS and isinstance(e, dict) and "value" in e]
+    for name, c, ours in todo:
+        big = c["T"] * c["B"] >= (1 << 20)
+        sub = argparse.Namespace(steps=1 if big else 5, warmup=1 if big else 2)
+        torch.cuda.empty_cache()
+        try:
+            r, why = run_reference_gpu(sub, c, dev)
+        except Exception as e:  # an out-of-memory or a compile failure of the reference
+            r, why = None, f"{type(e).__name__}: {e}"[:300]
+        if r is None:
+            out[name] = {"unavailable": why}
+        else:
+            r["steps"] = sub.steps
+            r["ours_over_reference"] = ours / r["value"]
+            out[name] = r
+        torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------------ main
 def main():
     ap = argparse.ArgumentParser()
@@ -1182,6 +1212,8 @@ def main():
                     help="capture the parallel step in a CUDA graph (auto: launch-bound steps on one GPU)")
     ap.add_argument("--no-configs", action="store_true",
                     help="time only the headline config (not configs[0-3] after it)")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own GPU paths beside each config")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.batch:
@@ -1291,6 +1323,10 @@ def main():
         torch.cuda.empty_cache()
         line["configs"]["cfg4_bf16"] = run_bf16_module(args, dict(CONFIGS["cfg4"]), world, dev, rank, steps=4)
         torch.cuda.empty_cache()
+    # The reference's own GPU paths on this GPU, beside each float32 config
+    # of this run: rank 0 at N=1, after everything else.
+    if rank == 0 and world == 1 and not args.no_reference_gpu:
+        line["reference_gpu"] = reference_gpu_beside(args, cfg, line, dev)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
