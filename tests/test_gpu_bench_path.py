@@ -83,6 +83,52 @@ def test_cfg4_micro_batch_full_size_vs_float64():
     torch.cuda.empty_cache()
 
 
+def test_fused_projection_scan_full_size_vs_float64():
+    """The projection with the scan forward in its epilogue
+    (hs_projection_scan_forward, the bench's `fused_projection_scan_step`)
+    on one configs[4] micro-batch at full size, with c0: Z, out, c, h_n, c_n
+    against float64 (Z from float64 products of the same x, W_ih, b_ih; the
+    scan from that Z), 512 chains of 128 time tiles each."""
+    from prlstm_b200 import _lib as L
+
+    dev = torch.device("cuda", 0)
+    params, _, _ = make_inputs(8, 1, D4, H4, a=0.0, bias_spread=8.0, seed=0)
+    W_ih, _, b_ih, _, _ = (t.to(dev) for t in params)
+    g = torch.Generator(device=dev).manual_seed(46)
+    x = torch.randn(T4, B4, D4, device=dev, generator=g)
+    c0 = torch.rand(B4, H4, device=dev, generator=g)
+    lib = L.load()
+    P, st = L.ptr, L.stream_ptr(dev)
+    M = T4 * B4
+    words = torch.zeros(64, dtype=torch.int32, device=dev)
+    xs = torch.empty(lib.hs_split_bytes(M, D4), dtype=torch.uint8, device=dev)
+    L.call("hs_split", P(x), M, D4, P(xs), P(words[0:]), st)
+    ws = L.workspace(lib.hs_projection_scan_workspace_bytes(T4, B4, D4, H4), dev)
+    z = torch.empty(T4, B4, 4 * H4, device=dev)
+    out = torch.empty(T4, B4, H4, device=dev)
+    c = torch.empty(T4, B4, H4, device=dev)
+    h_n = torch.empty(B4, H4, device=dev)
+    c_n = torch.empty(B4, H4, device=dev)
+    L.call("hs_projection_scan_forward", P(xs), P(words[0:]), P(W_ih), P(b_ih), P(c0), P(z), P(out), P(c),
+           P(h_n), P(c_n), T4, B4, D4, H4, 1e-6, P(ws), ws.numel(), P(words[16:]), P(L.status_word(dev)), st)
+    torch.cuda.synchronize(dev)
+    L.check_device_status(dev)
+    del xs, ws
+    W64, b64, x64 = W_ih.double(), b_ih.double(), x.double()
+    ez = 0.0
+    for t0 in range(0, T4, 1024):
+        ez = max(ez, _rel(z[t0:t0 + 1024], torch.nn.functional.linear(x64[t0:t0 + 1024], W64, b64)))
+    assert ez < 2e-6, f"z: {ez:.3e}"
+    del x64
+    zero = torch.zeros(1, B4, H4, dtype=torch.float64, device=dev).expand(T4, B4, H4)
+    r = O.par_linear_chunked(lambda t0, t1: z[t0:t1].double(), T4, c0.double(), zero, chunk=256)
+    errs = {k: _rel(v, r[k]) for k, v in dict(out=out, c=c, h_n=h_n, c_n=c_n).items()}
+    for k, e in errs.items():
+        assert e <= 1e-5, f"{k}: rel err {e:.3e} (all: {errs})"
+    del z, out, c, r
+    torch.cuda.empty_cache()
+
+
 def test_weight_gradient_split_k_at_benchmark_k():
     """dW_ih = dZ^T x and dX = dZ W_ih at the benchmark's micro-batch shape
     (M = T*B = 524,288 rows, N = 4H = 4096, K = D = 512) through
