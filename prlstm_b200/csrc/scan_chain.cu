@@ -655,9 +655,6 @@ scan_bwd_col2_kernel(const TS *z, const TS *__restrict__ cbuf, const float *__re
   const bool hv = h < H;
   const int64_t nchunk = (T + kBL - 1) / kBL;
   const int64_t zstep = B * 4 * H, sstep = B * H;
-  // 32-bit element offsets within a chunk (the launcher checks that kBL
-  // steps of the [T][B][4H] layout fit): one wide multiply-add per address
-  const unsigned zs32 = (unsigned)zstep, ss32 = (unsigned)sstep, H32 = (unsigned)H;
   float *buf0 = sm + warp * 2 * kB2Buf;
   slots[warp * 64 + lane] = 0ull;
   slots[warp * 64 + 32 + lane] = 0ull;
@@ -677,11 +674,9 @@ scan_bwd_col2_kernel(const TS *z, const TS *__restrict__ cbuf, const float *__re
       if (j < 6 * RC && h0 + k < H) {
         const TS *src = rr < 4 ? z + (t0 * B + b) * 4 * H + rr * H + h0 + k
                                : (rr == 4 ? cbuf : dout) + (t0 * B + b) * H + h0 + k;
-        const unsigned step = rr < 4 ? zs32 : ss32;
-        const unsigned d = sa(dst) + (unsigned)((rr * 64 + k) * EB);
-#pragma unroll
-        for (int s = 0; s < kBL; ++s)
-          if (s < n) cp16(d + (unsigned)(s * kB2Row * EB), src + s * step);
+        const int64_t step = rr < 4 ? zstep : sstep;
+        unsigned d = sa(dst) + (unsigned)((rr * 64 + k) * EB);
+        for (int s = 0; s < n; ++s, src += step, d += kB2Row * EB) cp16(d, src);
       }
     }
     if (lane < RC && t0 > 0 && h0 + lane * PER < H)
@@ -691,23 +686,19 @@ scan_bwd_col2_kernel(const TS *z, const TS *__restrict__ cbuf, const float *__re
   float acc[4][2] = {};
   float amax = 0.f;
   const float sc = OUT == kDzSplit ? pow2_scale(*dz_bound) : 1.f;
-  // the dZ pair at element offset o (even) from the chunk's base pointers
-  // (this lane's units at the chunk's first step, set per chunk below)
-  __half *hb = nullptr, *lb = nullptr;
-  float *fb = nullptr;
-  __nv_bfloat16 *bb = nullptr;
-  auto put2 = [&](unsigned o, float v0, float v1) {
+  // the dZ pair at element offset i (even) of the [T*B][4H] layout
+  auto put2 = [&](int64_t i, float v0, float v1) {
     if (OUT == kDzSplit) {
       const __half2 hi = __floats2half2_rn(v0 * sc, v1 * sc);
       const float2 hf = __half22float2(hi);
       const __half2 lo = __floats2half2_rn(v0 * sc - hf.x, v1 * sc - hf.y);
-      __stcs(reinterpret_cast<unsigned *>(hb + o), *reinterpret_cast<const unsigned *>(&hi));
-      __stcs(reinterpret_cast<unsigned *>(lb + o), *reinterpret_cast<const unsigned *>(&lo));
+      __stcs(reinterpret_cast<unsigned *>(dzh + i), *reinterpret_cast<const unsigned *>(&hi));
+      __stcs(reinterpret_cast<unsigned *>(dzl + i), *reinterpret_cast<const unsigned *>(&lo));
     } else if (OUT == kDzBf16) {
       const __nv_bfloat162 v = __floats2bfloat162_rn(v0, v1);
-      __stcs(reinterpret_cast<unsigned *>(bb + o), *reinterpret_cast<const unsigned *>(&v));
+      __stcs(reinterpret_cast<unsigned *>(dzb + i), *reinterpret_cast<const unsigned *>(&v));
     } else {
-      __stcs(reinterpret_cast<float2 *>(fb + o), make_float2(v0, v1));
+      __stcs(reinterpret_cast<float2 *>(dz + i), make_float2(v0, v1));
     }
   };
   int64_t q = warp;
@@ -729,14 +720,6 @@ scan_bwd_col2_kernel(const TS *z, const TS *__restrict__ cbuf, const float *__re
     float FP[kBL][2], DCD[kBL][2], KI[kBL][2], KF[kBL][2], KG[kBL][2];
     float A[2] = {1.f, 1.f}, C[2] = {0.f, 0.f};
     const int64_t dzs = (t0 * B + b) * 4 * H + h;
-    if (OUT == kDzSplit) {
-      hb = dzh + dzs;
-      lb = dzl + dzs;
-    } else if (OUT == kDzBf16) {
-      bb = dzb + dzs;
-    } else {
-      fb = dz + dzs;
-    }
 #pragma unroll
     for (int s = kBL - 1; s >= 0; --s) {
 #pragma unroll
@@ -773,7 +756,7 @@ scan_bwd_col2_kernel(const TS *z, const TS *__restrict__ cbuf, const float *__re
           C[u] = FP[s][u] * (C[u] + dcd);
           A[u] *= FP[s][u];
         }
-        put2(s * zs32 + 3 * H32, dzo[0], dzo[1]);
+        put2(dzs + s * zstep + 3 * H, dzo[0], dzo[1]);
       }
     }
     __syncwarp();
@@ -807,10 +790,10 @@ scan_bwd_col2_kernel(const TS *z, const TS *__restrict__ cbuf, const float *__re
             acc[2][u] += dg[u];
             amax = fmaxf(amax, fmaxf(fabsf(di[u]), fmaxf(fabsf(df[u]), fabsf(dg[u]))));
           }
-          const unsigned dzr = s * zs32;
+          const int64_t dzr = dzs + s * zstep;
           put2(dzr, di[0], di[1]);
-          put2(dzr + H32, df[0], df[1]);
-          put2(dzr + 2 * H32, dg[0], dg[1]);
+          put2(dzr + H, df[0], df[1]);
+          put2(dzr + 2 * H, dg[0], dg[1]);
         }
       }
       if (t0 == 0 && dc0) {
@@ -932,9 +915,7 @@ int scan_bwd_chain_launch(const float *z, const float *c, const float *c0, const
   const bool v16 = H % 4 == 0 && aligned(z, 16) && aligned(c, 16) && aligned(dout, 16);
   const bool split = dzh != nullptr;
   if (split && (!v16 || !dzl || !dz_bound)) return fail(HS_ERR_INVALID_ARG, "scan split: needs H % 4 == 0, aligned inputs");
-  // the two-unit kernel addresses a chunk's kBL steps with 32-bit offsets
-  const bool off32 = (kBL + 1) * B * 4 * H < (1ll << 32);
-  if (v16 && two_units() && off32 && (split ? (aligned(dzh, 4) && aligned(dzl, 4)) : aligned(dz, 8))) {
+  if (v16 && two_units() && (split ? (aligned(dzh, 4) && aligned(dzl, 4)) : aligned(dz, 8))) {
     const unsigned grid2 = (unsigned)(B * ((H + 63) / 64));
     const void *fn2 = split ? (const void *)scan_bwd_col2_kernel<kDzSplit, float>
                             : (const void *)scan_bwd_col2_kernel<kDzF32, float>;
@@ -1010,8 +991,7 @@ int scan_bwd_chain_launch_bf16(const void *z, const void *c, const float *c0, co
   if (!scan_chain_bf16_ok(H, {z, c, dout, dz}))
     return fail(HS_ERR_UNSUPPORTED, "bf16 scan: needs H % 8 == 0, 16-byte aligned z/c/dout/dz");
   using K = __nv_bfloat16;
-  // the two-unit kernel addresses a chunk's kBL steps with 32-bit offsets
-  if (two_units() && (kBL + 1) * B * 4 * H < (1ll << 32)) {
+  if (two_units()) {
     const void *fn2 = (const void *)scan_bwd_col2_kernel<kDzBf16, K>;
     if (int e = allow_dynamic_smem(fn2, kB2Smem, &g_bwd2_attr[2])) return e;
     scan_bwd_col2_kernel<kDzBf16, K><<<(unsigned)(B * ((H + 63) / 64)), kBNW * 32, kB2Smem, st>>>(
