@@ -91,17 +91,32 @@ def make_params(cfg, dtype=torch.float32):
     return W_ih, W_hh, b_ih, b_hh, a
 
 
+def micro_batches(B_local, H):
+    """Micro-batch sizes for a rank's B_local sequences: near-equal calls of
+    at most the number of sequences whose per-column scans fill the GPU in
+    one wave of columns (hs_scan_wave_sequences: 37 at H = 1024 on 148 SMs,
+    so configs[4]'s 256 sequences run as 4 x 37 + 3 x 36); MICRO_BATCH
+    where the library cannot say."""
+    from prlstm_b200 import _lib
+    cap = int(_lib.load().hs_scan_wave_sequences(H)) or MICRO_BATCH
+    cap = max(1, min(cap, B_local))
+    n = -(-B_local // cap)
+    base, rem = divmod(B_local, n)
+    return [base + 1] * rem + [base] * (n - rem)
+
+
 def make_data(cfg, B_local, rank, dev, mb=None):
-    """x ~ N(0,1) [T,B,D] and G ~ N(0,1) [T,B,H] for this rank.  With `mb`,
-    returned as lists of contiguous micro-batches of mb sequences each."""
+    """x ~ N(0,1) [T,B,D] and G ~ N(0,1) [T,B,H] for this rank.  With `mb`
+    (a size, or a list of sizes summing to B_local), returned as lists of
+    contiguous micro-batches."""
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     if mb is None:
         x = torch.randn(cfg["T"], B_local, cfg["D"], device=dev, generator=g)
         G = torch.randn(cfg["T"], B_local, cfg["H"], device=dev, generator=g)
         return x, G
-    n = B_local // mb
-    xs = [torch.randn(cfg["T"], mb, cfg["D"], device=dev, generator=g) for _ in range(n)]
-    Gs = [torch.randn(cfg["T"], mb, cfg["H"], device=dev, generator=g) for _ in range(n)]
+    sizes = [mb] * (B_local // mb) if isinstance(mb, int) else list(mb)
+    xs = [torch.randn(cfg["T"], n, cfg["D"], device=dev, generator=g) for n in sizes]
+    Gs = [torch.randn(cfg["T"], n, cfg["H"], device=dev, generator=g) for n in sizes]
     return xs, Gs
 
 
@@ -174,9 +189,13 @@ class ParallelStep:
         self.cfg = cfg
         self.dev = dev
         T, D, H = cfg["T"], cfg["D"], cfg["H"]
-        self.mb = min(MICRO_BATCH, B_local)
-        assert B_local % self.mb == 0
-        self.nmb = B_local // self.mb
+        # micro-batches (micro_batches: one wave of scan columns each); the
+        # buffers are sized for the largest, each call takes a contiguous
+        # view of its own size
+        self.sizes = micro_batches(B_local, H)
+        self.mb = max(self.sizes)
+        self.nmb = len(self.sizes)
+        self.mb_mean = B_local / self.nmb
         self.W_ih = params[0].to(dev).contiguous()
         self.b_ih = params[2].to(dev).contiguous()
         mb = self.mb
@@ -214,15 +233,23 @@ class ParallelStep:
         self.ms = {n: 0.0 for n in self.names}
         self.launches = 0
 
+    @staticmethod
+    def _part(t, m):
+        """The first m sequences' worth of a [T, mb, ...] buffer, as a
+        contiguous [T, m, ...] tensor (the same storage)."""
+        n = t.numel() // t.shape[1] * m
+        return t.view(-1)[:n].view(t.shape[0], m, *t.shape[2:])
+
     def run(self, x, G, record=False):
         L, P = self.L, self.L.ptr
         T, D, H = self.cfg["T"], self.cfg["D"], self.cfg["H"]
-        mb = self.mb
         st = L.stream_ptr(self.dev)
-        M = T * mb
         evs = []
-        for i in range(self.nmb):
+        for i, mb in enumerate(self.sizes):
+            M = T * mb
             xs, Gs = x[i], G[i]
+            z, out, c, dx = (self._part(t, mb) for t in (self.z, self.out, self.c, self.dx))
+            c0, h_n, c_n = self.c0[:mb], self.h_n[:mb], self.c_n[:mb]
             e = [torch.cuda.Event(enable_timing=True) for _ in range(len(self.names) + 1)] if record else None
             if record:
                 e[0].record()
@@ -232,26 +259,26 @@ class ParallelStep:
             if self.fused:
                 # Z, out, c, h_n, c_n and the backward's bound in one kernel
                 L.call("hs_projection_scan_forward", P(self.x_split), x_scale, P(self.W_ih), P(self.b_ih),
-                       P(self.c0), P(self.z), P(self.out), P(self.c), P(self.h_n), P(self.c_n), T, mb, D, H,
+                       P(c0), P(z), P(out), P(c), P(h_n), P(c_n), T, mb, D, H,
                        1e-6, P(self.ws), self.ws.numel(), cmax, P(self.status), st)
             else:
                 L.call("hs_linear_forward_presplit", P(self.x_split), x_scale, P(self.W_ih), P(self.b_ih),
-                       P(self.z), M, 4 * H, D, P(self.ws), self.ws.numel(), P(self.status), st)
+                       P(z), M, 4 * H, D, P(self.ws), self.ws.numel(), P(self.status), st)
                 if record:
                     e[1].record()
-                L.call("hs_scan_forward_kf", P(self.z), P(self.c0), P(self.out), P(self.c), P(self.h_n),
-                       P(self.c_n), T, mb, H, 1e-6, P(self.ws), self.ws.numel(), cmax, P(self.status), st)
+                L.call("hs_scan_forward_kf", P(z), P(c0), P(out), P(c), P(h_n),
+                       P(c_n), T, mb, H, 1e-6, P(self.ws), self.ws.numel(), cmax, P(self.status), st)
             if record:
                 e[len(self.names) - 2].record()
             # the scan backward writes dZ as the fp16 split the GEMMs read
-            L.call("hs_scan_backward_split", P(self.z), P(self.c), P(self.c0), P(Gs), None, None, cmax,
+            L.call("hs_scan_backward_split", P(z), P(c), P(c0), P(Gs), None, None, cmax,
                    P(self.dz_split), dz_scale, None, P(self.db_mb), T, mb, H, 1e-6, P(self.ws),
                    self.ws.numel(), P(self.status), st)
             if record:
                 e[len(self.names) - 1].record()
             # dX and dW_ih (accumulated over micro-batches) in one call
             L.call("hs_linear_backward_presplit", P(self.dz_split), dz_scale, None, P(self.x_split), x_scale,
-                   P(self.W_ih), P(self.dx), P(self.dW), M, 4 * H, D, 1 if i else 0, P(self.ws), self.ws.numel(),
+                   P(self.W_ih), P(dx), P(self.dW), M, 4 * H, D, 1 if i else 0, P(self.ws), self.ws.numel(),
                    P(self.status), st)
             if record:
                 e[len(self.names)].record()
@@ -279,7 +306,8 @@ class ParallelStep:
                 self.ms[n] += e[k].elapsed_time(e[k + 1])
 
     def units(self, kernel):
-        T, D, H, mb = self.cfg["T"], self.cfg["D"], self.cfg["H"], self.mb
+        """Work of one average call (launch counts are per micro-batch)."""
+        T, D, H, mb = self.cfg["T"], self.cfg["D"], self.cfg["H"], self.mb_mean
         if kernel in ("scan_fwd", "scan_bwd"):
             return T * mb * H
         nprod = 2 if kernel == "linear_bwd" else 1  # dX and dW_ih; proj_scan: the projection's flops
@@ -381,7 +409,7 @@ def run_ours(args, cfg, rank, world, dev):
         B_local = B_global  # recurrent configs: every rank runs the full config (replicas)
     params = make_params(cfg)
     if cfg["mode"] == "parallel":
-        x, G = make_data(cfg, B_local, rank, dev, mb=min(MICRO_BATCH, B_local))
+        x, G = make_data(cfg, B_local, rank, dev, mb=micro_batches(B_local, H))
     else:
         x, G = make_data(cfg, B_local, rank, dev)
     peak_hbm, peak_tf_burst, peak_tf, peak_kind = _peaks()
@@ -594,7 +622,7 @@ def fused_variant(args, cfg, params, x, G, B_local, dev, sync, max_over_ranks, p
     step.collect(allev)
     from prlstm_b200 import _lib
     _lib.check_device_status(dev)
-    units = T * step.mb * H  # (t, b, h) per micro-batch
+    units = T * step.mb_mean * H  # (t, b, h) per micro-batch
     nl = steps * step.nmb
     res = {
         "what": "the same training step with hs_projection_scan_forward in place of the projection GEMM and "
@@ -710,8 +738,8 @@ def e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync, max_over_ra
     import prlstm_b200
 
     T, D, H = cfg["T"], cfg["D"], cfg["H"]
-    mb = min(MICRO_BATCH, B_local)
-    nmb = B_local // mb
+    mb = x[0].shape[1]  # the micro-batches of make_data (micro_batches)
+    nmb = len(x)
     m = prlstm_b200.HeadStartLSTM(D, H, parallel=True).to(dev)
     with torch.no_grad():
         for p, v in zip(m.parameters(), params):
@@ -1341,9 +1369,9 @@ def run_bf16_module(args, cfg, world, dev, rank, steps=10, warmup=3):
     variant): fwd + sum(out*G) backward through prlstm_b200.HeadStartLSTM,
     inputs resident on the device, CUDA events around the steps.  Recurrent
     configs: every rank runs the full config (replicas).  Parallel configs:
-    the batch is split over ranks and run in micro-batches of MICRO_BATCH
-    sequences (gradients accumulated, then all-reduced), as the float32
-    headline.  tokens/s is the whole job's."""
+    the batch is split over ranks and run in the float32 headline's
+    micro-batches (micro_batches; gradients accumulated, then all-reduced).
+    tokens/s is the whole job's."""
     import torch.distributed as dist
 
     import prlstm_b200
@@ -1357,7 +1385,7 @@ def run_bf16_module(args, cfg, world, dev, rank, steps=10, warmup=3):
             p_.copy_(v)
     B_local = B // world if parallel else B
     if parallel:
-        xs, Gs = make_data(cfg, B_local, rank, dev, mb=min(MICRO_BATCH, B_local))
+        xs, Gs = make_data(cfg, B_local, rank, dev, mb=micro_batches(B_local, H))
         xs = [t.to(torch.bfloat16) for t in xs]
         Gs = [t.to(torch.bfloat16) for t in Gs]
     else:
@@ -1412,9 +1440,9 @@ def _config_obj(name, cfg, world, workload):
     o = {"workload": workload or (f"{name}: {cfg['mode']} mode fwd+bwd of sum(out*G), T={cfg['T']}, "
                                   f"B={cfg['B']}, D={cfg['D']}, H={cfg['H']}"),
          "T": cfg["T"], "B": cfg["B"], "D": cfg["D"], "H": cfg["H"], "mode": cfg["mode"],
-         "micro_batch": MICRO_BATCH if cfg["mode"] == "parallel" else None,
+         "micro_batch": micro_batches(cfg["B"] // world, cfg["H"]) if cfg["mode"] == "parallel" else None,
          "parallelism": f"dp{world}" if cfg["mode"] == "parallel" or world == 1 else f"{world} replicas",
-         "l2": ("inputs larger than L2 (z of one micro-batch is 8.6 GB)" if name == "cfg4"
+         "l2": ("inputs larger than L2 (z of one micro-batch is 8.6-9.9 GB)" if name == "cfg4"
                 else "no flush; the working set of one step is noted by T, B, D, H")}
     return o
 

@@ -242,6 +242,13 @@ HS_API int hs_projection_scan_forward(const void *x_split, const unsigned *x_sca
  * published: float32 results may differ in the last bits between runs).
  * HS_SCAN_PATH=chain|lookback forces one. */
 HS_API int hs_scan_uses_column_kernels(int64_t T, int64_t B, int64_t H);
+/* Sizing hint for callers that split a batch into several calls (micro-
+ * batches): the number of sequences whose per-column scan CTAs (one per
+ * sequence x 64 units) are all resident at once on the current device, in
+ * the forward and the backward; calls of about this many sequences fill the
+ * SMs with one wave of columns (0 if it cannot be queried).  No reference
+ * counterpart (the reference runs its batch as one call). */
+HS_API int64_t hs_scan_wave_sequences(int64_t H);
 HS_API size_t hs_scan_split_workspace_bytes(int64_t T, int64_t B, int64_t H);
 HS_API int hs_scan_backward_split(float *z, const float *c, const float *c0, const float *dout,
                                   const float *dh_n, const float *dc_n, const unsigned *kf_max,

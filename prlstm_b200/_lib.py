@@ -62,6 +62,7 @@ SIGNATURES = {
     "hs_projection_scan_supported": (_i32, [_i64] * 4),
     "hs_projection_scan_forward": (_i32, [_c_p] * 10 + [_i64] * 4 + [_f32, _c_p, _sz, _c_p, _c_p, _c_p]),
     "hs_scan_uses_column_kernels": (_i32, [_i64] * 3),
+    "hs_scan_wave_sequences": (_i64, [_i64]),
     "hs_scan_split_workspace_bytes": (_sz, [_i64] * 3),
     "hs_scan_backward_split": (_i32, [_c_p] * 11 + [_i64] * 3 + [_f32, _c_p, _sz, _c_p, _c_p]),
     "hs_scan_chunk_maps": (_i32, [_c_p] * 4 + [_i64] * 3 + [_f32, _c_p, _c_p, _i32, _c_p]),

@@ -48,6 +48,7 @@
 namespace hs {
 
 bool scan_chain_wanted(int64_t T, int64_t B, int64_t H);
+int64_t scan_wave_sequences(int64_t H);
 int scan_fwd_chain_launch(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
                           int64_t T, int64_t B, int64_t H, float eps, unsigned *kf_max, int *status,
                           cudaStream_t st);
@@ -953,6 +954,8 @@ int hs_scan_backward_bf16(const void *z, const void *c, const float *c0, const v
 int hs_scan_uses_column_kernels(int64_t T, int64_t B, int64_t H) {
   return (T > 0 && B > 0 && H > 0 && hs::scan_chain_wanted(T, B, H)) ? 1 : 0;
 }
+
+int64_t hs_scan_wave_sequences(int64_t H) { return hs::scan_wave_sequences(H); }
 
 size_t hs_scan_split_workspace_bytes(int64_t T, int64_t B, int64_t H) {
   return (T > 0 && B > 0 && H > 0) ? hs::scan_split_ws_bytes(T, B, H) : 0;

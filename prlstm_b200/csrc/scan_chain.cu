@@ -879,6 +879,27 @@ bool scan_chain_wanted(int64_t T, int64_t B, int64_t H) {
   return T >= 64 && ncol >= (int64_t)HS_CHAIN_MIN_COLS_PER_SM * sm_count();
 }
 
+// Sequences whose per-column scan CTAs (two units per lane, 64-unit columns)
+// are all resident at once on the current device, in both directions: the
+// batch per call at which one wave of columns fills the SMs.  0 if the
+// occupancy cannot be queried.
+int64_t scan_wave_sequences(int64_t H) {
+  if (H <= 0) return 0;
+  const void *f = (const void *)scan_fwd_col2_kernel<float>;
+  const void *b = (const void *)scan_bwd_col2_kernel<kDzSplit, float>;
+  if (allow_dynamic_smem(f, kF2Smem, &g_fwd2_attr[0]) || allow_dynamic_smem(b, kB2Smem, &g_bwd2_attr[1])) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  int nf = 0, nb = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nf, f, kFNW * 32, kF2Smem) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, b, kBNW * 32, kB2Smem) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  return (int64_t)std::min(nf, nb) * sm_count() / ((H + 63) / 64);
+}
+
 int scan_fwd_chain_launch(const float *z, const float *c0, float *out, float *c, float *h_n, float *c_n,
                           int64_t T, int64_t B, int64_t H, float eps, unsigned *kf_max, int *status,
                           cudaStream_t st) {
