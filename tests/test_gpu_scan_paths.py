@@ -258,3 +258,18 @@ def test_linear_backward_from_split(path):
            P(L.status_word(dev)), st)
     torch.cuda.synchronize(dev)
     assert _rel(y, x.double().cpu() @ wf.double().cpu().t() + bias.double().cpu()) < 2e-6
+
+
+def test_scan_wave_sequences_sizing_hint():
+    """hs_scan_wave_sequences(H): the sequences whose per-column scan CTAs
+    (one per sequence x 64 units) are all resident at once, i.e. resident
+    CTAs per SM x SMs / columns per sequence."""
+    from prlstm_b200 import _lib as L
+
+    lib = L.load()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    w64 = lib.hs_scan_wave_sequences(64)
+    assert w64 > 0 and w64 % sms == 0 and 1 <= w64 // sms <= 16, (w64, sms)
+    assert lib.hs_scan_wave_sequences(1024) == w64 // 16
+    assert lib.hs_scan_wave_sequences(1000) == w64 // 16  # 16 columns of 64 units
+    assert lib.hs_scan_wave_sequences(0) == 0
