@@ -34,12 +34,14 @@
 // tile can always proceed (the grid never exceeds the resident pairs).
 // With chains >= pairs the tile waited for finished rounds earlier.
 //
-// The scan inside a tile: each warp holds 32 steps (lane = step) and runs
-// an inclusive Kogge-Stone scan of the affine maps (f', (i g)') over its
-// lanes per unit; the four warps' aggregates meet in shared memory, where
-// one warp composes the tile's total map, waits for the carry, publishes the
-// tile's end carry (end = A_total c_in + C_total) and hands c_in to the
-// others.  Every product of maps is of nonnegative terms (no cancellation).
+// The scan inside a tile: the epilogue threads (thread = time step) write
+// each unit's f' and (i g)' into the staging buffers that the next store
+// will use, unit-major; then a thread per (unit, segment of 8 steps) walks
+// its 8 steps in order (the segment's map c -> A c + C), a 16-lane shuffle
+// scan combines the unit's 16 segments, the last segment's thread hands the
+// chain's carry in and out, every walker then produces c at its 8 steps
+// (and the backward's bound), and the step threads read c back.  Every
+// product of maps is of nonnegative terms (no cancellation).
 //
 // Every wait is bounded; a failed wait is made uniform across the 128
 // threads of an epilogue quad by a reducing named barrier.  No cluster
@@ -81,8 +83,7 @@ constexpr int PS_QU = PS_UB / PS_NQ;             // units per quad
 constexpr int PS_THREADS = 64 + PS_NQ * 128;     // producer, MMA, 16 epilogue warps
 constexpr int PS_BOX = PS_TT * PS_QU * 4;        // 4 KB staging box (32-byte rows)
 constexpr int PS_NBUF = 4;                       // staging boxes per quad
-constexpr int PS_AGG = 12 * PS_QU;               // per quad: 4 row blocks x (A, C, carry in)
-constexpr int PS_SMEM = PS_STAGES * PS_STAGE + PS_NQ * (PS_NBUF * PS_BOX + PS_AGG * 4) + 1024 + 256;
+constexpr int PS_SMEM = PS_STAGES * PS_STAGE + PS_NQ * PS_NBUF * PS_BOX + 1024 + 256;
 static_assert(PS_SMEM <= 232448, "shared memory per block");
 static_assert(PS_QU == 8, "the epilogue's boxes and TMEM loads are 8 columns wide");
 constexpr uint32_t PS_TMEM_COLS = PS_NACC * PS_N;  // 512
@@ -223,8 +224,7 @@ proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_con
   unsigned char *smem =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float *epi = reinterpret_cast<float *>(smem + PS_STAGES * PS_STAGE);  // 4 quads x PS_NBUF staging boxes
-  float *aggs = epi + PS_NQ * PS_NBUF * (PS_BOX / 4);                   // 4 quads x PS_AGG floats
-  uint64_t *full = reinterpret_cast<uint64_t *>(aggs + PS_NQ * PS_AGG);
+  uint64_t *full = reinterpret_cast<uint64_t *>(epi + PS_NQ * PS_NBUF * (PS_BOX / 4));
   uint64_t *empty = full + PS_STAGES;
   uint64_t *pfull = empty + PS_STAGES;
   uint64_t *pempty = pfull + PS_NACC;
@@ -362,8 +362,6 @@ proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_con
     const bool issuer = lead && lane == 0;
     float *stg = epi + quad * PS_NBUF * (PS_BOX / 4);
     int sp = 0;  // staged pairs so far (alternating buffer pairs)
-    // the row blocks' step maps and the carries into them
-    float *aggA = aggs + quad * PS_AGG, *aggC = aggA + 4 * PS_QU, *cwin = aggA + 8 * PS_QU;
     // Undo the two operand scales one at a time (each inverse is an exact
     // power of two within float range, their product may not be).
     const float inv_a = 1.0f / pow2_scale(*p.absmax_a), inv_b = 1.0f / pow2_scale(*p.absmax_b);
@@ -419,92 +417,95 @@ proj_scan_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_con
       }
       store_two<0, PS_QU>(v, stg, sp, &tmZ, &tmZ, r, issuer, bar, u0, H + u0, bq, t0);
 
-      // gates (z_i, z_f are staged; z_g, z_o stay until their boxes), then
-      // each warp's inclusive scan of the step maps over its 32 steps:
-      // c_r = A_r c_in + C_r.  f' -> v[8 + j], C -> v[j], A -> a[j],
-      // e^-o -> eo[j].
-      float a[PS_QU], eo[PS_QU];
+      // Gates (z_i, z_f are staged; z_g, z_o stay until their boxes): f'
+      // and (i g)' go to the staging pair the next store_two will use (free
+      // until then), unit-major, for the walk; e^-o stays in registers.
+      float *fpS = stg + (sp & 1) * 2 * (PS_BOX / 4), *bpS = fpS + PS_BOX / 4;  // [8 units][128 steps]
+      float eo[PS_QU];
 #pragma unroll
       for (int j = 0; j < PS_QU; ++j) {
-        const float fp = fmaxf(sigf(v[PS_QU + j]), eps);
-        float C = fmaxf(sig2(v[j], v[2 * PS_QU + j]), eps);
-        float A = fp;
-        v[PS_QU + j] = fp;
+        fpS[j * PS_TT + r] = fmaxf(sigf(v[PS_QU + j]), eps);
+        bpS[j * PS_TT + r] = fmaxf(sig2(v[j], v[2 * PS_QU + j]), eps);
         eo[j] = __expf(-v[3 * PS_QU + j]);
+      }
+      named_sync(bar);
+
+      // The walk: thread (unit u, segment sg) takes steps 8 sg .. 8 sg + 7 of
+      // unit u in order.  Its segment's map c -> A c + C, the 16 segments of
+      // the unit combined by a 16-lane shuffle scan, the chain's carry in and
+      // out by the last segment's thread, then c at every step of the
+      // segment (written over (i g)') and the backward's bound.
+      bool good = true;
+      {
+        const int tq = (e & 3) * 32 + lane, u = tq >> 4, sg = tq & 15;
+        const float4 f0 = *reinterpret_cast<const float4 *>(fpS + u * PS_TT + 8 * sg);
+        const float4 f1 = *reinterpret_cast<const float4 *>(fpS + u * PS_TT + 8 * sg + 4);
+        const float4 b0 = *reinterpret_cast<const float4 *>(bpS + u * PS_TT + 8 * sg);
+        const float4 b1 = *reinterpret_cast<const float4 *>(bpS + u * PS_TT + 8 * sg + 4);
+        const float fw[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+        const float bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        float A = 1.f, C = 0.f;
 #pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const float Ap = __shfl_up_sync(0xffffffffu, A, off), Cp = __shfl_up_sync(0xffffffffu, C, off);
-          if (lane >= off) {
+        for (int i = 0; i < 8; ++i) {
+          C = fmaf(fw[i], C, bw[i]);
+          A *= fw[i];
+        }
+#pragma unroll
+        for (int off = 1; off < 16; off <<= 1) {
+          const float Ap = __shfl_up_sync(0xffffffffu, A, off, 16), Cp = __shfl_up_sync(0xffffffffu, C, off, 16);
+          if (sg >= off) {
             C = fmaf(A, Cp, C);
             A *= Ap;
           }
         }
-        a[j] = A;
-        v[j] = C;
-      }
-      if (lane == 31) {
-#pragma unroll
-        for (int j = 0; j < PS_QU; ++j) {
-          aggA[q * PS_QU + j] = a[j];
-          aggC[q * PS_QU + j] = v[j];
-        }
-      }
-      // the Z of g and o; its barrier also makes the step maps visible
-      store_two<2 * PS_QU, 3 * PS_QU>(v, stg, sp, &tmZ, &tmZ, r, issuer, bar, 2 * H + u0, 3 * H + u0, bq, t0);
-
-      // The carry warp (lanes 0..7 = units): the tile's total map, the
-      // chain's carry in, the tile's end carry out (published first), then
-      // the carry into each row block.
-      bool good = true;
-      if (lead) {
-        const int j = lane & (PS_QU - 1);
-        float At = aggA[j], Ct = aggC[j];
-#pragma unroll
-        for (int k = 1; k < 4; ++k) {
-          const float a2 = aggA[k * PS_QU + j];
-          Ct = fmaf(a2, Ct, aggC[k * PS_QU + j]);
-          At *= a2;
+        // the map of the segments before this one (identity for the first)
+        float Ae = __shfl_up_sync(0xffffffffu, A, 1, 16), Ce = __shfl_up_sync(0xffffffffu, C, 1, 16);
+        if (sg == 0) {
+          Ae = 1.f;
+          Ce = 0.f;
         }
         float cin = eps;
-        if (bvalid) {
-          unsigned long long *slot = p.slots + (int64_t)bq * H + u0 + j;
-          if (tt == 0) cin = fmaxf(p.c0 ? p.c0[(int64_t)bq * H + u0 + j] : 0.f, eps);
+        if (sg == 15 && bvalid) {
+          unsigned long long *slot = p.slots + (int64_t)bq * H + u0 + u;
+          if (tt == 0) cin = fmaxf(p.c0 ? p.c0[(int64_t)bq * H + u0 + u] : 0.f, eps);
           else good = gslot_wait(slot, (unsigned)tt, &cin, p.status);
-          good = __all_sync(0xffffffffu, good);
-          if (good && tt + 1 < p.ntt && lane < PS_QU) gslot_put(slot, (unsigned)(tt + 1), fmaf(At, cin, Ct));
+          if (good && tt + 1 < p.ntt) gslot_put(slot, (unsigned)(tt + 1), fmaf(A, cin, C));
         }
-        if (lane < PS_QU) {
-          float cw = cin;
-          cwin[j] = cw;
+        cin = __shfl_sync(0xffffffffu, cin, (lane & 16) | 15);
+        float c = fmaf(Ae, cin, Ce);  // c just before this segment's first step
+        float cs[8];
 #pragma unroll
-          for (int k = 0; k < 3; ++k) {
-            cw = fmaf(aggA[k * PS_QU + j], cw, aggC[k * PS_QU + j]);
-            cwin[(k + 1) * PS_QU + j] = cw;
-          }
+        for (int i = 0; i < 8; ++i) {
+          if (bvalid && t0 + 8 * sg + i < p.T) kmax = fmaxf(kmax, c * fw[i] * (1.f - fw[i]));
+          c = fmaf(fw[i], c, bw[i]);
+          cs[i] = c;
         }
+        *reinterpret_cast<float4 *>(bpS + u * PS_TT + 8 * sg) = make_float4(cs[0], cs[1], cs[2], cs[3]);
+        *reinterpret_cast<float4 *>(bpS + u * PS_TT + 8 * sg + 4) = make_float4(cs[4], cs[5], cs[6], cs[7]);
       }
       if (!named_and(bar, good && ld_status(p.status) == 0)) break;
 
-      // c -> v[16 + j], out -> v[24 + j], and the backward's bound
-      const bool rvalid = bvalid && t0 + r < p.T;
+      // c and out at this thread's step
+      float cc[PS_QU], oo[PS_QU];
 #pragma unroll
       for (int j = 0; j < PS_QU; ++j) {
-        const float cw = cwin[q * PS_QU + j];  // c just before this warp's first step
-        const float c = fmaf(a[j], cw, v[j]);
-        float cprev = __shfl_up_sync(0xffffffffu, c, 1);
-        if (lane == 0) cprev = cw;
-        const float fp = v[PS_QU + j];
-        if (rvalid) kmax = fmaxf(kmax, cprev * fp * (1.f - fp));
-        v[2 * PS_QU + j] = c;
-        v[3 * PS_QU + j] = sig_tanh_pos(eo[j], c);
+        cc[j] = bpS[j * PS_TT + r];
+        oo[j] = sig_tanh_pos(eo[j], cc[j]);
+      }
+      named_sync(bar);  // the walk's buffers are read before the Z of g and o goes there
+      store_two<2 * PS_QU, 3 * PS_QU>(v, stg, sp, &tmZ, &tmZ, r, issuer, bar, 2 * H + u0, 3 * H + u0, bq, t0);
+#pragma unroll
+      for (int j = 0; j < PS_QU; ++j) {
+        v[2 * PS_QU + j] = cc[j];
+        v[3 * PS_QU + j] = oo[j];
       }
       store_two<2 * PS_QU, 3 * PS_QU>(v, stg, sp, &tmC, &tmO, r, issuer, bar, u0, u0, bq, t0);
-      if (rvalid && t0 + r == p.T - 1) {
+      if (bvalid && t0 + r == p.T - 1) {
         const int64_t ci = (int64_t)bq * H + u0;
 #pragma unroll
         for (int j = 0; j < PS_QU; ++j) {
-          if (p.h_n) p.h_n[ci + j] = v[3 * PS_QU + j];
-          if (p.c_n) p.c_n[ci + j] = v[2 * PS_QU + j];
+          if (p.h_n) p.h_n[ci + j] = oo[j];
+          if (p.c_n) p.c_n[ci + j] = cc[j];
         }
       }
     }
