@@ -611,10 +611,11 @@ int ps_capacity() {
 // HS_PROJ_SCAN: 0 never takes the fused kernel, 1 takes it for every shape
 // it can run; unset, it is taken when the sequence fits one time tile (no
 // carries between tiles).  Measured on B200 (configs[4]'s 32-sequence
-// micro-batch, T = 4096, run alone): 1.84 ms fused against 1.78 ms for the
-// projection GEMM (N = 256 tiles) and the column scan, the epilogue's ~100
-// instructions per (step, unit) not hidden behind the MMAs; at T = 128
-// (configs[1]) the fused step is 22% faster.
+// micro-batch, T = 4096, one box): run alone, 1.78 ms fused against
+// 1.83-1.89 ms for the projection GEMM (N = 256 tiles) and the column scan;
+// inside the power-capped training step, where tensor and SIMT work at once
+// draw more power, 10.7 ms against 9.4 ms per 37-sequence micro-batch; at
+// T = 128 the fused step is 22% faster.
 int ps_mode() {
   static int v = -2;
   if (v == -2) {
