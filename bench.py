@@ -4,12 +4,14 @@ Default workload (``--config cfg4``): configs[4] of the benchmark, the
 long-sequence parallel (Heinsen-scan) training step, T=16384, B=256 (global),
 D=512, H=1024, a=0, fp32, fwd + backward of sum(out*G).  The batch is split
 across ranks (strong scaling: the global batch is fixed) and each rank runs
-its share as micro-batches of 32 sequences with gradients accumulated, then
-one NCCL all-reduce SUM of the weight gradients.  Inputs are seeded
-synthetic data with the config's distributions (no dataset exists).
+its share as micro-batches sized to one wave of the scan kernels' columns
+(micro_batches: 4 x 37 + 3 x 36 on one GPU, 32 at 2-8 GPUs) with gradients
+accumulated, then one NCCL all-reduce SUM of the weight gradients.  Inputs
+are seeded synthetic data with the config's distributions (no dataset
+exists).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfgX]
-    python bench.py --impl reference ...   # CPU reference arm (the oracle port)
+    python bench.py --impl reference ...   # CPU reference arm (the stock reference package)
 
 ``value``: tokens/s (T*B per step, whole job) with inputs resident in HBM,
 timed with CUDA events on the launching stream, max over ranks.
