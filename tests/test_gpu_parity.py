@@ -337,6 +337,25 @@ def test_batch_first_and_hx_golden():
     assert_close(ours, exp, REC_TOL, "batch_first+hx")
 
 
+def test_fused_projection_scan_through_module_with_hx_batch_first():
+    """The module's parallel forward at a shape the library runs as one
+    fused projection + scan kernel (T <= 128 and the tensor-core GEMM size;
+    hs_projection_scan_supported), with hx (its c0 enters the kernel's first
+    time tile, and gets a gradient) and batch_first, against float64."""
+    from prlstm_b200 import _lib as L
+
+    T, B, D, H = 128, 24, 256, 256
+    assert L.load().hs_projection_scan_supported(T, B, D, H) == 1
+    params, x, G = make_inputs(T, B, D, H, a=0.0, bias_spread=8.0, seed=31)
+    g = torch.Generator().manual_seed(32)
+    hx = (torch.randn(B, H, generator=g) * 0.3, torch.rand(B, H, generator=g))
+    ours = run_ours(params, x, G, parallel=True, hx=hx, batch_first=True)
+    p64 = tuple(t.double() for t in params)
+    truth = O.module_forward_backward(p64, x.double(), G.double(), parallel=True,
+                                      hx=(hx[0].double(), hx[1].double()), linear_truth=True)
+    assert_close(ours, truth, 1e-5, "fused+hx+batch_first")
+
+
 # ------------------------------------------------------------ size-independent properties
 def test_parallel_batch_independence():
     """Each sequence's result does not depend on the others in the batch (up
