@@ -212,8 +212,10 @@ HS_API int hs_scan_forward_kf(const float *z, const float *c0, float *out, float
  * and dev_status; workspace >= hs_projection_scan_workspace_bytes (256-byte
  * aligned).  hs_projection_scan_supported says whether the library's own
  * forward (hs_parallel_forward*) takes this kernel for a shape by default
- * (it does for T <= 128, where it is faster than the GEMM and the scan as
- * two calls; at longer T it is about as fast and is not the default);
+ * (it does for 112 <= T <= 128, one mostly filled time tile of 128 steps,
+ * where it is faster than the GEMM and the scan as two calls; a tile
+ * always spans 128 steps, so much shorter sequences would pad it, and at
+ * longer T the two calls win inside a power-capped training step);
  * HS_PROJ_SCAN=0 / 1 turns that off / on for every shape it can run.  Replaces, with hs_split, the projection `linear` and the scan of
  * headstartlstm_parallel (_parallel.py:38-74, _parallel.py:21-35). */
 HS_API size_t hs_projection_scan_workspace_bytes(int64_t T, int64_t B, int64_t D, int64_t H);

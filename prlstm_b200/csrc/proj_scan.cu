@@ -609,8 +609,9 @@ int ps_capacity() {
 }
 
 // HS_PROJ_SCAN: 0 never takes the fused kernel, 1 takes it for every shape
-// it can run; unset, it is taken when the sequence fits one time tile (no
-// carries between tiles).  Measured on B200 (configs[4]'s 32-sequence
+// it can run; unset, it is taken when the sequence fills most of one time
+// tile (112 <= T <= 128: no carries between tiles, at most 1/8 of the
+// tile's rows padding).  Measured on B200 (configs[4]'s 32-sequence
 // micro-batch, T = 4096, one box): run alone, 1.78 ms fused against
 // 1.83-1.89 ms for the projection GEMM (N = 256 tiles) and the column scan;
 // inside the power-capped training step, where tensor and SIMT work at once
@@ -651,7 +652,9 @@ bool proj_scan_wanted(int64_t T, int64_t B, int64_t D, int64_t H) {
   const int npairs = ps_capacity();
   if (npairs < 1) return false;
   if (mode == 1) return true;
-  return T <= PS_TT;
+  // one time tile, mostly filled: a tile always spans PS_TT steps, so at
+  // small T most of its MMA rows would be padding
+  return T <= PS_TT && 8 * T >= 7 * PS_TT;
 }
 
 // Z, out, c [T][B][4H | H | H], h_n, c_n and *kf (max c_{t-1} f'(1-f')) from

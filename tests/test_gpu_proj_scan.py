@@ -124,13 +124,17 @@ def test_projection_scan_matches_oracle_and_two_call_path(case):
 
 
 def test_projection_scan_policy_and_errors():
-    """The default policy takes the fused kernel when T fits one time tile
-    (configs[1]), not over longer T (configs[4], where the two calls are as
-    fast); shapes it cannot run are refused with an error."""
+    """The default policy takes the fused kernel when T fills most of one
+    128-step time tile, not for short T (a tile would be mostly
+    padding) nor over longer T (configs[4], where the two calls are faster
+    in the step); shapes it cannot run are refused with an error."""
     from prlstm_b200 import _lib as L
 
     lib = L.load()
     assert lib.hs_projection_scan_supported(128, 32, 256, 256) == 1
+    assert lib.hs_projection_scan_supported(112, 32, 256, 256) == 1
+    assert lib.hs_projection_scan_supported(8, 2048, 512, 1024) == 0
+    assert lib.hs_projection_scan_supported(100, 32, 256, 256) == 0
     assert lib.hs_projection_scan_supported(16384, 32, 512, 1024) == 0
     assert lib.hs_projection_scan_supported(16384, 2, 512, 1024) == 0
     assert lib.hs_projection_scan_supported(256, 32, 512, 1000) == 0  # H % 32
