@@ -6,7 +6,8 @@ _parallel.py:21-74) and against the two calls it replaces
 
 Shapes: a partial last time tile (T not a multiple of 128), odd B (the
 second CTA of the last pair has no sequence), D not a multiple of 64 (a
-zero-filled k tail), no bias, c0 given or not, several time tiles per chain
+zero-filled k tail) or of 8 (padded split rows), the smallest H (one
+32-unit block), no bias, c0 given or not, several time tiles per chain
 (carries handed between tiles), one time tile (no carries), a configs[4]
 micro-batch width (512 chains of 2 sequences x 32 units), and configs[4]'s
 full T = 16384 on a few chains (128 tiles per chain)."""
@@ -24,6 +25,8 @@ CASES = [
     (128, 32, 256, 256, True, True),
     (512, 32, 512, 1024, True, True),
     (16384, 4, 64, 128, True, True),
+    (300, 9, 100, 32, True, True),   # D % 8 != 0 (padded split rows), H = 32 (one unit block)
+    (130, 7, 520, 64, False, True),  # T just past one tile, K tail of 8 in the last k-block
 ]
 EPS = 1e-6
 
