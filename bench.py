@@ -321,8 +321,11 @@ class PrefetchedInputs:
     host-to-device copies run on a copy stream into a device staging buffer,
     issued right after the previous step's replay was launched (so that they
     overlap it), and are moved into the graph's static input buffers (a
-    device-to-device copy) before the step's own replay.  Every step copies
-    its inputs from pinned host memory inside the timed region."""
+    device-to-device copy) before the step's own replay.  A step that finds
+    no copy in flight (the first of the warm-up or of the timed region: the
+    step before it does not prefetch across that boundary) issues its own, so
+    that every timed step copies its inputs from pinned host memory inside
+    the timed region."""
 
     def __init__(self, host, static, dev):
         self.host, self.static = host, static
@@ -341,7 +344,10 @@ class PrefetchedInputs:
             self.ready.record()
 
     def consume(self):
+        if self.ready is None:
+            self.issue()
         torch.cuda.current_stream().wait_event(self.ready)
+        self.ready = None
         for t, st in zip(self.static, self.stage):
             t.copy_(st, non_blocking=True)
         self.free = torch.cuda.Event()
@@ -754,16 +760,23 @@ def e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync, max_over_ra
     torch.cuda.empty_cache()
     loss_host = torch.empty(1, pin_memory=True)
     copy_stream = torch.cuda.Stream(dev)
+    ahead = []  # the next step's first micro-batch, when this step prefetched it
 
-    def one_step():
-        m.zero_grad(set_to_none=True)
-        loss = torch.zeros((), device=dev)
-        # double-buffered host->device copies on a side stream
-        nxt = None
+    def issue(i):
         with torch.cuda.stream(copy_stream):
-            nxt = (hx[0].to(dev, non_blocking=True), hG[0].to(dev, non_blocking=True))
+            nxt = (hx[i].to(dev, non_blocking=True), hG[i].to(dev, non_blocking=True))
             ev = torch.cuda.Event()
             ev.record()
+        return nxt, ev
+
+    def one_step(prefetch=True):
+        m.zero_grad(set_to_none=True)
+        loss = torch.zeros((), device=dev)
+        # double-buffered host->device copies on a side stream; during the
+        # last micro-batch the next step's first one is copied (not across the
+        # warm-up/timed boundary, so each timed step's copies are all inside
+        # the timed region)
+        nxt, ev = ahead.pop() if ahead else issue(0)
         for i in range(nmb):
             torch.cuda.current_stream(dev).wait_event(ev)
             xd, Gd = nxt
@@ -771,10 +784,9 @@ def e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync, max_over_ra
             xd.record_stream(torch.cuda.current_stream(dev))
             Gd.record_stream(torch.cuda.current_stream(dev))
             if i + 1 < nmb:
-                with torch.cuda.stream(copy_stream):
-                    nxt = (hx[i + 1].to(dev, non_blocking=True), hG[i + 1].to(dev, non_blocking=True))
-                    ev = torch.cuda.Event()
-                    ev.record()
+                nxt, ev = issue(i + 1)
+            elif prefetch:
+                ahead.append(issue(0))
             out, _ = m(xd)
             lo = (out * Gd).sum()
             lo.backward()
@@ -813,28 +825,29 @@ def e2e_parallel(args, cfg, params, x, G, B_local, world, dev, sync, max_over_ra
             sloss.backward()
 
         pf = PrefetchedInputs([hx[0], hG[0]], [sx, sG], dev)
-        pf.issue()
 
-        def graphed():
+        def graphed(prefetch=True):
             pf.consume()  # this step's inputs, copied while the previous step ran
             g.replay()
-            pf.issue()    # the next step's inputs, overlapping this replay
+            if prefetch:
+                pf.issue()  # the next step's inputs, overlapping this replay
             loss_host.copy_(sloss.detach().reshape(1), non_blocking=True)
             torch.cuda.current_stream(dev).synchronize()
             return float(loss_host.item())
 
         one_step = graphed
 
-    for _ in range(max(1, min(args.warmup, 2))):
-        one_step()
+    warm = max(1, min(args.warmup, 2))
+    for w in range(warm):
+        one_step(prefetch=w + 1 < warm)
     sync()
     steps = max(1, min(args.steps, 5))
     t0 = time.perf_counter()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(steps):
-        one_step()
+    for s in range(steps):
+        one_step(prefetch=s + 1 < steps)
     e1.record()
     sync()
     ms = max_over_ranks(e0.elapsed_time(e1))
@@ -983,7 +996,7 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
     hG_ = G.cpu().pin_memory()
     loss_host = torch.empty(1, pin_memory=True)
 
-    def e2e_step():
+    def e2e_step(prefetch=True):  # copies on the compute stream: nothing to prefetch
         m.zero_grad(set_to_none=True)
         xd = hx_.to(dev, non_blocking=True).requires_grad_(True)
         Gd = hG_.to(dev, non_blocking=True)
@@ -1019,23 +1032,23 @@ def run_recurrent(args, cfg, params, x, G, B_local, world, dev, sync, max_over_r
             sloss.backward()
 
         pf = PrefetchedInputs([hx_, hG_], [sx, sG], dev)
-        pf.issue()
 
-        def e2e_step():
+        def e2e_step(prefetch=True):
             pf.consume()
             g.replay()
-            pf.issue()
+            if prefetch:
+                pf.issue()
             loss_host.copy_(sloss.detach().reshape(1), non_blocking=True)
             torch.cuda.current_stream(dev).synchronize()
 
-    for _ in range(args.warmup):
-        e2e_step()
+    for w in range(args.warmup):
+        e2e_step(prefetch=w + 1 < args.warmup)
     sync()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        e2e_step()
+    for s in range(args.steps):
+        e2e_step(prefetch=s + 1 < args.steps)
     e1.record()
     sync()
     ms_e = max_over_ranks(e0.elapsed_time(e1))
