@@ -47,6 +47,14 @@ int colsum(const float *x, float *out, int64_t M, int64_t N, int beta, cudaStrea
 bool rec_tc_wanted(int dir, int64_t B, int64_t H, bool bf = false);
 bool rec_cluster_wanted(int64_t B, int64_t H);
 size_t rec_cluster_ws_bytes(int64_t H);
+bool rec_wide_wanted(int64_t B, int64_t H);
+size_t rec_wide_ws_bytes(int64_t H);
+int rec_wide_forward(const float *h0, const float *c0, const float *w_hh, const float *b_hh, const float *a,
+                     float *h_save, float *c_save, float *acts, int64_t T, int64_t B, int64_t H, void *ws,
+                     size_t ws_bytes, int *status, cudaStream_t st);
+int rec_wide_backward(const float *w_hh, const float *a, const float *c_save, float *acts, const float *dout,
+                      const float *dh_n, const float *dc_n, int64_t T, int64_t B, int64_t H, void *ws,
+                      size_t ws_bytes, int *status, cudaStream_t st);
 int rec_cluster_forward(const float *h0, const float *c0, const float *w_hh, const float *b_hh, const float *a,
                         float *h_save, float *c_save, float *acts, int64_t T, int64_t B, int64_t H, void *ws,
                         size_t ws_bytes, int *status, cudaStream_t st);
@@ -673,7 +681,7 @@ size_t rec_ws_bytes(int64_t T, int64_t B, int64_t D, int64_t H) {
   if (!make_plan(p, B, H, nsm > 0 ? nsm : 148)) return 0;
   // the GEMMs run before the persistent kernels (forward) or after them
   // (backward), so they reuse the same scratch
-  return std::max<size_t>({p.total, rec_tc_ws_bytes(B, H), rec_cluster_ws_bytes(H), linear_ws_bytes(T * B, 4 * H, D),
+  return std::max<size_t>({p.total, rec_tc_ws_bytes(B, H), rec_cluster_ws_bytes(H), rec_wide_ws_bytes(H), linear_ws_bytes(T * B, 4 * H, D),
                            linear_ws_bytes(T * B, 4 * H, H), linear_backward_ws(T * B, 4 * H, D, H)});
 }
 
@@ -699,6 +707,10 @@ int rec_forward(const float *x, const float *h0, const float *c0, const float *w
   // small H: the whole recurrence of a batch group on one cluster
   if (rec_cluster_wanted(B, H))
     return rec_cluster_forward(h0, c0, w_hh, b_hh, a, h_save, c_save, acts, T, B, H, ws, ws_bytes, status, st);
+  // H = 512: clusters of 16 with a few sequences each, the state exchanged in
+  // distributed shared memory
+  if (rec_wide_wanted(B, H))
+    return rec_wide_forward(h0, c0, w_hh, b_hh, a, h_save, c_save, acts, T, B, H, ws, ws_bytes, status, st);
   // the step product on the tensor cores where the shape allows
   if (rec_tc_wanted(0, B, H, bf))
     return rec_tc_forward(h0, c0, w_hh, b_hh, a, h_save, c_save, acts, T, B, H, ws, ws_bytes, status, st, bf);
@@ -754,6 +766,9 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
   char *w = static_cast<char *>(ws);
   if (rec_cluster_wanted(B, H)) {
     if (int e = rec_cluster_backward(w_hh, a, c_save, acts, dout, dh_n, dc_n, T, B, H, ws, ws_bytes, status, st))
+      return e;
+  } else if (rec_wide_wanted(B, H)) {
+    if (int e = rec_wide_backward(w_hh, a, c_save, acts, dout, dh_n, dc_n, T, B, H, ws, ws_bytes, status, st))
       return e;
   } else if (rec_tc_wanted(1, B, H, bf)) {
     // the step product on the tensor cores
@@ -814,13 +829,13 @@ int rec_backward(const float *x, const float *w_ih, const float *w_hh, const flo
 extern "C" {
 
 int hs_recurrent_uses_tensor_cores(int64_t B, int64_t H, int backward) {
-  if (B <= 0 || H <= 0 || hs::rec_cluster_wanted(B, H)) return 0;
+  if (B <= 0 || H <= 0 || hs::rec_cluster_wanted(B, H) || hs::rec_wide_wanted(B, H)) return 0;
   return hs::rec_tc_wanted(backward ? 1 : 0, B, H) ? 1 : 0;
 }
 
 int hs_recurrent_path(int64_t B, int64_t H, int backward) {
   if (B <= 0 || H <= 0) return -1;
-  if (hs::rec_cluster_wanted(B, H)) return 2;
+  if (hs::rec_cluster_wanted(B, H) || hs::rec_wide_wanted(B, H)) return 2;
   return hs::rec_tc_wanted(backward ? 1 : 0, B, H) ? 1 : 0;
 }
 

@@ -458,6 +458,431 @@ __global__ void __launch_bounds__(kCT, 1) rcl_bwd_kernel(RclArgs p) {
   ccluster_sync();
 }
 
+// ------------------------------------------------------------ H = 512 (wide)
+//
+// The same recurrence at H = 512 on clusters of 16 CTAs with S
+// <= 8 sequences per cluster, the batch spread over as many clusters as the
+// device runs at once.  CTA j owns units 32j..32j+31, i.e. the 128 gate rows
+// ul*4+g of a*W_hh (256 KB of float32, more than one CTA's shared memory):
+// each thread keeps the first KR of its 32 k values of the slice in
+// registers, the rest of the slice stays in shared memory.
+//   forward:  gates[128 rows][S] = Z + (a W)_j h_{t-1} over the 512 units;
+//             h_{t-1} [512][S] is all-gathered (every CTA sends its units'
+//             block to every CTA, as in the kernels above);
+//   backward: the CTA's share of dh[512][S] = (a W)_j^T dgates_j over its 128
+//             rows is reduce-scattered: warp w computes the units of CTA w
+//             and sends that block to CTA w, which adds the 16 blocks it
+//             receives (in rank order) before its cells run.
+// Product layout, 512 threads: a lane holds a block of 4 outputs (rows
+// forward, units backward) x S sequences for one of 4 k subsets; the warp's
+// 4 k subsets are added by shuffles (forward: then the 4 warps of a row group
+// through shared memory).  Barriers, double buffering and bounded waits
+// follow the kernels above.
+constexpr int kWC = 16;               // CTAs per cluster
+constexpr int kWUC = 32;              // units per CTA
+constexpr int kWH = kWC * kWUC;       // H
+constexpr int kWR = 4 * kWUC;         // gate rows per CTA
+constexpr int kWT = 512;              // threads per CTA
+constexpr int kWMaxS = 8;             // sequences per cluster
+
+// Shared-memory carve-ups in floats (16-byte aligned pieces).
+template <int S>
+struct WideFwd {
+  static constexpr int XS = S <= 4 ? 4 : 8;  // floats per state row
+  static constexpr int KR = 12;              // k values per thread in registers
+  static constexpr int KS = kWH - 16 * KR;   // k rows of the slice in shared memory
+  static constexpr int o_w = 0;
+  static constexpr int o_bias = o_w + KS * kWR;
+  static constexpr int o_rx = o_bias + kWR;           // [2][512][XS]
+  static constexpr int o_stage = o_rx + 2 * kWH * XS;  // [2][32][XS]
+  static constexpr int o_red = o_stage + 2 * kWUC * XS;  // [4 k groups][128][XS]
+  static constexpr int o_bars = o_red + 4 * kWR * XS;
+  static constexpr int bytes = (o_bars + 4) * 4;
+};
+template <int S>
+struct WideBwd {
+  static constexpr int XS = S <= 4 ? 4 : 8;
+  static constexpr int KR = S <= 4 ? 12 : 14;  // rows per thread in registers
+  static constexpr int KS = kWR - 4 * KR;      // rows of the slice in shared memory
+  static constexpr int o_w = 0;
+  static constexpr int o_rx = o_w + KS * kWH;                 // [2][16 senders][32][XS]
+  static constexpr int o_stage = o_rx + 2 * kWC * kWUC * XS;  // [2][16 receivers][32][XS]
+  static constexpr int o_dg = o_stage + 2 * kWC * kWUC * XS;  // [128 rows][XS]
+  static constexpr int o_bars = o_dg + kWR * XS;
+  static constexpr int bytes = (o_bars + 4) * 4;
+};
+
+struct RwArgs {
+  const float *w;     // forward [16][512 k][128 rows]; backward [16][128 rows][512 units]
+  const float *bias;  // forward [16][128]
+  float *zacts;       // forward: Z in, activations out; backward: activations in, dgates out
+  const float *h0, *c0;
+  float *h_save, *c_save;
+  const float *dout, *dh_n, *dc_n;
+  int *status;
+  int64_t T, Bt;
+};
+
+template <int S, int XS>
+HS_DEV void wide_ldx(const float *p, float (&v)[S]) {
+  const float4 a = *reinterpret_cast<const float4 *>(p);
+  float t[8] = {a.x, a.y, a.z, a.w, 0.f, 0.f, 0.f, 0.f};
+  if constexpr (S > 4) {
+    const float4 b = *reinterpret_cast<const float4 *>(p + 4);
+    t[4] = b.x; t[5] = b.y; t[6] = b.z; t[7] = b.w;
+  }
+#pragma unroll
+  for (int s = 0; s < S; ++s) v[s] = t[s];
+}
+template <int S, int XS>
+HS_DEV void wide_stx(float *p, const float (&v)[S]) {
+  float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int s = 0; s < S; ++s) t[s] = v[s];
+  *reinterpret_cast<float4 *>(p) = make_float4(t[0], t[1], t[2], t[3]);
+  if constexpr (XS == 8) *reinterpret_cast<float4 *>(p + 4) = make_float4(t[4], t[5], t[6], t[7]);
+}
+// Sum of the 4 k subsets of a warp (lanes l, l^8, l^16, l^24), halving the
+// values at each exchange: afterwards lane l holds output 4-block element
+// (l >> 3) for its S sequences.
+template <int S>
+HS_DEV void wide_reduce4(const float (&acc)[4][S], int lane, float (&v)[S]) {
+  const bool hi2 = (lane & 16) != 0, hi1 = (lane & 8) != 0;
+  float b2[2][S];
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      const float send = hi2 ? acc[r][s] : acc[r + 2][s];
+      const float keep = hi2 ? acc[r + 2][s] : acc[r][s];
+      b2[r][s] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    const float send = hi1 ? b2[0][s] : b2[1][s];
+    const float keep = hi1 ? b2[1][s] : b2[0][s];
+    v[s] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+}
+
+template <int S>
+__global__ void __launch_bounds__(kWT, 1) rcw_fwd_kernel(RwArgs p) {
+  using L = WideFwd<S>;
+  constexpr int XS = L::XS, KR = L::KR;
+  constexpr int64_t H = kWH;
+  constexpr uint32_t sbytes = kWUC * XS * 4;  // one CTA's state block
+  extern __shared__ __align__(16) float smw[];
+  float *Ws = smw + L::o_w, *bias = smw + L::o_bias, *rx = smw + L::o_rx, *stage = smw + L::o_stage,
+        *red = smw + L::o_red;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smw + L::o_bars);
+  const uint32_t j = crank();
+  const int64_t T = p.T, Bt = p.Bt;
+  const int64_t b0 = (int64_t)(blockIdx.x / kWC) * S;
+  const int Bc = (int)min((int64_t)S, Bt - b0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // product: rows r0..r0+3 (row group warp & 3), k = 16 i + q, i < 32
+  const int kgw = warp >> 2, ks = lane >> 3;
+  const int r0 = 32 * (warp & 3) + 4 * (lane & 7), q = kgw * 4 + ks;
+  const float *wj = p.w + (size_t)j * kWH * kWR;  // [k][128 rows]
+  {
+    const float4 *src = reinterpret_cast<const float4 *>(wj + 16 * KR * kWR);
+    for (int i = tid; i < L::KS * kWR / 4; i += kWT) reinterpret_cast<float4 *>(Ws)[i] = src[i];
+  }
+  float wr[4][KR];
+#pragma unroll
+  for (int i = 0; i < KR; ++i) {
+    const float4 v = *reinterpret_cast<const float4 *>(wj + (size_t)(16 * i + q) * kWR + r0);
+    wr[0][i] = v.x;
+    wr[1][i] = v.y;
+    wr[2][i] = v.z;
+    wr[3][i] = v.w;
+  }
+  for (int i = tid; i < kWR; i += kWT) bias[i] = p.bias[(size_t)j * kWR + i];
+  if (tid == 0) {
+    cmbar_init(&bars[0], 1);
+    cmbar_init(&bars[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    cmbar_arrive_expect(&bars[0], kWC * sbytes);  // h0 blocks
+    cmbar_arrive_expect(&bars[1], kWC * sbytes);  // step 0's blocks
+  }
+  __syncthreads();
+  ccluster_sync();
+
+  // the cell of this thread (tid < 32 S): unit ul, sequence s
+  const bool is_cell = tid < kWUC * S;
+  const int ul = tid & 31, s = tid >> 5;
+  const bool valid = is_cell && s < Bc;
+  const int64_t u = (int64_t)j * kWUC + ul, bb = b0 + s;
+  float cst = 0.f;
+  float *stg0 = stage + kWUC * XS;  // block 1 carries h0 (block 0 is step 0's)
+  if (is_cell) {
+    float h = 0.f, c = 0.f;
+    if (valid) {
+      h = p.h0 ? p.h0[bb * H + u] : 0.f;
+      c = p.c0 ? p.c0[bb * H + u] : 0.f;
+      p.h_save[bb * H + u] = h;
+      p.c_save[bb * H + u] = c;
+    }
+    cst = c;
+    stg0[ul * XS + s] = h;
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncthreads();
+  if (tid < kWC) cbulk_s2c(cpeer(rx + j * kWUC * XS, (uint32_t)tid), stg0, sbytes, cpeer(&bars[0], (uint32_t)tid));
+
+  __shared__ int s_fail;
+  int64_t waited = 0;
+  bool fail = false;
+  for (int64_t t = 0; t < T && !fail; ++t) {
+    const int par = (int)(t & 1);
+    float zg[4] = {0.f, 0.f, 0.f, 0.f};
+    if (valid) {
+      const float *zr = p.zacts + (t * Bt + bb) * 4 * H + u;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) zg[g] = zr[g * H];
+    }
+    if (tid == 0) {
+      s_fail = !cmbar_wait(&bars[par], (uint32_t)((t >> 1) & 1), p.status);
+      if (!s_fail) {
+        ++waited;
+        if (t + 2 < T) cmbar_arrive_expect(&bars[par], kWC * sbytes);
+      }
+    }
+    __syncthreads();
+    if (s_fail) { fail = true; break; }
+    const float *X = rx + par * kWH * XS;  // h_{t-1} [512][XS]
+    float acc[4][S];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int b = 0; b < S; ++b) acc[r][b] = 0.f;
+#pragma unroll
+    for (int i = 0; i < KR; ++i) {
+      float xv[S];
+      wide_ldx<S, XS>(X + (16 * i + q) * XS, xv);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int b = 0; b < S; ++b) acc[r][b] = fmaf(wr[r][i], xv[b], acc[r][b]);
+    }
+#pragma unroll 4
+    for (int i = KR; i < 32; ++i) {
+      const int k = 16 * i + q;
+      const float4 wv = *reinterpret_cast<const float4 *>(Ws + (k - 16 * KR) * kWR + r0);
+      const float w4[4] = {wv.x, wv.y, wv.z, wv.w};
+      float xv[S];
+      wide_ldx<S, XS>(X + k * XS, xv);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int b = 0; b < S; ++b) acc[r][b] = fmaf(w4[r], xv[b], acc[r][b]);
+    }
+    float v[S];
+    wide_reduce4<S>(acc, lane, v);
+    wide_stx<S, XS>(red + (kgw * kWR + r0 + ks) * XS, v);
+    __syncthreads();
+    // cells; h_t into staging block par (outputs no other CTA reads are
+    // stored after the send)
+    float *stg = stage + par * kWUC * XS;
+    float act[4] = {0.f, 0.f, 0.f, 0.f}, hv = 0.f;
+    if (is_cell) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int row = ul * 4 + g;
+        float sum = 0.f;
+#pragma unroll
+        for (int kq = 0; kq < 4; ++kq) sum += red[(kq * kWR + row) * XS + s];
+        act[g] = sigf(zg[g] + sum + bias[row]);
+      }
+      const float c = fmaf(act[1], cst, act[0] * act[2]);
+      hv = act[3] * tanh_any(c);
+      cst = c;
+      stg[ul * XS + s] = valid ? hv : 0.f;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (tid < kWC && t + 1 < T)
+      cbulk_s2c(cpeer(rx + (par ^ 1) * kWH * XS + j * kWUC * XS, (uint32_t)tid), stg, sbytes,
+                cpeer(&bars[par ^ 1], (uint32_t)tid));
+    if (valid) {
+      float *ar = p.zacts + (t * Bt + bb) * 4 * H + u;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) ar[g * H] = act[g];
+      p.h_save[((t + 1) * Bt + bb) * H + u] = hv;
+      p.c_save[((t + 1) * Bt + bb) * H + u] = cst;
+    }
+  }
+  if (tid == 0 && fail) {
+    for (int64_t u2 = waited; u2 < std::min<int64_t>(T, waited + 2); ++u2)
+      cmbar_drain(&bars[u2 & 1], (uint32_t)((u2 >> 1) & 1));
+  }
+  __syncthreads();
+  ccluster_sync();
+}
+
+template <int S>
+__global__ void __launch_bounds__(kWT, 1) rcw_bwd_kernel(RwArgs p) {
+  using L = WideBwd<S>;
+  constexpr int XS = L::XS, KR = L::KR;
+  constexpr int64_t H = kWH;
+  constexpr uint32_t bbytes = kWUC * XS * 4;  // one block: 32 units x XS
+  extern __shared__ __align__(16) float smw[];
+  float *Ws = smw + L::o_w, *rx = smw + L::o_rx, *stage = smw + L::o_stage, *DG = smw + L::o_dg;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smw + L::o_bars);
+  const uint32_t j = crank();
+  const int64_t T = p.T, Bt = p.Bt;
+  const int64_t b0 = (int64_t)(blockIdx.x / kWC) * S;
+  const int Bc = (int)min((int64_t)S, Bt - b0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // product: units u0..u0+3 (CTA warp's units), rows k = 4 i + ks, i < 32
+  const int ks = lane >> 3, u0 = 32 * warp + 4 * (lane & 7);
+  const float *wj = p.w + (size_t)j * kWR * kWH;  // [128 rows][512 units]
+  {
+    const float4 *src = reinterpret_cast<const float4 *>(wj + 4 * KR * kWH);
+    for (int i = tid; i < L::KS * kWH / 4; i += kWT) reinterpret_cast<float4 *>(Ws)[i] = src[i];
+  }
+  float wr[4][KR];
+#pragma unroll
+  for (int i = 0; i < KR; ++i) {
+    const float4 v = *reinterpret_cast<const float4 *>(wj + (size_t)(4 * i + ks) * kWH + u0);
+    wr[0][i] = v.x;
+    wr[1][i] = v.y;
+    wr[2][i] = v.z;
+    wr[3][i] = v.w;
+  }
+  if (tid == 0) {
+    cmbar_init(&bars[0], 1);
+    cmbar_init(&bars[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // step T-1 sends into parity (T-2)&1, read by step T-2; one use each to start
+    cmbar_arrive_expect(&bars[0], kWC * bbytes);
+    cmbar_arrive_expect(&bars[1], kWC * bbytes);
+  }
+  __syncthreads();
+  ccluster_sync();
+
+  const bool is_cell = tid < kWUC * S;
+  const int ul = tid & 31, s = tid >> 5;
+  const bool valid = is_cell && s < Bc;
+  const int64_t u = (int64_t)j * kWUC + ul, bb = b0 + s;
+  float dcst = (valid && p.dc_n) ? p.dc_n[bb * H + u] : 0.f;
+  __shared__ int s_fail;
+  int64_t waited = 0;
+  bool fail = false;
+  for (int64_t t = T - 1; t >= 0 && !fail; --t) {
+    const int par = (int)(t & 1);  // the blocks for step t arrived in rx[par]
+    float ld[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // i, f, g, o, c_t, c_{t-1}, dh
+    if (valid) {
+      const float *ar = p.zacts + (t * Bt + bb) * 4 * H + u;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) ld[g] = ar[g * H];
+      ld[4] = p.c_save[((t + 1) * Bt + bb) * H + u];
+      ld[5] = p.c_save[(t * Bt + bb) * H + u];
+      ld[6] = p.dout[(t * Bt + bb) * H + u] + ((t == T - 1 && p.dh_n) ? p.dh_n[bb * H + u] : 0.f);
+    }
+    if (t < T - 1) {
+      const int64_t use = (T - 2 - t) >> 1;
+      if (tid == 0) {
+        s_fail = !cmbar_wait(&bars[par], (uint32_t)(use & 1), p.status);
+        if (!s_fail) {
+          ++waited;
+          if (t - 2 >= 0) cmbar_arrive_expect(&bars[par], kWC * bbytes);
+        }
+      }
+      __syncthreads();
+      if (s_fail) { fail = true; break; }
+    }
+    float dg[4] = {0.f, 0.f, 0.f, 0.f};
+    if (is_cell) {
+      float dh = ld[6];
+      if (t < T - 1) {
+        const float *R = rx + (par * kWC * kWUC + ul) * XS + s;
+#pragma unroll
+        for (int src = 0; src < kWC; ++src) dh += R[src * kWUC * XS];
+      }
+      const float i = ld[0], f = ld[1], g = ld[2], o = ld[3];
+      const float th = tanh_any(ld[4]);
+      const float dct = dcst + dh * o * (1.f - th * th);
+      dg[0] = dct * g * i * (1.f - i);
+      dg[1] = dct * ld[5] * f * (1.f - f);
+      dg[2] = dct * i * g * (1.f - g);
+      dg[3] = dh * th * o * (1.f - o);
+      dcst = dct * f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) DG[(ul * 4 + q) * XS + s] = valid ? dg[q] : 0.f;
+    }
+    __syncthreads();
+    if (t > 0) {
+      // this CTA's rows' share of dh_{t-1} for the units of CTA warp
+      float acc[4][S];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int b = 0; b < S; ++b) acc[r][b] = 0.f;
+#pragma unroll
+      for (int i = 0; i < KR; ++i) {
+        float xv[S];
+        wide_ldx<S, XS>(DG + (4 * i + ks) * XS, xv);
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int b = 0; b < S; ++b) acc[r][b] = fmaf(wr[r][i], xv[b], acc[r][b]);
+      }
+#pragma unroll 4
+      for (int i = KR; i < 32; ++i) {
+        const int k = 4 * i + ks;
+        const float4 wv = *reinterpret_cast<const float4 *>(Ws + (k - 4 * KR) * kWH + u0);
+        const float w4[4] = {wv.x, wv.y, wv.z, wv.w};
+        float xv[S];
+        wide_ldx<S, XS>(DG + k * XS, xv);
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int b = 0; b < S; ++b) acc[r][b] = fmaf(w4[r], xv[b], acc[r][b]);
+      }
+      float v[S];
+      wide_reduce4<S>(acc, lane, v);
+      // staging block par of receiver warp (reused two steps later, after
+      // that receiver has sent blocks that needed this one)
+      float *blk = stage + (par * kWC + warp) * kWUC * XS;
+      wide_stx<S, XS>(blk + (4 * (lane & 7) + ks) * XS, v);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0)
+        cbulk_s2c(cpeer(rx + ((par ^ 1) * kWC + j) * kWUC * XS, (uint32_t)warp), blk, bbytes,
+                  cpeer(&bars[par ^ 1], (uint32_t)warp));
+    }
+    if (valid) {
+      float *ar = p.zacts + (t * Bt + bb) * 4 * H + u;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) ar[q * H] = dg[q];
+    }
+  }
+  if (tid == 0 && fail) {
+    for (int64_t u2 = waited; u2 < std::min<int64_t>(T - 1, waited + 2); ++u2) {
+      const int64_t t2 = T - 2 - u2;  // the step that reads the use-u2 blocks
+      cmbar_drain(&bars[t2 & 1], (uint32_t)(((T - 2 - t2) >> 1) & 1));
+    }
+  }
+  __syncthreads();
+  ccluster_sync();
+}
+
+// Backward weights of the wide kernels: [16][128 rows][512 units], row
+// ul*4+g of CTA jc = a[g] W_hh[g H + 32 jc + ul][u].
+__global__ void rcw_prep_bwd_kernel(const float *__restrict__ w_hh, const float *__restrict__ a,
+                                    float *__restrict__ wb) {
+  const int64_t n = (int64_t)4 * kWH * kWH;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const int64_t uu = i % kWH;
+    const int row = (int)((i / kWH) % kWR);
+    const int64_t jc = i / ((int64_t)kWH * kWR);
+    const int g = row % 4, ul = row / 4;
+    wb[i] = a[g] * w_hh[((int64_t)g * kWH + jc * kWUC + ul) * kWH + uu];
+  }
+}
+
 // Weights of the cluster kernels: forward [C][H][4UC], row ul*4+g =
 // a[g] W_hh[g H + j UC + ul][k]; backward [C][4H][UC], row u*4+g =
 // a[g] W_hh[g H + u][j UC + ul]; bias [C][4UC] = a[g] b_hh[g H + j UC + ul].
@@ -623,6 +1048,117 @@ int rcl_override() {
   return 2;
 }
 
+// ------------------------------------------------------------ wide: host side
+const void *rcw_fn(int dir, int S) {
+#define HS_RCW_CASE(n) \
+  case n:              \
+    return dir ? (const void *)rcw_bwd_kernel<n> : (const void *)rcw_fwd_kernel<n>;
+  switch (S) {
+    HS_RCW_CASE(1) HS_RCW_CASE(2) HS_RCW_CASE(3) HS_RCW_CASE(4)
+    HS_RCW_CASE(5) HS_RCW_CASE(6) HS_RCW_CASE(7) HS_RCW_CASE(8)
+    default: return nullptr;
+  }
+#undef HS_RCW_CASE
+}
+size_t rcw_smem(int dir, int S) {
+#define HS_RCW_CASE(n) \
+  case n:              \
+    return dir ? (size_t)WideBwd<n>::bytes : (size_t)WideFwd<n>::bytes;
+  switch (S) {
+    HS_RCW_CASE(1) HS_RCW_CASE(2) HS_RCW_CASE(3) HS_RCW_CASE(4)
+    HS_RCW_CASE(5) HS_RCW_CASE(6) HS_RCW_CASE(7) HS_RCW_CASE(8)
+    default: return 0;
+  }
+#undef HS_RCW_CASE
+}
+
+// Attributes of one wide kernel (its shared memory, clusters of 16), set once
+// per device so that launches inside a stream capture make no attribute calls.
+std::atomic<unsigned long long> g_rcw_attr[2][kWMaxS + 1];
+int rcw_prepare(int dir, int S) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("cudaGetDevice");
+  std::atomic<unsigned long long> &done = g_rcw_attr[dir][S];
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return HS_OK;
+  const void *fn = rcw_fn(dir, S);
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rcw_smem(dir, S)) != cudaSuccess)
+    return check_launch("cudaFuncSetAttribute(wide recurrent shared memory)");
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+    return check_launch("cudaFuncSetAttribute(non-portable cluster)");
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return HS_OK;
+}
+
+cudaLaunchConfig_t rcw_config(int dir, int S, int ngrp, cudaStream_t st, cudaLaunchAttribute *at) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(kWC * ngrp));
+  cfg.blockDim = dim3(kWT);
+  cfg.dynamicSmemBytes = rcw_smem(dir, S);
+  cfg.stream = st;
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = (unsigned)kWC;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// Clusters of 16 that the device runs at once with the wide kernels (both
+// directions, the largest shared-memory variant; every variant runs one CTA
+// per SM), cached per device; 0 where they do not run.
+int rcw_max_clusters() {
+  static std::mutex mu;
+  static int cache[64];
+  static bool have[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) { (void)cudaGetLastError(); return 0; }
+  std::lock_guard<std::mutex> lock(mu);
+  if (have[dev & 63]) return cache[dev & 63];
+  int best = 1 << 30;
+  for (int d = 0; d < 2; ++d) {
+    int nc = 0;
+    cudaLaunchAttribute at[1];
+    cudaLaunchConfig_t cfg = rcw_config(d, kWMaxS, 1, nullptr, at);
+    if (rcw_prepare(d, kWMaxS) != HS_OK ||
+        cudaOccupancyMaxActiveClusters(&nc, rcw_fn(d, kWMaxS), &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      nc = 0;
+    }
+    best = std::min(best, nc);
+  }
+  cache[dev & 63] = best;
+  have[dev & 63] = true;
+  return best;
+}
+
+// Sequences per cluster: the batch over every cluster that runs at once, at
+// most kWMaxS per cluster.
+bool rcw_plan(int64_t B, int64_t H, int &S, int &ngrp) {
+  if (H != kWH || B <= 0) return false;
+  const int ncl = rcw_max_clusters();
+  if (ncl < 1) return false;
+  const int64_t s = (B + ncl - 1) / ncl;
+  if (s > kWMaxS) return false;
+  S = (int)s;
+  ngrp = (int)((B + S - 1) / S);
+  return true;
+}
+
+size_t rcw_o_bias() { return round_up((size_t)4 * kWH * kWH * 4, 256); }
+size_t rcw_o_wb() { return rcw_o_bias() + round_up((size_t)4 * kWH * 4, 256); }
+
+int rcw_launch(int dir, int S, int ngrp, RwArgs &args, cudaStream_t st) {
+  if (int e = rcw_prepare(dir, S)) return e;
+  cudaLaunchAttribute at[1];
+  cudaLaunchConfig_t cfg = rcw_config(dir, S, ngrp, st, at);
+  void *kargs[] = {&args};
+  if (cudaLaunchKernelExC(&cfg, rcw_fn(dir, S), kargs) != cudaSuccess)
+    return check_launch("cudaLaunchKernelEx(wide recurrent)");
+  return HS_OK;
+}
+
 }  // namespace
 
 bool rec_cluster_wanted(int64_t B, int64_t H) {
@@ -696,6 +1232,72 @@ int rec_cluster_backward(const float *w_hh, const float *a, const float *c_save,
   args.UC = pl.UC;
   const int ngrp = (int)((B + kBC - 1) / kBC);
   return rcl_launch((const void *)rcl_bwd_kernel, pl.C, ngrp, pl.smem_b, &g_rcl_attr[1], args, st);
+}
+
+
+// H = 512 on clusters of 16 with a few sequences per cluster (rcw_* kernels).
+bool rec_wide_wanted(int64_t B, int64_t H) {
+  if (H != kWH || rcl_override() == 2) return false;
+  int S = 0, ngrp = 0;
+  return rcw_plan(B, H, S, ngrp);
+}
+
+size_t rec_wide_ws_bytes(int64_t H) {
+  return H == kWH ? rcw_o_wb() + round_up((size_t)4 * kWH * kWH * 4, 256) : 0;
+}
+
+// acts holds Z on entry (the input projection) and the gate activations on return.
+int rec_wide_forward(const float *h0, const float *c0, const float *w_hh, const float *b_hh, const float *a,
+                     float *h_save, float *c_save, float *acts, int64_t T, int64_t B, int64_t H, void *ws,
+                     size_t ws_bytes, int *status, cudaStream_t st) {
+  int S = 0, ngrp = 0;
+  if (!rcw_plan(B, H, S, ngrp))
+    return fail(HS_ERR_UNSUPPORTED, "recurrent (wide cluster): B=%lld H=%lld", (long long)B, (long long)H);
+  const size_t need = rec_wide_ws_bytes(H);
+  if (!ws || ws_bytes < need || !aligned(ws, 256))
+    return fail(HS_ERR_WORKSPACE, "recurrent (wide cluster): workspace %zu < %zu bytes", ws_bytes, need);
+  char *w = static_cast<char *>(ws);
+  float *wf = reinterpret_cast<float *>(w), *bias = reinterpret_cast<float *>(w + rcw_o_bias());
+  rcl_prep_kernel<<<1024, 256, 0, st>>>(w_hh, b_hh, a, wf, bias, nullptr, H, kWC, kWUC);
+  if (int e = check_launch("rcl_prep_kernel")) return e;
+  RwArgs args{};
+  args.w = wf;
+  args.bias = bias;
+  args.zacts = acts;
+  args.h0 = h0;
+  args.c0 = c0;
+  args.h_save = h_save;
+  args.c_save = c_save;
+  args.status = status;
+  args.T = T;
+  args.Bt = B;
+  return rcw_launch(0, S, ngrp, args, st);
+}
+
+// acts holds the forward's gate activations on entry and dgates on return.
+int rec_wide_backward(const float *w_hh, const float *a, const float *c_save, float *acts, const float *dout,
+                      const float *dh_n, const float *dc_n, int64_t T, int64_t B, int64_t H, void *ws,
+                      size_t ws_bytes, int *status, cudaStream_t st) {
+  int S = 0, ngrp = 0;
+  if (!rcw_plan(B, H, S, ngrp))
+    return fail(HS_ERR_UNSUPPORTED, "recurrent backward (wide cluster): B=%lld H=%lld", (long long)B, (long long)H);
+  const size_t need = rec_wide_ws_bytes(H);
+  if (!ws || ws_bytes < need || !aligned(ws, 256))
+    return fail(HS_ERR_WORKSPACE, "recurrent backward (wide cluster): workspace %zu < %zu bytes", ws_bytes, need);
+  float *wb = reinterpret_cast<float *>(static_cast<char *>(ws) + rcw_o_wb());
+  rcw_prep_bwd_kernel<<<1024, 256, 0, st>>>(w_hh, a, wb);
+  if (int e = check_launch("rcw_prep_bwd_kernel")) return e;
+  RwArgs args{};
+  args.w = wb;
+  args.zacts = acts;
+  args.c_save = const_cast<float *>(c_save);
+  args.dout = dout;
+  args.dh_n = dh_n;
+  args.dc_n = dc_n;
+  args.status = status;
+  args.T = T;
+  args.Bt = B;
+  return rcw_launch(1, S, ngrp, args, st);
 }
 
 }  // namespace hs
