@@ -495,8 +495,8 @@ struct WideFwd {
   static constexpr int o_bias = o_w + KS * kWR;
   static constexpr int o_rx = o_bias + kWR;           // [2][512][XS]
   static constexpr int o_stage = o_rx + 2 * kWH * XS;  // [2][32][XS]
-  static constexpr int o_red = o_stage + 2 * kWUC * XS;  // [4 k groups][128][XS]
-  static constexpr int o_bars = o_red + 4 * kWR * XS;
+  static constexpr int o_red = o_stage + 2 * kWUC * XS;  // [4 k groups][4 gates][S][32 units]
+  static constexpr int o_bars = o_red + ((4 * 4 * S * kWUC + 3) & ~3);
   static constexpr int bytes = (o_bars + 4) * 4;
 };
 template <int S>
@@ -505,15 +505,15 @@ struct WideBwd {
   static constexpr int KR = S <= 4 ? 12 : 14;  // rows per thread in registers
   static constexpr int KS = kWR - 4 * KR;      // rows of the slice in shared memory
   static constexpr int o_w = 0;
-  static constexpr int o_rx = o_w + KS * kWH;                 // [2][16 senders][32][XS]
-  static constexpr int o_stage = o_rx + 2 * kWC * kWUC * XS;  // [2][16 receivers][32][XS]
-  static constexpr int o_dg = o_stage + 2 * kWC * kWUC * XS;  // [128 rows][XS]
+  static constexpr int o_rx = o_w + KS * kWH;                // [2][16 senders][S][32 units]
+  static constexpr int o_stage = o_rx + 2 * kWC * S * kWUC;  // [2][16 receivers][S][32 units]
+  static constexpr int o_dg = o_stage + 2 * kWC * S * kWUC;  // [128 rows g*32+ul][XS]
   static constexpr int o_bars = o_dg + kWR * XS;
   static constexpr int bytes = (o_bars + 4) * 4;
 };
 
 struct RwArgs {
-  const float *w;     // forward [16][512 k][128 rows]; backward [16][128 rows][512 units]
+  const float *w;     // forward [16][512 k][128 rows ul*4+g]; backward [16][128 rows g*32+ul][512 units]
   const float *bias;  // forward [16][128]
   float *zacts;       // forward: Z in, activations out; backward: activations in, dgates out
   const float *h0, *c0;
@@ -533,14 +533,6 @@ HS_DEV void wide_ldx(const float *p, float (&v)[S]) {
   }
 #pragma unroll
   for (int s = 0; s < S; ++s) v[s] = t[s];
-}
-template <int S, int XS>
-HS_DEV void wide_stx(float *p, const float (&v)[S]) {
-  float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int s = 0; s < S; ++s) t[s] = v[s];
-  *reinterpret_cast<float4 *>(p) = make_float4(t[0], t[1], t[2], t[3]);
-  if constexpr (XS == 8) *reinterpret_cast<float4 *>(p + 4) = make_float4(t[4], t[5], t[6], t[7]);
 }
 // Sum of the 4 k subsets of a warp (lanes l, l^8, l^16, l^24), halving the
 // values at each exchange: afterwards lane l holds output 4-block element
@@ -679,7 +671,11 @@ __global__ void __launch_bounds__(kWT, 1) rcw_fwd_kernel(RwArgs p) {
     }
     float v[S];
     wide_reduce4<S>(acc, lane, v);
-    wide_stx<S, XS>(red + (kgw * kWR + r0 + ks) * XS, v);
+    {  // row r0 + ks = unit 8 (warp & 3) + (lane & 7), gate ks: unit-contiguous for the cells' reads
+      float *dst = red + (kgw * 4 + ks) * S * kWUC + 8 * (warp & 3) + (lane & 7);
+#pragma unroll
+      for (int b = 0; b < S; ++b) dst[b * kWUC] = v[b];
+    }
     __syncthreads();
     // cells; h_t into staging block par (outputs no other CTA reads are
     // stored after the send)
@@ -688,11 +684,10 @@ __global__ void __launch_bounds__(kWT, 1) rcw_fwd_kernel(RwArgs p) {
     if (is_cell) {
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
-        const int row = ul * 4 + g;
         float sum = 0.f;
 #pragma unroll
-        for (int kq = 0; kq < 4; ++kq) sum += red[(kq * kWR + row) * XS + s];
-        act[g] = sigf(zg[g] + sum + bias[row]);
+        for (int kq = 0; kq < 4; ++kq) sum += red[((kq * 4 + g) * S + s) * kWUC + ul];
+        act[g] = sigf(zg[g] + sum + bias[ul * 4 + g]);
       }
       const float c = fmaf(act[1], cst, act[0] * act[2]);
       hv = act[3] * tanh_any(c);
@@ -725,7 +720,7 @@ __global__ void __launch_bounds__(kWT, 1) rcw_bwd_kernel(RwArgs p) {
   using L = WideBwd<S>;
   constexpr int XS = L::XS, KR = L::KR;
   constexpr int64_t H = kWH;
-  constexpr uint32_t bbytes = kWUC * XS * 4;  // one block: 32 units x XS
+  constexpr uint32_t bbytes = S * kWUC * 4;  // one block: S sequences x 32 units
   extern __shared__ __align__(16) float smw[];
   float *Ws = smw + L::o_w, *rx = smw + L::o_rx, *stage = smw + L::o_stage, *DG = smw + L::o_dg;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smw + L::o_bars);
@@ -796,9 +791,9 @@ __global__ void __launch_bounds__(kWT, 1) rcw_bwd_kernel(RwArgs p) {
     if (is_cell) {
       float dh = ld[6];
       if (t < T - 1) {
-        const float *R = rx + (par * kWC * kWUC + ul) * XS + s;
+        const float *R = rx + (par * kWC * S + s) * kWUC + ul;
 #pragma unroll
-        for (int src = 0; src < kWC; ++src) dh += R[src * kWUC * XS];
+        for (int src = 0; src < kWC; ++src) dh += R[src * S * kWUC];
       }
       const float i = ld[0], f = ld[1], g = ld[2], o = ld[3];
       const float th = tanh_any(ld[4]);
@@ -809,7 +804,7 @@ __global__ void __launch_bounds__(kWT, 1) rcw_bwd_kernel(RwArgs p) {
       dg[3] = dh * th * o * (1.f - o);
       dcst = dct * f;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) DG[(ul * 4 + q) * XS + s] = valid ? dg[q] : 0.f;
+      for (int q = 0; q < 4; ++q) DG[(q * kWUC + ul) * XS + s] = valid ? dg[q] : 0.f;
     }
     __syncthreads();
     if (t > 0) {
@@ -844,12 +839,13 @@ __global__ void __launch_bounds__(kWT, 1) rcw_bwd_kernel(RwArgs p) {
       wide_reduce4<S>(acc, lane, v);
       // staging block par of receiver warp (reused two steps later, after
       // that receiver has sent blocks that needed this one)
-      float *blk = stage + (par * kWC + warp) * kWUC * XS;
-      wide_stx<S, XS>(blk + (4 * (lane & 7) + ks) * XS, v);
+      float *blk = stage + (par * kWC + warp) * S * kWUC;
+#pragma unroll
+      for (int b = 0; b < S; ++b) blk[b * kWUC + 4 * (lane & 7) + ks] = v[b];
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0)
-        cbulk_s2c(cpeer(rx + ((par ^ 1) * kWC + j) * kWUC * XS, (uint32_t)warp), blk, bbytes,
+        cbulk_s2c(cpeer(rx + ((par ^ 1) * kWC + j) * S * kWUC, (uint32_t)warp), blk, bbytes,
                   cpeer(&bars[par ^ 1], (uint32_t)warp));
     }
     if (valid) {
@@ -869,7 +865,7 @@ __global__ void __launch_bounds__(kWT, 1) rcw_bwd_kernel(RwArgs p) {
 }
 
 // Backward weights of the wide kernels: [16][128 rows][512 units], row
-// ul*4+g of CTA jc = a[g] W_hh[g H + 32 jc + ul][u].
+// g*32+ul of CTA jc = a[g] W_hh[g H + 32 jc + ul][u].
 __global__ void rcw_prep_bwd_kernel(const float *__restrict__ w_hh, const float *__restrict__ a,
                                     float *__restrict__ wb) {
   const int64_t n = (int64_t)4 * kWH * kWH;
@@ -878,7 +874,7 @@ __global__ void rcw_prep_bwd_kernel(const float *__restrict__ w_hh, const float 
     const int64_t uu = i % kWH;
     const int row = (int)((i / kWH) % kWR);
     const int64_t jc = i / ((int64_t)kWH * kWR);
-    const int g = row % 4, ul = row / 4;
+    const int g = row / kWUC, ul = row % kWUC;
     wb[i] = a[g] * w_hh[((int64_t)g * kWH + jc * kWUC + ul) * kWH + uu];
   }
 }
