@@ -489,7 +489,7 @@ constexpr int kWMaxS = 8;             // sequences per cluster
 template <int S>
 struct WideFwd {
   static constexpr int XS = S <= 4 ? 4 : 8;  // floats per state row
-  static constexpr int KR = 12;              // k values per thread in registers
+  static constexpr int KR = S <= 6 ? 16 : 12;  // k values per thread in registers (no spills)
   static constexpr int KS = kWH - 16 * KR;   // k rows of the slice in shared memory
   static constexpr int o_w = 0;
   static constexpr int o_bias = o_w + KS * kWR;
