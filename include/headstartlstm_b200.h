@@ -415,9 +415,11 @@ HS_API size_t hs_recurrent_workspace_bytes(int64_t T, int64_t B, int64_t D, int6
 HS_API int hs_recurrent_uses_tensor_cores(int64_t B, int64_t H, int backward);
 /* Diagnostic: which kernels run the recurrence of this B, H on the current
  * device: 0 FFMA kernels over the whole GPU (one grid barrier per step),
- * 1 tensor-core kernels, 2 one thread-block cluster per batch group of 32
- * sequences with the weights resident and the state exchanged in
- * distributed shared memory (H <= 128); -1 for bad arguments.
+ * 1 tensor-core kernels, 2 thread-block clusters with the weights resident
+ * and the state exchanged in distributed shared memory: one cluster per
+ * batch group of 32 sequences for H <= 128, and for H = 512 clusters of 16
+ * CTAs with up to 8 sequences each, the batch spread over the clusters the
+ * device runs at once (B up to 8 times that count); -1 for bad arguments.
  * HS_REC_PATH=ffma|tc|cluster forces one where it applies. */
 HS_API int hs_recurrent_path(int64_t B, int64_t H, int backward);
 
