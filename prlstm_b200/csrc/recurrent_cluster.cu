@@ -1130,14 +1130,13 @@ int rcw_max_clusters() {
 }
 
 // Sequences per cluster: the batch over every cluster that runs at once, at
-// most kWMaxS per cluster.
+// most kWMaxS per cluster; a larger batch runs as further waves of clusters
+// (independent of one another: a cluster waits only on its own CTAs).
 bool rcw_plan(int64_t B, int64_t H, int &S, int &ngrp) {
   if (H != kWH || B <= 0) return false;
   const int ncl = rcw_max_clusters();
   if (ncl < 1) return false;
-  const int64_t s = (B + ncl - 1) / ncl;
-  if (s > kWMaxS) return false;
-  S = (int)s;
+  S = (int)std::min<int64_t>((B + ncl - 1) / ncl, kWMaxS);
   ngrp = (int)((B + S - 1) / S);
   return true;
 }

@@ -8,9 +8,10 @@ kernels (HS_REC_PATH=ffma), through the module API.
 Shapes: configs[2] (T=256, B=32, D=256, H=512); batches that give every
 sequence count per cluster from 1 to 8 on a device running 7 or 8 such
 clusters at once (B = 5, 13, 20, 28, 40, 49, 56), with a partial last
-cluster; T=1 and T=2 (the shortest barrier sequences); a non-zero initial
-state and gradients entering through h_n and c_n.  Bound: 1e-5 normwise,
-the recurrent-mode bound of every parity test.
+cluster; batches beyond 8 sequences per cluster, run as a second wave of
+clusters (B = 64, 100); T=1 and T=2 (the shortest barrier sequences); a
+non-zero initial state and gradients entering through h_n and c_n.  Bound:
+1e-5 normwise, the recurrent-mode bound of every parity test.
 """
 
 import pytest
@@ -28,6 +29,8 @@ CASES = [
     (7, 40, 16, 512, 0.4),
     (4, 49, 16, 512, None),
     (12, 56, 32, 512, 0.4),
+    (5, 64, 16, 512, 0.3),
+    (3, 100, 16, 512, None),
     (1, 3, 8, 512, 0.2),
     (2, 7, 8, 512, 0.2),
 ]
