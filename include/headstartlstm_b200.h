@@ -419,8 +419,8 @@ HS_API int hs_recurrent_uses_tensor_cores(int64_t B, int64_t H, int backward);
  * and the state exchanged in distributed shared memory: one cluster per
  * batch group of 32 sequences for H <= 128, and for H = 512 clusters of 16
  * CTAs with up to 8 sequences each, the batch spread over the clusters the
- * device runs at once (larger batches as further waves of clusters); -1 for
- * bad arguments.
+ * device runs at once (B up to 8 times that count; HS_REC_PATH=cluster also
+ * runs larger batches, as further waves of clusters); -1 for bad arguments.
  * HS_REC_PATH=ffma|tc|cluster forces one where it applies. */
 HS_API int hs_recurrent_path(int64_t B, int64_t H, int backward);
 

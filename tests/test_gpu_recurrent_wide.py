@@ -9,10 +9,12 @@ Shapes: configs[2] (T=256, B=32, D=256, H=512); batches that give every
 sequence count per cluster from 1 to 8 on a device running 7 or 8 such
 clusters at once (B = 5, 13, 20, 28, 40, 49, 56), with a partial last
 cluster; batches beyond 8 sequences per cluster, run as a second wave of
-clusters (B = 64, 100); T=1 and T=2 (the shortest barrier sequences); a
+clusters (B = 64, 100; HS_REC_PATH=cluster, not the default there); T=1 and T=2 (the shortest barrier sequences); a
 non-zero initial state and gradients entering through h_n and c_n.  Bound:
 1e-5 normwise, the recurrent-mode bound of every parity test.
 """
+
+import os
 
 import pytest
 
@@ -41,7 +43,17 @@ def test_wide_cluster_recurrence_matches_float64_and_ffma(T, B, D, H, a):
     from prlstm_b200 import _lib
 
     lib = _lib.load()
-    assert lib.hs_recurrent_path(B, H, 0) == 2 and lib.hs_recurrent_path(B, H, 1) == 2
+    if B == 32:  # configs[2]: the default path
+        assert lib.hs_recurrent_path(B, H, 0) == 2 and lib.hs_recurrent_path(B, H, 1) == 2
+    old = os.environ.get("HS_REC_PATH")
+    os.environ["HS_REC_PATH"] = "cluster"
+    try:
+        assert lib.hs_recurrent_path(B, H, 0) == 2 and lib.hs_recurrent_path(B, H, 1) == 2
+    finally:
+        if old is None:
+            os.environ.pop("HS_REC_PATH", None)
+        else:
+            os.environ["HS_REC_PATH"] = old
     prob = _problem(T, B, D, H, a, seed=T * 1000 + B * 10 + H + 11)
     truth = _truth(*prob)
     cl = _ours(*prob, path="cluster")
